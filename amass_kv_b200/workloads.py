@@ -1,0 +1,262 @@
+"""Seeded synthetic decode workloads with the reference's tensor layouts.
+
+The reference measures on real model KV caches; this build stands in seeded
+synthetic inputs with the shapes, sizes and value distributions that the
+benchmark configurations describe (K ~ N(0,1) with a few outlier channels,
+V ~ N(0,1), planted "heavy" pages whose keys are shifted toward the query,
+randomly permuted block tables drawn from one shared page pool).
+
+Two families:
+  * ``make_quad_case`` / ``make_r8_case`` (numpy, CPU): small, internally
+    consistent cases whose page summaries are computed from the keys (page
+    mean, a per-head orthonormal rank-r basis from a seeded QR, eigenvalue-style
+    scatter sig2_k = sum_t ((k_t - mu) . b_k)^2), quantised like
+    ``selection/build.py:297-348`` (symmetric round-half-even, +/-127 or +/-7
+    levels, amax/lvl scales clamped to >= 1e-8).  Used by tests and fixtures.
+  * ``make_quad_case_gpu`` (torch, on a CUDA device): full-size benchmark
+    batches built directly in HBM (codes and scales drawn at random -- the
+    Stage-A/B cost does not depend on summary values under a fixed budget).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+
+
+# --------------------------------------------------------------------------- #
+# helpers                                                                     #
+# --------------------------------------------------------------------------- #
+def _bf16(x):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    u = x.view(np.uint32).astype(np.uint64)
+    u = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+    return u.astype(np.uint32).view(np.float32)
+
+
+def quantize(x, axis, bits):
+    """code = round_half_even(x / s), s = max(amax(|x|, axis) / lvl, 1e-8)."""
+    lvl = float((1 << (bits - 1)) - 1)
+    amax = np.abs(x).max(axis=axis, keepdims=True)
+    s = np.maximum(amax / lvl, 1e-8).astype(np.float32)
+    code = np.clip(np.round(x / s), -lvl, lvl).astype(np.int8)
+    return code, s
+
+
+def pack_int4(code):
+    c = code.astype(np.int32) & 0xF
+    return (c[..., 0::2] | (c[..., 1::2] << 4)).astype(np.uint8).view(np.int8)
+
+
+def log_uniform_contexts(rng, n, lo, hi):
+    """ctx = floor(exp(U(ln lo, ln hi))) -- the ragged C3 context draw."""
+    return np.floor(np.exp(rng.uniform(math.log(lo), math.log(hi), n))
+                    ).astype(np.int64)
+
+
+@dataclass
+class QuadCase:
+    """One layer's worth of decode inputs in the reference layouts."""
+    q: np.ndarray            # (n_req, H, d) float32 holding bf16 values
+    K: np.ndarray            # (NB, page, n_kv, d) float32 holding bf16 values
+    V: np.ndarray            # (NB, page, n_kv, d)
+    block_table: np.ndarray  # (n_req, max_blocks) int32
+    seq_lens: np.ndarray     # (n_req,) int32
+    mu: np.ndarray           # (NB, n_kv, d) int8
+    mu_s: np.ndarray         # (NB, n_kv) float16
+    Vq: np.ndarray           # (NB, n_kv, d, rv) int8
+    V_s: np.ndarray          # (NB, n_kv, r) float16
+    sig2: np.ndarray         # (NB, n_kv, r) float16
+    G: int
+    r: int
+    v_bits: int
+    page: int
+    MP: int
+    scale: float
+    extra: dict = field(default_factory=dict)
+
+    @property
+    def n_kv(self):
+        return self.K.shape[2]
+
+    @property
+    def d(self):
+        return self.K.shape[3]
+
+
+def _layout(rng, ctxs, page, slack, max_pages):
+    npg = [(int(c) + page - 1) // page for c in ctxs]
+    NB = sum(npg) + slack
+    perm = rng.permutation(NB).astype(np.int32)
+    MP = max_pages if max_pages else max(npg)
+    bt = np.zeros((len(ctxs), MP), dtype=np.int32)
+    o = 0
+    for i, n in enumerate(npg):
+        bt[i, :n] = perm[o:o + n]
+        o += n
+    return NB, bt, MP
+
+
+def summarize_quad(K, basis, r, v_bits):
+    """Page summaries from keys: mean, per-head basis, scatter eigenvalues."""
+    Kf = K.astype(np.float64)
+    mu = Kf.mean(axis=1)                                     # (NB, kv, d)
+    Kc = Kf - mu[:, None]
+    proj = np.einsum("btkd,kdr->btkr", Kc, basis)            # (NB, page, kv, r)
+    sig2 = (proj ** 2).sum(axis=1)                           # (NB, kv, r)
+    mu_code, mu_s = quantize(mu.astype(np.float32), -1, 8)
+    Vb = np.broadcast_to(basis[None], (K.shape[0],) + basis.shape)
+    v_code, v_s = quantize(Vb.astype(np.float32), -2, v_bits)
+    if v_bits == 4:
+        v_code = pack_int4(v_code)
+    return (mu_code, mu_s[..., 0].astype(np.float16), v_code,
+            v_s[:, :, 0, :].astype(np.float16), sig2.astype(np.float16))
+
+
+def make_quad_case(seed=0, *, n_req=2, n_kv=2, G=4, d=64, page=16,
+                   ctxs=(2048, 2048), r=8, v_bits=8, slack=8, heavy=4,
+                   shift=2.0, outlier_frac=0.0, outlier_mult=8.0,
+                   max_pages=None, sink=1, window=1):
+    """Small consistent quad case (BASELINE C1 shape by default)."""
+    rng = np.random.default_rng(seed)
+    NB, bt, MP = _layout(rng, ctxs, page, slack, max_pages)
+    H = n_kv * G
+    K = rng.standard_normal((NB, page, n_kv, d)).astype(np.float32)
+    V = rng.standard_normal((NB, page, n_kv, d)).astype(np.float32)
+    if outlier_frac > 0:
+        n_out = max(1, int(round(outlier_frac * d)))
+        for kv in range(n_kv):
+            ch = rng.choice(d, n_out, replace=False)
+            K[:, :, kv, ch] *= outlier_mult
+    q = _bf16(rng.standard_normal((len(ctxs), H, d)).astype(np.float32))
+    planted = np.zeros((len(ctxs), n_kv, MP), dtype=bool)
+    for i, c in enumerate(ctxs):
+        npg = (int(c) + page - 1) // page
+        nsh = npg - window
+        if nsh - sink < heavy + 1:
+            continue
+        for kv in range(n_kv):
+            qh = q[i, kv * G:(kv + 1) * G].mean(axis=0)
+            qh = qh / (np.linalg.norm(qh) + 1e-12)
+            pages = sink + rng.permutation(nsh - sink)[:heavy]
+            planted[i, kv, pages] = True
+            for p in pages:
+                K[bt[i, p], :, kv, :] += shift * qh
+    K = _bf16(K)
+    V = _bf16(V)
+    basis = np.stack([np.linalg.qr(rng.standard_normal((d, r)))[0]
+                      for _ in range(n_kv)]).astype(np.float64)   # (kv, d, r)
+    mu, mu_s, Vq, V_s, sig2 = summarize_quad(K, basis, r, v_bits)
+    return QuadCase(q=q, K=K, V=V, block_table=bt,
+                    seq_lens=np.asarray(ctxs, dtype=np.int32), mu=mu,
+                    mu_s=mu_s, Vq=Vq, V_s=V_s, sig2=sig2, G=G, r=r,
+                    v_bits=v_bits, page=page, MP=MP, scale=1.0 / math.sqrt(d),
+                    extra=dict(planted=planted, basis=basis))
+
+
+@dataclass
+class R8Case:
+    q: np.ndarray
+    K: np.ndarray
+    V: np.ndarray
+    block_table: np.ndarray
+    seq_lens: np.ndarray
+    mu: np.ndarray           # (NB, n_kv, d) int8
+    mu_s: np.ndarray         # (NB, n_kv) fp16
+    Vk: np.ndarray           # (NB, n_kv, d, rv) int8
+    Vk_s: np.ndarray         # (NB, n_kv, r) fp16
+    c: np.ndarray            # (NB, n_kv, page, rc) int8
+    c_s: np.ndarray          # (NB, n_kv, page) fp16
+    G: int
+    r: int
+    vk_bits: int
+    c_bits: int
+    page: int
+    MP: int
+    scale: float
+
+
+def make_r8_case(seed=0, *, n_req=2, n_kv=2, G=4, d=64, page=16,
+                 ctxs=(1024, 700), r=8, vk_bits=8, c_bits=8, c_grain="page",
+                 slack=4, heavy=4, shift=2.0, max_pages=None):
+    """Small consistent r8 case: per-head basis, centered coordinates c."""
+    base = make_quad_case(seed, n_req=n_req, n_kv=n_kv, G=G, d=d, page=page,
+                          ctxs=ctxs, r=r, v_bits=8, slack=slack, heavy=heavy,
+                          shift=shift, max_pages=max_pages)
+    K = base.K.astype(np.float64)
+    basis = base.extra["basis"]
+    mu = K.mean(axis=1)
+    coords = np.einsum("btkd,kdr->bktr", K - mu[:, None], basis)   # (NB,kv,t,r)
+    mu_code, mu_s = quantize(mu.astype(np.float32), -1, 8)
+    Vb = np.broadcast_to(basis[None], (K.shape[0],) + basis.shape)
+    vk_code, vk_s = quantize(Vb.astype(np.float32), -2, vk_bits)
+    if vk_bits == 4:
+        vk_code = pack_int4(vk_code)
+    if c_grain == "page":
+        c_code, c_sc = quantize(coords.astype(np.float32), -1, c_bits)
+        c_sc = c_sc[..., 0]
+    else:
+        c_code, c_sc = quantize(coords.astype(np.float32), (-2, -1), c_bits)
+        c_sc = np.broadcast_to(c_sc[..., 0], coords.shape[:-1]).copy()
+    if c_bits == 4:
+        c_code = pack_int4(c_code)
+    return R8Case(q=base.q, K=base.K, V=base.V, block_table=base.block_table,
+                  seq_lens=base.seq_lens, mu=mu_code,
+                  mu_s=mu_s[..., 0].astype(np.float16), Vk=vk_code,
+                  Vk_s=vk_s[:, :, 0, :].astype(np.float16), c=c_code,
+                  c_s=c_sc.astype(np.float16), G=G, r=r, vk_bits=vk_bits,
+                  c_bits=c_bits, page=page, MP=base.MP, scale=base.scale)
+
+
+# --------------------------------------------------------------------------- #
+# full-size GPU batches (benchmark)                                           #
+# --------------------------------------------------------------------------- #
+def c3_contexts(seed, n_req=64, lo=4096, hi=65536):
+    """BASELINE C3 ragged contexts: log-uniform on [4K, 64K]."""
+    rng = np.random.default_rng(seed)
+    return log_uniform_contexts(rng, n_req, lo, hi)
+
+
+def make_quad_case_gpu(device, *, seed, ctxs, n_kv=8, G=4, d=128, page=16,
+                       r=2, v_bits=4, layers=1, slack=64, max_pages=None):
+    """Full-size decode batch resident in HBM, reference layouts:
+    kv_cache (L, NB, 2, page, n_kv, d) bf16; quad slabs (L, NB, n_kv, ...);
+    block_table rows drawn from one shared random permutation of NB."""
+    import torch
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    npg = [(int(c) + page - 1) // page for c in ctxs]
+    NB = sum(npg) + slack
+    MP = max_pages if max_pages else max(npg)
+    perm = torch.randperm(NB, generator=g).to(torch.int32)
+    bt = torch.zeros(len(ctxs), MP, dtype=torch.int32)
+    o = 0
+    for i, n in enumerate(npg):
+        bt[i, :n] = perm[o:o + n]
+        o += n
+    dev = torch.device(device)
+    gd = torch.Generator(device=dev).manual_seed(seed + 1)
+    rv = r // 2 if v_bits == 4 else r
+    kv = torch.empty((layers, NB, 2, page, n_kv, d), dtype=torch.bfloat16,
+                     device=dev)
+    for l in range(layers):
+        kv[l].normal_(generator=gd)
+    lvl = 7 if v_bits == 4 else 127
+    st = dict(
+        quad_mu=torch.randint(-127, 128, (layers, NB, n_kv, d), generator=gd,
+                              device=dev, dtype=torch.int8),
+        mu_scale=(torch.rand((layers, NB, n_kv), generator=gd, device=dev)
+                  * 0.02 + 0.005).half(),
+        quad_V=torch.randint(-128, 128, (layers, NB, n_kv, d, rv),
+                             generator=gd, device=dev, dtype=torch.int8),
+        V_scale=(torch.rand((layers, NB, n_kv, r), generator=gd, device=dev)
+                 * (0.3 / lvl) + 0.01 / lvl).half(),
+        quad_sig2=(torch.rand((layers, NB, n_kv, r), generator=gd, device=dev)
+                   * 40 + 1).half(),
+    )
+    q = torch.randn((layers, len(ctxs), n_kv * G, d), generator=gd, device=dev
+                    ).to(torch.bfloat16)
+    return dict(kv_cache=kv, q=q, block_table=bt.to(dev),
+                seq_lens=torch.as_tensor(np.asarray(ctxs), dtype=torch.int32,
+                                         device=dev),
+                NB=NB, MP=MP, **st)

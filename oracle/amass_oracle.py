@@ -1,0 +1,491 @@
+"""CPU oracle for the AMASS decode-time sparse paged-attention hot path.
+
+TEST INFRASTRUCTURE ONLY.  This module is the checker the parity tests, the
+``__graft_entry__.smoke()`` check and the ``cpu_baseline`` / ``--impl reference``
+legs of ``bench.py`` compare against.  The shipped product path
+(``amass_kv_b200``) never imports it and has no CPU fallback.
+
+Every function is a numpy restatement of the reference algorithm (Python +
+Triton in Js-Hwang1/amass-kv, ``src/amass/...``); each docstring cites the
+file:line it follows.  Pinning: ``tests/test_oracle_golden.py`` checks these
+functions against golden vectors produced by the reference's own Triton kernels
+(run under ``TRITON_INTERPRET=1`` on CPU by ``tests/golden/make_golden.py``).
+
+Conventions (identical to the reference's tensors):
+  q           (T, H, d)           bf16 values held as float32
+  block_table (n_req, max_blocks) int32
+  quad_mu     (NB, n_kv, d) int8          mu_scale (NB, n_kv) fp16
+  quad_V      (NB, n_kv, d, rv) int8      V_scale  (NB, n_kv, r)  fp16
+              rv = r (int8 codes) or r//2 (two signed nibbles per byte:
+              low nibble = even column, high nibble = odd column)
+  quad_sig2   (NB, n_kv, r) fp16
+  K, V        (NB, page, n_kv, d)  bf16 values held as float32
+  score       (R, n_kv, MP) fp32; page_table (R, n_kv, MP) int32 (-1 pad)
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+F32 = np.float32
+
+
+# --------------------------------------------------------------------------- #
+# small helpers                                                               #
+# --------------------------------------------------------------------------- #
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """Round float32 to the nearest bf16 (ties to even), returned as float32."""
+    x = np.ascontiguousarray(x, dtype=F32)
+    u = x.view(np.uint32).astype(np.uint64)
+    lsb = (u >> 16) & 1
+    u = ((u + 0x7FFF + lsb) >> 16) << 16
+    out = u.astype(np.uint32).view(F32)
+    return np.where(np.isnan(x), x, out).astype(F32)
+
+
+def unpack_codes(codes: np.ndarray, r: int, bits: int) -> np.ndarray:
+    """int8 codes (..., rv) -> signed integer codes (..., r) as float32.
+
+    int4 packing follows ``selection/build.py:304-312`` (low nibble = column
+    2j, high nibble = column 2j+1) as read back by
+    ``selection/quad_score.py:75-83``."""
+    c = codes.astype(np.int32)
+    if bits == 8:
+        return c[..., :r].astype(F32)
+    lo = c & 0xF
+    hi = (c >> 4) & 0xF
+    lo = np.where(lo >= 8, lo - 16, lo)
+    hi = np.where(hi >= 8, hi - 16, hi)
+    out = np.empty(c.shape[:-1] + (c.shape[-1] * 2,), dtype=np.int32)
+    out[..., 0::2] = lo
+    out[..., 1::2] = hi
+    return out[..., :r].astype(F32)
+
+
+def pack_int4(codes: np.ndarray) -> np.ndarray:
+    """Signed int codes in [-8, 7] (..., r) -> packed int8 (..., r//2)."""
+    c = codes.astype(np.int32) & 0xF
+    packed = c[..., 0::2] | (c[..., 1::2] << 4)
+    return packed.astype(np.uint8).view(np.int8)
+
+
+# --------------------------------------------------------------------------- #
+# a2: derive_page_params  (selection/select.py:30-45)                         #
+# --------------------------------------------------------------------------- #
+def derive_page_params(seq_lens, budget: float, page: int, window: int,
+                       sink: int):
+    """npg = ceil(sl/page); n_sel_hi = npg - window;
+    b = clamp(ceil(fp64(n_sel_hi - sink) * budget), 1, max(n_sel, 1))
+    (``selection/select.py:30-45``)."""
+    sl = np.asarray(seq_lens, dtype=np.int64)
+    npg = (sl + page - 1) // page
+    nsh = npg - window
+    s = nsh - sink
+    bf = np.ceil(s.astype(np.float64) * np.float64(budget)).astype(np.int64)
+    b = np.minimum(np.maximum(bf, 1), np.maximum(s, 1))
+    return npg.astype(np.int32), nsh.astype(np.int32), b.astype(np.int32)
+
+
+# --------------------------------------------------------------------------- #
+# a3: quad page score  (selection/quad_score.py:35-107)                       #
+# --------------------------------------------------------------------------- #
+def quad_score_h(q, mu, mu_s, V, V_s, sig2, block_table, n_sel_hi, *,
+                 scale: float, page: int, G: int, r: int, v_bits: int,
+                 MP: int):
+    """Per-head quad score S[g] for every scored page p < n_sel_hi.
+
+        q~   = V^T q_g                    V = V_code * V_scale (per column)
+        quad = (s^2 / 2P) * sum_k sig2_k q~_k^2
+        S_g  = s * mu.q_g + quad          mu = mu_code * mu_scale
+
+    (``selection/quad_score.py:55-107``).  Returns (R, n_kv, G, MP) float32,
+    NaN where no score is written (p >= n_sel_hi)."""
+    n_req = block_table.shape[0]
+    n_kv = mu.shape[1]
+    d = mu.shape[2]
+    out = np.full((n_req, n_kv, G, MP), np.nan, dtype=F32)
+    coef = F32(F32(scale) * F32(scale) * F32(1.0 / (2.0 * page)))
+    for rq in range(n_req):
+        nsh = int(n_sel_hi[rq])
+        if nsh <= 0:
+            continue
+        blks = block_table[rq, :nsh].astype(np.int64)
+        qg = q[rq].reshape(n_kv, G, d).astype(F32)                    # (kv,G,d)
+        mu_f = mu[blks].astype(F32) * mu_s[blks].astype(F32)[..., None]
+        Vc = unpack_codes(V[blks], r, v_bits)                          # (P,kv,d,r)
+        Vf = Vc * V_s[blks].astype(F32)[:, :, None, :]
+        s2 = sig2[blks].astype(F32)                                    # (P,kv,r)
+        qt = np.einsum("kgd,pkdr->pkgr", qg, Vf, dtype=F32)            # (P,kv,G,r)
+        quad = np.sum(s2[:, :, None, :] * qt * qt, axis=-1, dtype=F32) * coef
+        qmu = np.einsum("kgd,pkd->pkg", qg, mu_f, dtype=F32) * F32(scale)
+        S = (qmu + quad).astype(F32)                                   # (P,kv,G)
+        out[rq, :, :, :nsh] = S.transpose(1, 2, 0)
+    return out
+
+
+def combine_max(score_h, n_sel_hi):
+    """kv-union group max: score = max_g S[g] (``quad_score.py:104-105``)."""
+    return np.max(score_h, axis=2)
+
+
+def combine_nrm(score_h, n_sel_hi):
+    """nrm combine: hmax_g = max_{p<n_sel_hi} S_g[p];
+    score[p] = sum_g exp(S_g[p] - hmax_g)
+    (``selection/quad_score.py:276-315``)."""
+    R, n_kv, G, MP = score_h.shape
+    out = np.full((R, n_kv, MP), np.nan, dtype=F32)
+    for rq in range(R):
+        nsh = int(n_sel_hi[rq])
+        if nsh <= 0:
+            continue
+        S = score_h[rq, :, :, :nsh]
+        hm = S.max(axis=-1, keepdims=True)
+        out[rq, :, :nsh] = np.sum(np.exp(S - hm), axis=1, dtype=F32)
+    return out
+
+
+# --------------------------------------------------------------------------- #
+# a5: top-b threshold select  (selection/select.py:60-101)                    #
+# --------------------------------------------------------------------------- #
+def _threshold_keep(sc, n_pages, n_sel_hi, sink, b):
+    """keep mask over pages [0, n_pages) for one (req, kv) unit."""
+    P = max(int(n_pages), 0)
+    keep = np.zeros(P, dtype=bool)
+    if P == 0:
+        return keep
+    nsh = int(n_sel_hi)
+    keep_all = (nsh - sink) <= 1
+    offs = np.arange(P)
+    always = (offs < sink) | (offs >= nsh)
+    if keep_all:
+        return np.ones(P, dtype=bool)
+    sel = sc[sink:nsh]
+    srt = np.sort(sel)[::-1]
+    tau = srt[int(b) - 1]
+    selmask = (offs >= sink) & (offs < nsh)
+    sc_full = np.full(P, -np.inf, dtype=F32)
+    sc_full[:nsh] = sc[:nsh]
+    keep = (selmask & (sc_full >= tau)) | always
+    return keep
+
+
+def topb_select(score, n_pages, n_sel_hi, b_fix, *, sink: int, MP: int):
+    """tau = b-th largest score over the selectable region [sink, n_sel_hi);
+    keep = (selectable & score >= tau) | p < sink | p >= n_sel_hi | n_sel <= 1;
+    ascending compaction, -1 pad to MP (``selection/select.py:60-101``)."""
+    R, n_kv = score.shape[0], score.shape[1]
+    tab = np.full((R, n_kv, MP), -1, dtype=np.int32)
+    cnt = np.zeros((R, n_kv), dtype=np.int32)
+    for rq in range(R):
+        for kh in range(n_kv):
+            keep = _threshold_keep(score[rq, kh], n_pages[rq], n_sel_hi[rq],
+                                   sink, b_fix[rq])
+            idx = np.nonzero(keep)[0].astype(np.int32)
+            tab[rq, kh, :idx.size] = idx
+            cnt[rq, kh] = idx.size
+    return tab, cnt
+
+
+# --------------------------------------------------------------------------- #
+# a6: per-(req, kv-head) coverage (nucleus) select                            #
+#     semantic source: backend/_selection_bridge.py:95-99,117-133             #
+# --------------------------------------------------------------------------- #
+def page_mass(score_row, n_sel_hi, combine: str):
+    """Non-negative page mass over the scored region [0, n_sel_hi):
+    ``nrm`` scores are already mass sums (``quad_score.py:293-315``);
+    ``max`` scores are log-masses, turned into exp(score - max)."""
+    s = score_row[:n_sel_hi].astype(np.float64)
+    if combine == "nrm":
+        return s
+    return np.exp(s - s.max())
+
+
+def nucleus_b(mass, sink: int, n_sel_hi: int, coverage: float) -> int:
+    """Smallest b such that the top-b selectable pages (descending mass) hold
+    ``coverage`` of the scored mass minus the always-kept sink share; the
+    per-unit form of ``_nucleus_b`` (``_selection_bridge.py:117-133``):
+    need = max(coverage - always, 0), always = sink mass / total."""
+    n_sel = n_sel_hi - sink
+    total = mass.sum()
+    always = mass[:sink].sum()
+    need = max(coverage * total - always, 0.0)
+    sp = np.sort(mass[sink:n_sel_hi])[::-1]
+    csum = np.cumsum(sp)
+    hit = np.nonzero(csum >= need)[0]
+    b = int(hit[0]) + 1 if hit.size else n_sel
+    return max(1, min(b, max(n_sel, 1)))
+
+
+def coverage_select(score, n_pages, n_sel_hi, *, sink: int, MP: int,
+                    coverage: float, combine: str):
+    """Per-(req, kv-head) nucleus b_u, then the top-b threshold rule of
+    ``select.py:76-101`` with b = b_u.  Returns (page_table, page_cnt, b_u)."""
+    R, n_kv = score.shape[0], score.shape[1]
+    tab = np.full((R, n_kv, MP), -1, dtype=np.int32)
+    cnt = np.zeros((R, n_kv), dtype=np.int32)
+    bu = np.zeros((R, n_kv), dtype=np.int32)
+    for rq in range(R):
+        nsh = int(n_sel_hi[rq])
+        for kh in range(n_kv):
+            if nsh - sink <= 1:
+                b = 1
+            else:
+                m = page_mass(score[rq, kh], nsh, combine)
+                b = nucleus_b(m, sink, nsh, coverage)
+            bu[rq, kh] = b
+            keep = _threshold_keep(score[rq, kh], n_pages[rq], nsh, sink, b)
+            idx = np.nonzero(keep)[0].astype(np.int32)
+            tab[rq, kh, :idx.size] = idx
+            cnt[rq, kh] = idx.size
+    return tab, cnt, bu
+
+
+def selection_diff_ok(tab_a, cnt_a, tab_b, cnt_b, score, tau_tol=1e-3):
+    """True when two selections differ only on pages whose score lies within
+    ``tau_tol`` (relative, floor 1) of the smallest kept selectable score --
+    the tie band the parity contract allows."""
+    R, n_kv = cnt_a.shape
+    for rq in range(R):
+        for kh in range(n_kv):
+            a = set(tab_a[rq, kh, :cnt_a[rq, kh]].tolist())
+            b = set(tab_b[rq, kh, :cnt_b[rq, kh]].tolist())
+            diff = a ^ b
+            if not diff:
+                continue
+            both = sorted(a & b)
+            sc = score[rq, kh]
+            vals = [sc[p] for p in both if np.isfinite(sc[p])]
+            tau = min(vals) if vals else 0.0
+            for p in diff:
+                if not (abs(float(sc[p]) - float(tau))
+                        <= tau_tol * max(1.0, abs(float(tau)))):
+                    return False
+    return True
+
+
+# --------------------------------------------------------------------------- #
+# a7: sparse paged decode over the selected pages (+ LSE merge)               #
+#     attention/decode.py:145-241, attention/merge.py:30-50                   #
+# --------------------------------------------------------------------------- #
+def sparse_decode(q, K, V, block_table, seq_lens, page_table, page_cnt, *,
+                  scale: float, G: int):
+    """Exact fp32 softmax attention of each query head over the tokens of its
+    kv-head's selected pages (tokens >= seq_len masked).  Split-K + LSE merge
+    (``decode.py:145-241`` + ``merge.py:30-50``) is an exact re-association
+    of this; an empty selection writes 0 (``merge.py:47-48``).
+    Returns (n_req, H, d) float32."""
+    n_req = block_table.shape[0]
+    _, page, n_kv, d = K.shape
+    out = np.zeros((n_req, n_kv * G, d), dtype=F32)
+    for rq in range(n_req):
+        sl = int(seq_lens[rq])
+        for kh in range(n_kv):
+            c = int(page_cnt[rq, kh])
+            if c <= 0:
+                continue
+            pts = page_table[rq, kh, :c].astype(np.int64)
+            blks = block_table[rq, pts].astype(np.int64)
+            k = K[blks, :, kh, :].reshape(-1, d).astype(F32)           # (c*P, d)
+            v = V[blks, :, kh, :].reshape(-1, d).astype(F32)
+            tok = (pts[:, None] * page + np.arange(page)[None, :]).reshape(-1)
+            qg = q[rq, kh * G:(kh + 1) * G].astype(F32)                # (G, d)
+            s = (qg @ k.T).astype(F32) * F32(scale)
+            s[:, tok >= sl] = -np.inf
+            m = s.max(axis=1, keepdims=True)
+            p = np.exp(s - m)
+            l = p.sum(axis=1, keepdims=True)
+            out[rq, kh * G:(kh + 1) * G] = (p @ v) / l
+    return out
+
+
+def dense_page_mass(q, K, block_table, seq_lens, *, scale, G, page):
+    """Exact per-(req, kv, g, page) log-sum-exp masses (the bridge's
+    ``pmass``, ``_selection_bridge.py:79-82``); used by the synthetic-input
+    generators to calibrate planted pages."""
+    n_req = block_table.shape[0]
+    _, P, n_kv, d = K.shape
+    outs = []
+    for rq in range(n_req):
+        sl = int(seq_lens[rq])
+        npg = (sl + page - 1) // page
+        blks = block_table[rq, :npg].astype(np.int64)
+        k = K[blks].astype(F32)                                        # (npg,P,kv,d)
+        qg = q[rq].reshape(n_kv, G, d).astype(F32)
+        lg = np.einsum("kgd,ptkd->kgpt", qg, k, dtype=F32) * F32(scale)
+        tok = np.arange(npg)[:, None] * page + np.arange(P)[None, :]
+        lg = np.where(tok[None, None] < sl, lg, -np.inf)
+        mx = lg.max(axis=-1, keepdims=True)
+        outs.append((mx[..., 0] + np.log(np.exp(lg - mx).sum(-1))).astype(F32))
+    return outs
+
+
+# --------------------------------------------------------------------------- #
+# a8: r8 low-rank page score  (selection/score.py:30-120)                     #
+# --------------------------------------------------------------------------- #
+def r8_score(q, mu, mu_s, Vk, Vk_s, c, c_s, block_table, seq_lens, n_sel_hi,
+             *, scale: float, page: int, G: int, r: int, vk_bits: int,
+             c_bits: int, MP: int, combine: str = "lse"):
+    """S_g = s * mu.q_g + logsumexp_{t: tok < seq_len}(s * c_t . (Vk^T q_g));
+    page score = max_g S_g (``selection/score.py:30-120``).
+
+    ``combine="tokmax"`` replaces the log-sum-exp over tokens by a max (the
+    variant the BASELINE C4 text describes; not the reference form)."""
+    n_req = block_table.shape[0]
+    n_kv, d = mu.shape[1], mu.shape[2]
+    out = np.full((n_req, n_kv, MP), np.nan, dtype=F32)
+    for rq in range(n_req):
+        nsh = int(n_sel_hi[rq])
+        if nsh <= 0:
+            continue
+        sl = int(seq_lens[rq])
+        blks = block_table[rq, :nsh].astype(np.int64)
+        qg = q[rq].reshape(n_kv, G, d).astype(F32)
+        mu_f = mu[blks].astype(F32) * mu_s[blks].astype(F32)[..., None]
+        Vf = unpack_codes(Vk[blks], r, vk_bits) * \
+            Vk_s[blks].astype(F32)[:, :, None, :]                      # (P,kv,d,r)
+        cc = unpack_codes(c[blks], r, c_bits) * \
+            c_s[blks].astype(F32)[..., None]                           # (P,kv,t,r)
+        qt = np.einsum("kgd,pkdr->pkgr", qg, Vf, dtype=F32)
+        tok = np.einsum("pkgr,pktr->pkgt", qt, cc, dtype=F32) * F32(scale)
+        tpos = np.arange(nsh)[:, None] * page + np.arange(page)[None, :]
+        tok = np.where((tpos < sl)[:, None, None, :], tok, -np.inf)
+        m = tok.max(axis=-1)
+        if combine == "tokmax":
+            agg = m
+        else:
+            agg = m + np.log(np.exp(tok - m[..., None]).sum(-1))
+        qmu = np.einsum("kgd,pkd->pkg", qg, mu_f, dtype=F32) * F32(scale)
+        S = qmu + agg
+        out[rq, :, :nsh] = S.max(axis=-1).T
+    return out
+
+
+# --------------------------------------------------------------------------- #
+# a10/a11: exact-LRU residency plan + miss fetch                              #
+#          tier/residency.py:45-139 (plan), :196-248 (fetch)                  #
+# --------------------------------------------------------------------------- #
+I32_MAX = 2147483647
+
+
+def residency_step(page_table, page_cnt, block_table, seq_lens, *, page: int,
+                   page2slot, slot2page, lru, clock: int):
+    """One ``gather_plan`` call for one layer: the clock is advanced by the
+    caller; hits touch lru=clock; misses of complete pages (in request, then
+    page-table order) take the exact-LRU victim (min lru among slots with
+    lru < clock, lowest index on ties), evicting its old page; a page already
+    installed this step is deduplicated (``residency.py:45-139``).
+    Mutates page2slot (n_kv, NB), slot2page (n_kv, S), lru (n_kv, S) in place
+    and returns (fetch list [(kv, blk, slot)], overflow flag)."""
+    n_req, n_kv = page_cnt.shape
+    misses = [[[] for _ in range(n_kv)] for _ in range(n_req)]
+    for rq in range(n_req):
+        sl = int(seq_lens[rq])
+        for kv in range(n_kv):
+            for j in range(int(page_cnt[rq, kv])):
+                pt = int(page_table[rq, kv, j])
+                blk = int(block_table[rq, pt])
+                complete = (pt + 1) * page <= sl
+                if not complete:
+                    continue
+                slot = int(page2slot[kv, blk])
+                if slot >= 0:
+                    lru[kv, slot] = clock
+                else:
+                    misses[rq][kv].append(blk)
+    flist = []
+    ovf = False
+    for kv in range(n_kv):
+        for rq in range(n_req):
+            for blk in misses[rq][kv]:
+                if page2slot[kv, blk] >= 0:
+                    continue
+                ck = np.where(lru[kv] >= clock, I32_MAX, lru[kv])
+                s = int(np.argmin(ck))
+                if ck[s] == I32_MAX:
+                    ovf = True
+                    continue
+                old = int(slot2page[kv, s])
+                if old >= 0:
+                    page2slot[kv, old] = -1
+                page2slot[kv, blk] = s
+                slot2page[kv, s] = blk
+                lru[kv, s] = clock
+                flist.append((kv, blk, s))
+    return flist, ovf
+
+
+def residency_fetch(flist, *, hot, pool, pool_valid, vbo, v_pool, layer: int):
+    """Copy each installed miss page into its hot slot: from the pinned pool
+    when ``pool_valid``; else from the staging pool via ``vbo`` with
+    write-through to the pinned pool (and ``pool_valid`` set); else from the
+    pinned pool (``residency.py:196-248``).  Bit copies.
+    hot (n_kv, S, page, d); pool (L, NB, n_kv, page, d);
+    pool_valid (n_kv, NB); v_pool (NV, page, n_kv, d)."""
+    for kv, blk, slot in flist:
+        if pool_valid[kv, blk] > 0:
+            hot[kv, slot] = pool[layer, blk, kv]
+        elif vbo[blk] >= 0:
+            tile = v_pool[vbo[blk], :, kv, :]
+            hot[kv, slot] = tile
+            pool[layer, blk, kv] = tile
+            pool_valid[kv, blk] = 1
+        else:
+            hot[kv, slot] = pool[layer, blk, kv]
+
+
+def tier_decode(q, K, block_table, seq_lens, page_table, page_cnt, *, scale,
+                G, hot, page2slot, vbo, v_pool, pool, layer: int):
+    """mem-v ptr-select decode (``tier/decode_mem.py:78-166``): each selected
+    page's V comes from the hot buffer when complete and resident, else the
+    staging pool when ``vbo >= 0``, else the pinned pool; K is resident."""
+    n_req = block_table.shape[0]
+    NBk, page, n_kv, d = K.shape
+    Vsel = np.zeros_like(K)
+    for rq in range(n_req):
+        sl = int(seq_lens[rq])
+        for kv in range(n_kv):
+            for j in range(int(page_cnt[rq, kv])):
+                pt = int(page_table[rq, kv, j])
+                blk = int(block_table[rq, pt])
+                complete = (pt + 1) * page <= sl
+                slot = int(page2slot[kv, blk])
+                if complete and slot >= 0:
+                    Vsel[blk, :, kv] = hot[kv, slot]
+                elif vbo[blk] >= 0:
+                    Vsel[blk, :, kv] = v_pool[vbo[blk], :, kv]
+                else:
+                    Vsel[blk, :, kv] = pool[layer, blk, kv]
+    return sparse_decode(q, K, Vsel, block_table, seq_lens, page_table,
+                         page_cnt, scale=scale, G=G)
+
+
+# --------------------------------------------------------------------------- #
+# whole hot path for one layer                                                #
+# --------------------------------------------------------------------------- #
+def quad_layer_step(q, mu, mu_s, V, V_s, sig2, K, Vv, block_table, seq_lens, *,
+                    scale, page, G, r, v_bits, MP, sink, window, combine,
+                    budget=None, coverage=None):
+    """derive -> quad score (+combine) -> select -> decode, one layer."""
+    npg, nsh, b = derive_page_params(seq_lens, budget if budget else 0.1,
+                                     page, window, sink)
+    sh = quad_score_h(q, mu, mu_s, V, V_s, sig2, block_table, nsh,
+                      scale=scale, page=page, G=G, r=r, v_bits=v_bits, MP=MP)
+    score = combine_nrm(sh, nsh) if combine == "nrm" else combine_max(sh, nsh)
+    if budget is not None:
+        tab, cnt = topb_select(score, npg, nsh, b, sink=sink, MP=MP)
+    else:
+        tab, cnt, _ = coverage_select(score, npg, nsh, sink=sink, MP=MP,
+                                      coverage=coverage, combine=combine)
+    out = sparse_decode(q, K, Vv, block_table, seq_lens, tab, cnt,
+                        scale=scale, G=G)
+    return dict(n_pages=npg, n_sel_hi=nsh, b_fix=b, score_h=sh, score=score,
+                page_table=tab, page_cnt=cnt, out=out)
+
+
+def ceil_div(a: int, b: int) -> int:
+    return -(-a // b)
+
+
+__all__ = [n for n in dir() if not n.startswith("_") and n not in
+           ("annotations", "math", "np")]

@@ -1,0 +1,297 @@
+"""Generate golden vectors by running the REFERENCE's own kernels on CPU.
+
+Run in a container that has the reference source tree (read-only) at
+``$AMASS_REF_SRC`` (default ``/root/reference/src``):
+
+    python tests/golden/make_golden.py
+
+It imports the reference package with ``TRITON_INTERPRET=1`` (its Triton
+kernels execute in the CPU interpreter), feeds it seeded inputs from
+``amass_kv_b200.workloads`` and writes ``tests/golden/*.npz``: inputs plus the
+reference outputs of derive_page_params, quad_score (+ nrm/max combine),
+topb_select, sparse_paged_decode_batched (+ merge), r8_score, the residency
+gather (exact LRU + fetch) and the ptr-select tiered decode.  The fixtures are
+committed; nothing at test time reads the reference tree.
+
+Coverage selection has no graph-safe reference (the reference's
+``_nucleus_b`` is a scalar over heads, ``backend/_selection_bridge.py:117-133``);
+its golden is ``_nucleus_b`` applied to each (request, kv-head) unit's masses
+followed by the reference ``topb_select`` kernel run with that unit's b.
+"""
+from __future__ import annotations
+
+import os
+import sys
+import types
+
+os.environ["TRITON_INTERPRET"] = "1"
+os.environ.setdefault("AMASS_EIGH", "torch")
+REF = os.environ.get("AMASS_REF_SRC", "/root/reference/src")
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+sys.path.insert(0, REF)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+from amass_kv_b200.workloads import make_quad_case, make_r8_case  # noqa: E402
+
+from amass.selection import (QuadState, R8State, derive_page_params,  # noqa
+                             quad_score, r8_score, topb_select)
+from amass.attention.decode import (ResidentVSource,  # noqa: E402
+                                    ensure_stage_b_buffers,
+                                    sparse_paged_decode_batched)
+from amass.backend._selection_bridge import _nucleus_b  # noqa: E402
+from amass.tier.residency import Residency  # noqa: E402
+from amass.tier.decode_mem import mem_decode_ptrsel  # noqa: E402
+
+
+def t_bf16(x):
+    return torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(
+        torch.bfloat16)
+
+
+def bf16_bits(t):
+    return t.contiguous().view(torch.int16).numpy()
+
+
+def kv_cache_of(case):
+    """(NB, 2, page, n_kv, d) bf16 -- the vLLM 0.24 layout."""
+    return torch.stack([t_bf16(case.K), t_bf16(case.V)], dim=1).contiguous()
+
+
+def quad_state(case, *, budget, combine, n_req, sink=1, window=1):
+    NB = case.K.shape[0]
+    st = QuadState("cpu", num_layers=1, num_blocks=NB, n_kv=case.n_kv,
+                   G=case.G, head_dim=case.d, page=case.page, max_reqs=n_req,
+                   max_pages=case.MP, rank=case.r, budget=budget,
+                   sink_pages=sink, window_pages=window, v_bits=case.v_bits,
+                   combine=combine)
+    st.quad_mu[0].copy_(torch.from_numpy(case.mu))
+    st.mu_scale[0].copy_(torch.from_numpy(case.mu_s))
+    st.quad_V[0].copy_(torch.from_numpy(case.Vq))
+    st.V_scale[0].copy_(torch.from_numpy(case.V_s))
+    st.quad_sig2[0].copy_(torch.from_numpy(case.sig2))
+    st.score.fill_(float("nan"))
+    if combine == "nrm":
+        st.score_h.fill_(float("nan"))
+    return st
+
+
+def run_decode(case, st, q, kv, bt, sl, split=8):
+    """The reference decode + merge.  The Triton CPU interpreter mis-evaluates
+    ``tl.dot`` on bf16 operands, so q and the cache go in as float32 tensors
+    holding the exact bf16 values (the kernel's fp16 P.V path is unchanged)."""
+    st.D = case.d
+    ensure_stage_b_buffers(st, "cpu", split)
+    q, kv = q.float(), kv.float()
+    out = torch.zeros(q.shape, dtype=torch.float32)
+    sparse_paged_decode_batched(q, kv, bt, sl, st, out, ResidentVSource(kv),
+                                scale=case.scale)
+    return out
+
+
+def quad_inputs(case):
+    return dict(q=bf16_bits(t_bf16(case.q)),
+                kv=bf16_bits(kv_cache_of(case)),
+                block_table=case.block_table, seq_lens=case.seq_lens,
+                mu=case.mu, mu_s=case.mu_s, Vq=case.Vq, V_s=case.V_s,
+                sig2=case.sig2,
+                meta=np.array([case.G, case.r, case.v_bits, case.page,
+                               case.MP], dtype=np.int64),
+                scale=np.array([case.scale], dtype=np.float64))
+
+
+def gen_quad(name, case, *, budget, combine, coverage=None):
+    n_req = case.block_table.shape[0]
+    st = quad_state(case, budget=budget, combine=combine, n_req=n_req)
+    q = t_bf16(case.q)
+    bt = torch.from_numpy(case.block_table)
+    sl = torch.from_numpy(case.seq_lens)
+    kv = kv_cache_of(case)
+    derive_page_params(st, sl, n_req)
+    quad_score(st, 0, q, bt, sl, n_req, case.scale)
+    res = dict(n_pages=st.n_pages.numpy().copy(),
+               n_sel_hi=st.n_sel_hi.numpy().copy(),
+               b_fix=st.b_fix.numpy().copy(), score=st.score.numpy().copy())
+    if combine == "nrm":
+        res["score_h"] = st.score_h.numpy().copy()
+    if coverage is None:
+        topb_select(st, n_req)
+        res["page_table"] = st.page_table.numpy().copy()
+        res["page_cnt"] = st.page_cnt.numpy().copy()
+    else:
+        # per-unit nucleus b via the reference _nucleus_b, then the reference
+        # topb kernel with that b, one (request, kv-head) unit at a time.
+        tab = np.full((n_req, case.n_kv, case.MP), -1, np.int32)
+        cnt = np.zeros((n_req, case.n_kv), np.int32)
+        bu = np.zeros((n_req, case.n_kv), np.int32)
+        nsh = st.n_sel_hi.numpy().copy()
+        b_saved = st.b_fix.clone()
+        for rq in range(n_req):
+            for kh in range(case.n_kv):
+                n = int(nsh[rq])
+                if n - 1 <= 1:
+                    b = 1
+                else:
+                    sc = st.score[rq, kh, :n].double()
+                    lm = sc.log() if combine == "nrm" else sc
+                    b = _nucleus_b(lm[None, None, :], 1, n, coverage)
+                bu[rq, kh] = b
+                st.b_fix.copy_(b_saved)
+                st.b_fix[rq] = b
+                topb_select(st, n_req)
+                tab[rq, kh] = st.page_table[rq, kh].numpy()
+                cnt[rq, kh] = int(st.page_cnt[rq, kh])
+        st.page_table.copy_(torch.from_numpy(tab))
+        st.page_cnt.copy_(torch.from_numpy(cnt))
+        res.update(page_table=tab, page_cnt=cnt, b_u=bu,
+                   coverage=np.array([coverage]))
+    out = run_decode(case, st, q, kv, bt, sl)
+    res["out"] = out.float().numpy()
+    np.savez_compressed(os.path.join(HERE, name + ".npz"),
+                        budget=np.array([budget]),
+                        combine=np.array([combine]),
+                        **quad_inputs(case), **res)
+    print(name, "cnt", res["page_cnt"].tolist())
+
+
+def gen_r8(name, case, *, budget):
+    n_req = case.block_table.shape[0]
+    NB = case.K.shape[0]
+    st = R8State("cpu", num_layers=1, num_blocks=NB, n_kv=case.K.shape[2],
+                 G=case.G, head_dim=case.K.shape[3], page=case.page,
+                 max_reqs=n_req, max_pages=case.MP, rank=case.r,
+                 budget=budget, vk_bits=case.vk_bits, c_bits=case.c_bits)
+    st.r8_mu[0].copy_(torch.from_numpy(case.mu))
+    st.mu_scale[0].copy_(torch.from_numpy(case.mu_s))
+    st.r8_Vk[0].copy_(torch.from_numpy(case.Vk))
+    st.Vk_scale[0].copy_(torch.from_numpy(case.Vk_s))
+    st.r8_c[0].copy_(torch.from_numpy(case.c))
+    st.c_scale[0].copy_(torch.from_numpy(case.c_s))
+    st.score.fill_(float("nan"))
+    q = t_bf16(case.q)
+    bt = torch.from_numpy(case.block_table)
+    sl = torch.from_numpy(case.seq_lens)
+    derive_page_params(st, sl, n_req)
+    r8_score(st, 0, q, bt, sl, n_req, case.scale)
+    topb_select(st, n_req)
+    np.savez_compressed(
+        os.path.join(HERE, name + ".npz"),
+        q=bf16_bits(q), block_table=case.block_table, seq_lens=case.seq_lens,
+        mu=case.mu, mu_s=case.mu_s, Vk=case.Vk, Vk_s=case.Vk_s, c=case.c,
+        c_s=case.c_s,
+        meta=np.array([case.G, case.r, case.vk_bits, case.c_bits, case.page,
+                       case.MP, case.K.shape[2], case.K.shape[3]], np.int64),
+        scale=np.array([case.scale]), budget=np.array([budget]),
+        n_sel_hi=st.n_sel_hi.numpy(), n_pages=st.n_pages.numpy(),
+        b_fix=st.b_fix.numpy(), score=st.score.numpy(),
+        page_table=st.page_table.numpy(), page_cnt=st.page_cnt.numpy())
+    print(name, "cnt", st.page_cnt.tolist())
+
+
+def gen_tier(name, case, *, budget, hot_slots=10, steps=3, seed=5):
+    """Residency gather over several steps with forced eviction, staged and
+    flushed sources, then the ptr-select tiered decode."""
+    rng = np.random.default_rng(seed)
+    n_req = case.block_table.shape[0]
+    NB, page, n_kv, d = case.K.shape
+    st = quad_state(case, budget=budget, combine="max", n_req=n_req)
+    q = t_bf16(case.q)
+    bt = torch.from_numpy(case.block_table)
+    sl = torch.from_numpy(case.seq_lens)
+    kv = kv_cache_of(case)
+    derive_page_params(st, sl, n_req)
+    res = Residency(num_layers=1, num_blocks=NB, n_kv=n_kv,
+                    hot_slots=hot_slots, page=page, d=d, max_reqs=n_req,
+                    max_pages=case.MP, dtype=torch.bfloat16, device="cpu")
+    # pinned-pool stand-in (int16 bits), staging pool + vbo
+    Vb = t_bf16(case.V)                                   # (NB, page, kv, d)
+    pool = Vb.permute(0, 2, 1, 3).contiguous().view(torch.int16)[None].clone()
+    NV = 6
+    v_pool = torch.zeros((1, NV, page, n_kv, d), dtype=torch.bfloat16)
+    vbo = torch.full((NB,), -1, dtype=torch.int32)
+    staged = rng.choice(NB, NV, replace=False)
+    for i, blk in enumerate(staged):
+        vbo[blk] = i
+        v_pool[0, i] = Vb[blk]
+        pool[0, blk] = 0                                  # not flushed yet
+    res.pool_valid.fill_(1)
+    res.pool_valid[0, :, torch.from_numpy(staged)] = 0
+    staging = types.SimpleNamespace(v_pool=v_pool, vbo=vbo, k_pool=None)
+    tier = types.SimpleNamespace(residency=res, staging=staging,
+                                 offload_k=False,
+                                 pool=types.SimpleNamespace(dev_view=pool[0]
+                                                            .view(-1)))
+    rec = dict(staged=staged.astype(np.int32), NV=np.array([NV]),
+               hot_slots=np.array([hot_slots]))
+    pool_init = pool.clone()
+    valid_init = res.pool_valid.clone()
+    for s in range(steps):
+        qs = t_bf16(case.q + 1.5 * s * rng.standard_normal(case.q.shape))
+        quad_score(st, 0, qs, bt, sl, n_req, case.scale)
+        topb_select(st, n_req)
+        rec[f"q_{s}"] = bf16_bits(qs)
+        rec[f"page_table_{s}"] = st.page_table.numpy().copy()
+        rec[f"page_cnt_{s}"] = st.page_cnt.numpy().copy()
+        res.gather(0, st.page_table, st.page_cnt, bt, sl, n_req, staging,
+                   pool[0].view(-1))
+        rec[f"page2slot_{s}"] = res.page2slot[0].numpy().copy()
+        rec[f"slot2page_{s}"] = res.slot2page[0].numpy().copy()
+        rec[f"lru_{s}"] = res.lru_clock[0].numpy().copy()
+        rec[f"hot_{s}"] = res.hot_i16[0].numpy().copy()
+        rec[f"pool_valid_{s}"] = res.pool_valid[0].numpy().copy()
+        rec[f"fetch_cnt_{s}"] = res.fetch_cnt.numpy().copy()
+        rec[f"overflow_{s}"] = res.overflow.numpy().copy()
+        st.D = d
+        ensure_stage_b_buffers(st, "cpu", 8)
+        out = torch.zeros(qs.shape, dtype=torch.float32)
+        mem_decode_ptrsel(qs.float(), kv.float(), bt, sl, st, out, tier, 0,
+                          scale=case.scale)
+        rec[f"out_{s}"] = out.float().numpy()
+        out2 = run_decode(case, st, qs, kv, bt, sl)
+        rec[f"out_resident_{s}"] = out2.float().numpy()
+        print(name, "step", s, "fetch", int(res.fetch_cnt), "ovf",
+              int(res.overflow))
+    np.savez_compressed(os.path.join(HERE, name + ".npz"),
+                        **quad_inputs(case), budget=np.array([budget]),
+                        pool_init=pool_init.numpy(),
+                        pool_valid_init=valid_init[0].numpy(),
+                        v_pool=bf16_bits(v_pool), vbo=vbo.numpy(),
+                        pool_final=pool.numpy(), steps=np.array([steps]),
+                        **rec)
+
+
+def main():
+    torch.manual_seed(0)
+    # C1: B=2, 8 q / 2 kv heads, d=64, ctx 2048, r'=8 int8 V, budget 0.10, nrm
+    c1 = make_quad_case(0, n_req=2, n_kv=2, G=4, d=64, ctxs=(2048, 2048),
+                        r=8, v_bits=8, heavy=4, shift=2.0)
+    gen_quad("quad_c1_nrm", c1, budget=0.10, combine="nrm")
+    gen_quad("quad_c1_max", c1, budget=0.10, combine="max")
+    # Llama geometry slice: d=128, G=4, r'=2 int4 V; ragged incl. a 1-page,
+    # a 2-page (keep-all) and an empty (seq_len 0) request.
+    c2 = make_quad_case(1, n_req=5, n_kv=2, G=4, d=128,
+                        ctxs=(1000, 517, 16, 20, 0), r=2, v_bits=4, heavy=3,
+                        shift=3.0, outlier_frac=0.02)
+    gen_quad("quad_d128_i4_nrm", c2, budget=0.2, combine="nrm")
+    gen_quad("quad_d128_i4_max", c2, budget=0.05, combine="max")
+    gen_quad("quad_d128_i4_cov", c2, budget=0.1, combine="nrm",
+             coverage=0.9)
+    c3 = make_quad_case(2, n_req=2, n_kv=2, G=8, d=128, ctxs=(700, 333),
+                        r=2, v_bits=8, heavy=3, shift=3.0)
+    gen_quad("quad_g8_i8_cov_max", c3, budget=0.1, combine="max",
+             coverage=0.95)
+    r8a = make_r8_case(3, n_req=2, n_kv=2, G=4, d=64, ctxs=(1024, 700), r=8)
+    gen_r8("r8_i8", r8a, budget=0.1)
+    r8b = make_r8_case(4, n_req=2, n_kv=2, G=4, d=128, ctxs=(600, 250), r=8,
+                       vk_bits=4, c_bits=4)
+    gen_r8("r8_i4", r8b, budget=0.1)
+    t = make_quad_case(6, n_req=2, n_kv=2, G=4, d=64, ctxs=(500, 301),
+                       r=2, v_bits=8, heavy=3, shift=2.5)
+    gen_tier("tier_lru", t, budget=0.25, hot_slots=24, steps=3)
+    gen_tier("tier_overflow", t, budget=0.25, hot_slots=10, steps=1)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,160 @@
+"""Pin the CPU oracle against golden vectors made by the reference's own
+Triton kernels (``tests/golden/make_golden.py``)."""
+import numpy as np
+import pytest
+
+from oracle import amass_oracle as O
+from tests.conftest import bits_to_f32, load_golden
+
+QUAD = ["quad_c1_nrm", "quad_c1_max", "quad_d128_i4_nrm", "quad_d128_i4_max",
+        "quad_d128_i4_cov", "quad_g8_i8_cov_max"]
+
+
+def _quad(z):
+    G, r, vb, page, MP = [int(x) for x in z["meta"]]
+    kv = bits_to_f32(z["kv"])
+    return dict(G=G, r=r, v_bits=vb, page=page, MP=MP,
+                scale=float(z["scale"][0]), q=bits_to_f32(z["q"]),
+                K=kv[:, 0], V=kv[:, 1])
+
+
+@pytest.mark.parametrize("name", QUAD)
+def test_derive(name):
+    z = load_golden(name)
+    g = _quad(z)
+    npg, nsh, b = O.derive_page_params(z["seq_lens"], float(z["budget"][0]),
+                                       g["page"], 1, 1)
+    assert np.array_equal(npg, z["n_pages"])
+    assert np.array_equal(nsh, z["n_sel_hi"])
+    assert np.array_equal(b, z["b_fix"])
+
+
+@pytest.mark.parametrize("name", QUAD)
+def test_quad_score(name):
+    z = load_golden(name)
+    g = _quad(z)
+    sh = O.quad_score_h(g["q"], z["mu"], z["mu_s"], z["Vq"], z["V_s"],
+                        z["sig2"], z["block_table"], z["n_sel_hi"],
+                        scale=g["scale"], page=g["page"], G=g["G"], r=g["r"],
+                        v_bits=g["v_bits"], MP=g["MP"])
+    comb = str(z["combine"][0])
+    sc = O.combine_nrm(sh, z["n_sel_hi"]) if comb == "nrm" else \
+        O.combine_max(sh, z["n_sel_hi"])
+    for rq, n in enumerate(z["n_sel_hi"]):
+        if n <= 0:
+            continue
+        np.testing.assert_allclose(sc[rq, :, :n], z["score"][rq, :, :n],
+                                   rtol=2e-5, atol=2e-5)
+        if comb == "nrm":
+            np.testing.assert_allclose(sh[rq, :, :, :n],
+                                       z["score_h"][rq, :, :, :n],
+                                       rtol=2e-5, atol=2e-5)
+
+
+@pytest.mark.parametrize("name", QUAD)
+def test_select(name):
+    z = load_golden(name)
+    g = _quad(z)
+    sc = np.where(np.isnan(z["score"]), -np.inf, z["score"]).astype(np.float32)
+    if "coverage" in z:
+        tab, cnt, bu = O.coverage_select(
+            sc, z["n_pages"], z["n_sel_hi"], sink=1, MP=g["MP"],
+            coverage=float(z["coverage"][0]), combine=str(z["combine"][0]))
+        assert np.array_equal(bu, z["b_u"])
+    else:
+        tab, cnt = O.topb_select(sc, z["n_pages"], z["n_sel_hi"], z["b_fix"],
+                                 sink=1, MP=g["MP"])
+    assert np.array_equal(cnt, z["page_cnt"])
+    assert np.array_equal(tab, z["page_table"])
+
+
+@pytest.mark.parametrize("name", QUAD)
+def test_decode(name):
+    z = load_golden(name)
+    g = _quad(z)
+    out = O.sparse_decode(g["q"], g["K"], g["V"], z["block_table"],
+                          z["seq_lens"], z["page_table"], z["page_cnt"],
+                          scale=g["scale"], G=g["G"])
+    # reference: bf16 output, fp16 P  ->  bf16-level agreement
+    np.testing.assert_allclose(out, z["out"], atol=2e-2, rtol=1e-2)
+    assert np.abs(out - z["out"]).mean() < 2e-3
+
+
+@pytest.mark.parametrize("name", ["r8_i8", "r8_i4"])
+def test_r8(name):
+    z = load_golden(name)
+    G, r, vkb, cb, page, MP, n_kv, d = [int(x) for x in z["meta"]]
+    q = bits_to_f32(z["q"])
+    sc = O.r8_score(q, z["mu"], z["mu_s"], z["Vk"], z["Vk_s"], z["c"],
+                    z["c_s"], z["block_table"], z["seq_lens"], z["n_sel_hi"],
+                    scale=float(z["scale"][0]), page=page, G=G, r=r,
+                    vk_bits=vkb, c_bits=cb, MP=MP)
+    for rq, n in enumerate(z["n_sel_hi"]):
+        np.testing.assert_allclose(sc[rq, :, :n], z["score"][rq, :, :n],
+                                   rtol=1e-4, atol=1e-4)
+    scm = np.where(np.isnan(z["score"]), -np.inf, z["score"]).astype(np.float32)
+    tab, cnt = O.topb_select(scm, z["n_pages"], z["n_sel_hi"], z["b_fix"],
+                             sink=1, MP=MP)
+    assert np.array_equal(tab, z["page_table"])
+    assert np.array_equal(cnt, z["page_cnt"])
+
+
+@pytest.mark.parametrize("name", ["tier_lru", "tier_overflow"])
+def test_tier(name):
+    z = load_golden(name)
+    g = _quad(z)
+    kvb = z["kv"]
+    NB, page, n_kv, d = g["K"].shape
+    S = int(z["hot_slots"][0])
+    p2s = np.full((n_kv, NB), -1, np.int32)
+    s2p = np.full((n_kv, S), -1, np.int32)
+    lru = np.zeros((n_kv, S), np.int32)
+    hot = np.zeros((n_kv, S, page, d), np.int16)
+    pool = z["pool_init"].copy()
+    valid = z["pool_valid_init"].copy()
+    v_pool = z["v_pool"][0]
+    vbo = z["vbo"]
+    clock = 1
+    for s in range(int(z["steps"][0])):
+        clock += 1
+        fl, ovf = O.residency_step(z[f"page_table_{s}"], z[f"page_cnt_{s}"],
+                                   z["block_table"], z["seq_lens"], page=page,
+                                   page2slot=p2s, slot2page=s2p, lru=lru,
+                                   clock=clock)
+        O.residency_fetch(fl, hot=hot, pool=pool, pool_valid=valid, vbo=vbo,
+                          v_pool=v_pool, layer=0)
+        assert np.array_equal(p2s, z[f"page2slot_{s}"])
+        assert np.array_equal(s2p, z[f"slot2page_{s}"])
+        assert np.array_equal(lru, z[f"lru_{s}"])
+        assert np.array_equal(valid, z[f"pool_valid_{s}"])
+        assert len(fl) == int(z[f"fetch_cnt_{s}"][0])
+        assert bool(ovf) == bool(z[f"overflow_{s}"][0])
+        # hot bytes equal wherever a page is resident
+        for kv in range(n_kv):
+            for sl_ in range(S):
+                if s2p[kv, sl_] >= 0:
+                    assert np.array_equal(hot[kv, sl_],
+                                          z[f"hot_{s}"][kv, sl_])
+        q = bits_to_f32(z[f"q_{s}"])
+        out = O.tier_decode(q, g["K"], z["block_table"], z["seq_lens"],
+                            z[f"page_table_{s}"], z[f"page_cnt_{s}"],
+                            scale=g["scale"], G=g["G"],
+                            hot=bits_to_f32(hot), page2slot=p2s, vbo=vbo,
+                            v_pool=bits_to_f32(v_pool),
+                            pool=bits_to_f32(pool), layer=0)
+        np.testing.assert_allclose(out, z[f"out_{s}"], atol=2e-2, rtol=1e-2)
+        if name == "tier_lru":
+            # the tier delivers the same V bytes as the resident cache
+            assert np.array_equal(z[f"out_{s}"], z[f"out_resident_{s}"])
+    assert np.array_equal(pool, z["pool_final"])
+
+
+def test_bf16_round():
+    x = np.array([1.0, 1.00390625, 1.005859375, -3.3, 0.0], np.float32)
+    y = O.bf16_round(x)
+    assert y[0] == 1.0 and y[1] == 1.0 and y[2] == 1.0078125
+
+
+def test_int4_roundtrip():
+    c = np.arange(-8, 8, dtype=np.int32).reshape(2, 8)
+    assert np.array_equal(O.unpack_codes(O.pack_int4(c), 8, 4), c)
