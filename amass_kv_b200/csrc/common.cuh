@@ -1,0 +1,176 @@
+// Shared device helpers for the AMASS sm_100a kernels.
+//
+// Tensor-core fragments use the warp-level m16n8k16 MMA (fp16/bf16 inputs,
+// fp32 accumulate).  The hot path is HBM-bound (~2-6 flop per byte read), so
+// the MMA only has to keep the integer->half conversions and the q.K / P.V
+// products off the fp32 pipe; operand staging is cp.async into XOR-swizzled
+// shared memory.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/amass_b200.h"
+
+#define AMASS_DEV __device__ __forceinline__
+
+namespace amass {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// --------------------------------------------------------------------------
+// launch helpers
+// --------------------------------------------------------------------------
+inline int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? AMASS_OK : AMASS_ERR_CUDA;
+}
+
+inline int num_sms() {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  return sms;
+}
+
+// --------------------------------------------------------------------------
+// order-preserving float <-> uint32 keys (larger float -> larger key)
+// --------------------------------------------------------------------------
+AMASS_DEV uint32_t float_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+AMASS_DEV float key_float(uint32_t k) {
+  uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+
+// --------------------------------------------------------------------------
+// exact small-integer -> fp16 conversion (magic-bias method: an 8-bit
+// unsigned u placed in the low mantissa of 1024.0h reads as 1024+u, so a
+// signed code v is recovered by (0x6400 | (v + bias)) - (1024 + bias)).  Each
+// helper converts the two bytes at positions 0 and 2 of x into one half2.
+// Reference for the method: Kim et al., "Who Says Elephants Can't Run:
+// Bringing Large Scale MoE Models into Cloud Scale Production" (2022).
+// --------------------------------------------------------------------------
+AMASS_DEV uint32_t lop3_sel(uint32_t a, uint32_t b, uint32_t c) {
+  // f = b ? (a ^ c) : c   (immLut 0x6A)
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+// signed int8 bytes (positions 0,2) -> half2 (exact)
+AMASS_DEV uint32_t i8pair_to_h2(uint32_t x) {
+  uint32_t h = lop3_sel(x, 0x00FF00FFu, 0x64806480u);  // 1024 + (v + 128)
+  const uint32_t bias = 0x64806480u;                   // 1152.0h x2
+  uint32_t r;
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(bias));
+  return r;
+}
+// signed int4 nibbles (low nibble of bytes 0,2) -> half2 (exact)
+AMASS_DEV uint32_t i4pair_to_h2(uint32_t x) {
+  uint32_t h = lop3_sel(x, 0x000F000Fu, 0x64086408u);  // 1024 + (v + 8)
+  const uint32_t bias = 0x64086408u;                   // 1032.0h x2
+  uint32_t r;
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(bias));
+  return r;
+}
+// place byte BI of word a at position 0 and byte BJ of word b at position 2
+template <int BI, int BJ>
+AMASS_DEV uint32_t pick2(uint32_t a, uint32_t b) {
+  return __byte_perm(a, b, (BI & 3) | ((4 + (BJ & 3)) << 8));
+}
+
+AMASS_DEV uint32_t pack_h2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+AMASS_DEV uint32_t pack_bf2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+AMASS_DEV float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+AMASS_DEV float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// --------------------------------------------------------------------------
+// warp MMA m16n8k16, fp32 accumulate
+// --------------------------------------------------------------------------
+AMASS_DEV void mma_f16(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+AMASS_DEV void mma_bf16(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+AMASS_DEV void ldsm_x4(uint32_t* r, uint32_t saddr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(saddr));
+}
+AMASS_DEV void ldsm_x4_t(uint32_t* r, uint32_t saddr) {
+  asm volatile(
+      "ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+      : "r"(saddr));
+}
+
+// --------------------------------------------------------------------------
+// cp.async (16 B, L2-only caching; src_bytes = 0 zero-fills the destination)
+// --------------------------------------------------------------------------
+AMASS_DEV uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+AMASS_DEV void cp_async16(uint32_t dst, const void* src, bool valid) {
+  int n = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
+               :: "r"(dst), "l"(src), "r"(n));
+}
+AMASS_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
+template <int N>
+AMASS_DEV void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" :: "n"(N));
+}
+
+// read-only global loads that do not allocate in L1 (streamed summaries)
+AMASS_DEV uint4 ldg_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+AMASS_DEV uint2 ldg_nc_v2(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+               : "=r"(r.x), "=r"(r.y) : "l"(p));
+  return r;
+}
+AMASS_DEV uint32_t ldg_nc_u32(const void* p) {
+  uint32_t r;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];"
+               : "=r"(r) : "l"(p));
+  return r;
+}
+
+// Programmatic dependent launch: wait for the producing grid's memory.
+AMASS_DEV void grid_dep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+AMASS_DEV void grid_dep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;");
+}
+
+}  // namespace amass

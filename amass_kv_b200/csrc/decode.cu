@@ -1,0 +1,440 @@
+// Stage B on sm_100a: split-K sparse paged decode over the selected pages
+// with a log-sum-exp merge (reference attention/decode.py:128-241,
+// attention/merge.py:21-50).
+//
+// Work decomposition.  A (request, kv-head) unit with cnt selected pages is
+// cut into chunks of pps = max(ceil(cnt/split), pps_min) pages (the
+// reference's rule, decode.py:154-160); a chunk is one work item.  A
+// persistent grid of 4-warp CTAs walks the flat item list (each CTA first
+// scans the per-unit chunk counts into shared memory, then strides over the
+// items), so ragged batches balance across the SMs without empty programs.
+// Inside an item the four warps take pages round-robin; each warp streams its
+// pages through its own NST-deep cp.async ring in shared memory (16-byte
+// copies into an XOR-swizzled [token][d] tile, zero-filled beyond seq_len) and
+// the ring runs across item boundaries.
+//
+// Per page a warp computes S = Q K^T (m16n8k16 bf16 MMAs: rows = the G query
+// heads of the group, cols = 16 tokens), an online softmax in the log2
+// domain, and O += P V (P in bf16, V via ldmatrix.trans).  At the end of an
+// item the four warp states are merged through shared memory and written as
+// one (m, l, acc) partial; a second kernel merges the partials of each
+// (request, query head) and writes bf16 output.
+#include "common.cuh"
+
+namespace amass {
+namespace {
+
+constexpr int kDecWarps = 4;
+constexpr int kDecThreads = kDecWarps * 32;
+
+struct DecArgs {
+  const __nv_bfloat16* q;
+  int64_t q_st, q_sh;
+  const __nv_bfloat16* k;
+  int64_t k_sb, k_st, k_sh;
+  const __nv_bfloat16* v;
+  int64_t v_sb, v_st, v_sh;
+  const int32_t* bt;
+  int64_t bt_stride;
+  const int32_t* tab;
+  const int32_t* cnt;
+  const int32_t* sl;
+  float* m_part;
+  float* l_part;
+  float* acc_part;
+  __nv_bfloat16* out;
+  int64_t o_st, o_sh;
+  float scale_log2;
+  int split, pps_min;
+  int n_req, n_kv, G, MP, units;
+};
+
+AMASS_DEV int unit_pps(int cnt, int split, int pps_min) {
+  return max((cnt + split - 1) / split, pps_min);
+}
+
+// Cursor over the (item, page) sequence one warp consumes.
+struct Cursor {
+  int item;   // flat item index (>= W: exhausted)
+  int unit;
+  int j, j1;  // next page index inside the unit's page table, chunk end
+};
+
+template <int D>
+struct Tile {
+  static constexpr int kRowBytes = D * 2;
+  static constexpr int kChunks = D / 8;              // 16-byte chunks per row
+  static constexpr int kTileBytes = 16 * kRowBytes;  // one K or V page tile
+  static constexpr int kStageBytes = 2 * kTileBytes;
+};
+
+AMASS_DEV uint32_t swz(int row, int chunk) { return chunk ^ (row & 7); }
+
+template <int D, int NST>
+__global__ void __launch_bounds__(kDecThreads)
+decode_kernel(DecArgs a) {
+  using T = Tile<D>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* stages = smem;                                    // warps x NST
+  float* mbuf = reinterpret_cast<float*>(smem + kDecWarps * NST * T::kStageBytes);
+  float* lbuf = mbuf + kDecWarps * 8;
+  float* abuf = lbuf + kDecWarps * 8;                        // warps x G x D
+  int* meta = reinterpret_cast<int*>(abuf + kDecWarps * a.G * D);  // warps x NST
+  int* prefix = meta + kDecWarps * NST;                      // units + 1
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int U = a.units;
+
+  // ---- chunk-count prefix over units (each CTA redundantly; tiny) ---------
+  {
+    const int per = (U + kDecThreads - 1) / kDecThreads;
+    const int u0 = threadIdx.x * per;
+    int local = 0;
+    for (int u = u0; u < min(u0 + per, U); ++u) {
+      const int c = a.cnt[u];
+      local += c > 0 ? (c + unit_pps(c, a.split, a.pps_min) - 1) /
+                           unit_pps(c, a.split, a.pps_min)
+                     : 0;
+    }
+    // block exclusive scan of `local`
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    __shared__ int wtot[kDecWarps];
+    if (lane == 31) wtot[warp] = incl;
+    __syncthreads();
+    int woff = 0;
+    for (int w = 0; w < warp; ++w) woff += wtot[w];
+    int run = woff + incl - local;
+    for (int u = u0; u < min(u0 + per, U); ++u) {
+      prefix[u] = run;
+      const int c = a.cnt[u];
+      run += c > 0 ? (c + unit_pps(c, a.split, a.pps_min) - 1) /
+                         unit_pps(c, a.split, a.pps_min)
+                   : 0;
+    }
+    if (threadIdx.x == kDecThreads - 1) prefix[U] = run;
+    __syncthreads();
+  }
+  const int W = prefix[U];
+  if ((int)blockIdx.x >= W) return;
+
+  // locate the unit of item i: largest u with prefix[u] <= i
+  auto find_unit = [&](int i) {
+    int lo = 0, hi = U - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (prefix[mid] <= i) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+  };
+  auto set_item = [&](Cursor& cu, int item) {
+    cu.item = item;
+    if (item >= W) return;
+    const int u = find_unit(item);
+    const int c = a.cnt[u];
+    const int pps = unit_pps(c, a.split, a.pps_min);
+    const int j0 = (item - prefix[u]) * pps;
+    cu.unit = u;
+    cu.j = j0 + warp;
+    cu.j1 = min(j0 + pps, c);
+  };
+
+  uint8_t* my_stages = stages + warp * NST * T::kStageBytes;
+  int* my_meta = meta + warp * NST;
+
+  // issue the cp.async loads of the cursor's current page (if any) into slot
+  auto issue = [&](Cursor& cu, int slot) {
+    // advance past items where this warp has no page
+    while (cu.item < W && cu.j >= cu.j1) set_item(cu, cu.item + gridDim.x);
+    if (cu.item < W) {
+      const int u = cu.unit;
+      const int r = u / a.n_kv, kv = u - r * a.n_kv;
+      const int pt = a.tab[(int64_t)u * a.MP + cu.j];
+      const int64_t blk = a.bt[(int64_t)r * a.bt_stride + pt];
+      const int valid = min(16, a.sl[r] - pt * 16);
+      if (lane == 0) my_meta[slot] = valid;
+      const uint32_t sbase = smem_u32(my_stages + slot * T::kStageBytes);
+      const __nv_bfloat16* kp = a.k + blk * a.k_sb + kv * a.k_sh;
+      const __nv_bfloat16* vp = a.v + blk * a.v_sb + kv * a.v_sh;
+#pragma unroll
+      for (int i = 0; i < (16 * T::kChunks) / 32; ++i) {
+        const int id = lane + 32 * i;
+        const int row = id / T::kChunks, ch = id % T::kChunks;
+        const bool ok = row < valid;
+        const uint32_t doff = row * T::kRowBytes + swz(row, ch) * 16;
+        const int rr = ok ? row : 0;
+        cp_async16(sbase + doff, kp + rr * a.k_st + ch * 8, ok);
+        cp_async16(sbase + T::kTileBytes + doff, vp + rr * a.v_st + ch * 8, ok);
+      }
+      cu.j += kDecWarps;
+    }
+    cp_async_commit();
+  };
+
+  Cursor ic, cc;  // issue cursor, compute cursor
+  set_item(ic, blockIdx.x);
+  set_item(cc, blockIdx.x);
+#pragma unroll
+  for (int s = 0; s < NST - 1; ++s) issue(ic, s);
+  int slot_c = 0, slot_i = NST - 1;
+
+  const int g = lane >> 2, c4 = lane & 3;
+  constexpr int KS = D / 16;
+
+  for (int item = blockIdx.x; item < W; item += gridDim.x) {
+    // cc tracks `item` here (set_item already done for the first one)
+    if (cc.item != item) set_item(cc, item);
+    const int u = cc.unit;
+    const int r = u / a.n_kv, kv = u - r * a.n_kv;
+    // Q fragment (A operand): rows = query heads of the group
+    uint32_t qa[KS][2];
+    {
+      const bool gv = g < a.G;
+      const __nv_bfloat16* qp = a.q + (int64_t)r * a.q_st +
+                                (int64_t)(kv * a.G + (gv ? g : 0)) * a.q_sh;
+#pragma unroll
+      for (int s = 0; s < KS; ++s) {
+        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(qp + 16 * s + 2 * c4);
+        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(qp + 16 * s + 8 + 2 * c4);
+        qa[s][0] = gv ? w0 : 0u;
+        qa[s][1] = gv ? w1 : 0u;
+      }
+    }
+    float m_i = -INFINITY, l_i = 0.f;
+    float o[D / 8][2];
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = 0.f;
+
+    for (; cc.j < cc.j1; cc.j += kDecWarps) {
+      issue(ic, slot_i);
+      slot_i = (slot_i + 1 == NST) ? 0 : slot_i + 1;
+      cp_async_wait<NST - 1>();
+      __syncwarp();
+      const uint32_t kbase = smem_u32(my_stages + slot_c * T::kStageBytes);
+      const uint32_t vbase = kbase + T::kTileBytes;
+      const int valid = my_meta[slot_c];
+
+      // S = Q K^T  (two n-tiles of 8 tokens)
+      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        const int mat = lane >> 3, rin = lane & 7;
+        const int tok = (mat >> 1) * 8 + rin;
+        const int ch = 2 * ks + (mat & 1);
+        uint32_t b[4];
+        ldsm_x4(b, kbase + tok * T::kRowBytes + swz(tok, ch) * 16);
+        const uint32_t afr[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
+        mma_bf16(s[0], afr, b[0], b[1]);
+        mma_bf16(s[1], afr, b[2], b[3]);
+      }
+      // online softmax (log2 domain), row g; tokens 8nt + 2c4 + {0,1}
+      float x[4];
+      x[0] = (2 * c4 < valid) ? s[0][0] * a.scale_log2 : -INFINITY;
+      x[1] = (2 * c4 + 1 < valid) ? s[0][1] * a.scale_log2 : -INFINITY;
+      x[2] = (8 + 2 * c4 < valid) ? s[1][0] * a.scale_log2 : -INFINITY;
+      x[3] = (9 + 2 * c4 < valid) ? s[1][1] * a.scale_log2 : -INFINITY;
+      float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(m_i, mx);
+      const float alpha = exp2f(m_i - m_new);
+      float p[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) p[i] = exp2f(x[i] - m_new);
+      l_i = l_i * alpha + (p[0] + p[1] + p[2] + p[3]);
+      m_i = m_new;
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        o[i][0] *= alpha;
+        o[i][1] *= alpha;
+      }
+      const uint32_t pa[4] = {pack_bf2(p[0], p[1]), 0u, pack_bf2(p[2], p[3]), 0u};
+      // O += P V
+#pragma unroll
+      for (int dt = 0; dt < D / 8; dt += 2) {
+        const int mat = lane >> 3, rin = lane & 7;
+        const int tok = (mat & 1) * 8 + rin;
+        const int ch = dt + (mat >> 1);
+        uint32_t b[4];
+        ldsm_x4_t(b, vbase + tok * T::kRowBytes + swz(tok, ch) * 16);
+        float c0[4] = {o[dt][0], o[dt][1], 0.f, 0.f};
+        float c1[4] = {o[dt + 1][0], o[dt + 1][1], 0.f, 0.f};
+        mma_bf16(c0, pa, b[0], b[1]);
+        mma_bf16(c1, pa, b[2], b[3]);
+        o[dt][0] = c0[0]; o[dt][1] = c0[1];
+        o[dt + 1][0] = c1[0]; o[dt + 1][1] = c1[1];
+      }
+      __syncwarp();
+      slot_c = (slot_c + 1 == NST) ? 0 : slot_c + 1;
+    }
+
+    // ---- merge the 4 warp states of this item and write one partial ------
+    l_i += __shfl_xor_sync(0xffffffffu, l_i, 1);
+    l_i += __shfl_xor_sync(0xffffffffu, l_i, 2);
+    if (g < a.G) {
+      if (c4 == 0) {
+        mbuf[warp * 8 + g] = m_i;
+        lbuf[warp * 8 + g] = l_i;
+      }
+      float* ab = abuf + (warp * a.G + g) * D;
+#pragma unroll
+      for (int dt = 0; dt < D / 8; ++dt) {
+        ab[8 * dt + 2 * c4] = o[dt][0];
+        ab[8 * dt + 2 * c4 + 1] = o[dt][1];
+      }
+    }
+    __syncthreads();
+    {
+      const int chunk = item - prefix[u];
+      const int64_t slotp = (int64_t)u * a.split + chunk;
+      for (int e = threadIdx.x; e < a.G * D; e += kDecThreads) {
+        const int gg = e / D, dd = e - gg * D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, mbuf[w * 8 + gg]);
+        float acc = 0.f, L = 0.f;
+#pragma unroll
+        for (int w = 0; w < kDecWarps; ++w) {
+          const float mw = mbuf[w * 8 + gg];
+          const float sc = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+          acc += sc * abuf[(w * a.G + gg) * D + dd];
+          L += sc * lbuf[w * 8 + gg];
+        }
+        a.acc_part[(slotp * a.G + gg) * D + dd] = acc;
+        if (dd == 0) {
+          a.m_part[slotp * a.G + gg] = M;
+          a.l_part[slotp * a.G + gg] = L;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+}
+
+// ---- merge of the chunk partials (reference attention/merge.py:30-50) -----
+template <int D>
+__global__ void __launch_bounds__(128)
+merge_kernel(DecArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H = a.n_kv * a.G;
+  const int idx = blockIdx.x * 4 + warp;  // (r, h)
+  if (idx >= a.n_req * H) return;
+  const int r = idx / H, h = idx - r * H;
+  const int kv = h / a.G, g = h - kv * a.G;
+  const int u = r * a.n_kv + kv;
+  const int c = a.cnt[u];
+  constexpr int PER = D / 32;
+  float acc[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) acc[i] = 0.f;
+  float M = -INFINITY, L = 0.f;
+  if (c > 0) {
+    const int pps = unit_pps(c, a.split, a.pps_min);
+    const int nact = (c + pps - 1) / pps;
+    for (int ch = 0; ch < nact; ++ch) {
+      const int64_t sp = ((int64_t)u * a.split + ch) * a.G + g;
+      const float m = a.m_part[sp];
+      const float l = a.l_part[sp];
+      if (!(l > 0.f)) continue;
+      const float Mn = fmaxf(M, m);
+      const float s_old = exp2f(M - Mn), s_new = exp2f(m - Mn);
+      const float* ap = a.acc_part + sp * D + lane * PER;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) acc[i] = acc[i] * s_old + ap[i] * s_new;
+      L = L * s_old + l * s_new;
+      M = Mn;
+    }
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  __nv_bfloat16* op = a.out + (int64_t)r * a.o_st + (int64_t)h * a.o_sh + lane * PER;
+#pragma unroll
+  for (int i = 0; i < PER; i += 2) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(acc[i] * inv, acc[i + 1] * inv);
+    *reinterpret_cast<__nv_bfloat162*>(op + i) = v;
+  }
+}
+
+template <int D, int NST>
+size_t decode_smem(int G, int units) {
+  return (size_t)kDecWarps * NST * Tile<D>::kStageBytes +
+         (size_t)kDecWarps * 8 * 2 * sizeof(float) +
+         (size_t)kDecWarps * G * D * sizeof(float) +
+         (size_t)kDecWarps * NST * sizeof(int) + (size_t)(units + 1) * sizeof(int);
+}
+
+template <int D, int NST>
+int launch_decode(const DecArgs& a, cudaStream_t st) {
+  const size_t smem = decode_smem<D, NST>(a.G, a.units);
+  if (smem > 220 * 1024) return AMASS_ERR_UNSUPPORTED;
+  auto kern = decode_kernel<D, NST>;
+  static int configured = 0;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         220 * 1024);
+    configured = 1;
+  }
+  int per_sm = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecThreads, smem);
+  if (per_sm < 1) per_sm = 1;
+  const int grid = num_sms() * per_sm;
+  kern<<<grid, kDecThreads, smem, st>>>(a);
+  int rc = launch_status();
+  if (rc) return rc;
+  const int heads = a.n_req * a.n_kv * a.G;
+  merge_kernel<D><<<(heads + 3) / 4, 128, 0, st>>>(a);
+  return launch_status();
+}
+
+}  // namespace
+}  // namespace amass
+
+extern "C" int amass_sparse_decode(
+    const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k,
+    int64_t k_sb, int64_t k_st, int64_t k_sh, const void* v, int64_t v_sb,
+    int64_t v_st, int64_t v_sh, const int32_t* block_table, int64_t bt_stride,
+    const int32_t* page_table, const int32_t* page_cnt,
+    const int32_t* seq_lens, float* m_part, float* l_part, float* acc_part,
+    int split, int pps_min, void* out, int64_t o_stride_t, int64_t o_stride_h,
+    float scale, int n_req, int n_kv, int G, int head_dim, int page,
+    int max_pages, void* stream) {
+  using namespace amass;
+  if (n_req < 0 || n_kv <= 0 || G <= 0 || split <= 0 || pps_min <= 0 ||
+      max_pages <= 0)
+    return AMASS_ERR_ARG;
+  if (n_req == 0) return AMASS_OK;
+  if (!q || !k || !v || !block_table || !page_table || !page_cnt || !seq_lens ||
+      !m_part || !l_part || !acc_part || !out)
+    return AMASS_ERR_ARG;
+  if (G > 8 || page != 16) return AMASS_ERR_UNSUPPORTED;
+  // 16-byte cp.async rows and 4-byte q/out accesses
+  if ((k_st % 8) || (k_sb % 8) || (k_sh % 8) || (v_st % 8) || (v_sb % 8) ||
+      (v_sh % 8) || (reinterpret_cast<uintptr_t>(k) & 15) ||
+      (reinterpret_cast<uintptr_t>(v) & 15) || (q_stride_h % 2) ||
+      (q_stride_t % 2) || (o_stride_h % 2) || (o_stride_t % 2))
+    return AMASS_ERR_ARG;
+  DecArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.q_st = q_stride_t; a.q_sh = q_stride_h;
+  a.k = static_cast<const __nv_bfloat16*>(k);
+  a.k_sb = k_sb; a.k_st = k_st; a.k_sh = k_sh;
+  a.v = static_cast<const __nv_bfloat16*>(v);
+  a.v_sb = v_sb; a.v_st = v_st; a.v_sh = v_sh;
+  a.bt = block_table; a.bt_stride = bt_stride;
+  a.tab = page_table; a.cnt = page_cnt; a.sl = seq_lens;
+  a.m_part = m_part; a.l_part = l_part; a.acc_part = acc_part;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.o_st = o_stride_t; a.o_sh = o_stride_h;
+  a.scale_log2 = scale * kLog2e;
+  a.split = split; a.pps_min = pps_min;
+  a.n_req = n_req; a.n_kv = n_kv; a.G = G; a.MP = max_pages;
+  a.units = n_req * n_kv;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (head_dim == 128) return launch_decode<128, 2>(a, st);
+  if (head_dim == 64) return launch_decode<64, 3>(a, st);
+  return AMASS_ERR_UNSUPPORTED;
+}

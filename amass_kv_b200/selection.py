@@ -1,0 +1,206 @@
+"""Stage A (page scoring + selection) -- host side of the sm_100a kernels.
+
+Mirrors the reference's ``amass.selection`` surface for the hot path:
+
+  QuadState                     selection/quad_state.py:36-151 (same tensors)
+  derive_page_params(st, ...)   selection/select.py:48-56
+  quad_score_cuda(st, ...)      selection/quad_score_cuda.py:1724-1794
+  topb_select_cuda(st, n_req)   selection/select_cuda.py:370-391
+  select_pages_quad(st, ...)    selection/quad_score.py:142-153
+
+Every function launches through ``libamass_b200.so`` on the current torch
+stream, allocates nothing and never synchronises (CUDA-graph capturable).
+The state objects own all buffers; the reference's own ``QuadState`` works
+here too since only attributes are read.
+
+Per-(request, kv-head) coverage selection (the reference's AmassConfig
+``coverage``, D1 of its graph-safe path) is available through
+``select_pages_quad(..., coverage=c)`` or a state built with ``coverage=``.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import ptr
+
+TAGW = 8
+
+COMBINE = {"max": 0, "nrm": 1}
+
+
+class QuadState:
+    """Persistent quad selection state (alloc-once, physical-block keyed,
+    L-major), laid out exactly like the reference's QuadState:
+
+      quad_mu    (L, NB, n_kv, d)      int8   mu_scale (L, NB, n_kv)     fp16
+      quad_V     (L, NB, n_kv, d, rv)  int8   V_scale  (L, NB, n_kv, r)  fp16
+      quad_sig2  (L, NB, n_kv, r)      fp16   quad_tag (L, NB, n_kv, 8)  bf16
+      score (R, n_kv, MP) fp32, page_table (R, n_kv, MP) int32,
+      page_cnt (R, n_kv) int32, n_pages / n_sel_hi / b_fix (R,) int32,
+      budget64 (1,) fp64, score_h (R, n_kv, G, MP) + hmax (R, n_kv, G) (nrm).
+
+    ``coverage`` (optional) switches selection to per-unit nucleus coverage;
+    ``b_unit`` (R, n_kv) then records each unit's budget.
+    """
+
+    def __init__(self, device, *, num_layers, num_blocks, n_kv, G, head_dim,
+                 page, max_reqs, max_pages, rank=2, budget=0.1,
+                 sink_pages=1, window_pages=1, tagw=TAGW, v_grain="col",
+                 v_bits=8, mu_bits=8, coords="none", c_bits=4,
+                 c_grain="token", combine="max", coverage=None):
+        if window_pages < 1:
+            raise ValueError("window_pages >= 1 (the partial tail must be in "
+                             "the always-attended window)")
+        if v_bits not in (4, 8) or mu_bits != 8:
+            raise ValueError("quad V codes are int4 or int8; mu stays int8")
+        if v_bits == 4 and rank % 2:
+            raise ValueError("int4 V packs two nibbles per byte: rank even")
+        if combine not in COMBINE:
+            raise ValueError(f"combine must be 'max' or 'nrm', got {combine!r}")
+        if coords != "none":
+            raise NotImplementedError("CLSE coords are outside this build")
+        L, NB, D, r, MP, R = (num_layers, num_blocks, head_dim, rank,
+                              max_pages, max_reqs)
+        self.L, self.NB, self.n_kv, self.G, self.d = L, NB, n_kv, G, D
+        self.D = D
+        self.page, self.r, self.tagw = page, r, tagw
+        self.max_reqs, self.max_pages = R, MP
+        self.budget = float(budget)
+        self.coverage = None if coverage is None else float(coverage)
+        self.sink_pages, self.window_pages = int(sink_pages), int(window_pages)
+        self.v_grain, self.v_bits, self.mu_bits = v_grain, int(v_bits), 8
+        self.coords, self.combine = coords, combine
+        self.device = device
+        rv = r // 2 if v_bits == 4 else r
+        kw = dict(device=device)
+        self.quad_mu = torch.zeros(L, NB, n_kv, D, dtype=torch.int8, **kw)
+        self.mu_scale = torch.zeros(L, NB, n_kv, dtype=torch.float16, **kw)
+        self.quad_V = torch.zeros(L, NB, n_kv, D, rv, dtype=torch.int8, **kw)
+        self.V_scale = torch.zeros(L, NB, n_kv, r, dtype=torch.float16, **kw)
+        self.quad_sig2 = torch.zeros(L, NB, n_kv, r, dtype=torch.float16, **kw)
+        self.quad_tag = torch.full((L, NB, n_kv, tagw), float("nan"),
+                                   dtype=torch.bfloat16, **kw)
+        self.quad_c = self.c_scale = self.quad_resid = None
+        self.score = torch.empty(R, n_kv, MP, dtype=torch.float32, **kw)
+        self.page_table = torch.empty(R, n_kv, MP, dtype=torch.int32, **kw)
+        self.page_cnt = torch.zeros(R, n_kv, dtype=torch.int32, **kw)
+        if combine == "nrm":
+            self.score_h = torch.empty(R, n_kv, G, MP, dtype=torch.float32,
+                                       **kw)
+            self.hmax = torch.zeros(R, n_kv, G, dtype=torch.float32, **kw)
+        else:
+            self.score_h = self.hmax = None
+        self.b_unit = torch.zeros(R, n_kv, dtype=torch.int32, **kw)
+        self.n_pages = torch.zeros(R, dtype=torch.int32, **kw)
+        self.n_sel_hi = torch.zeros(R, dtype=torch.int32, **kw)
+        self.b_fix = torch.ones(R, dtype=torch.int32, **kw)
+        self.budget64 = torch.tensor([self.budget], dtype=torch.float64, **kw)
+
+    def bytes_per_layer(self) -> int:
+        ts = (self.quad_mu, self.mu_scale, self.quad_V, self.V_scale,
+              self.quad_sig2, self.quad_tag)
+        return sum(t[0].numel() * t.element_size() for t in ts)
+
+    def layer_state(self, layer: int):
+        return (self.quad_mu[layer], self.mu_scale[layer], self.quad_V[layer],
+                self.V_scale[layer], self.quad_sig2[layer],
+                self.quad_tag[layer])
+
+
+# --------------------------------------------------------------------------- #
+def derive_page_params(st, seq_lens, n_req: int) -> None:
+    """Refresh st.{n_pages, n_sel_hi, b_fix} for this step (one launch)."""
+    if n_req > st.max_reqs:
+        raise ValueError(f"n_req {n_req} > max_reqs {st.max_reqs}")
+    _lib.call("amass_derive_page_params", ptr(seq_lens), ptr(st.budget64),
+              ptr(st.n_pages), ptr(st.n_sel_hi), ptr(st.b_fix), int(n_req),
+              int(st.page), int(st.window_pages), int(st.sink_pages),
+              _lib.stream_of(seq_lens.device))
+
+
+def _check_q(q, st):
+    if q.dtype != torch.bfloat16 or q.stride(-1) != 1:
+        raise ValueError("q must be bf16 with a contiguous head_dim")
+
+
+def _rank_bits(st, V):
+    r = int(getattr(st, "r", V.shape[-1]))
+    v_bits = int(getattr(st, "v_bits", 8 if V.shape[-1] == r else 4))
+    return r, v_bits
+
+
+def _score_launch(st, layer, q, block_table, n_req, scale, write_h):
+    mu, mu_s, V, V_s, sig2 = (st.quad_mu[layer], st.mu_scale[layer],
+                              st.quad_V[layer], st.V_scale[layer],
+                              st.quad_sig2[layer])
+    r, v_bits = _rank_bits(st, V)
+    _check_q(q, st)
+    _lib.call("amass_quad_score", ptr(q), q.stride(0), q.stride(1), ptr(mu),
+              ptr(mu_s), ptr(V), ptr(V_s), ptr(sig2), ptr(block_table),
+              block_table.stride(0), ptr(st.n_sel_hi), ptr(st.score),
+              ptr(st.score_h) if write_h else 0, float(scale), int(n_req),
+              int(st.n_kv), int(st.G), int(st.d), int(st.page), r, v_bits,
+              int(st.max_pages), 1 if write_h else 0,
+              _lib.stream_of(q.device))
+
+
+def quad_score_cuda(st, layer: int, q, block_table, seq_lens, n_req: int,
+                    scale: float) -> None:
+    """Drop-in for the reference ``quad_score_cuda``: writes ``st.score`` over
+    the scored region (and ``st.score_h`` + the nrm fold when
+    ``st.combine == "nrm"``).  ``seq_lens`` is accepted for signature parity;
+    finalized pages need no token mask."""
+    nrm = getattr(st, "combine", "max") == "nrm"
+    _score_launch(st, layer, q, block_table, n_req, scale, nrm)
+    if nrm:
+        _lib.call("amass_nrm_combine", ptr(st.score_h), ptr(st.n_sel_hi),
+                  ptr(st.hmax), ptr(st.score), int(n_req), int(st.n_kv),
+                  int(st.G), int(st.max_pages), _lib.stream_of(q.device))
+
+
+quad_score = quad_score_cuda
+
+
+def topb_select_cuda(st, n_req: int) -> None:
+    """Drop-in for the reference ``topb_select_cuda``: static top-b from
+    ``st.score`` and ``st.b_fix`` into ``st.page_table`` / ``st.page_cnt``."""
+    _lib.call("amass_topb_select", ptr(st.score), ptr(st.n_pages),
+              ptr(st.n_sel_hi), ptr(st.b_fix), ptr(st.page_table),
+              ptr(st.page_cnt), int(n_req), int(st.n_kv),
+              int(st.sink_pages), int(st.max_pages),
+              _lib.stream_of(st.score.device))
+
+
+topb_select = topb_select_cuda
+
+
+def select_pages(st, n_req: int, *, coverage=None, from_score_h=None) -> None:
+    """Fused Stage-A.2: nrm fold (when the state's combine is nrm and the
+    per-head scores are pending) + top-b or per-unit coverage selection."""
+    nrm = getattr(st, "combine", "max") == "nrm"
+    if from_score_h is None:
+        from_score_h = nrm
+    cov = coverage if coverage is not None else getattr(st, "coverage", None)
+    b_unit = getattr(st, "b_unit", None)
+    _lib.call("amass_select_pages",
+              ptr(st.score_h) if from_score_h else 0, ptr(st.score),
+              ptr(st.n_pages), ptr(st.n_sel_hi), ptr(st.b_fix),
+              ptr(st.page_table), ptr(st.page_cnt), ptr(b_unit), int(n_req),
+              int(st.n_kv), int(st.G), int(st.sink_pages),
+              int(st.max_pages), COMBINE["nrm" if nrm else "max"],
+              1 if cov is not None else 0,
+              float(cov) if cov is not None else 0.0,
+              _lib.stream_of(st.score.device))
+
+
+def select_pages_quad(st, layer: int, q, block_table, seq_lens, n_req: int,
+                      scale: float, *, derive: bool = True,
+                      coverage=None) -> None:
+    """One-call Stage A (quad): (derive) + score + fused fold/select.
+    Writes st.page_table / st.page_cnt (and st.score)."""
+    if derive:
+        derive_page_params(st, seq_lens, n_req)
+    nrm = getattr(st, "combine", "max") == "nrm"
+    _score_launch(st, layer, q, block_table, n_req, scale, nrm)
+    select_pages(st, n_req, coverage=coverage, from_score_h=nrm)

@@ -1,0 +1,134 @@
+/*
+ * amass_b200.h -- C ABI of libamass_b200.so, the sm_100a implementation of
+ * the AMASS decode-time sparse paged-attention hot path.
+ *
+ * Every entry point takes raw device pointers (or UVA device pointers of
+ * pinned host memory), element strides, sizes and a cudaStream_t passed as
+ * void*.  No entry point allocates, frees or synchronises; all launches are
+ * fixed-shape for given sizes, so they can be captured in a CUDA graph.
+ * Return value: AMASS_OK or one of the error codes below.  Dtypes:
+ * bf16/fp16 tensors are passed as void*, fp32 as float*, indices as int32_t*.
+ *
+ * Citations name the reference interface each entry point replaces, as
+ * path:line inside the reference project (Js-Hwang1/amass-kv, src/amass/).
+ */
+#ifndef AMASS_B200_H
+#define AMASS_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  AMASS_OK = 0,
+  AMASS_ERR_ARG = 1,          /* null pointer / negative size / bad stride   */
+  AMASS_ERR_UNSUPPORTED = 2,  /* geometry outside the compiled variants       */
+  AMASS_ERR_CAPACITY = 3,     /* a caller buffer is too small for the request */
+  AMASS_ERR_CUDA = 4          /* a CUDA launch error (cudaGetLastError)       */
+};
+
+/* combine modes for the GQA group (AmassConfig.quad_combine) */
+enum { AMASS_COMBINE_MAX = 0, AMASS_COMBINE_NRM = 1 };
+/* selection modes */
+enum { AMASS_SELECT_TOPB = 0, AMASS_SELECT_COVERAGE = 1 };
+/* r8 token aggregation */
+enum { AMASS_R8_LSE = 0, AMASS_R8_TOKMAX = 1 };
+
+const char* amass_status_string(int status);
+int amass_version(void);
+
+/* One-time per-device setup (kernel attributes).  Call once per device
+ * before stream capture; every other entry point calls it lazily too. */
+int amass_init(void);
+
+/* derive_page_params -- replaces selection/select.py:48-56 (kernel :30-45).
+ * n_pages = ceil(seq_len/page); n_sel_hi = n_pages - window;
+ * b_fix = clamp(ceil(fp64(n_sel_hi - sink) * budget64[0]), 1, max(n_sel,1)). */
+int amass_derive_page_params(const int32_t* seq_lens, const double* budget64,
+                             int32_t* n_pages, int32_t* n_sel_hi,
+                             int32_t* b_fix, int n_req, int page,
+                             int window_pages, int sink_pages, void* stream);
+
+/* quad_score -- replaces selection/quad_score_cuda.py:1724-1794 (Triton
+ * golden selection/quad_score.py:35-139).  Reads one layer's quad slabs:
+ *   mu (NB, n_kv, d) int8, mu_scale (NB, n_kv) fp16,
+ *   V (NB, n_kv, d, rv) int8 (rv = rank, or rank/2 packed int4),
+ *   V_scale (NB, n_kv, rank) fp16, sig2 (NB, n_kv, rank) fp16 (contiguous).
+ * write_h = 0: score[r, kv, p] = max_g S_g (R, n_kv, MP) fp32.
+ * write_h = 1: score_h[r, kv, g, p] = S_g (R, n_kv, G, MP) fp32 (the nrm
+ *              path; fold it with amass_nrm_combine or amass_select_pages).
+ * Pages p < n_sel_hi[r] are written; others are left untouched.
+ * Compiled variants: head_dim in {64, 128}, rank in {1, 2, 4, 8},
+ * v_bits in {4, 8} (int4 needs an even rank), G <= 8, page = 16. */
+int amass_quad_score(const void* q, int64_t q_stride_t, int64_t q_stride_h,
+                     const int8_t* mu, const void* mu_scale, const int8_t* V,
+                     const void* V_scale, const void* sig2,
+                     const int32_t* block_table, int64_t bt_stride,
+                     const int32_t* n_sel_hi, float* score, float* score_h,
+                     float scale, int n_req, int n_kv, int G, int head_dim,
+                     int page, int rank, int v_bits, int max_pages,
+                     int write_h, void* stream);
+
+/* nrm combine -- replaces the two passes of selection/quad_score.py:276-315
+ * (CUDA twin quad_score_cuda.py:1446-1547): hmax[r,kv,g] = max_{p<n_sel_hi}
+ * score_h; score[r,kv,p] = sum_g exp(score_h[r,kv,g,p] - hmax[r,kv,g]). */
+int amass_nrm_combine(const float* score_h, const int32_t* n_sel_hi,
+                      float* hmax, float* score, int n_req, int n_kv, int G,
+                      int max_pages, void* stream);
+
+/* topb_select -- replaces selection/select_cuda.py:370-391 (Triton golden
+ * selection/select.py:60-116): tau = b_fix[r]-th largest score over the
+ * selectable region [sink, n_sel_hi); keep score >= tau, sinks, window and
+ * tail; ascending page ids, -1 padded to max_pages; page_cnt per unit. */
+int amass_topb_select(const float* score, const int32_t* n_pages,
+                      const int32_t* n_sel_hi, const int32_t* b_fix,
+                      int32_t* page_table, int32_t* page_cnt, int n_req,
+                      int n_kv, int sink_pages, int max_pages, void* stream);
+
+/* select_pages -- fused Stage-A.2: (optional nrm fold of score_h into score)
+ * then per-(request, kv-head) selection.  mode TOPB uses b_fix (as
+ * amass_topb_select); mode COVERAGE computes each unit's nucleus budget b_u
+ * (smallest b whose top-b selectable pages hold `coverage` of the scored page
+ * mass minus the sink share; the per-unit form of the reference's
+ * backend/_selection_bridge.py:117-133) and applies the same threshold rule.
+ * combine MAX: reads score (mass = exp(score - max)); NRM: reads score_h,
+ * writes score (mass = score).  b_unit (R, n_kv) receives the b used per unit
+ * (may be NULL).  Has no single reference counterpart: it replaces the pair
+ * nrm_combine + topb_select_cuda on the graph-safe path
+ * (backend/_runtime.py:183-263) and adds the per-head coverage the
+ * reference only has in its eager bridge. */
+int amass_select_pages(const float* score_h, float* score,
+                       const int32_t* n_pages, const int32_t* n_sel_hi,
+                       const int32_t* b_fix, int32_t* page_table,
+                       int32_t* page_cnt, int32_t* b_unit, int n_req, int n_kv,
+                       int G, int sink_pages, int max_pages, int combine,
+                       int mode, float coverage, void* stream);
+
+/* sparse_paged_decode -- replaces attention/decode_cuda.py:1376-1465
+ * (Triton golden attention/decode.py:247-304 + merge.py:21-50).
+ * K/V tiles are addressed as base + blk*s_b + tok*s_t + kv*s_h (elements,
+ * bf16), which covers vLLM's (nb, 2, page, n_kv, d) and (2, nb, ...) caches.
+ * Per (request, kv-head) unit: pps = max(ceil(cnt/split), pps_min) pages per
+ * chunk; chunk partials go to m_part/l_part (R, n_kv, split, G) and acc_part
+ * (R, n_kv, split, G, d) fp32; a merge writes out (T, H, d) bf16 rows
+ * [0, n_req) in place (0 for empty units).  head_dim in {64, 128}, G <= 8,
+ * page = 16. */
+int amass_sparse_decode(const void* q, int64_t q_stride_t, int64_t q_stride_h,
+                        const void* k, int64_t k_sb, int64_t k_st,
+                        int64_t k_sh, const void* v, int64_t v_sb,
+                        int64_t v_st, int64_t v_sh,
+                        const int32_t* block_table, int64_t bt_stride,
+                        const int32_t* page_table, const int32_t* page_cnt,
+                        const int32_t* seq_lens, float* m_part, float* l_part,
+                        float* acc_part, int split, int pps_min, void* out,
+                        int64_t o_stride_t, int64_t o_stride_h, float scale,
+                        int n_req, int n_kv, int G, int head_dim, int page,
+                        int max_pages, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AMASS_B200_H */

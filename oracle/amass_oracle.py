@@ -264,6 +264,43 @@ def selection_diff_ok(tab_a, cnt_a, tab_b, cnt_b, score, tau_tol=1e-3):
     return True
 
 
+def coverage_diff_ok(tab, cnt, score, n_pages, n_sel_hi, *, sink, coverage,
+                     combine, rel_tol=1e-3):
+    """Coverage-mode acceptance: for every unit the kept selectable pages form
+    a threshold set (all pages scoring >= its smallest member) whose size k is
+    a valid nucleus size up to the fp tie band -- the top-(k-1) mass is below
+    need*(1+rel_tol) and the top-k mass reaches need*(1-rel_tol)."""
+    R, n_kv = cnt.shape
+    for rq in range(R):
+        nsh = int(n_sel_hi[rq])
+        npg = int(n_pages[rq])
+        for kh in range(n_kv):
+            kept = set(tab[rq, kh, :cnt[rq, kh]].tolist())
+            if nsh - sink <= 1:
+                if kept != set(range(max(npg, 0))):
+                    return False
+                continue
+            always = set(range(sink)) | set(range(nsh, npg))
+            if not always <= kept:
+                return False
+            sel = sorted(p for p in kept if sink <= p < nsh)
+            sc = score[rq, kh]
+            tau = min(sc[p] for p in sel)
+            if set(sel) != {p for p in range(sink, nsh) if sc[p] >= tau}:
+                return False
+            m = page_mass(sc, nsh, combine)
+            need = max(coverage * m.sum() - m[:sink].sum(), 0.0)
+            srt = np.sort(m[sink:nsh])[::-1]
+            csum = np.concatenate([[0.0], np.cumsum(srt)])
+            k = len(sel)
+            tol = rel_tol * max(need, 1e-30)
+            if not (csum[k - 1] < need + tol or k == 1):
+                return False
+            if not (csum[k] >= need - tol or k == nsh - sink):
+                return False
+    return True
+
+
 # --------------------------------------------------------------------------- #
 # a7: sparse paged decode over the selected pages (+ LSE merge)               #
 #     attention/decode.py:145-241, attention/merge.py:30-50                   #

@@ -158,3 +158,15 @@ def test_bf16_round():
 def test_int4_roundtrip():
     c = np.arange(-8, 8, dtype=np.int32).reshape(2, 8)
     assert np.array_equal(O.unpack_codes(O.pack_int4(c), 8, 4), c)
+
+
+@pytest.mark.parametrize("name", ["quad_d128_i4_cov", "quad_g8_i8_cov_max"])
+def test_coverage_acceptance_accepts_golden(name):
+    """The coverage acceptance rule used by the GPU tests accepts the
+    reference-built coverage selection itself."""
+    z = load_golden(name)
+    sc = np.where(np.isnan(z["score"]), -np.inf, z["score"]).astype(np.float32)
+    assert O.coverage_diff_ok(z["page_table"], z["page_cnt"], sc, z["n_pages"],
+                              z["n_sel_hi"], sink=1,
+                              coverage=float(z["coverage"][0]),
+                              combine=str(z["combine"][0]))
