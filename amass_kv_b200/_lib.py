@@ -32,6 +32,9 @@ _SIGS = {
     "amass_sparse_decode": [_P, _L, _L, _P, _L, _L, _L, _P, _L, _L, _L, _P,
                             _L, _P, _P, _P, _P, _P, _P, _I, _I, _P, _L, _L,
                             _F, _I, _I, _I, _I, _I, _I, _P],
+    "amass_sparse_decode_noalloc": [_P, _L, _L, _P, _L, _L, _L, _P, _L, _L,
+                                    _L, _P, _L, _P, _P, _P, _I, _I, _P, _L,
+                                    _L, _F, _I, _I, _I, _I, _I, _I, _P],
 }
 
 _lib = None
@@ -40,7 +43,8 @@ _lock = threading.Lock()
 
 def exported_symbols():
     """Every C entry point this binding declares (tests check the .so)."""
-    return sorted(list(_SIGS) + ["amass_status_string"])
+    return sorted(list(_SIGS) + ["amass_status_string",
+                                 "amass_sparse_decode_noalloc_capacity"])
 
 
 def load():
@@ -60,6 +64,8 @@ def load():
             fn = getattr(lib, name)
             fn.argtypes = args
             fn.restype = ctypes.c_int
+        lib.amass_sparse_decode_noalloc_capacity.argtypes = []
+        lib.amass_sparse_decode_noalloc_capacity.restype = ctypes.c_size_t
         lib.amass_status_string.argtypes = [ctypes.c_int]
         lib.amass_status_string.restype = ctypes.c_char_p
         _lib = lib

@@ -438,3 +438,71 @@ extern "C" int amass_sparse_decode(
   if (head_dim == 64) return launch_decode<64, 3>(a, st);
   return AMASS_ERR_UNSUPPORTED;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of amass_sparse_decode.
+//
+// Some callers cannot allocate device memory at all: a plugin that runs
+// inside another runtime's memory pool, a host loop that must not touch the
+// CUDA allocator once serving has started, or a binding with no tensor
+// library to own buffers.  For them the split-K partials live in one
+// file-scope device array, fixed in size, that every GPU loading this
+// library keeps until the process exits.  Nothing is allocated or freed.
+// ---------------------------------------------------------------------------
+namespace amass {
+namespace {
+
+constexpr size_t kNoAllocFloats = size_t(4) << 20;   // 16 MiB of fp32 partials
+static __device__ __align__(256) float g_decode_scratch[kNoAllocFloats];
+
+constexpr int kMaxDevices = 64;
+float* g_scratch_ptr[kMaxDevices] = {};
+
+// Device address of the scratch array for the current device; resolved once
+// per device (the host-side symbol is not a device address).
+int scratch_for_current_device(float** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return AMASS_ERR_CUDA;
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess || !p)
+      return AMASS_ERR_CUDA;
+    g_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_scratch_ptr[dev];
+  return AMASS_OK;
+}
+
+}  // namespace
+}  // namespace amass
+
+extern "C" size_t amass_sparse_decode_noalloc_capacity(void) {
+  return amass::kNoAllocFloats;
+}
+
+extern "C" int amass_sparse_decode_noalloc(
+    const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k,
+    int64_t k_sb, int64_t k_st, int64_t k_sh, const void* v, int64_t v_sb,
+    int64_t v_st, int64_t v_sh, const int32_t* block_table, int64_t bt_stride,
+    const int32_t* page_table, const int32_t* page_cnt,
+    const int32_t* seq_lens, int split, int pps_min, void* out,
+    int64_t o_stride_t, int64_t o_stride_h, float scale, int n_req, int n_kv,
+    int G, int head_dim, int page, int max_pages, void* stream) {
+  using namespace amass;
+  if (n_req < 0 || n_kv <= 0 || G <= 0 || split <= 0 || head_dim <= 0)
+    return AMASS_ERR_ARG;
+  // partial layout: m (units*split*G), l (same), acc (units*split*G*D)
+  const size_t slots = (size_t)n_req * n_kv * split * G;
+  const size_t need = slots * (2 + (size_t)head_dim);
+  if (need > kNoAllocFloats) return AMASS_ERR_CAPACITY;
+  float* base = nullptr;
+  const int rc = scratch_for_current_device(&base);
+  if (rc) return rc;
+  return amass_sparse_decode(q, q_stride_t, q_stride_h, k, k_sb, k_st, k_sh, v,
+                             v_sb, v_st, v_sh, block_table, bt_stride,
+                             page_table, page_cnt, seq_lens, base,
+                             base + slots, base + 2 * slots, split, pps_min,
+                             out, o_stride_t, o_stride_h, scale, n_req, n_kv,
+                             G, head_dim, page, max_pages, stream);
+}

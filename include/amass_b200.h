@@ -15,6 +15,7 @@
 #ifndef AMASS_B200_H
 #define AMASS_B200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -126,6 +127,29 @@ int amass_sparse_decode(const void* q, int64_t q_stride_t, int64_t q_stride_h,
                         int64_t o_stride_t, int64_t o_stride_h, float scale,
                         int n_req, int n_kv, int G, int head_dim, int page,
                         int max_pages, void* stream);
+
+/* sparse_paged_decode_noalloc -- no counterpart in the reference.  For
+ * callers that cannot allocate device memory (a plugin running inside another
+ * runtime's memory pool, a serving loop that must not touch the allocator, a
+ * binding with no tensor library): the same decode as amass_sparse_decode,
+ * but the split-K partials live in a fixed file-scope device array of
+ * amass_sparse_decode_noalloc_capacity() floats (16 MiB) that every GPU
+ * loading this library holds until exit.  Requires
+ * n_req*n_kv*split*G*(head_dim+2) <= capacity, else AMASS_ERR_CAPACITY (use a
+ * smaller split).  Allocates and frees nothing.  The first call on a device
+ * resolves the array's device address (cudaGetSymbolAddress), so make that
+ * first call before any stream capture.  All calls share the one array:
+ * calls that overlap on the GPU (other streams, other threads) race and must
+ * be serialised by the caller.  No part of the array needs to start zeroed. */
+size_t amass_sparse_decode_noalloc_capacity(void);
+int amass_sparse_decode_noalloc(
+    const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k,
+    int64_t k_sb, int64_t k_st, int64_t k_sh, const void* v, int64_t v_sb,
+    int64_t v_st, int64_t v_sh, const int32_t* block_table, int64_t bt_stride,
+    const int32_t* page_table, const int32_t* page_cnt,
+    const int32_t* seq_lens, int split, int pps_min, void* out,
+    int64_t o_stride_t, int64_t o_stride_h, float scale, int n_req, int n_kv,
+    int G, int head_dim, int page, int max_pages, void* stream);
 
 #ifdef __cplusplus
 }
