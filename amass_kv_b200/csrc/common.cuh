@@ -28,6 +28,28 @@ inline int launch_status() {
   return e == cudaSuccess ? AMASS_OK : AMASS_ERR_CUDA;
 }
 
+// Launch with programmatic dependent launch enabled: the grid may be
+// scheduled while the previous kernel on the stream is still finishing; every
+// kernel here calls grid_dep_wait() before touching memory that kernel wrote,
+// and grid_dep_launch() early so its own successor can be scheduled.
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                      size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...) == cudaSuccess
+             ? AMASS_OK
+             : AMASS_ERR_CUDA;
+}
+
 inline int num_sms() {
   static int sms = 0;
   if (sms == 0) {

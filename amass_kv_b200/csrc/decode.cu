@@ -19,6 +19,8 @@
 // item the four warp states are merged through shared memory and written as
 // one (m, l, acc) partial; a second kernel merges the partials of each
 // (request, query head) and writes bf16 output.
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace amass {
@@ -73,6 +75,8 @@ AMASS_DEV uint32_t swz(int row, int chunk) { return chunk ^ (row & 7); }
 template <int D, int NST>
 __global__ void __launch_bounds__(kDecThreads)
 decode_kernel(DecArgs a) {
+  grid_dep_wait();     // inputs written by the previous kernel
+  grid_dep_launch();
   using T = Tile<D>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;                                    // warps x NST
@@ -320,6 +324,8 @@ decode_kernel(DecArgs a) {
 template <int D>
 __global__ void __launch_bounds__(128)
 merge_kernel(DecArgs a) {
+  grid_dep_wait();     // inputs written by the previous kernel
+  grid_dep_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int H = a.n_kv * a.G;
   const int idx = blockIdx.x * 4 + warp;  // (r, h)
@@ -332,22 +338,59 @@ merge_kernel(DecArgs a) {
   float acc[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) acc[i] = 0.f;
-  float M = -INFINITY, L = 0.f;
+  float Mrun = -INFINITY;
+  float L = 0.f;
   if (c > 0) {
+    // all chunk weights in one parallel round of loads (lane = chunk), then
+    // independent acc loads per chunk: no dependent chain across chunks
     const int pps = unit_pps(c, a.split, a.pps_min);
     const int nact = (c + pps - 1) / pps;
-    for (int ch = 0; ch < nact; ++ch) {
-      const int64_t sp = ((int64_t)u * a.split + ch) * a.G + g;
-      const float m = a.m_part[sp];
-      const float l = a.l_part[sp];
-      if (!(l > 0.f)) continue;
-      const float Mn = fmaxf(M, m);
-      const float s_old = exp2f(M - Mn), s_new = exp2f(m - Mn);
-      const float* ap = a.acc_part + sp * D + lane * PER;
+    const int64_t s0 = (int64_t)u * a.split;
+    for (int base = 0; base < nact; base += 32) {
+      const int ch = base + lane;
+      float m = -INFINITY, l = 0.f;
+      if (ch < nact) {
+        m = a.m_part[(s0 + ch) * a.G + g];
+        l = a.l_part[(s0 + ch) * a.G + g];
+        if (!(l > 0.f)) m = -INFINITY;
+      }
+      float M = m;
 #pragma unroll
-      for (int i = 0; i < PER; ++i) acc[i] = acc[i] * s_old + ap[i] * s_new;
-      L = L * s_old + l * s_new;
-      M = Mn;
+      for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+      // chunks of this round are merged relative to their own max; rounds
+      // (only when nact > 32) are rare and combined by rescaling below
+      const float w = (m == -INFINITY) ? 0.f : exp2f(m - M);
+      float lw = w * l;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, o);
+      float racc[PER];
+#pragma unroll
+      for (int i = 0; i < PER; ++i) racc[i] = 0.f;
+      const int n = min(32, nact - base);
+#pragma unroll 8
+      for (int j = 0; j < n; ++j) {
+        const float wj = __shfl_sync(0xffffffffu, w, j);
+        const float* ap = a.acc_part + ((s0 + base + j) * a.G + g) * D + lane * PER;
+#pragma unroll
+        for (int i = 0; i < PER; i += 2) {
+          const float2 x = __ldcg(reinterpret_cast<const float2*>(ap + i));
+          racc[i] += wj * x.x;
+          racc[i + 1] += wj * x.y;
+        }
+      }
+      if (base == 0 || Mrun == -INFINITY) {
+#pragma unroll
+        for (int i = 0; i < PER; ++i) acc[i] = racc[i];
+        L = lw;
+        Mrun = M;
+      } else if (M > -INFINITY) {
+        const float Mn = fmaxf(Mrun, M);
+        const float so = exp2f(Mrun - Mn), sn = exp2f(M - Mn);
+#pragma unroll
+        for (int i = 0; i < PER; ++i) acc[i] = acc[i] * so + racc[i] * sn;
+        L = L * so + lw * sn;
+        Mrun = Mn;
+      }
     }
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
@@ -382,11 +425,11 @@ int launch_decode(const DecArgs& a, cudaStream_t st) {
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecThreads, smem);
   if (per_sm < 1) per_sm = 1;
   const int grid = num_sms() * per_sm;
-  kern<<<grid, kDecThreads, smem, st>>>(a);
+  if (int rc = launch_pdl(kern, dim3(grid), dim3(kDecThreads), smem, st, a)) return rc;
   int rc = launch_status();
   if (rc) return rc;
   const int heads = a.n_req * a.n_kv * a.G;
-  merge_kernel<D><<<(heads + 3) / 4, 128, 0, st>>>(a);
+  if (int rc = launch_pdl(merge_kernel<D>, dim3((heads + 3) / 4), dim3(128), 0, st, a)) return rc;
   return launch_status();
 }
 

@@ -5,19 +5,36 @@
 //     qmu_g  = mu_code . q_g            q~_{g,k} = V_code[:,k] . q_g
 //     S_g    = s*mu_scale*qmu_g + s^2/(2P) * sum_k sig2_k (V_scale_k q~_{g,k})^2
 //
-// Layout of the work.  One CTA = 8 warps covers 16*TPC pages of one request
-// for every kv-head; a warp owns (16-page tile, kv-head) items, so the 8 heads
-// of a block -- whose summaries are contiguous rows -- are read by sibling
-// warps at the same time and share their DRAM sectors.  Within a warp the
-// three (or 1+rank) dot products per (page, head) run on the tensor cores as
-// m16n8k16 MMAs:  A = integer codes (16 pages x 16 d) converted exactly to
-// fp16 in registers,  B = q^T (16 d x 8 query heads, fp16),  C = fp32.  The
-// d <-> k-slot assignment is a fixed permutation shared by A and B, chosen so
-// each lane's loads are contiguous.
+// Work decomposition.  A work item is (16-page tile of one request, kv-head).
+// The grid is persistent; warp gw owns kv-head gw % n_kv and one contiguous
+// range of tiles, so the n_kv heads of a tile -- whose summary rows are
+// adjacent in memory -- are read by sibling warps at the same time and share
+// DRAM sectors, and a warp's q operand changes only when its range enters a
+// new request.  Each warp runs a three-deep register pipeline: block-table
+// reads two tiles ahead, the 16-byte summary loads one tile ahead, the
+// tensor-core math on the current tile.
+//
+// Math on the tensor cores: the 1+rank dot products of 16 pages with the G
+// query heads are integer MMAs (m16n8k32, s8 x s8 -> s32).  A = the raw int8
+// summary codes (an int4 code is used as 16*code, one mask away from its
+// packed byte), B = q split exactly into two int8 limbs,
+// q ~= s_q * (128*hi + lo) with s_q = max|q_g| / 16256 (a prologue kernel
+// writes the limbs once per call into caller scratch).  Products and sums are
+// exact integers; the only rounding is the 15-bit limb form of q
+// (|dq| <= max|q| / 32512).  Lane (m, c) owns pages m and m+8 and the
+// contiguous head_dim slice [c*D/4, (c+1)*D/4); A and B use the same
+// d <-> k-slot assignment, so code words feed the MMA without byte shuffles.
+//
+// With the nrm combine the kernel also max-accumulates the per-head page
+// maximum into hmax[r, h, g]; the fold (nrm_combine / select_pages) consumes
+// it and resets it to -inf, so the fold is a single pass.
 #include "common.cuh"
 
 namespace amass {
 namespace {
+
+constexpr int kQuadWarps = 8;
+constexpr int kQuadMaxReq = 4096;
 
 struct QuadArgs {
   const __nv_bfloat16* q;
@@ -32,208 +49,453 @@ struct QuadArgs {
   const int32_t* nsh;
   float* score;
   float* score_h;
+  float* hmax;
+  int8_t* q8;        // (n_req, H, 2, D): hi limb then lo limb per head
+  float* qs;         // (n_req, H) limb scale
   float scale, coef;
-  int n_kv, G, MP, tpc;
+  int n_req, n_kv, G, MP;
 };
 
-template <int NB>
-struct VecLoad;
-template <>
-struct VecLoad<4> {
-  static AMASS_DEV void ld(const int8_t* p, uint32_t* w) {
-    w[0] = __ldg(reinterpret_cast<const unsigned int*>(p));
-  }
-};
-template <>
-struct VecLoad<8> {
-  static AMASS_DEV void ld(const int8_t* p, uint32_t* w) {
-    uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
-    w[0] = v.x; w[1] = v.y;
-  }
-};
-template <>
-struct VecLoad<16> {
-  static AMASS_DEV void ld(const int8_t* p, uint32_t* w) {
-    uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
-    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
-  }
-};
-template <>
-struct VecLoad<32> {
-  static AMASS_DEV void ld(const int8_t* p, uint32_t* w) {
-    VecLoad<16>::ld(p, w);
-    VecLoad<16>::ld(p + 16, w + 4);
-  }
-};
+AMASS_DEV void atomic_max_float(float* addr, float v) {
+  if (v >= 0.f)
+    atomicMax(reinterpret_cast<int*>(addr), __float_as_int(v));
+  else
+    atomicMin(reinterpret_cast<unsigned int*>(addr), __float_as_uint(v));
+}
 
-// Code pair (d0+i, d0+i+1) of column k from a k-step's V bytes (4 d values).
-template <int R, int VB, int K, int I>
-AMASS_DEV uint32_t v_pair(const uint32_t* w) {
-  if constexpr (VB == 8) {
-    constexpr int BI = I * R + K, BJ = (I + 1) * R + K;
-    return i8pair_to_h2(pick2<BI, BJ>(w[BI / 4], w[BJ / 4]));
+AMASS_DEV void mma_s8(int* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// ---- prologue: q -> two exact-range int8 limbs per (request, head) --------
+template <int D>
+__global__ void __launch_bounds__(256) q_limbs_kernel(QuadArgs a) {
+  grid_dep_wait();     // inputs written by the previous kernel
+  grid_dep_launch();
+  const int H = a.n_kv * a.G;
+  const int idx = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (idx >= a.n_req * H) return;
+  const int r = idx / H, h = idx - r * H;
+  const __nv_bfloat16* qp = a.q + (int64_t)r * a.q_st + (int64_t)h * a.q_sh;
+  constexpr int PER = D / 32;
+  float v[PER];
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    v[i] = __bfloat162float(qp[lane * PER + i]);
+    mx = fmaxf(mx, fabsf(v[i]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const float sq = mx > 0.f ? mx / 16256.f : 1.f;
+  const float inv = 1.f / sq;
+  int8_t* hi = a.q8 + (int64_t)idx * 2 * D;
+  int8_t* lo = hi + D;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int qi = __float2int_rn(v[i] * inv);            // |qi| <= 16256
+    const int h8 = (qi >= 0 ? qi + 64 : qi - 63) / 128;   // nearest, |h8|<=127
+    hi[lane * PER + i] = (int8_t)h8;
+    lo[lane * PER + i] = (int8_t)(qi - 128 * h8);         // |lo| <= 64
+  }
+  if (lane == 0) a.qs[idx] = sq;
+}
+
+// 4 code bytes (d0..d0+3) of byte-column KB from a step's V words, RB bytes/d
+template <int RB, int KB>
+AMASS_DEV uint32_t gather4(const uint32_t* w) {
+  if constexpr (RB == 1) {
+    return w[0];
+  } else if constexpr (RB == 2) {
+    return __byte_perm(w[0], w[1], KB | ((2 + KB) << 4) | ((4 + KB) << 8) |
+                                        ((6 + KB) << 12));
   } else {
-    constexpr int RB = R / 2;
-    constexpr int BI = I * RB + K / 2, BJ = (I + 1) * RB + K / 2;
-    uint32_t x = pick2<BI, BJ>(w[BI / 4], w[BJ / 4]);
-    if (K & 1) x >>= 4;
-    return i4pair_to_h2(x);
+    constexpr int B0 = KB, B1 = RB + KB, B2 = 2 * RB + KB, B3 = 3 * RB + KB;
+    const uint32_t x = __byte_perm(w[B0 / 4], w[B1 / 4], (B0 & 3) | ((4 + (B1 & 3)) << 4));
+    const uint32_t y = __byte_perm(w[B2 / 4], w[B3 / 4], (B2 & 3) | ((4 + (B3 & 3)) << 4));
+    return __byte_perm(x, y, 0x5410);
+  }
+}
+// column K of 4 consecutive d: int8 codes, or 16 * int4 codes
+template <int R, int VB, int K>
+AMASS_DEV uint32_t vcol4(const uint32_t* w) {
+  if constexpr (VB == 8) {
+    return gather4<R, K>(w);
+  } else {
+    const uint32_t x = gather4<R / 2, K / 2>(w);
+    return (K & 1) ? (x & 0xF0F0F0F0u) : ((x << 4) & 0xF0F0F0F0u);
   }
 }
 
 template <int R, int VB, int K>
 struct VCols {
-  static AMASS_DEV void run(float (*acc)[4], const uint32_t* wa,
-                            const uint32_t* wb, uint32_t b0, uint32_t b1) {
+  // wa/wb: the step's V words for rows a/b (2*RB words: d0..d0+7)
+  static AMASS_DEV void run(int (*acc)[2][4], const uint32_t* wa,
+                            const uint32_t* wb, const uint32_t* bh,
+                            const uint32_t* bl) {
+    constexpr int RB = (VB == 8) ? R : R / 2;
     uint32_t a[4];
-    a[0] = v_pair<R, VB, K, 0>(wa);
-    a[1] = v_pair<R, VB, K, 0>(wb);
-    a[2] = v_pair<R, VB, K, 2>(wa);
-    a[3] = v_pair<R, VB, K, 2>(wb);
-    mma_f16(acc[1 + K], a, b0, b1);
-    if constexpr (K + 1 < R) VCols<R, VB, K + 1>::run(acc, wa, wb, b0, b1);
+    a[0] = vcol4<R, VB, K>(wa);
+    a[1] = vcol4<R, VB, K>(wb);
+    a[2] = vcol4<R, VB, K>(wa + RB);
+    a[3] = vcol4<R, VB, K>(wb + RB);
+    mma_s8(acc[1 + K][0], a, bh[0], bh[1]);
+    mma_s8(acc[1 + K][1], a, bl[0], bl[1]);
+    if constexpr (K + 1 < R) VCols<R, VB, K + 1>::run(acc, wa, wb, bh, bl);
   }
 };
 
-template <int D, int R, int VB, bool WRITE_H>
-__global__ void __launch_bounds__(256)
-quad_score_kernel(QuadArgs a) {
-  constexpr int KS = D / 16;                 // MMA k-steps over head_dim
-  constexpr int RB = (VB == 8) ? R : R / 2;  // V code bytes per d
-  constexpr int VSTEP = 4 * RB;              // V bytes per k-step per page
-  const int r = blockIdx.y;
-  const int nsh = a.nsh[r];
-  const int pbase = blockIdx.x * 16 * a.tpc;
-  if (pbase >= nsh) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m = lane >> 2, c = lane & 3;
-  const int n_items = a.tpc * a.n_kv;
+// Per-lane view of one item: two page rows (m, m+8) of one kv-head.
+template <int D, int R, int VB>
+struct Item {
+  static constexpr int RB = (VB == 8) ? R : R / 2;   // V code bytes per d
+  static constexpr int MU_U4 = D / 64;               // mu bytes per lane / 16
+  static constexpr int V_BYTES = (D / 4) * RB;       // V bytes per lane
+  static constexpr bool V_PRE = V_BYTES <= 64;       // keep V in registers
+  static constexpr int V_U4 = V_PRE ? V_BYTES / 16 : 1;
+  static constexpr int RW = (R + 1) / 2;             // 32-bit words / row
+  int r, h, p0;
+  bool va, vb;
+  int rowa, rowb;               // block id, then block * n_kv + head
+  uint4 mu[2][MU_U4];
+  uint4 v[2][V_U4];
+  __half2 mus;                  // (row a, row b)
+  uint32_t vs[2][RW], s2[2][RW];  // fp16 scales, two per word
+  AMASS_DEV float vsf(int half, int k) const {
+    const uint32_t w = vs[half][k >> 1];
+    return __half2float(__ushort_as_half((uint16_t)((k & 1) ? (w >> 16) : w)));
+  }
+  AMASS_DEV float s2f(int half, int k) const {
+    const uint32_t w = s2[half][k >> 1];
+    return __half2float(__ushort_as_half((uint16_t)((k & 1) ? (w >> 16) : w)));
+  }
+};
 
-  for (int item = warp; item < n_items; item += 8) {
-    const int t = item / a.n_kv, h = item - t * a.n_kv;
-    const int p0 = pbase + 16 * t;
-    if (p0 >= nsh) break;
-    const int pa = p0 + m, pb = pa + 8;
-    const bool va = pa < nsh, vb = pb < nsh;
-    const int32_t* btr = a.bt + (int64_t)r * a.bt_stride;
-    const int64_t blka = va ? btr[pa] : 0;
-    const int64_t blkb = vb ? btr[pb] : 0;
-    const int64_t rowa = blka * a.n_kv + h, rowb = blkb * a.n_kv + h;
-
-    // B operand: q^T for query heads g = m of this kv group (zero beyond G)
-    uint32_t qb[KS][2];
-    {
-      const bool gv = m < a.G;
-      const __nv_bfloat16* qp =
-          a.q + (int64_t)r * a.q_st + (int64_t)(h * a.G + (gv ? m : 0)) * a.q_sh;
+// R fp16 values at p into RW words (two per word; R odd only for R == 1)
+template <int R>
+AMASS_DEV void load_halves(uint32_t* w, const __half* p) {
+  if constexpr (R == 1) {
+    w[0] = __ldg(reinterpret_cast<const unsigned short*>(p));
+  } else {
 #pragma unroll
-      for (int s = 0; s < KS; ++s) {
-        uint2 w = __ldg(reinterpret_cast<const uint2*>(qp + 16 * s + 4 * c));
-        qb[s][0] = gv ? pack_h2(bf16_lo(w.x), bf16_hi(w.x)) : 0u;
-        qb[s][1] = gv ? pack_h2(bf16_lo(w.y), bf16_hi(w.y)) : 0u;
+    for (int k = 0; k < R / 2; ++k)
+      w[k] = __ldg(reinterpret_cast<const unsigned int*>(p) + k);
+  }
+}
+
+// index phase: tile -> (request, first page), block-table reads -> rows
+template <int D, int R, int VB>
+AMASS_DEV void load_idx(Item<D, R, VB>& it, const QuadArgs& a,
+                        const int* prefix, const int* nshs, int item,
+                        int lane, int* rhint = nullptr) {
+  const int t = item / a.n_kv;
+  const int h = item - t * a.n_kv;
+  int r;
+  if (rhint) {                       // tiles ascend: walk forward from hint
+    r = *rhint;
+    while (prefix[r + 1] <= t) ++r;
+    *rhint = r;
+  } else {
+    int lo = 0, hi = a.n_req - 1;    // request of tile t
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (prefix[mid] <= t) lo = mid; else hi = mid - 1;
+    }
+    r = lo;
+  }
+  const int nsh = nshs[r];
+  const int p0 = (t - prefix[r]) * 16;
+  const int m = lane >> 2;
+  const int pa = p0 + m, pb = pa + 8;
+  it.r = r; it.h = h; it.p0 = p0;
+  it.va = pa < nsh; it.vb = pb < nsh;
+  const int32_t* btr = a.bt + (int64_t)r * a.bt_stride;
+  it.rowa = it.va ? __ldg(btr + pa) : 0;    // block ids; scaled in load_data
+  it.rowb = it.vb ? __ldg(btr + pb) : 0;
+}
+
+// data phase: the 16-byte summary loads of an item whose block ids are known
+template <int D, int R, int VB>
+AMASS_DEV void load_data(Item<D, R, VB>& it, const QuadArgs& a, int lane) {
+  using I = Item<D, R, VB>;
+  const int c = lane & 3;
+  it.rowa = it.rowa * a.n_kv + it.h;
+  it.rowb = it.rowb * a.n_kv + it.h;
+  const int8_t* mua = a.mu + (int64_t)it.rowa * D + c * (D / 4);
+  const int8_t* mub = a.mu + (int64_t)it.rowb * D + c * (D / 4);
+#pragma unroll
+  for (int i = 0; i < I::MU_U4; ++i) {
+    it.mu[0][i] = ldg_nc_v4(mua + 16 * i);
+    it.mu[1][i] = ldg_nc_v4(mub + 16 * i);
+  }
+  if constexpr (I::V_PRE) {
+    const int8_t* Va = a.V + (int64_t)it.rowa * (D * I::RB) + c * I::V_BYTES;
+    const int8_t* Vb = a.V + (int64_t)it.rowb * (D * I::RB) + c * I::V_BYTES;
+#pragma unroll
+    for (int i = 0; i < I::V_U4; ++i) {
+      it.v[0][i] = ldg_nc_v4(Va + 16 * i);
+      it.v[1][i] = ldg_nc_v4(Vb + 16 * i);
+    }
+  }
+  __half2 ms;
+  ms.x = a.mus[it.rowa];
+  ms.y = a.mus[it.rowb];
+  it.mus = ms;
+  load_halves<R>(it.vs[0], a.Vs + (int64_t)it.rowa * R);
+  load_halves<R>(it.vs[1], a.Vs + (int64_t)it.rowb * R);
+  load_halves<R>(it.s2[0], a.sig2 + (int64_t)it.rowa * R);
+  load_halves<R>(it.s2[1], a.sig2 + (int64_t)it.rowb * R);
+}
+
+// q operand of one (request, kv-head): limbs for B fragments + limb scales
+template <int D>
+struct QFrag {
+  static constexpr int KS = D / 32;
+  uint32_t bh[KS][2], bl[KS][2];
+  float sq[2];
+};
+
+template <int D>
+AMASS_DEV void load_qfrag(QFrag<D>& f, const QuadArgs& a, int r, int h,
+                          int lane) {
+  constexpr int KS = D / 32;
+  const int m = lane >> 2, c = lane & 3;
+  const int H = a.n_kv * a.G;
+  const bool gv = m < a.G;
+  const int64_t qrow = (int64_t)r * H + h * a.G + (gv ? m : 0);
+  const int8_t* qh = a.q8 + qrow * 2 * D + c * (D / 4);
+  const int8_t* ql = qh + D;
+#pragma unroll
+  for (int i = 0; i < KS / 2; ++i) {
+    const uint4 x = __ldg(reinterpret_cast<const uint4*>(qh) + i);
+    const uint4 y = __ldg(reinterpret_cast<const uint4*>(ql) + i);
+    f.bh[2 * i][0] = gv ? x.x : 0u; f.bh[2 * i][1] = gv ? x.y : 0u;
+    f.bh[2 * i + 1][0] = gv ? x.z : 0u; f.bh[2 * i + 1][1] = gv ? x.w : 0u;
+    f.bl[2 * i][0] = gv ? y.x : 0u; f.bl[2 * i][1] = gv ? y.y : 0u;
+    f.bl[2 * i + 1][0] = gv ? y.z : 0u; f.bl[2 * i + 1][1] = gv ? y.w : 0u;
+  }
+  const int g0 = min(2 * c, a.G - 1), g1 = min(2 * c + 1, a.G - 1);
+  const float* qsr = a.qs + (int64_t)r * H + h * a.G;
+  f.sq[0] = __ldg(qsr + g0);
+  f.sq[1] = __ldg(qsr + g1);
+}
+
+template <int D, int R, int VB, bool WRITE_H>
+AMASS_DEV void score_item(const Item<D, R, VB>& it, const QFrag<D>& qf,
+                          const QuadArgs& a, int lane) {
+  using I = Item<D, R, VB>;
+  constexpr int KS = D / 32;                 // m16n8k32 steps
+  constexpr int RB = I::RB;
+  const int m = lane >> 2, c = lane & 3;
+  const uint32_t (*bh)[2] = qf.bh;
+  const uint32_t (*bl)[2] = qf.bl;
+  int acc[1 + R][2][4];
+#pragma unroll
+  for (int i = 0; i <= R; ++i)
+#pragma unroll
+    for (int l = 0; l < 2; ++l)
+      acc[i][l][0] = acc[i][l][1] = acc[i][l][2] = acc[i][l][3] = 0;
+  const uint32_t* mwa = reinterpret_cast<const uint32_t*>(it.mu[0]);
+  const uint32_t* mwb = reinterpret_cast<const uint32_t*>(it.mu[1]);
+#pragma unroll
+  for (int s = 0; s < KS; ++s) {
+    const uint32_t am[4] = {mwa[2 * s], mwb[2 * s], mwa[2 * s + 1], mwb[2 * s + 1]};
+    mma_s8(acc[0][0], am, bh[s][0], bh[s][1]);
+    mma_s8(acc[0][1], am, bl[s][0], bl[s][1]);
+    uint32_t wva[2 * RB], wvb[2 * RB];
+    if constexpr (I::V_PRE) {
+      const uint32_t* va = reinterpret_cast<const uint32_t*>(it.v[0]);
+      const uint32_t* vb = reinterpret_cast<const uint32_t*>(it.v[1]);
+#pragma unroll
+      for (int j = 0; j < 2 * RB; ++j) {
+        wva[j] = va[s * 2 * RB + j];
+        wvb[j] = vb[s * 2 * RB + j];
+      }
+    } else {
+      const int8_t* Va = a.V + (int64_t)it.rowa * (D * RB) + c * I::V_BYTES + s * 8 * RB;
+      const int8_t* Vb = a.V + (int64_t)it.rowb * (D * RB) + c * I::V_BYTES + s * 8 * RB;
+#pragma unroll
+      for (int j = 0; j < 2 * RB; j += 4) {
+        const uint4 x = __ldg(reinterpret_cast<const uint4*>(Va) + j / 4);
+        const uint4 y = __ldg(reinterpret_cast<const uint4*>(Vb) + j / 4);
+        wva[j] = x.x; wva[j + 1] = x.y; wva[j + 2] = x.z; wva[j + 3] = x.w;
+        wvb[j] = y.x; wvb[j + 1] = y.y; wvb[j + 2] = y.z; wvb[j + 3] = y.w;
       }
     }
+    VCols<R, VB, 0>::run(acc, wva, wvb, bh[s], bl[s]);
+  }
 
-    float acc[1 + R][4];
+  // epilogue: rows pa (idx 0,1) and pb (idx 2,3); cols g = 2c, 2c+1
+  const float* sq = qf.sq;
+  constexpr float vdiv = (VB == 8) ? 1.f : 1.f / 16.f;
+  float S[2][2];
 #pragma unroll
-    for (int i = 0; i <= R; ++i)
-      acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-
-    const int8_t* mua = a.mu + rowa * D;
-    const int8_t* mub = a.mu + rowb * D;
-    const int8_t* Va = a.V + rowa * (D * RB);
-    const int8_t* Vb = a.V + rowb * (D * RB);
+  for (int half = 0; half < 2; ++half) {
+    const float mus = half ? __high2float(it.mus) : __low2float(it.mus);
 #pragma unroll
-    for (int s = 0; s < KS; ++s) {
-      const int d0 = 16 * s + 4 * c;
-      uint32_t wma, wmb;
-      VecLoad<4>::ld(mua + d0, &wma);
-      VecLoad<4>::ld(mub + d0, &wmb);
-      uint32_t wva[VSTEP / 4 > 0 ? VSTEP / 4 : 1], wvb[VSTEP / 4 > 0 ? VSTEP / 4 : 1];
-      VecLoad<VSTEP>::ld(Va + d0 * RB, wva);
-      VecLoad<VSTEP>::ld(Vb + d0 * RB, wvb);
-      uint32_t am[4];
-      am[0] = i8pair_to_h2(pick2<0, 1>(wma, wma));
-      am[1] = i8pair_to_h2(pick2<0, 1>(wmb, wmb));
-      am[2] = i8pair_to_h2(pick2<2, 3>(wma, wma));
-      am[3] = i8pair_to_h2(pick2<2, 3>(wmb, wmb));
-      mma_f16(acc[0], am, qb[s][0], qb[s][1]);
-      VCols<R, VB, 0>::run(acc, wva, wvb, qb[s][0], qb[s][1]);
+    for (int j = 0; j < 2; ++j) {
+      const int idx = 2 * half + j;
+      float quad = 0.f;
+#pragma unroll
+      for (int k = 0; k < R; ++k) {
+        const float vs = it.vsf(half, k);
+        const float s2 = it.s2f(half, k);
+        const float qt = (float)(128 * acc[1 + k][0][idx] + acc[1 + k][1][idx]) *
+                         (sq[j] * vdiv) * vs;
+        quad += s2 * qt * qt;
+      }
+      const float qmu = (float)(128 * acc[0][0][idx] + acc[0][1][idx]) * sq[j];
+      S[half][j] = qmu * mus * a.scale + quad * a.coef;
     }
-
-    // epilogue: rows pa (acc[.][0..1]) and pb (acc[.][2..3]); cols g = 2c, 2c+1
+  }
+  const int pa = it.p0 + m, pb = pa + 8;
+  if constexpr (WRITE_H) {
+    float* base = a.score_h + ((int64_t)it.r * a.n_kv + it.h) * a.G * a.MP;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int g = 2 * c + j;
+      float mx = -INFINITY;
+      if (g < a.G) {
+        if (it.va) { base[(int64_t)g * a.MP + pa] = S[0][j]; mx = S[0][j]; }
+        if (it.vb) { base[(int64_t)g * a.MP + pb] = S[1][j]; mx = fmaxf(mx, S[1][j]); }
+      }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      if (m == 0 && g < a.G && mx > -INFINITY)
+        atomic_max_float(a.hmax + ((int64_t)it.r * a.n_kv + it.h) * a.G + g, mx);
+    }
+  } else {
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
-      const int p = half ? pb : pa;
-      const bool pv = half ? vb : va;
-      const int64_t row = half ? rowb : rowa;
-      float S[2] = {-INFINITY, -INFINITY};
-      if (pv) {
-        const float mus = __half2float(a.mus[row]);
-        float vs[R], s2[R];
-#pragma unroll
-        for (int k = 0; k < R; ++k) {
-          vs[k] = __half2float(a.Vs[row * R + k]);
-          s2[k] = __half2float(a.sig2[row * R + k]);
-        }
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int idx = 2 * half + j;
-          float quad = 0.f;
-#pragma unroll
-          for (int k = 0; k < R; ++k) {
-            const float qt = acc[1 + k][idx] * vs[k];
-            quad += s2[k] * qt * qt;
-          }
-          S[j] = acc[0][idx] * mus * a.scale + quad * a.coef;
-        }
-      }
-      if constexpr (WRITE_H) {
-        if (pv) {
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const int g = 2 * c + j;
-            if (g < a.G)
-              a.score_h[(((int64_t)r * a.n_kv + h) * a.G + g) * a.MP + p] = S[j];
-          }
-        }
-      } else {
-        float mx = (2 * c < a.G) ? S[0] : -INFINITY;
-        if (2 * c + 1 < a.G) mx = fmaxf(mx, S[1]);
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        if (pv && c == 0)
-          a.score[((int64_t)r * a.n_kv + h) * a.MP + p] = mx;
-      }
+      float mx = (2 * c < a.G) ? S[half][0] : -INFINITY;
+      if (2 * c + 1 < a.G) mx = fmaxf(mx, S[half][1]);
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const bool pv = half ? it.vb : it.va;
+      if (pv && c == 0)
+        a.score[((int64_t)it.r * a.n_kv + it.h) * a.MP + (half ? pb : pa)] = mx;
     }
+  }
+}
+
+// two CTAs per SM (<= 128 registers) when a lane's V slice is <= 32 bytes
+template <int D, int R, int VB>
+constexpr int quad_min_blocks() {
+  return (D / 4) * ((VB == 8) ? R : R / 2) <= 32 ? 2 : 1;
+}
+
+template <int D, int R, int VB, bool WRITE_H>
+__global__ void __launch_bounds__(kQuadWarps * 32, (quad_min_blocks<D, R, VB>()))
+quad_score_kernel(QuadArgs a) {
+  grid_dep_wait();     // inputs written by the previous kernel
+  grid_dep_launch();
+  __shared__ int prefix[kQuadMaxReq + 1];   // per-request tile offsets
+  __shared__ int nshs[kQuadMaxReq];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) {
+    int run = 0;
+    for (int base = 0; base < a.n_req; base += 32) {
+      const int r = base + lane;
+      const int nsh = r < a.n_req ? max(a.nsh[r], 0) : 0;
+      const int t = (nsh + 15) / 16;
+      int incl = t;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int x = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += x;
+      }
+      if (r < a.n_req) { prefix[r] = run + incl - t; nshs[r] = nsh; }
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) prefix[a.n_req] = run;
+  }
+  __syncthreads();
+  // warp gw owns head gw % n_kv and a contiguous range of tiles, so its q
+  // operand changes only when the range crosses into the next request; the
+  // n_kv heads of a tile run on sibling warps at the same time
+  const int T = prefix[a.n_req];
+  const int gw = blockIdx.x * kQuadWarps + warp;
+  const int NJ = gridDim.x * kQuadWarps / a.n_kv;
+  const int j = gw / a.n_kv;
+  if (j >= NJ) return;
+  const int h = gw - j * a.n_kv;
+  const int t_lo = (int)((int64_t)T * j / NJ);
+  const int t_hi = (int)((int64_t)T * (j + 1) / NJ);
+  if (t_lo >= t_hi) return;
+  // three-deep pipeline per warp: block ids two tiles ahead, summary data
+  // one tile ahead, compute on the current one
+  int rh = 0;
+  {
+    int lo = 0, hi = a.n_req - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (prefix[mid] <= t_lo) lo = mid; else hi = mid - 1;
+    }
+    rh = lo;
+  }
+  Item<D, R, VB> cur, nxt, nn;
+  QFrag<D> qf;
+  int qr = -1;
+  int t = t_lo;
+  load_idx(cur, a, prefix, nshs, t * a.n_kv + h, lane, &rh);
+  load_data(cur, a, lane);
+  if (t + 1 < t_hi) load_idx(nxt, a, prefix, nshs, (t + 1) * a.n_kv + h, lane, &rh);
+  while (true) {
+    const bool more = t + 1 < t_hi;
+    if (t + 2 < t_hi) load_idx(nn, a, prefix, nshs, (t + 2) * a.n_kv + h, lane, &rh);
+    if (more) load_data(nxt, a, lane);
+    if (cur.r != qr) {
+      load_qfrag(qf, a, cur.r, h, lane);
+      qr = cur.r;
+    }
+    score_item<D, R, VB, WRITE_H>(cur, qf, a, lane);
+    if (!more) break;
+    cur = nxt;
+    nxt = nn;
+    ++t;
   }
 }
 
 template <int D, int R, int VB>
-int launch_quad(const QuadArgs& a, int n_req, bool write_h, cudaStream_t st) {
-  dim3 grid((a.MP + 16 * a.tpc - 1) / (16 * a.tpc), n_req);
-  if (write_h)
-    quad_score_kernel<D, R, VB, true><<<grid, 256, 0, st>>>(a);
-  else
-    quad_score_kernel<D, R, VB, false><<<grid, 256, 0, st>>>(a);
+int launch_quad(const QuadArgs& a, bool write_h, cudaStream_t st) {
+  auto k = write_h ? quad_score_kernel<D, R, VB, true>
+                   : quad_score_kernel<D, R, VB, false>;
+  static int per_sm[2] = {0, 0};
+  int& ps = per_sm[write_h ? 1 : 0];
+  if (ps == 0) {
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ps, k, kQuadWarps * 32, 0);
+    if (ps < 1) ps = 1;
+  }
+  const int heads = a.n_req * a.n_kv * a.G;
+  if (int rc = launch_pdl(q_limbs_kernel<D>, dim3((heads + 7) / 8), dim3(256), 0, st, a)) return rc;
+  int grid = num_sms() * ps;
+  const int per = a.n_kv > kQuadWarps ? a.n_kv / kQuadWarps : 1;
+  grid = (grid / per) * per;   // warps per grid a multiple of n_kv
+  if (int rc = launch_pdl(k, dim3(grid), dim3(kQuadWarps * 32), 0, st, a)) return rc;
   return launch_status();
 }
 
 template <int D>
-int dispatch_rank(const QuadArgs& a, int n_req, int rank, int v_bits,
-                  bool write_h, cudaStream_t st) {
+int dispatch_rank(const QuadArgs& a, int rank, int v_bits, bool write_h,
+                  cudaStream_t st) {
   if (v_bits == 8) {
     switch (rank) {
-      case 1: return launch_quad<D, 1, 8>(a, n_req, write_h, st);
-      case 2: return launch_quad<D, 2, 8>(a, n_req, write_h, st);
-      case 4: return launch_quad<D, 4, 8>(a, n_req, write_h, st);
-      case 8: return launch_quad<D, 8, 8>(a, n_req, write_h, st);
+      case 1: return launch_quad<D, 1, 8>(a, write_h, st);
+      case 2: return launch_quad<D, 2, 8>(a, write_h, st);
+      case 4: return launch_quad<D, 4, 8>(a, write_h, st);
+      case 8: return launch_quad<D, 8, 8>(a, write_h, st);
     }
   } else if (v_bits == 4) {
     switch (rank) {
-      case 2: return launch_quad<D, 2, 4>(a, n_req, write_h, st);
-      case 4: return launch_quad<D, 4, 4>(a, n_req, write_h, st);
-      case 8: return launch_quad<D, 8, 4>(a, n_req, write_h, st);
+      case 2: return launch_quad<D, 2, 4>(a, write_h, st);
+      case 4: return launch_quad<D, 4, 4>(a, write_h, st);
+      case 8: return launch_quad<D, 8, 4>(a, write_h, st);
     }
   }
   return AMASS_ERR_UNSUPPORTED;
@@ -248,7 +510,8 @@ extern "C" int amass_quad_score(const void* q, int64_t q_stride_t,
                                 const void* V_scale, const void* sig2,
                                 const int32_t* block_table, int64_t bt_stride,
                                 const int32_t* n_sel_hi, float* score,
-                                float* score_h, float scale, int n_req,
+                                float* score_h, float* hmax, int8_t* q8_ws,
+                                float* qs_ws, float scale, int n_req,
                                 int n_kv, int G, int head_dim, int page,
                                 int rank, int v_bits, int max_pages,
                                 int write_h, void* stream) {
@@ -256,12 +519,15 @@ extern "C" int amass_quad_score(const void* q, int64_t q_stride_t,
   if (n_req < 0 || n_kv <= 0 || G <= 0 || max_pages <= 0) return AMASS_ERR_ARG;
   if (n_req == 0) return AMASS_OK;
   if (!q || !mu || !mu_scale || !V || !V_scale || !sig2 || !block_table ||
-      !n_sel_hi)
+      !n_sel_hi || !q8_ws || !qs_ws)
     return AMASS_ERR_ARG;
-  if (write_h ? !score_h : !score) return AMASS_ERR_ARG;
-  if (G > 8 || page != 16) return AMASS_ERR_UNSUPPORTED;
-  if ((q_stride_h % 4) != 0 || (q_stride_t % 4) != 0 ||
-      (reinterpret_cast<uintptr_t>(q) & 7))
+  if (write_h ? (!score_h || !hmax) : !score) return AMASS_ERR_ARG;
+  if (G > 8 || page != 16 || n_req > kQuadMaxReq) return AMASS_ERR_UNSUPPORTED;
+  // 16-byte loads of summary rows and of the q limbs
+  if ((q_stride_h % 2) || (q_stride_t % 2) ||
+      (reinterpret_cast<uintptr_t>(mu) & 15) ||
+      (reinterpret_cast<uintptr_t>(V) & 15) ||
+      (reinterpret_cast<uintptr_t>(q8_ws) & 15))
     return AMASS_ERR_ARG;
   QuadArgs a;
   a.q = static_cast<const __nv_bfloat16*>(q);
@@ -277,17 +543,18 @@ extern "C" int amass_quad_score(const void* q, int64_t q_stride_t,
   a.nsh = n_sel_hi;
   a.score = score;
   a.score_h = score_h;
+  a.hmax = hmax;
+  a.q8 = q8_ws;
+  a.qs = qs_ws;
   a.scale = scale;
   a.coef = scale * scale * (1.0f / (2.0f * page));
+  a.n_req = n_req;
   a.n_kv = n_kv;
   a.G = G;
   a.MP = max_pages;
-  // pages per CTA: 16 * tpc; aim for >= 8 warp items per CTA
-  int tpc = (n_kv >= 8) ? 1 : 8 / n_kv;
-  if (n_req >= 16) tpc *= 4;
-  a.tpc = tpc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (head_dim == 128) return dispatch_rank<128>(a, n_req, rank, v_bits, write_h, st);
-  if (head_dim == 64) return dispatch_rank<64>(a, n_req, rank, v_bits, write_h, st);
+  if (head_dim == 128) return dispatch_rank<128>(a, rank, v_bits, write_h, st);
+  if (head_dim == 64) return dispatch_rank<64>(a, rank, v_bits, write_h, st);
   return AMASS_ERR_UNSUPPORTED;
 }
+

@@ -4,18 +4,37 @@
 // Selection is a threshold rule (reference selection/select.py:60-101): tau is
 // the b-th largest score of the selectable region [sink, n_sel_hi); every page
 // with score >= tau is kept (ties all kept), plus the sinks, the recent window
-// and the partial tail; ids are written ascending and -1 padded.  tau is found
-// by an MSD radix select over order-preserving 32-bit keys held in shared
-// memory (4 passes x 8-bit digits).  The coverage mode runs the same radix
-// walk on per-digit MASS sums instead of counts, which lands on the smallest
-// b whose top-b pages hold the required mass.
+// and the partial tail; ids are written ascending and -1 padded.
+//
+// tau is found by an adaptive-range histogram select over order-preserving
+// 32-bit keys held in shared memory: each level histograms the keys of the
+// current range [lo, hi] into at most 1024 power-of-two-wide bins
+// (bin = (key - lo) >> shift), one warp scans the bins from the top to the
+// one holding the target rank -- or, in coverage mode, the target cumulative
+// MASS -- and the range shrinks to that bin.  A bin of at most 64 keys is
+// resolved exactly by ranking its members.  Typical units finish in one
+// level: one pass over global memory, one histogram pass, one compaction.
 #include "common.cuh"
 
 namespace amass {
 namespace {
 
-constexpr int kSelThreads = 512;
+constexpr int kSelThreads = 256;
 constexpr int kSelWarps = kSelThreads / 32;
+constexpr int kBins = 1024;
+constexpr int kCand = 64;
+
+#ifdef AMASS_SEL_PROBE
+__device__ unsigned long long g_sel_probe[8192 * 8];
+#define SEL_PROBE(k)                                                        \
+  if (threadIdx.x == 0) {                                                   \
+    unsigned long long t_;                                                  \
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                  \
+    g_sel_probe[blockIdx.x * 8 + (k)] = t_;                                 \
+  }
+#else
+#define SEL_PROBE(k)
+#endif
 
 // ---------------------------------------------------------------------------
 // derive_page_params (reference selection/select.py:30-45)
@@ -24,6 +43,8 @@ __global__ void derive_kernel(const int32_t* __restrict__ sl,
                               const double* __restrict__ budget,
                               int32_t* npg_o, int32_t* nsh_o, int32_t* b_o,
                               int n_req, int page, int win, int sink) {
+  grid_dep_wait();     // inputs written by the previous kernel
+  grid_dep_launch();
   const double bud = budget[0];
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_req;
        i += gridDim.x * blockDim.x) {
@@ -41,7 +62,6 @@ __global__ void derive_kernel(const int32_t* __restrict__ sl,
   }
 }
 
-// block-wide reductions for 512 threads
 template <typename T, typename Op>
 AMASS_DEV T block_reduce(T v, T* red, Op op) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -57,8 +77,9 @@ AMASS_DEV T block_reduce(T v, T* red, Op op) {
 }
 
 struct SelArgs {
-  const float* score_h;   // (R, n_kv, G, MP)      NRM input
-  float* score;           // (R, n_kv, MP)         MAX input / NRM output
+  const float* score_h;   // (R, n_kv, G, MP)   per-head scores (fold input)
+  float* hmax;            // (R, n_kv, G)       per-head page max (fold input)
+  float* score;           // (R, n_kv, MP)      combined score (in or out)
   const int32_t* npg;
   const int32_t* nsh;
   const int32_t* b_fix;
@@ -69,266 +90,427 @@ struct SelArgs {
   float coverage;
 };
 
-// nrm fold of one unit into shared sc[0, nsh); also writes score (contract of
-// reference quad_score.py:293-315).  hmax_out (R, n_kv, G) optional.
-AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int nsh, float* sc,
-                        float* red, float* hmax_out) {
+// nrm fold of one unit (reference quad_score.py:293-315): sc[p] =
+// sum_g exp(S_g[p] - hmax_g) for p < nsh; writes score; resets hmax to -inf.
+AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int nsh, float* sc) {
   const float* sh = a.score_h + (int64_t)unit * a.G * a.MP;
+  float* hm_g = a.hmax + (int64_t)unit * a.G;
   float hm[8];
 #pragma unroll
-  for (int g = 0; g < 8; ++g) hm[g] = -INFINITY;
-  for (int p = threadIdx.x; p < nsh; p += kSelThreads) {
-#pragma unroll
-    for (int g = 0; g < 8; ++g)
-      if (g < a.G) hm[g] = fmaxf(hm[g], sh[(int64_t)g * a.MP + p]);
-  }
-  auto mx = [](float x, float y) { return fmaxf(x, y); };
-#pragma unroll
-  for (int g = 0; g < 8; ++g)
-    if (g < a.G) hm[g] = block_reduce(hm[g], red, mx);
-  if (hmax_out && threadIdx.x < a.G) {
-#pragma unroll
-    for (int g = 0; g < 8; ++g)
-      if (g == (int)threadIdx.x) hmax_out[(int64_t)unit * a.G + g] = hm[g];
-  }
+  for (int g = 0; g < 8; ++g) hm[g] = g < a.G ? hm_g[g] : 0.f;
   float* so = a.score + (int64_t)unit * a.MP;
-  for (int p = threadIdx.x; p < nsh; p += kSelThreads) {
-    float s = 0.f;
+  // batches of pages per thread: every load of a batch issues before any
+  // use, so a long unit costs a few memory round trips, not one per page
+  if ((a.MP & 3) == 0) {
+    // 16-byte loads: thread owns page quads tid, tid + kSelThreads, ...
+    constexpr int kQ = 1;
+    const int nq = (nsh + 3) >> 2;
+    for (int q0 = threadIdx.x; q0 < nq; q0 += kQ * kSelThreads) {
+      float4 v[kQ][8];
 #pragma unroll
-    for (int g = 0; g < 8; ++g)
-      if (g < a.G) s += expf(sh[(int64_t)g * a.MP + p] - hm[g]);
-    sc[p] = s;
-    so[p] = s;
+      for (int i = 0; i < kQ; ++i) {
+        const int q = q0 + i * kSelThreads;
+#pragma unroll
+        for (int g = 0; g < 8; ++g)
+          v[i][g] = (g < a.G && q < nq)
+                        ? __ldcg(reinterpret_cast<const float4*>(sh + (int64_t)g * a.MP) + q)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int i = 0; i < kQ; ++i) {
+        const int q = q0 + i * kSelThreads;
+        if (q < nq) {
+          float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            if (g < a.G) {
+              s4[0] += expf(v[i][g].x - hm[g]);
+              s4[1] += expf(v[i][g].y - hm[g]);
+              s4[2] += expf(v[i][g].z - hm[g]);
+              s4[3] += expf(v[i][g].w - hm[g]);
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int p = 4 * q + e;
+            if (p < nsh) { sc[p] = s4[e]; so[p] = s4[e]; }
+          }
+        }
+      }
+    }
+  } else {
+    constexpr int kB = 8;
+    for (int p0 = threadIdx.x; p0 < nsh; p0 += kB * kSelThreads) {
+      float v[kB][8];
+#pragma unroll
+      for (int i = 0; i < kB; ++i) {
+        const int p = p0 + i * kSelThreads;
+#pragma unroll
+        for (int g = 0; g < 8; ++g)
+          v[i][g] = (g < a.G && p < nsh) ? __ldcg(sh + (int64_t)g * a.MP + p) : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < kB; ++i) {
+        const int p = p0 + i * kSelThreads;
+        if (p < nsh) {
+          float s1 = 0.f;
+#pragma unroll
+          for (int g = 0; g < 8; ++g)
+            if (g < a.G) s1 += expf(v[i][g] - hm[g]);
+          sc[p] = s1;
+          so[p] = s1;
+        }
+      }
+    }
   }
+  __syncthreads();
+  if (threadIdx.x < a.G) hm_g[threadIdx.x] = -INFINITY;
 }
 
 __global__ void __launch_bounds__(kSelThreads)
-nrm_combine_kernel(SelArgs a, float* hmax) {
+nrm_combine_kernel(SelArgs a) {
+  grid_dep_wait();     // inputs written by the previous kernel
+  grid_dep_launch();
   extern __shared__ float sc[];
-  __shared__ float red[kSelWarps];
   const int unit = blockIdx.x;
-  const int r = unit / a.n_kv;
-  const int nsh = a.nsh[r];
-  if (nsh <= 0) return;
-  nrm_fold(a, unit, nsh, sc, red, hmax);
+  const int nsh = a.nsh[unit / a.n_kv];
+  if (nsh <= 0) {
+    if (threadIdx.x < a.G) a.hmax[(int64_t)unit * a.G + threadIdx.x] = -INFINITY;
+    return;
+  }
+  nrm_fold(a, unit, nsh, sc);
 }
 
-// Radix walk: returns the key tau of the selected threshold element.
-//   COVERAGE = false: the k-th largest key (1-based) among the selectable.
-//   COVERAGE = true : the key at which the descending cumulative mass first
-//                     reaches `need` (the lowest key if it never does).
-template <bool COVERAGE>
-AMASS_DEV uint32_t radix_tau(const float* sc, int lo, int hi, int k,
-                             float need, float mass_shift, bool mass_exp,
-                             uint32_t* hist, float* hmass, int* bcast,
-                             float* fbcast) {
-  uint32_t prefix = 0, pmask = 0;
+struct SelShared {
+  uint32_t hist[kBins];
+  float hmass[kBins];
+  uint32_t cand[kCand];
+  float cmass[kCand];
+  float red[kSelWarps];
+  int wsum[kSelWarps];
+  uint32_t wc[kSelWarps];
+  float wm[kSelWarps];
+  int hit;
+  int maxd;
+  int ncand;
+  int bin;
+  uint32_t above_c;
+  float above_m;
+  uint32_t tau;
+  uint32_t lowest;
+};
+
+// tau over the keys of sc[lo_p, hi_p).  COV: mass walk to `need`; else the
+// k-th largest key.  mass(v) = LIN ? v : exp(v - shift).
+template <bool COV, bool LIN>
+AMASS_DEV uint32_t find_tau(const float* sc, int lo_p, int hi_p, int k,
+                            float need, float shift_v, uint32_t kmin,
+                            uint32_t kmax, SelShared& sh) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = threadIdx.x; i < 256; i += kSelThreads) {
-      hist[i] = 0;
-      if (COVERAGE) hmass[i] = 0.f;
+  uint32_t lo = kmin, hi = kmax;
+  if (COV && !(need > 0.f)) return kmax;      // b = 1: the top page only
+  for (int level = 0; level < 6; ++level) {
+    const uint64_t width = (uint64_t)(hi - lo) + 1;
+    int shift = 0;
+    while (((width - 1) >> shift) >= (uint64_t)kBins) ++shift;
+    for (int i = threadIdx.x; i < kBins; i += kSelThreads) {
+      sh.hist[i] = 0;
+      if (COV) sh.hmass[i] = 0.f;
     }
+    if (threadIdx.x == 0) sh.ncand = 0;
     __syncthreads();
-    for (int p = lo + threadIdx.x; p < hi; p += kSelThreads) {
+    for (int p = lo_p + threadIdx.x; p < hi_p; p += kSelThreads) {
       const float v = sc[p];
       const uint32_t key = float_key(v);
-      if ((key & pmask) == prefix) {
-        const int dg = (key >> shift) & 255;
-        atomicAdd(&hist[dg], 1u);
-        if (COVERAGE) atomicAdd(&hmass[dg], mass_exp ? expf(v - mass_shift) : v);
+      if (key >= lo && key <= hi) {
+        const int b = (int)((key - lo) >> shift);
+        atomicAdd(&sh.hist[b], 1u);
+        if (COV) atomicAdd(&sh.hmass[b], LIN ? v : expf(v - shift_v));
       }
     }
     __syncthreads();
-    if (warp == 0) {
-      // lane l owns digits [255-8l .. 248-8l] (descending)
-      uint32_t c[8];
-      float ms[8];
-      uint32_t csum = 0;
-      float msum = 0.f;
+    // bin scan by the whole block: warp w owns the w-th 1/kSelWarps of the
+    // bins counted from the top, each lane kPL consecutive bins
+    {
+      constexpr int kPW = kBins / kSelWarps, kPL = kPW / 32;
+      const int d0 = warp * kPW + lane * kPL;          // descending index
+      uint32_t cl = 0;
+      float ml = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        c[i] = hist[255 - 8 * lane - i];
-        csum += c[i];
-        if (COVERAGE) {
-          ms[i] = hmass[255 - 8 * lane - i];
-          msum += ms[i];
-        }
+      for (int i = 0; i < kPL; ++i) {
+        cl += sh.hist[kBins - 1 - (d0 + i)];
+        if (COV) ml += sh.hmass[kBins - 1 - (d0 + i)];
       }
-      // exclusive scan over lanes (lane 0 = highest digits)
-      uint32_t cex = csum;
-      float mex = msum;
+      uint32_t ci = cl;
+      float mi = ml;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
-        uint32_t tc = __shfl_up_sync(0xffffffffu, cex, o);
-        float tm = __shfl_up_sync(0xffffffffu, mex, o);
-        if (lane >= o) { cex += tc; mex += tm; }
+        const uint32_t tc = __shfl_up_sync(0xffffffffu, ci, o);
+        const float tm = __shfl_up_sync(0xffffffffu, mi, o);
+        if (lane >= o) { ci += tc; mi += tm; }
       }
-      cex -= csum;
-      mex -= msum;
-      int found = -1;
-      uint32_t above_c = cex;
-      float above_m = mex;
-      int last_nz = -1;
-      uint32_t last_c = 0;
-      float last_m = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if (c[i] != 0) {
-          if (found < 0) {
-            bool hit;
-            if (COVERAGE) hit = above_m + ms[i] >= need;
-            else hit = above_c + c[i] >= (uint32_t)k;
-            if (hit) found = i;
+      if (lane == 31) { sh.wc[warp] = ci; sh.wm[warp] = mi; }
+      if (threadIdx.x == 0) { sh.hit = 0; sh.maxd = -1; }
+      __syncthreads();
+      uint32_t cex = ci - cl;
+      float mex = mi - ml;
+      for (int w = 0; w < warp; ++w) { cex += sh.wc[w]; if (COV) mex += sh.wm[w]; }
+      bool mine;
+      if (COV) mine = cl > 0 && (mex + ml >= need) && (mex < need);
+      else mine = cl > 0 && (cex < (uint32_t)k) && (cex + cl >= (uint32_t)k);
+      if (mine) {
+        uint32_t ac = cex;
+        float am = mex;
+        for (int i = 0; i < kPL; ++i) {
+          const int b = kBins - 1 - (d0 + i);
+          const uint32_t cb = sh.hist[b];
+          if (cb == 0) continue;
+          const float mm = COV ? sh.hmass[b] : 0.f;
+          if (COV ? (am + mm >= need) : (ac + cb >= (uint32_t)k)) {
+            sh.bin = b; sh.above_c = ac; sh.above_m = am; sh.hit = 1;
+            break;
           }
-          if (found < 0) { last_nz = i; last_c = above_c; last_m = above_m; }
-        }
-        if (found < 0) {
-          above_c += c[i];
-          if (COVERAGE) above_m += ms[i];
+          ac += cb;
+          am += mm;
         }
       }
-      const unsigned hitmask = __ballot_sync(0xffffffffu, found >= 0);
-      if (hitmask) {
-        const int src = __ffs(hitmask) - 1;
-        if (lane == src) {
-          bcast[0] = 255 - 8 * lane - found;
-          bcast[1] = (int)above_c;
-          fbcast[0] = above_m;
-        }
-      } else {
-        // mass never reached `need` (rounding): descend into the lowest
-        // non-empty digit so that every selectable page ends up kept
-        const unsigned nzmask = __ballot_sync(0xffffffffu, last_nz >= 0);
-        const int src = nzmask ? 31 - __clz(nzmask) : 0;
-        if (lane == src) {
-          bcast[0] = last_nz >= 0 ? 255 - 8 * lane - last_nz : 0;
-          bcast[1] = (int)last_c;
-          fbcast[0] = last_m;
+      if (cl > 0) atomicMax(&sh.maxd, d0 + kPL - 1);
+      __syncthreads();
+      if (!sh.hit) {
+        // coverage never reached (fp rounding): the lowest non-empty bin
+        const int md = sh.maxd;
+        if (md >= d0 && md < d0 + kPL) {
+          uint32_t ac = cex;
+          float am = mex;
+          int last = -1;
+          uint32_t lc = 0;
+          float lm = 0.f;
+          for (int i = 0; i < kPL; ++i) {
+            const int b = kBins - 1 - (d0 + i);
+            const uint32_t cb = sh.hist[b];
+            if (cb == 0) continue;
+            last = b; lc = ac; lm = am;
+            ac += cb;
+            am += COV ? sh.hmass[b] : 0.f;
+          }
+          sh.bin = last < 0 ? 0 : last;
+          sh.above_c = lc;
+          sh.above_m = lm;
         }
       }
     }
     __syncthreads();
-    const uint32_t dg = (uint32_t)bcast[0];
-    prefix |= dg << shift;
-    pmask |= 0xFFu << shift;
-    if (COVERAGE) need -= fbcast[0];
-    else k -= bcast[1];
+    const int bin = sh.bin;
+    const uint32_t cnt_bin = sh.hist[bin];
+    k -= (int)sh.above_c;
+    need -= sh.above_m;
+    const uint32_t blo = lo + ((uint32_t)bin << shift);
+    const uint64_t bend = (uint64_t)blo + ((1ull << shift) - 1);
+    const uint32_t bhi = bend < (uint64_t)hi ? (uint32_t)bend : hi;
+#ifdef AMASS_SEL_PROBE
+    if (threadIdx.x == 0) g_sel_probe[blockIdx.x * 8 + 6] = level + 1 + 100 * (cnt_bin <= (uint32_t)kCand);
+#endif
+    if (blo == bhi) return blo;
+    if (cnt_bin <= (uint32_t)kCand) {
+      for (int p = lo_p + threadIdx.x; p < hi_p; p += kSelThreads) {
+        const float v = sc[p];
+        const uint32_t key = float_key(v);
+        if (key >= blo && key <= bhi) {
+          const int j = atomicAdd(&sh.ncand, 1);
+          sh.cand[j] = key;
+          if (COV) sh.cmass[j] = LIN ? v : expf(v - shift_v);
+        }
+      }
+      if (threadIdx.x == 0) { sh.tau = 0xffffffffu; sh.lowest = 0xffffffffu; }
+      __syncthreads();
+      {
+        // rank the members in parallel: 4 threads per candidate, each
+        // comparing against a quarter of the members
+        const int n = sh.ncand;
+        const int j = threadIdx.x >> 2, part = threadIdx.x & 3;
+        const uint32_t key = j < n ? sh.cand[j] : 0u;
+        uint32_t ab = 0, eq = 0;
+        float mab = 0.f, meq = 0.f;
+        if (j < n) {
+          for (int t = part; t < n; t += 4) {
+            const uint32_t o = sh.cand[t];
+            if (o > key) { ab++; if (COV) mab += sh.cmass[t]; }
+            else if (o == key) { eq++; if (COV) meq += sh.cmass[t]; }
+          }
+        }
+#pragma unroll
+        for (int o = 1; o < 4; o <<= 1) {
+          ab += __shfl_xor_sync(0xffffffffu, ab, o);
+          eq += __shfl_xor_sync(0xffffffffu, eq, o);
+          if (COV) {
+            mab += __shfl_xor_sync(0xffffffffu, mab, o);
+            meq += __shfl_xor_sync(0xffffffffu, meq, o);
+          }
+        }
+        if (j < n && part == 0) {
+          atomicMin(&sh.lowest, key);
+          bool ok;
+          if (COV) ok = (mab < need) && (mab + meq >= need);
+          else ok = (ab < (uint32_t)k) && (ab + eq >= (uint32_t)k);
+          if (ok) atomicMin(&sh.tau, key);
+        }
+      }
+      __syncthreads();
+      if (threadIdx.x == 0 && sh.tau == 0xffffffffu) sh.tau = sh.lowest;
+      __syncthreads();
+      return sh.tau;
+    }
+    lo = blo;
+    hi = bhi;
     __syncthreads();
   }
-  return prefix;
+  return lo;
 }
 
 // FOLD: fold score_h (nrm) into score first.  LIN: page mass = score (nrm
 // semantics) instead of exp(score - max) (max semantics).
 template <bool FOLD, bool LIN, bool COVERAGE>
-__global__ void __launch_bounds__(kSelThreads)
+__global__ void __launch_bounds__(kSelThreads, 4)
 select_kernel(SelArgs a) {
+  grid_dep_wait();     // inputs written by the previous kernel
+  grid_dep_launch();
   extern __shared__ float sc[];
-  __shared__ uint32_t hist[256];
-  __shared__ float hmass[COVERAGE ? 256 : 1];
-  __shared__ float red[kSelWarps];
-  __shared__ int bcast[2];
-  __shared__ float fbcast[1];
-  __shared__ int wsum[kSelWarps];
+  __shared__ SelShared sh;
   const int unit = blockIdx.x;
   const int r = unit / a.n_kv;
   const int npg = max(a.npg[r], 0);
   const int nsh = a.nsh[r];
   const int sink = a.sink;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-
+  SEL_PROBE(0);
   if (nsh > 0) {
     if (FOLD) {
-      nrm_fold(a, unit, nsh, sc, red, nullptr);
+      nrm_fold(a, unit, nsh, sc);
     } else {
       const float* si = a.score + (int64_t)unit * a.MP;
-      for (int p = threadIdx.x; p < nsh; p += kSelThreads) sc[p] = si[p];
+      constexpr int kB = 8;
+      for (int p0 = threadIdx.x; p0 < nsh; p0 += kB * kSelThreads) {
+        float v[kB];
+#pragma unroll
+        for (int i = 0; i < kB; ++i) {
+          const int p = p0 + i * kSelThreads;
+          v[i] = p < nsh ? __ldcg(si + p) : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < kB; ++i) {
+          const int p = p0 + i * kSelThreads;
+          if (p < nsh) sc[p] = v[i];
+        }
+      }
     }
+  } else if (FOLD && threadIdx.x < a.G) {
+    a.hmax[(int64_t)unit * a.G + threadIdx.x] = -INFINITY;
   }
   __syncthreads();
-
+  SEL_PROBE(1);
   const int nsel = nsh - sink;
   const bool keep_all = nsel <= 1;
   uint32_t tau = 0;
   int b_used = 1;
   if (!keep_all) {
+    uint32_t kmin = 0xffffffffu, kmax = 0;
+    for (int p = sink + threadIdx.x; p < nsh; p += kSelThreads) {
+      const uint32_t key = float_key(sc[p]);
+      kmin = min(kmin, key);
+      kmax = max(kmax, key);
+    }
+    kmin = block_reduce(kmin, reinterpret_cast<uint32_t*>(sh.red),
+                        [](uint32_t x, uint32_t y) { return min(x, y); });
+    kmax = block_reduce(kmax, reinterpret_cast<uint32_t*>(sh.red),
+                        [](uint32_t x, uint32_t y) { return max(x, y); });
     if (COVERAGE) {
-      // page masses over the scored region [0, nsh)
       float shiftv = 0.f;
-      const bool mexp = !LIN;
-      if (mexp) {
-        float mx = -INFINITY;
-        for (int p = threadIdx.x; p < nsh; p += kSelThreads) mx = fmaxf(mx, sc[p]);
-        mx = block_reduce(mx, red, [](float x, float y) { return fmaxf(x, y); });
-        shiftv = mx;
+      if (!LIN) {
+        float vmax = -INFINITY;
+        for (int p = threadIdx.x; p < nsh; p += kSelThreads)
+          vmax = fmaxf(vmax, sc[p]);
+        shiftv = block_reduce(vmax, sh.red,
+                              [](float x, float y) { return fmaxf(x, y); });
       }
       float tot = 0.f, alw = 0.f;
       for (int p = threadIdx.x; p < nsh; p += kSelThreads) {
-        const float m = mexp ? expf(sc[p] - shiftv) : sc[p];
+        const float m = LIN ? sc[p] : expf(sc[p] - shiftv);
         tot += m;
         if (p < sink) alw += m;
       }
       auto add = [](float x, float y) { return x + y; };
-      tot = block_reduce(tot, red, add);
-      alw = block_reduce(alw, red, add);
+      tot = block_reduce(tot, sh.red, add);
+      alw = block_reduce(alw, sh.red, add);
       const float need = fmaxf(a.coverage * tot - alw, 0.f);
-      tau = radix_tau<true>(sc, sink, nsh, 0, need, shiftv, mexp, hist, hmass,
-                            bcast, fbcast);
-      // b_u = (# selectable strictly above tau) + 1
+      tau = find_tau<true, LIN>(sc, sink, nsh, 0, need, shiftv, kmin, kmax, sh);
       int above = 0;
       for (int p = sink + threadIdx.x; p < nsh; p += kSelThreads)
         above += float_key(sc[p]) > tau;
-      above = block_reduce(above, reinterpret_cast<int*>(red),
+      above = block_reduce(above, reinterpret_cast<int*>(sh.red),
                            [](int x, int y) { return x + y; });
       b_used = above + 1;
     } else {
       const int b = a.b_fix[r];
       b_used = b;
-      tau = radix_tau<false>(sc, sink, nsh, b, 0.f, 0.f, false, hist, hmass,
-                             bcast, fbcast);
+      SEL_PROBE(2);
+      tau = find_tau<false, true>(sc, sink, nsh, b, 0.f, 0.f, kmin, kmax, sh);
     }
   }
+  SEL_PROBE(3);
   if (a.b_unit && threadIdx.x == 0) a.b_unit[unit] = b_used;
 
-  // ascending compaction of kept pages over [0, npg)
+  // ascending compaction over [0, npg): each thread owns a contiguous run of
+  // pages; one block-wide exclusive scan of the per-thread counts
   int32_t* tab = a.tab + (int64_t)unit * a.MP;
-  int base_out = 0;
-  for (int base = 0; base < npg; base += kSelThreads) {
-    const int p = base + threadIdx.x;
-    bool keep = false;
-    if (p < npg) {
-      if (keep_all || p < sink || p >= nsh) keep = true;
-      else keep = float_key(sc[p]) >= tau;
-    }
-    const unsigned bal = __ballot_sync(0xffffffffu, keep);
-    if (lane == 0) wsum[warp] = __popc(bal);
-    __syncthreads();
-    int off = base_out, tot = 0;
+  const int per = (npg + kSelThreads - 1) / kSelThreads;
+  const int p_lo = threadIdx.x * per, p_hi = min(p_lo + per, npg);
+  auto keep_page = [&](int p) {
+    return keep_all || p < sink || p >= nsh || float_key(sc[p]) >= tau;
+  };
+  int mine = 0;
+  for (int p = p_lo; p < p_hi; ++p) mine += keep_page(p);
+  int incl = mine;
 #pragma unroll
-    for (int w = 0; w < kSelWarps; ++w) {
-      const int v = wsum[w];
-      if (w < warp) off += v;
-      tot += v;
-    }
-    if (keep) tab[off + __popc(bal & ((1u << lane) - 1u))] = p;
-    base_out += tot;
-    __syncthreads();
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
   }
-  for (int p = base_out + threadIdx.x; p < a.MP; p += kSelThreads) tab[p] = -1;
-  if (threadIdx.x == 0) a.cnt[unit] = base_out;
+  if (lane == 31) sh.wsum[warp] = incl;
+  __syncthreads();
+  int off = 0, total = 0;
+#pragma unroll
+  for (int w = 0; w < kSelWarps; ++w) {
+    const int v = sh.wsum[w];
+    if (w < warp) off += v;
+    total += v;
+  }
+  off += incl - mine;
+  SEL_PROBE(4);
+  for (int p = p_lo; p < p_hi; ++p)
+    if (keep_page(p)) tab[off++] = p;
+  for (int p = total + threadIdx.x; p < a.MP; p += kSelThreads) tab[p] = -1;
+  if (threadIdx.x == 0) a.cnt[unit] = total;
+  SEL_PROBE(5);
 }
+
+constexpr int kMaxSmem = 160 * 1024;
 
 template <bool FOLD, bool LIN, bool COV>
 int launch_select(const SelArgs& a, int units, cudaStream_t st) {
   const size_t smem = (size_t)a.MP * sizeof(float);
   auto k = select_kernel<FOLD, LIN, COV>;
-  if (smem > 48 * 1024) {
+  static int configured = 0;
+  if (!configured) {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
+                         kMaxSmem);
+    configured = 1;
   }
-  k<<<units, kSelThreads, smem, st>>>(a);
+  if (int rc = launch_pdl(k, dim3(units), dim3(kSelThreads), smem, st, a)) return rc;
   return launch_status();
+}
+
+int max_pages_ok(int mp) {
+  return mp > 0 && (size_t)mp * sizeof(float) <= (size_t)kMaxSmem;
 }
 
 }  // namespace
@@ -347,14 +529,12 @@ extern "C" int amass_derive_page_params(const int32_t* seq_lens,
     return AMASS_ERR_ARG;
   const int threads = 256;
   const int blocks = (n_req + threads - 1) / threads;
-  derive_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
-      seq_lens, budget64, n_pages, n_sel_hi, b_fix, n_req, page, window_pages,
-      sink_pages);
+  if (int rc = launch_pdl(derive_kernel, dim3(blocks), dim3(threads), 0,
+                          static_cast<cudaStream_t>(stream), seq_lens, budget64,
+                          n_pages, n_sel_hi, b_fix, n_req, page, window_pages,
+                          sink_pages))
+    return rc;
   return launch_status();
-}
-
-static int max_pages_ok(int mp) {
-  return mp > 0 && (size_t)mp * sizeof(float) <= 200 * 1024;
 }
 
 extern "C" int amass_nrm_combine(const float* score_h, const int32_t* n_sel_hi,
@@ -363,26 +543,32 @@ extern "C" int amass_nrm_combine(const float* score_h, const int32_t* n_sel_hi,
   using namespace amass;
   if (n_req < 0 || n_kv <= 0 || G <= 0) return AMASS_ERR_ARG;
   if (n_req == 0) return AMASS_OK;
-  if (!score_h || !n_sel_hi || !score) return AMASS_ERR_ARG;
+  if (!score_h || !n_sel_hi || !score || !hmax) return AMASS_ERR_ARG;
   if (G > 8 || !max_pages_ok(max_pages)) return AMASS_ERR_UNSUPPORTED;
   SelArgs a{};
   a.score_h = score_h;
+  a.hmax = hmax;
   a.score = score;
   a.nsh = n_sel_hi;
   a.n_kv = n_kv;
   a.G = G;
   a.MP = max_pages;
   const size_t smem = (size_t)max_pages * sizeof(float);
-  if (smem > 48 * 1024)
+  static int configured = 0;
+  if (!configured) {
     cudaFuncSetAttribute(nrm_combine_kernel,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  nrm_combine_kernel<<<n_req * n_kv, kSelThreads, smem,
-                       static_cast<cudaStream_t>(stream)>>>(a, hmax);
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+    configured = 1;
+  }
+  if (int rc = launch_pdl(nrm_combine_kernel, dim3(n_req * n_kv),
+                          dim3(kSelThreads), smem,
+                          static_cast<cudaStream_t>(stream), a))
+    return rc;
   return launch_status();
 }
 
-extern "C" int amass_select_pages(const float* score_h, float* score,
-                                  const int32_t* n_pages,
+extern "C" int amass_select_pages(const float* score_h, float* hmax,
+                                  float* score, const int32_t* n_pages,
                                   const int32_t* n_sel_hi,
                                   const int32_t* b_fix, int32_t* page_table,
                                   int32_t* page_cnt, int32_t* b_unit,
@@ -394,7 +580,8 @@ extern "C" int amass_select_pages(const float* score_h, float* score,
   if (n_req == 0) return AMASS_OK;
   if (!score || !n_pages || !n_sel_hi || !page_table || !page_cnt)
     return AMASS_ERR_ARG;
-  if (score_h && (G <= 0 || combine != AMASS_COMBINE_NRM)) return AMASS_ERR_ARG;
+  if (score_h && (G <= 0 || !hmax || combine != AMASS_COMBINE_NRM))
+    return AMASS_ERR_ARG;
   if (mode == AMASS_SELECT_TOPB && !b_fix) return AMASS_ERR_ARG;
   if (mode == AMASS_SELECT_COVERAGE && !(coverage > 0.f && coverage <= 1.f))
     return AMASS_ERR_ARG;
@@ -402,6 +589,7 @@ extern "C" int amass_select_pages(const float* score_h, float* score,
     return AMASS_ERR_UNSUPPORTED;
   SelArgs a{};
   a.score_h = score_h;
+  a.hmax = hmax;
   a.score = score;
   a.npg = n_pages;
   a.nsh = n_sel_hi;
@@ -433,8 +621,8 @@ extern "C" int amass_topb_select(const float* score, const int32_t* n_pages,
                                  int32_t* page_table, int32_t* page_cnt,
                                  int n_req, int n_kv, int sink_pages,
                                  int max_pages, void* stream) {
-  return amass_select_pages(nullptr, const_cast<float*>(score), n_pages,
-                            n_sel_hi, b_fix, page_table, page_cnt, nullptr,
-                            n_req, n_kv, 0, sink_pages, max_pages,
+  return amass_select_pages(nullptr, nullptr, const_cast<float*>(score),
+                            n_pages, n_sel_hi, b_fix, page_table, page_cnt,
+                            nullptr, n_req, n_kv, 0, sink_pages, max_pages,
                             AMASS_COMBINE_MAX, AMASS_SELECT_TOPB, 0.f, stream);
 }

@@ -88,10 +88,15 @@ class QuadState:
         if combine == "nrm":
             self.score_h = torch.empty(R, n_kv, G, MP, dtype=torch.float32,
                                        **kw)
-            self.hmax = torch.zeros(R, n_kv, G, dtype=torch.float32, **kw)
+            # -inf: the scorer max-accumulates into it, the fold resets it
+            self.hmax = torch.full((R, n_kv, G), float("-inf"),
+                                   dtype=torch.float32, **kw)
         else:
             self.score_h = self.hmax = None
         self.b_unit = torch.zeros(R, n_kv, dtype=torch.int32, **kw)
+        # scratch: q as two exact int8 limbs per (request, head) + its scale
+        self.q8 = torch.zeros(R, n_kv * G, 2, D, dtype=torch.int8, **kw)
+        self.qs = torch.zeros(R, n_kv * G, dtype=torch.float32, **kw)
         self.n_pages = torch.zeros(R, dtype=torch.int32, **kw)
         self.n_sel_hi = torch.zeros(R, dtype=torch.int32, **kw)
         self.b_fix = torch.ones(R, dtype=torch.int32, **kw)
@@ -130,7 +135,25 @@ def _rank_bits(st, V):
     return r, v_bits
 
 
+def _prepare(st, device, write_h):
+    """One-time fix-ups for a state built elsewhere (e.g. the reference's own
+    QuadState, which zero-fills hmax and has no q-limb scratch); runs outside
+    any graph on first use."""
+    if getattr(st, "_amass_ready", False):
+        return
+    if write_h and st.hmax is not None and not isinstance(st, QuadState):
+        st.hmax.fill_(float("-inf"))
+    if getattr(st, "q8", None) is None:
+        H = st.n_kv * st.G
+        st.q8 = torch.zeros(st.max_reqs, H, 2, st.d, dtype=torch.int8,
+                            device=device)
+        st.qs = torch.zeros(st.max_reqs, H, dtype=torch.float32,
+                            device=device)
+    st._amass_ready = True
+
+
 def _score_launch(st, layer, q, block_table, n_req, scale, write_h):
+    _prepare(st, q.device, write_h)
     mu, mu_s, V, V_s, sig2 = (st.quad_mu[layer], st.mu_scale[layer],
                               st.quad_V[layer], st.V_scale[layer],
                               st.quad_sig2[layer])
@@ -139,7 +162,9 @@ def _score_launch(st, layer, q, block_table, n_req, scale, write_h):
     _lib.call("amass_quad_score", ptr(q), q.stride(0), q.stride(1), ptr(mu),
               ptr(mu_s), ptr(V), ptr(V_s), ptr(sig2), ptr(block_table),
               block_table.stride(0), ptr(st.n_sel_hi), ptr(st.score),
-              ptr(st.score_h) if write_h else 0, float(scale), int(n_req),
+              ptr(st.score_h) if write_h else 0,
+              ptr(st.hmax) if write_h else 0, ptr(st.q8), ptr(st.qs),
+              float(scale), int(n_req),
               int(st.n_kv), int(st.G), int(st.d), int(st.page), r, v_bits,
               int(st.max_pages), 1 if write_h else 0,
               _lib.stream_of(q.device))
@@ -184,7 +209,8 @@ def select_pages(st, n_req: int, *, coverage=None, from_score_h=None) -> None:
     cov = coverage if coverage is not None else getattr(st, "coverage", None)
     b_unit = getattr(st, "b_unit", None)
     _lib.call("amass_select_pages",
-              ptr(st.score_h) if from_score_h else 0, ptr(st.score),
+              ptr(st.score_h) if from_score_h else 0,
+              ptr(st.hmax) if from_score_h else 0, ptr(st.score),
               ptr(st.n_pages), ptr(st.n_sel_hi), ptr(st.b_fix),
               ptr(st.page_table), ptr(st.page_cnt), ptr(b_unit), int(n_req),
               int(st.n_kv), int(st.G), int(st.sink_pages),

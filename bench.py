@@ -146,7 +146,9 @@ class Batch:
         self.scale = 1.0 / math.sqrt(D)
         self.out = torch.empty(N_REQ, N_KV * G, D, dtype=torch.bfloat16,
                                device=dev)
-        self.launches_per_step = 5
+        # derive, q-limbs, score, select, decode, merge
+        self.launches_per_step = 6
+        self.pps_min = None
 
     def step(self, layer, q=None, events=None):
         from amass_kv_b200 import attention as A
@@ -164,7 +166,8 @@ class Batch:
         if events:
             events[2].record()
         A.sparse_paged_decode_batched_cuda(q, self.kv[l], self.bt, self.sl, st,
-                                           self.out, scale=self.scale)
+                                           self.out, scale=self.scale,
+                                           pps_min=self.pps_min)
         if events:
             events[3].record()
 
@@ -198,6 +201,7 @@ def run_gpu(args):
     from amass_kv_b200 import _lib
     _lib.load()
     batch = Batch(dev, seed=1000 + rank, layers=args.layers)
+    batch.pps_min = args.pps_min
     L = args.layers
     alg = [batch.algorithmic_bytes(l) for l in range(L)]
 
@@ -476,6 +480,8 @@ def main():
                     choices=["amass_b200", "reference"])
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--pps-min", type=int, default=None,
+                    help="decode pages-per-chunk floor (default: by batch)")
     ap.add_argument("--requests", type=int, default=N_REQ,
                     help="batch size per GPU (64 = BASELINE C3; smaller only "
                          "for profiling captures)")

@@ -56,25 +56,36 @@ int amass_derive_page_params(const int32_t* seq_lens, const double* budget64,
  * golden selection/quad_score.py:35-139).  Reads one layer's quad slabs:
  *   mu (NB, n_kv, d) int8, mu_scale (NB, n_kv) fp16,
  *   V (NB, n_kv, d, rv) int8 (rv = rank, or rank/2 packed int4),
- *   V_scale (NB, n_kv, rank) fp16, sig2 (NB, n_kv, rank) fp16 (contiguous).
+ *   V_scale (NB, n_kv, rank) fp16, sig2 (NB, n_kv, rank) fp16 (contiguous,
+ *   mu and V 16-byte aligned).
  * write_h = 0: score[r, kv, p] = max_g S_g (R, n_kv, MP) fp32.
  * write_h = 1: score_h[r, kv, g, p] = S_g (R, n_kv, G, MP) fp32 (the nrm
- *              path; fold it with amass_nrm_combine or amass_select_pages).
+ *              path) and hmax[r, kv, g] = max(hmax, max_p S_g) (R, n_kv, G)
+ *              fp32; hmax must hold -inf before the call -- the fold
+ *              (amass_nrm_combine / amass_select_pages) consumes it and
+ *              resets it to -inf.
+ * q8_ws (n_req, H, 2, d) int8 (16-byte aligned) and qs_ws (n_req, H) fp32
+ * are caller scratch for the exact two-limb int8 form of q the integer MMAs
+ * use (|dq| <= max|q_head| / 32512).
  * Pages p < n_sel_hi[r] are written; others are left untouched.
  * Compiled variants: head_dim in {64, 128}, rank in {1, 2, 4, 8},
- * v_bits in {4, 8} (int4 needs an even rank), G <= 8, page = 16. */
+ * v_bits in {4, 8} (int4 needs an even rank), G <= 8, page = 16,
+ * n_req <= 4096. */
 int amass_quad_score(const void* q, int64_t q_stride_t, int64_t q_stride_h,
                      const int8_t* mu, const void* mu_scale, const int8_t* V,
                      const void* V_scale, const void* sig2,
                      const int32_t* block_table, int64_t bt_stride,
                      const int32_t* n_sel_hi, float* score, float* score_h,
-                     float scale, int n_req, int n_kv, int G, int head_dim,
-                     int page, int rank, int v_bits, int max_pages,
-                     int write_h, void* stream);
+                     float* hmax, int8_t* q8_ws, float* qs_ws, float scale,
+                     int n_req, int n_kv, int G, int head_dim, int page,
+                     int rank, int v_bits, int max_pages, int write_h,
+                     void* stream);
 
 /* nrm combine -- replaces the two passes of selection/quad_score.py:276-315
- * (CUDA twin quad_score_cuda.py:1446-1547): hmax[r,kv,g] = max_{p<n_sel_hi}
- * score_h; score[r,kv,p] = sum_g exp(score_h[r,kv,g,p] - hmax[r,kv,g]). */
+ * (CUDA twin quad_score_cuda.py:1446-1547): with hmax[r,kv,g] = the per-head
+ * page max that amass_quad_score accumulated, score[r,kv,p] =
+ * sum_g exp(score_h[r,kv,g,p] - hmax[r,kv,g]) for p < n_sel_hi; hmax is then
+ * reset to -inf for the next call. */
 int amass_nrm_combine(const float* score_h, const int32_t* n_sel_hi,
                       float* hmax, float* score, int n_req, int n_kv, int G,
                       int max_pages, void* stream);
@@ -94,13 +105,14 @@ int amass_topb_select(const float* score, const int32_t* n_pages,
  * (smallest b whose top-b selectable pages hold `coverage` of the scored page
  * mass minus the sink share; the per-unit form of the reference's
  * backend/_selection_bridge.py:117-133) and applies the same threshold rule.
- * combine MAX: reads score (mass = exp(score - max)); NRM: reads score_h,
- * writes score (mass = score).  b_unit (R, n_kv) receives the b used per unit
+ * With score_h (and hmax) given, the nrm fold runs first (as
+ * amass_nrm_combine) and writes score.  combine MAX: page mass =
+ * exp(score - max); NRM: page mass = score.  b_unit (R, n_kv) receives the b used per unit
  * (may be NULL).  Has no single reference counterpart: it replaces the pair
  * nrm_combine + topb_select_cuda on the graph-safe path
  * (backend/_runtime.py:183-263) and adds the per-head coverage the
  * reference only has in its eager bridge. */
-int amass_select_pages(const float* score_h, float* score,
+int amass_select_pages(const float* score_h, float* hmax, float* score,
                        const int32_t* n_pages, const int32_t* n_sel_hi,
                        const int32_t* b_fix, int32_t* page_table,
                        int32_t* page_cnt, int32_t* b_unit, int n_req, int n_kv,
