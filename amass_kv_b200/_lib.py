@@ -24,12 +24,12 @@ _SIGS = {
     "amass_version": [],
     "amass_derive_page_params": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "amass_quad_score": [_P, _L, _L, _P, _P, _P, _P, _P, _P, _L, _P, _P, _P,
-                         _P, _P, _P, _F, _I, _I, _I, _I, _I, _I, _I, _I, _I,
-                         _P],
-    "amass_nrm_combine": [_P, _P, _P, _P, _I, _I, _I, _I, _P],
+                         _L, _P, _P, _P, _F, _I, _I, _I, _I, _I, _I, _I, _I,
+                         _I, _P],
+    "amass_nrm_combine": [_P, _L, _P, _P, _P, _I, _I, _I, _I, _P],
     "amass_topb_select": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
-    "amass_select_pages": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I,
-                           _I, _I, _I, _I, _F, _P],
+    "amass_select_pages": [_P, _L, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I,
+                           _I, _I, _I, _I, _I, _F, _P],
     "amass_sparse_decode": [_P, _L, _L, _P, _L, _L, _L, _P, _L, _L, _L, _P,
                             _L, _P, _P, _P, _P, _P, _P, _I, _I, _P, _L, _L,
                             _F, _I, _I, _I, _I, _I, _I, _P],

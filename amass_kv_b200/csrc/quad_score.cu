@@ -54,6 +54,7 @@ struct QuadArgs {
   float* qs;         // (n_req, H) limb scale
   float scale, coef;
   int n_req, n_kv, G, MP;
+  int64_t SHS;       // score_h row stride (elements; >= MP)
 };
 
 AMASS_DEV void atomic_max_float(float* addr, float v) {
@@ -355,14 +356,14 @@ AMASS_DEV void score_item(const Item<D, R, VB>& it, const QFrag<D>& qf,
   }
   const int pa = it.p0 + m, pb = pa + 8;
   if constexpr (WRITE_H) {
-    float* base = a.score_h + ((int64_t)it.r * a.n_kv + it.h) * a.G * a.MP;
+    float* base = a.score_h + ((int64_t)it.r * a.n_kv + it.h) * a.G * a.SHS;
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const int g = 2 * c + j;
       float mx = -INFINITY;
       if (g < a.G) {
-        if (it.va) { base[(int64_t)g * a.MP + pa] = S[0][j]; mx = S[0][j]; }
-        if (it.vb) { base[(int64_t)g * a.MP + pb] = S[1][j]; mx = fmaxf(mx, S[1][j]); }
+        if (it.va) { base[(int64_t)g * a.SHS + pa] = S[0][j]; mx = S[0][j]; }
+        if (it.vb) { base[(int64_t)g * a.SHS + pb] = S[1][j]; mx = fmaxf(mx, S[1][j]); }
       }
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
@@ -510,7 +511,8 @@ extern "C" int amass_quad_score(const void* q, int64_t q_stride_t,
                                 const void* V_scale, const void* sig2,
                                 const int32_t* block_table, int64_t bt_stride,
                                 const int32_t* n_sel_hi, float* score,
-                                float* score_h, float* hmax, int8_t* q8_ws,
+                                float* score_h, int64_t sh_stride,
+                                float* hmax, int8_t* q8_ws,
                                 float* qs_ws, float scale, int n_req,
                                 int n_kv, int G, int head_dim, int page,
                                 int rank, int v_bits, int max_pages,
@@ -521,7 +523,8 @@ extern "C" int amass_quad_score(const void* q, int64_t q_stride_t,
   if (!q || !mu || !mu_scale || !V || !V_scale || !sig2 || !block_table ||
       !n_sel_hi || !q8_ws || !qs_ws)
     return AMASS_ERR_ARG;
-  if (write_h ? (!score_h || !hmax) : !score) return AMASS_ERR_ARG;
+  if (write_h ? (!score_h || !hmax || sh_stride < max_pages) : !score)
+    return AMASS_ERR_ARG;
   if (G > 8 || page != 16 || n_req > kQuadMaxReq) return AMASS_ERR_UNSUPPORTED;
   // 16-byte loads of summary rows and of the q limbs
   if ((q_stride_h % 2) || (q_stride_t % 2) ||
@@ -543,6 +546,7 @@ extern "C" int amass_quad_score(const void* q, int64_t q_stride_t,
   a.nsh = n_sel_hi;
   a.score = score;
   a.score_h = score_h;
+  a.SHS = sh_stride;
   a.hmax = hmax;
   a.q8 = q8_ws;
   a.qs = qs_ws;

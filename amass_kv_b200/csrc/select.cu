@@ -87,13 +87,14 @@ struct SelArgs {
   int32_t* cnt;
   int32_t* b_unit;
   int n_kv, G, sink, MP;
+  int64_t SHS;            // score_h row stride (elements; >= MP)
   float coverage;
 };
 
 // nrm fold of one unit (reference quad_score.py:293-315): sc[p] =
 // sum_g exp(S_g[p] - hmax_g) for p < nsh; writes score; resets hmax to -inf.
 AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int nsh, float* sc) {
-  const float* sh = a.score_h + (int64_t)unit * a.G * a.MP;
+  const float* sh = a.score_h + (int64_t)unit * a.G * a.SHS;
   float* hm_g = a.hmax + (int64_t)unit * a.G;
   float hm[8];
 #pragma unroll
@@ -101,7 +102,7 @@ AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int nsh, float* sc) {
   float* so = a.score + (int64_t)unit * a.MP;
   // batches of pages per thread: every load of a batch issues before any
   // use, so a long unit costs a few memory round trips, not one per page
-  if ((a.MP & 3) == 0) {
+  if ((a.SHS & 3) == 0 && (reinterpret_cast<uintptr_t>(a.score_h) & 15) == 0) {
     // 16-byte loads: thread owns page quads tid, tid + kSelThreads, ...
     constexpr int kQ = 1;
     const int nq = (nsh + 3) >> 2;
@@ -113,7 +114,7 @@ AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int nsh, float* sc) {
 #pragma unroll
         for (int g = 0; g < 8; ++g)
           v[i][g] = (g < a.G && q < nq)
-                        ? __ldcg(reinterpret_cast<const float4*>(sh + (int64_t)g * a.MP) + q)
+                        ? __ldcg(reinterpret_cast<const float4*>(sh + (int64_t)g * a.SHS) + q)
                         : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
@@ -147,7 +148,7 @@ AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int nsh, float* sc) {
         const int p = p0 + i * kSelThreads;
 #pragma unroll
         for (int g = 0; g < 8; ++g)
-          v[i][g] = (g < a.G && p < nsh) ? __ldcg(sh + (int64_t)g * a.MP + p) : 0.f;
+          v[i][g] = (g < a.G && p < nsh) ? __ldcg(sh + (int64_t)g * a.SHS + p) : 0.f;
       }
 #pragma unroll
       for (int i = 0; i < kB; ++i) {
@@ -198,6 +199,7 @@ struct SelShared {
   float above_m;
   uint32_t tau;
   uint32_t lowest;
+  uint32_t kmin, kmax;
 };
 
 // tau over the keys of sc[lo_p, hi_p).  COV: mass walk to `need`; else the
@@ -382,6 +384,7 @@ select_kernel(SelArgs a) {
   const int nsh = a.nsh[r];
   const int sink = a.sink;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) { sh.kmin = 0xffffffffu; sh.kmax = 0u; }
   SEL_PROBE(0);
   if (nsh > 0) {
     if (FOLD) {
@@ -419,10 +422,18 @@ select_kernel(SelArgs a) {
       kmin = min(kmin, key);
       kmax = max(kmax, key);
     }
-    kmin = block_reduce(kmin, reinterpret_cast<uint32_t*>(sh.red),
-                        [](uint32_t x, uint32_t y) { return min(x, y); });
-    kmax = block_reduce(kmax, reinterpret_cast<uint32_t*>(sh.red),
-                        [](uint32_t x, uint32_t y) { return max(x, y); });
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+      kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+    }
+    if (lane == 0) {
+      atomicMin(&sh.kmin, kmin);
+      atomicMax(&sh.kmax, kmax);
+    }
+    __syncthreads();
+    kmin = sh.kmin;
+    kmax = sh.kmax;
     if (COVERAGE) {
       float shiftv = 0.f;
       if (!LIN) {
@@ -467,8 +478,11 @@ select_kernel(SelArgs a) {
   auto keep_page = [&](int p) {
     return keep_all || p < sink || p >= nsh || float_key(sc[p]) >= tau;
   };
-  int mine = 0;
-  for (int p = p_lo; p < p_hi; ++p) mine += keep_page(p);
+  // keep bits of this thread's run (at most 64 pages per thread: MP <= 16K)
+  uint64_t bits = 0;
+  for (int p = p_lo; p < p_hi; ++p)
+    if (keep_page(p)) bits |= 1ull << (p - p_lo);
+  const int mine = __popcll(bits);
   int incl = mine;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -477,6 +491,7 @@ select_kernel(SelArgs a) {
   }
   if (lane == 31) sh.wsum[warp] = incl;
   __syncthreads();
+  SEL_PROBE(4);
   int off = 0, total = 0;
 #pragma unroll
   for (int w = 0; w < kSelWarps; ++w) {
@@ -485,9 +500,11 @@ select_kernel(SelArgs a) {
     total += v;
   }
   off += incl - mine;
-  SEL_PROBE(4);
-  for (int p = p_lo; p < p_hi; ++p)
-    if (keep_page(p)) tab[off++] = p;
+  while (bits) {
+    const int i = __ffsll(bits) - 1;
+    bits &= bits - 1;
+    tab[off++] = p_lo + i;
+  }
   for (int p = total + threadIdx.x; p < a.MP; p += kSelThreads) tab[p] = -1;
   if (threadIdx.x == 0) a.cnt[unit] = total;
   SEL_PROBE(5);
@@ -510,7 +527,9 @@ int launch_select(const SelArgs& a, int units, cudaStream_t st) {
 }
 
 int max_pages_ok(int mp) {
-  return mp > 0 && (size_t)mp * sizeof(float) <= (size_t)kMaxSmem;
+  // compaction keeps one 64-bit keep mask per thread: MP <= 64 * kSelThreads
+  return mp > 0 && mp <= 64 * kSelThreads &&
+         (size_t)mp * sizeof(float) <= (size_t)kMaxSmem;
 }
 
 }  // namespace
@@ -537,16 +556,19 @@ extern "C" int amass_derive_page_params(const int32_t* seq_lens,
   return launch_status();
 }
 
-extern "C" int amass_nrm_combine(const float* score_h, const int32_t* n_sel_hi,
-                                 float* hmax, float* score, int n_req,
-                                 int n_kv, int G, int max_pages, void* stream) {
+extern "C" int amass_nrm_combine(const float* score_h, int64_t sh_stride,
+                                 const int32_t* n_sel_hi, float* hmax,
+                                 float* score, int n_req, int n_kv, int G,
+                                 int max_pages, void* stream) {
   using namespace amass;
   if (n_req < 0 || n_kv <= 0 || G <= 0) return AMASS_ERR_ARG;
   if (n_req == 0) return AMASS_OK;
   if (!score_h || !n_sel_hi || !score || !hmax) return AMASS_ERR_ARG;
   if (G > 8 || !max_pages_ok(max_pages)) return AMASS_ERR_UNSUPPORTED;
+  if (sh_stride < max_pages) return AMASS_ERR_ARG;
   SelArgs a{};
   a.score_h = score_h;
+  a.SHS = sh_stride;
   a.hmax = hmax;
   a.score = score;
   a.nsh = n_sel_hi;
@@ -567,8 +589,8 @@ extern "C" int amass_nrm_combine(const float* score_h, const int32_t* n_sel_hi,
   return launch_status();
 }
 
-extern "C" int amass_select_pages(const float* score_h, float* hmax,
-                                  float* score, const int32_t* n_pages,
+extern "C" int amass_select_pages(const float* score_h, int64_t sh_stride,
+                                  float* hmax, float* score, const int32_t* n_pages,
                                   const int32_t* n_sel_hi,
                                   const int32_t* b_fix, int32_t* page_table,
                                   int32_t* page_cnt, int32_t* b_unit,
@@ -580,7 +602,8 @@ extern "C" int amass_select_pages(const float* score_h, float* hmax,
   if (n_req == 0) return AMASS_OK;
   if (!score || !n_pages || !n_sel_hi || !page_table || !page_cnt)
     return AMASS_ERR_ARG;
-  if (score_h && (G <= 0 || !hmax || combine != AMASS_COMBINE_NRM))
+  if (score_h && (G <= 0 || !hmax || combine != AMASS_COMBINE_NRM ||
+                  sh_stride < max_pages))
     return AMASS_ERR_ARG;
   if (mode == AMASS_SELECT_TOPB && !b_fix) return AMASS_ERR_ARG;
   if (mode == AMASS_SELECT_COVERAGE && !(coverage > 0.f && coverage <= 1.f))
@@ -589,6 +612,7 @@ extern "C" int amass_select_pages(const float* score_h, float* hmax,
     return AMASS_ERR_UNSUPPORTED;
   SelArgs a{};
   a.score_h = score_h;
+  a.SHS = sh_stride;
   a.hmax = hmax;
   a.score = score;
   a.npg = n_pages;
@@ -621,7 +645,7 @@ extern "C" int amass_topb_select(const float* score, const int32_t* n_pages,
                                  int32_t* page_table, int32_t* page_cnt,
                                  int n_req, int n_kv, int sink_pages,
                                  int max_pages, void* stream) {
-  return amass_select_pages(nullptr, nullptr, const_cast<float*>(score),
+  return amass_select_pages(nullptr, 0, nullptr, const_cast<float*>(score),
                             n_pages, n_sel_hi, b_fix, page_table, page_cnt,
                             nullptr, n_req, n_kv, 0, sink_pages, max_pages,
                             AMASS_COMBINE_MAX, AMASS_SELECT_TOPB, 0.f, stream);

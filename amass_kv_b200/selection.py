@@ -86,8 +86,9 @@ class QuadState:
         self.page_table = torch.empty(R, n_kv, MP, dtype=torch.int32, **kw)
         self.page_cnt = torch.zeros(R, n_kv, dtype=torch.int32, **kw)
         if combine == "nrm":
-            self.score_h = torch.empty(R, n_kv, G, MP, dtype=torch.float32,
-                                       **kw)
+            # rows padded to a multiple of 4 pages: 16-byte loads in the fold
+            self.score_h = torch.empty(R, n_kv, G, (MP + 3) // 4 * 4,
+                                       dtype=torch.float32, **kw)[..., :MP]
             # -inf: the scorer max-accumulates into it, the fold resets it
             self.hmax = torch.full((R, n_kv, G), float("-inf"),
                                    dtype=torch.float32, **kw)
@@ -163,6 +164,7 @@ def _score_launch(st, layer, q, block_table, n_req, scale, write_h):
               ptr(mu_s), ptr(V), ptr(V_s), ptr(sig2), ptr(block_table),
               block_table.stride(0), ptr(st.n_sel_hi), ptr(st.score),
               ptr(st.score_h) if write_h else 0,
+              st.score_h.stride(2) if write_h else 0,
               ptr(st.hmax) if write_h else 0, ptr(st.q8), ptr(st.qs),
               float(scale), int(n_req),
               int(st.n_kv), int(st.G), int(st.d), int(st.page), r, v_bits,
@@ -179,7 +181,8 @@ def quad_score_cuda(st, layer: int, q, block_table, seq_lens, n_req: int,
     nrm = getattr(st, "combine", "max") == "nrm"
     _score_launch(st, layer, q, block_table, n_req, scale, nrm)
     if nrm:
-        _lib.call("amass_nrm_combine", ptr(st.score_h), ptr(st.n_sel_hi),
+        _lib.call("amass_nrm_combine", ptr(st.score_h), st.score_h.stride(2),
+                  ptr(st.n_sel_hi),
                   ptr(st.hmax), ptr(st.score), int(n_req), int(st.n_kv),
                   int(st.G), int(st.max_pages), _lib.stream_of(q.device))
 
@@ -210,6 +213,7 @@ def select_pages(st, n_req: int, *, coverage=None, from_score_h=None) -> None:
     b_unit = getattr(st, "b_unit", None)
     _lib.call("amass_select_pages",
               ptr(st.score_h) if from_score_h else 0,
+              st.score_h.stride(2) if from_score_h else 0,
               ptr(st.hmax) if from_score_h else 0, ptr(st.score),
               ptr(st.n_pages), ptr(st.n_sel_hi), ptr(st.b_fix),
               ptr(st.page_table), ptr(st.page_cnt), ptr(b_unit), int(n_req),

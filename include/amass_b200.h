@@ -59,7 +59,9 @@ int amass_derive_page_params(const int32_t* seq_lens, const double* budget64,
  *   V_scale (NB, n_kv, rank) fp16, sig2 (NB, n_kv, rank) fp16 (contiguous,
  *   mu and V 16-byte aligned).
  * write_h = 0: score[r, kv, p] = max_g S_g (R, n_kv, MP) fp32.
- * write_h = 1: score_h[r, kv, g, p] = S_g (R, n_kv, G, MP) fp32 (the nrm
+ * write_h = 1: score_h[r, kv, g, p] = S_g (R, n_kv, G, sh_stride) fp32, rows
+ *              of sh_stride >= MP elements (a multiple of 4 enables 16-byte
+ *              loads in the fold) (the nrm
  *              path) and hmax[r, kv, g] = max(hmax, max_p S_g) (R, n_kv, G)
  *              fp32; hmax must hold -inf before the call -- the fold
  *              (amass_nrm_combine / amass_select_pages) consumes it and
@@ -76,7 +78,8 @@ int amass_quad_score(const void* q, int64_t q_stride_t, int64_t q_stride_h,
                      const void* V_scale, const void* sig2,
                      const int32_t* block_table, int64_t bt_stride,
                      const int32_t* n_sel_hi, float* score, float* score_h,
-                     float* hmax, int8_t* q8_ws, float* qs_ws, float scale,
+                     int64_t sh_stride, float* hmax, int8_t* q8_ws,
+                     float* qs_ws, float scale,
                      int n_req, int n_kv, int G, int head_dim, int page,
                      int rank, int v_bits, int max_pages, int write_h,
                      void* stream);
@@ -86,9 +89,9 @@ int amass_quad_score(const void* q, int64_t q_stride_t, int64_t q_stride_h,
  * page max that amass_quad_score accumulated, score[r,kv,p] =
  * sum_g exp(score_h[r,kv,g,p] - hmax[r,kv,g]) for p < n_sel_hi; hmax is then
  * reset to -inf for the next call. */
-int amass_nrm_combine(const float* score_h, const int32_t* n_sel_hi,
-                      float* hmax, float* score, int n_req, int n_kv, int G,
-                      int max_pages, void* stream);
+int amass_nrm_combine(const float* score_h, int64_t sh_stride,
+                      const int32_t* n_sel_hi, float* hmax, float* score,
+                      int n_req, int n_kv, int G, int max_pages, void* stream);
 
 /* topb_select -- replaces selection/select_cuda.py:370-391 (Triton golden
  * selection/select.py:60-116): tau = b_fix[r]-th largest score over the
@@ -112,7 +115,8 @@ int amass_topb_select(const float* score, const int32_t* n_pages,
  * nrm_combine + topb_select_cuda on the graph-safe path
  * (backend/_runtime.py:183-263) and adds the per-head coverage the
  * reference only has in its eager bridge. */
-int amass_select_pages(const float* score_h, float* hmax, float* score,
+int amass_select_pages(const float* score_h, int64_t sh_stride, float* hmax,
+                       float* score,
                        const int32_t* n_pages, const int32_t* n_sel_hi,
                        const int32_t* b_fix, int32_t* page_table,
                        int32_t* page_cnt, int32_t* b_unit, int n_req, int n_kv,

@@ -43,6 +43,6 @@ def test_arg_validation_without_gpu():
     # unsupported geometry (G > 8) on the quad scorer
     one = ctypes.c_void_p(16)
     rc = lib.amass_quad_score(one, 512, 128, one, one, one, one, one, one, 64,
-                              one, one, 0, 0, one, one, ctypes.c_float(0.1), 1,
+                              one, one, 0, 0, 0, one, one, ctypes.c_float(0.1), 1,
                               1, 16, 128, 16, 2, 4, 64, 0, 0)
     assert rc == 2
