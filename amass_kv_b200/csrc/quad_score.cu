@@ -28,6 +28,8 @@
 // With the nrm combine the kernel also max-accumulates the per-head page
 // maximum into hmax[r, h, g]; the fold (nrm_combine / select_pages) consumes
 // it and resets it to -inf, so the fold is a single pass.
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace amass {
@@ -55,6 +57,11 @@ struct QuadArgs {
   float scale, coef;
   int n_req, n_kv, G, MP;
   int64_t SHS;       // score_h row stride (elements; >= MP)
+  // r8 scorer only
+  const int8_t* c;   // (NB, n_kv, page, rc) int8 per-token coordinates
+  const __half* cs;  // (NB, n_kv, page) fp16 per-token scale
+  const int32_t* sl; // (n_req,) seq_lens
+  int page, tokmax;
 };
 
 AMASS_DEV void atomic_max_float(float* addr, float v) {
@@ -286,16 +293,18 @@ AMASS_DEV void load_qfrag(QFrag<D>& f, const QuadArgs& a, int r, int h,
   f.sq[1] = __ldg(qsr + g1);
 }
 
-template <int D, int R, int VB, bool WRITE_H>
-AMASS_DEV void score_item(const Item<D, R, VB>& it, const QFrag<D>& qf,
-                          const QuadArgs& a, int lane) {
+// The (1+R) x 2-limb integer dot products of one item: acc[comp][limb][4]
+// (comp 0 = mu, 1+k = V column k), C-fragment layout (rows pages m, m+8;
+// cols query heads 2c, 2c+1).
+template <int D, int R, int VB>
+AMASS_DEV void item_dots(const Item<D, R, VB>& it, const QFrag<D>& qf,
+                         const QuadArgs& a, int lane, int (*acc)[2][4]) {
   using I = Item<D, R, VB>;
   constexpr int KS = D / 32;                 // m16n8k32 steps
   constexpr int RB = I::RB;
-  const int m = lane >> 2, c = lane & 3;
+  const int c = lane & 3;
   const uint32_t (*bh)[2] = qf.bh;
   const uint32_t (*bl)[2] = qf.bl;
-  int acc[1 + R][2][4];
 #pragma unroll
   for (int i = 0; i <= R; ++i)
 #pragma unroll
@@ -331,6 +340,14 @@ AMASS_DEV void score_item(const Item<D, R, VB>& it, const QFrag<D>& qf,
     VCols<R, VB, 0>::run(acc, wva, wvb, bh[s], bl[s]);
   }
 
+}
+
+template <int D, int R, int VB, bool WRITE_H>
+AMASS_DEV void score_item(const Item<D, R, VB>& it, const QFrag<D>& qf,
+                          const QuadArgs& a, int lane) {
+  const int m = lane >> 2, c = lane & 3;
+  int acc[1 + R][2][4];
+  item_dots(it, qf, a, lane, acc);
   // epilogue: rows pa (idx 0,1) and pb (idx 2,3); cols g = 2c, 2c+1
   const float* sq = qf.sq;
   constexpr float vdiv = (VB == 8) ? 1.f : 1.f / 16.f;
@@ -463,6 +480,204 @@ quad_score_kernel(QuadArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// r8 low-rank scorer (reference selection/score.py:30-120):
+//   q~_g   = Vk^T q_g                       (rank R columns, integer MMA as above)
+//   tok_gt = s * c_scale_t * (c_code_t . (Vk_scale * q~_g))   t < page, tok < seq_len
+//   S_g    = s * mu_scale * (mu_code . q_g) + logsumexp_t tok_gt   (or max_t)
+//   score  = max_g S_g
+// The item's per-token coordinate codes (16 pages x page x rank) and scales
+// are staged in a warp-private shared buffer; lane (m, c) evaluates the page
+// tokens of pages m, m+8 for query heads 2c, 2c+1 on the FP32 pipe.
+// ---------------------------------------------------------------------------
+constexpr int kR8MaxReq = 2048;
+
+template <int R, int CB>
+struct R8Tok {
+  static constexpr int RC = (CB == 8) ? R : R / 2;   // code bytes per token
+};
+
+template <int D, int R, int VB, int CB>
+__global__ void __launch_bounds__(kQuadWarps * 32, 1)
+r8_score_kernel(QuadArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
+  constexpr int RC = R8Tok<R, CB>::RC;
+  constexpr int PG = 16;                                    // tokens per page
+  constexpr int kCBytes = 16 * PG * RC;                     // 16 pages of codes
+  constexpr int kSBytes = 16 * PG * 2;                      // their scales
+  __shared__ int prefix[kR8MaxReq + 1];
+  __shared__ int nshs[kR8MaxReq];
+  __shared__ __align__(16) uint8_t cbuf[kQuadWarps][kCBytes + kSBytes];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) {
+    int run = 0;
+    for (int base = 0; base < a.n_req; base += 32) {
+      const int r = base + lane;
+      const int nsh = r < a.n_req ? max(a.nsh[r], 0) : 0;
+      const int t = (nsh + 15) / 16;
+      int incl = t;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int x = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += x;
+      }
+      if (r < a.n_req) { prefix[r] = run + incl - t; nshs[r] = nsh; }
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) prefix[a.n_req] = run;
+  }
+  __syncthreads();
+  const int T = prefix[a.n_req];
+  const int gw = blockIdx.x * kQuadWarps + warp;
+  const int NJ = gridDim.x * kQuadWarps / a.n_kv;
+  const int j = gw / a.n_kv;
+  if (j >= NJ) return;
+  const int h = gw - j * a.n_kv;
+  const int t_lo = (int)((int64_t)T * j / NJ);
+  const int t_hi = (int)((int64_t)T * (j + 1) / NJ);
+  if (t_lo >= t_hi) return;
+  int rh = 0;
+  {
+    int lo = 0, hi = a.n_req - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (prefix[mid] <= t_lo) lo = mid; else hi = mid - 1;
+    }
+    rh = lo;
+  }
+  const int m = lane >> 2, c = lane & 3;
+  uint8_t* cb = cbuf[warp];
+  const __half* csb = reinterpret_cast<const __half*>(cb + kCBytes);
+  QFrag<D> qf;
+  int qr = -1;
+  Item<D, R, VB> it;
+  for (int t = t_lo; t < t_hi; ++t) {
+    load_idx(it, a, prefix, nshs, t * a.n_kv + h, lane, &rh);
+    // block ids of all 16 pages of the tile (for the coordinate staging)
+    const int32_t* btr = a.bt + (int64_t)it.r * a.bt_stride;
+    const int nsh = nshs[it.r];
+    load_data(it, a, lane);
+    if (it.r != qr) {
+      load_qfrag(qf, a, it.r, h, lane);
+      qr = it.r;
+    }
+    // stage codes + scales: 16-byte pieces, page-major
+    __syncwarp();
+    for (int e = lane; e < kCBytes / 16; e += 32) {
+      const int pg = e / (PG * RC / 16), off = e - pg * (PG * RC / 16);
+      const int p = it.p0 + pg;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (p < nsh) {
+        const int64_t blk = __ldg(btr + p);
+        v = __ldg(reinterpret_cast<const uint4*>(a.c + ((blk * a.n_kv + h) * PG) * RC) + off);
+      }
+      *reinterpret_cast<uint4*>(cb + e * 16) = v;
+    }
+    for (int e = lane; e < kSBytes / 16; e += 32) {
+      const int pg = e / (PG * 2 / 16), off = e - pg * (PG * 2 / 16);
+      const int p = it.p0 + pg;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (p < nsh) {
+        const int64_t blk = __ldg(btr + p);
+        v = __ldg(reinterpret_cast<const uint4*>(a.cs + (blk * a.n_kv + h) * PG) + off);
+      }
+      *reinterpret_cast<uint4*>(cb + kCBytes + e * 16) = v;
+    }
+    int acc[1 + R][2][4];
+    item_dots(it, qf, a, lane, acc);
+    __syncwarp();
+    const int sl_r = __ldg(a.sl + it.r);
+    constexpr float vdiv = (VB == 8) ? 1.f : 1.f / 16.f;
+    float best[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int pl = m + 8 * half;                 // page within the tile
+      const int p = it.p0 + pl;
+      const float mus = half ? __high2float(it.mus) : __low2float(it.mus);
+      float qt[2][R];
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const int idx = 2 * half + jj;
+#pragma unroll
+        for (int k = 0; k < R; ++k)
+          qt[jj][k] = (float)(128 * acc[1 + k][0][idx] + acc[1 + k][1][idx]) *
+                      (qf.sq[jj] * vdiv) * it.vsf(half, k);
+      }
+      float mx[2] = {-INFINITY, -INFINITY}, sm[2] = {0.f, 0.f};
+#pragma unroll 4
+      for (int tk = 0; tk < PG; ++tk) {
+        const bool tv = p * PG + tk < sl_r;
+        const uint8_t* row = cb + (pl * PG + tk) * RC;
+        float code[R];
+        if constexpr (CB == 8) {
+#pragma unroll
+          for (int k = 0; k < R; ++k) code[k] = (float)(int8_t)row[k];
+        } else {
+#pragma unroll
+          for (int k = 0; k < R; k += 2) {
+            const int b = (int8_t)row[k / 2];
+            code[k] = (float)((b << 28) >> 28);
+            code[k + 1] = (float)(b >> 4);
+          }
+        }
+        const float cs = __half2float(csb[pl * PG + tk]) * a.scale;
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          float d = 0.f;
+#pragma unroll
+          for (int k = 0; k < R; ++k) d += code[k] * qt[jj][k];
+          const float tok = tv ? d * cs : -INFINITY;
+          if (a.tokmax) {
+            mx[jj] = fmaxf(mx[jj], tok);
+          } else if (tok > mx[jj]) {
+            sm[jj] = sm[jj] * expf(mx[jj] - tok) + 1.f;
+            mx[jj] = tok;
+          } else if (tok > -INFINITY) {
+            sm[jj] += expf(tok - mx[jj]);
+          }
+        }
+      }
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const int idx = 2 * half + jj;
+        const float qmu = (float)(128 * acc[0][0][idx] + acc[0][1][idx]) * qf.sq[jj] *
+                          mus * a.scale;
+        const float agg = a.tokmax ? mx[jj] : mx[jj] + logf(sm[jj]);
+        const float S = qmu + agg;
+        if (2 * c + jj < a.G) best[half] = fmaxf(best[half], S);
+      }
+    }
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      float v = best[half];
+      v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+      v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+      const bool pv = half ? it.vb : it.va;
+      if (pv && c == 0)
+        a.score[((int64_t)it.r * a.n_kv + h) * a.MP + it.p0 + m + 8 * half] = v;
+    }
+  }
+}
+
+template <int D, int CB, int VB>
+int launch_r8(const QuadArgs& a, cudaStream_t st) {
+  constexpr int R = 8;
+  auto k = r8_score_kernel<D, R, VB, CB>;
+  static int ps = 0;
+  if (ps == 0) {
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ps, k, kQuadWarps * 32, 0);
+    if (ps < 1) ps = 1;
+  }
+  const int heads = a.n_req * a.n_kv * a.G;
+  if (int rc = launch_pdl(q_limbs_kernel<D>, dim3((heads + 7) / 8), dim3(256), 0, st, a)) return rc;
+  int grid = num_sms() * ps;
+  const int per = a.n_kv > kQuadWarps ? a.n_kv / kQuadWarps : 1;
+  grid = (grid / per) * per;
+  if (int rc = launch_pdl(k, dim3(grid), dim3(kQuadWarps * 32), 0, st, a)) return rc;
+  return launch_status();
+}
+
 template <int D, int R, int VB>
 int launch_quad(const QuadArgs& a, bool write_h, cudaStream_t st) {
   auto k = write_h ? quad_score_kernel<D, R, VB, true>
@@ -562,3 +777,69 @@ extern "C" int amass_quad_score(const void* q, int64_t q_stride_t,
   return AMASS_ERR_UNSUPPORTED;
 }
 
+
+extern "C" int amass_r8_score(const void* q, int64_t q_stride_t,
+                              int64_t q_stride_h, const int8_t* mu,
+                              const void* mu_scale, const int8_t* Vk,
+                              const void* Vk_scale, const int8_t* c,
+                              const void* c_scale, const int32_t* block_table,
+                              int64_t bt_stride, const int32_t* seq_lens,
+                              const int32_t* n_sel_hi, float* score,
+                              int8_t* q8_ws, float* qs_ws, float scale,
+                              int n_req, int n_kv, int G, int head_dim,
+                              int page, int rank, int vk_bits, int c_bits,
+                              int max_pages, int token_agg, void* stream) {
+  using namespace amass;
+  if (n_req < 0 || n_kv <= 0 || G <= 0 || max_pages <= 0) return AMASS_ERR_ARG;
+  if (n_req == 0) return AMASS_OK;
+  if (!q || !mu || !mu_scale || !Vk || !Vk_scale || !c || !c_scale ||
+      !block_table || !seq_lens || !n_sel_hi || !score || !q8_ws || !qs_ws)
+    return AMASS_ERR_ARG;
+  if (G > 8 || page != 16 || rank != 8 || n_req > kR8MaxReq ||
+      (vk_bits != 8 && vk_bits != 4) || (c_bits != 8 && c_bits != 4))
+    return AMASS_ERR_UNSUPPORTED;
+  if ((q_stride_h % 2) || (q_stride_t % 2) ||
+      (reinterpret_cast<uintptr_t>(mu) & 15) ||
+      (reinterpret_cast<uintptr_t>(Vk) & 15) ||
+      (reinterpret_cast<uintptr_t>(c) & 15) ||
+      (reinterpret_cast<uintptr_t>(c_scale) & 15) ||
+      (reinterpret_cast<uintptr_t>(Vk_scale) & 3) ||
+      (reinterpret_cast<uintptr_t>(q8_ws) & 15))
+    return AMASS_ERR_ARG;
+  QuadArgs a{};
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.q_st = q_stride_t;
+  a.q_sh = q_stride_h;
+  a.mu = mu;
+  a.mus = static_cast<const __half*>(mu_scale);
+  a.V = Vk;
+  a.Vs = static_cast<const __half*>(Vk_scale);
+  a.sig2 = static_cast<const __half*>(Vk_scale);   // unused by r8
+  a.c = c;
+  a.cs = static_cast<const __half*>(c_scale);
+  a.sl = seq_lens;
+  a.bt = block_table;
+  a.bt_stride = bt_stride;
+  a.nsh = n_sel_hi;
+  a.score = score;
+  a.q8 = q8_ws;
+  a.qs = qs_ws;
+  a.scale = scale;
+  a.n_req = n_req;
+  a.n_kv = n_kv;
+  a.G = G;
+  a.MP = max_pages;
+  a.page = page;
+  a.tokmax = token_agg == AMASS_R8_TOKMAX ? 1 : 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto go = [&](auto d) -> int {
+    constexpr int D = decltype(d)::value;
+    if (vk_bits == 8 && c_bits == 8) return launch_r8<D, 8, 8>(a, st);
+    if (vk_bits == 8 && c_bits == 4) return launch_r8<D, 4, 8>(a, st);
+    if (vk_bits == 4 && c_bits == 8) return launch_r8<D, 8, 4>(a, st);
+    return launch_r8<D, 4, 4>(a, st);
+  };
+  if (head_dim == 128) return go(std::integral_constant<int, 128>{});
+  if (head_dim == 64) return go(std::integral_constant<int, 64>{});
+  return AMASS_ERR_UNSUPPORTED;
+}

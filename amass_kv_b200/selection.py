@@ -234,3 +234,103 @@ def select_pages_quad(st, layer: int, q, block_table, seq_lens, n_req: int,
     nrm = getattr(st, "combine", "max") == "nrm"
     _score_launch(st, layer, q, block_table, n_req, scale, nrm)
     select_pages(st, n_req, coverage=coverage, from_score_h=nrm)
+
+
+# --------------------------------------------------------------------------- #
+# r8 low-rank scorer                                                          #
+# --------------------------------------------------------------------------- #
+class R8State:
+    """Persistent r8 selection state, laid out like the reference's R8State
+    (``selection/state.py:35-112``):
+
+      r8_mu (L,NB,n_kv,d) int8 + mu_scale (L,NB,n_kv) fp16
+      r8_Vk (L,NB,n_kv,d,rv) int8 + Vk_scale (L,NB,n_kv,r) fp16
+      r8_c  (L,NB,n_kv,page,rc) int8 + c_scale (L,NB,n_kv,page) fp16
+      score / page_table / page_cnt / n_pages / n_sel_hi / b_fix / budget64.
+    """
+
+    def __init__(self, device, *, num_layers, num_blocks, n_kv, G, head_dim,
+                 page, max_reqs, max_pages, rank=8, budget=0.1, sink_pages=1,
+                 window_pages=1, tagw=TAGW, vk_grain="col", c_grain="page",
+                 vk_bits=8, c_bits=8, mu_bits=8, coverage=None):
+        if window_pages < 1:
+            raise ValueError("window_pages >= 1")
+        if vk_bits not in (4, 8) or c_bits not in (4, 8) or mu_bits != 8:
+            raise ValueError("Vk/c codes are int4 or int8; mu stays int8")
+        L, NB, D, r, MP, R = (num_layers, num_blocks, head_dim, rank,
+                              max_pages, max_reqs)
+        self.L, self.NB, self.n_kv, self.G, self.d, self.D = L, NB, n_kv, G, D, D
+        self.page, self.r, self.tagw = page, r, tagw
+        self.max_reqs, self.max_pages = R, MP
+        self.budget = float(budget)
+        self.coverage = None if coverage is None else float(coverage)
+        self.sink_pages, self.window_pages = int(sink_pages), int(window_pages)
+        self.vk_grain, self.c_grain = vk_grain, c_grain
+        self.vk_bits, self.c_bits, self.mu_bits = int(vk_bits), int(c_bits), 8
+        self.combine = "max"
+        self.device = device
+        kw = dict(device=device)
+        rvk = r // 2 if vk_bits == 4 else r
+        rc = r // 2 if c_bits == 4 else r
+        self.r8_mu = torch.zeros(L, NB, n_kv, D, dtype=torch.int8, **kw)
+        self.mu_scale = torch.zeros(L, NB, n_kv, dtype=torch.float16, **kw)
+        self.r8_Vk = torch.zeros(L, NB, n_kv, D, rvk, dtype=torch.int8, **kw)
+        self.Vk_scale = torch.zeros(L, NB, n_kv, r, dtype=torch.float16, **kw)
+        self.r8_c = torch.zeros(L, NB, n_kv, page, rc, dtype=torch.int8, **kw)
+        self.c_scale = torch.zeros(L, NB, n_kv, page, dtype=torch.float16, **kw)
+        self.r8_tag = torch.full((L, NB, n_kv, tagw), float("nan"),
+                                 dtype=torch.bfloat16, **kw)
+        self.score = torch.empty(R, n_kv, MP, dtype=torch.float32, **kw)
+        self.page_table = torch.empty(R, n_kv, MP, dtype=torch.int32, **kw)
+        self.page_cnt = torch.zeros(R, n_kv, dtype=torch.int32, **kw)
+        self.score_h = self.hmax = None
+        self.b_unit = torch.zeros(R, n_kv, dtype=torch.int32, **kw)
+        self.q8 = torch.zeros(R, n_kv * G, 2, D, dtype=torch.int8, **kw)
+        self.qs = torch.zeros(R, n_kv * G, dtype=torch.float32, **kw)
+        self.n_pages = torch.zeros(R, dtype=torch.int32, **kw)
+        self.n_sel_hi = torch.zeros(R, dtype=torch.int32, **kw)
+        self.b_fix = torch.ones(R, dtype=torch.int32, **kw)
+        self.budget64 = torch.tensor([self.budget], dtype=torch.float64, **kw)
+
+    def layer_state(self, layer: int):
+        return (self.r8_mu[layer], self.mu_scale[layer], self.r8_Vk[layer],
+                self.Vk_scale[layer], self.r8_c[layer], self.c_scale[layer],
+                self.r8_tag[layer])
+
+
+R8_AGG = {"lse": 0, "tokmax": 1}
+
+
+def r8_score_cuda(st, layer: int, q, block_table, seq_lens, n_req: int,
+                  scale: float, *, token_agg: str = "lse") -> None:
+    """Drop-in for the reference ``r8_score_cuda`` (``selection/score_cuda.py
+    :888``): writes ``st.score`` over the scored region.  ``token_agg="tokmax"``
+    replaces the per-page log-sum-exp over tokens by a max."""
+    _prepare(st, q.device, False)
+    _check_q(q, st)
+    mu, mu_s, Vk, Vk_s, c, c_s = (st.r8_mu[layer], st.mu_scale[layer],
+                                  st.r8_Vk[layer], st.Vk_scale[layer],
+                                  st.r8_c[layer], st.c_scale[layer])
+    _lib.call("amass_r8_score", ptr(q), q.stride(0), q.stride(1), ptr(mu),
+              ptr(mu_s), ptr(Vk), ptr(Vk_s), ptr(c), ptr(c_s),
+              ptr(block_table), block_table.stride(0), ptr(seq_lens),
+              ptr(st.n_sel_hi), ptr(st.score), ptr(st.q8), ptr(st.qs),
+              float(scale), int(n_req), int(st.n_kv), int(st.G), int(st.d),
+              int(st.page), int(st.r), int(getattr(st, "vk_bits", 8)),
+              int(getattr(st, "c_bits", 8)), int(st.max_pages),
+              R8_AGG[token_agg], _lib.stream_of(q.device))
+
+
+r8_score = r8_score_cuda
+
+
+def select_pages_r8(st, layer: int, q, block_table, seq_lens, n_req: int,
+                    scale: float, *, derive: bool = True, coverage=None,
+                    token_agg: str = "lse") -> None:
+    """One-call Stage A (r8): (derive) + r8 score + top-b / coverage select
+    (reference ``selection/select.py:119-130``)."""
+    if derive:
+        derive_page_params(st, seq_lens, n_req)
+    r8_score_cuda(st, layer, q, block_table, seq_lens, n_req, scale,
+                  token_agg=token_agg)
+    select_pages(st, n_req, coverage=coverage, from_score_h=False)

@@ -123,6 +123,25 @@ int amass_select_pages(const float* score_h, int64_t sh_stride, float* hmax,
                        int G, int sink_pages, int max_pages, int combine,
                        int mode, float coverage, void* stream);
 
+/* r8_score -- replaces selection/score_cuda.py:888-913 (Triton golden
+ * selection/score.py:30-148).  One layer's R8State slabs: mu (NB,n_kv,d) int8
+ * + mu_scale (NB,n_kv) fp16, Vk (NB,n_kv,d,rv) int8 (rv = 8, or 4 packed
+ * int4) + Vk_scale (NB,n_kv,8) fp16, c (NB,n_kv,page,rc) int8 (rc = 8 or 4)
+ * + c_scale (NB,n_kv,page) fp16.  score[r,kv,p] = max_g (s*mu.q_g +
+ * agg_t(s*c_t.(Vk^T q_g))), agg = log-sum-exp over tokens < seq_len
+ * (token_agg AMASS_R8_LSE, the reference form) or max (AMASS_R8_TOKMAX).
+ * q8_ws/qs_ws: scratch as for amass_quad_score.  rank 8, page 16, G <= 8,
+ * head_dim in {64, 128}. */
+int amass_r8_score(const void* q, int64_t q_stride_t, int64_t q_stride_h,
+                   const int8_t* mu, const void* mu_scale, const int8_t* Vk,
+                   const void* Vk_scale, const int8_t* c, const void* c_scale,
+                   const int32_t* block_table, int64_t bt_stride,
+                   const int32_t* seq_lens, const int32_t* n_sel_hi,
+                   float* score, int8_t* q8_ws, float* qs_ws, float scale,
+                   int n_req, int n_kv, int G, int head_dim, int page,
+                   int rank, int vk_bits, int c_bits, int max_pages,
+                   int token_agg, void* stream);
+
 /* sparse_paged_decode -- replaces attention/decode_cuda.py:1376-1465
  * (Triton golden attention/decode.py:247-304 + merge.py:21-50).
  * K/V tiles are addressed as base + blk*s_b + tok*s_t + kv*s_h (elements,

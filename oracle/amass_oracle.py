@@ -241,10 +241,13 @@ def coverage_select(score, n_pages, n_sel_hi, *, sink: int, MP: int,
     return tab, cnt, bu
 
 
-def selection_diff_ok(tab_a, cnt_a, tab_b, cnt_b, score, tau_tol=1e-3):
-    """True when two selections differ only on pages whose score lies within
-    ``tau_tol`` (relative, floor 1) of the smallest kept selectable score --
-    the tie band the parity contract allows."""
+def selection_diff_ok(tab_a, cnt_a, tab_b, cnt_b, score, tau_tol=1e-3,
+                      sink=1):
+    """True when selection A differs from the reference selection B only on
+    pages whose reference score lies within ``tau_tol`` (relative, floor 1) of
+    B's threshold -- the smallest reference score B keeps in the selectable
+    region (p >= sink, finite score): the tie band the parity contract
+    allows."""
     R, n_kv = cnt_a.shape
     for rq in range(R):
         for kh in range(n_kv):
@@ -253,9 +256,8 @@ def selection_diff_ok(tab_a, cnt_a, tab_b, cnt_b, score, tau_tol=1e-3):
             diff = a ^ b
             if not diff:
                 continue
-            both = sorted(a & b)
             sc = score[rq, kh]
-            vals = [sc[p] for p in both if np.isfinite(sc[p])]
+            vals = [sc[p] for p in b if p >= sink and np.isfinite(sc[p])]
             tau = min(vals) if vals else 0.0
             for p in diff:
                 if not (abs(float(sc[p]) - float(tau))

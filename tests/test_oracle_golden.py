@@ -170,3 +170,15 @@ def test_coverage_acceptance_accepts_golden(name):
                               z["n_sel_hi"], sink=1,
                               coverage=float(z["coverage"][0]),
                               combine=str(z["combine"][0]))
+
+
+def test_selection_tie_band():
+    """A swap of two pages whose scores differ by < 1e-3 of the threshold is
+    accepted; a swap across a real gap is rejected."""
+    sc = np.array([[[9.0, 5.0, 3.0000, 3.0004, 1.0, np.nan]]], np.float32)
+    ref = np.array([[[0, 1, 3, 5, -1, -1]]], np.int32)
+    tie = np.array([[[0, 1, 2, 5, -1, -1]]], np.int32)
+    gap = np.array([[[0, 1, 4, 5, -1, -1]]], np.int32)
+    cnt = np.array([[4]], np.int32)
+    assert O.selection_diff_ok(tie, cnt, ref, cnt, sc)
+    assert not O.selection_diff_ok(gap, cnt, ref, cnt, sc)
