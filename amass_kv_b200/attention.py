@@ -81,7 +81,8 @@ def sparse_paged_decode_batched_cuda(q, kv_cache, block_table, seq_lens, st,
     LSE merge into ``out[:n_req]`` (bf16, in place).  Same contract as the
     reference function; ``n_req = seq_lens.shape[0]``."""
     if scale is None:
-        scale = st.scale
+        # the state's softmax scale, else 1/sqrt(head_dim)
+        scale = getattr(st, "scale", None) or q.shape[-1] ** -0.5
     n_req = seq_lens.shape[0]
     k, v = split_kv(kv_cache)
     if vsource is not None:

@@ -49,6 +49,20 @@ struct DecArgs {
   float scale_log2;
   int split, pps_min;
   int n_req, n_kv, G, MP, units;
+  // mem-v / mem-kv tier sources (TIER kernels only): per page the V tile
+  // (and the K tile when hot_k is set) comes from the hot buffer when the
+  // page is complete and resident, else the staging pool when vbo >= 0,
+  // else the pinned pool (reference tier/decode_mem.py:118-147)
+  const __nv_bfloat16* hot_v;   // (n_kv, S, 16, D)
+  const __nv_bfloat16* hot_k;   // null: K from the resident cache k
+  const __nv_bfloat16* stg_v;   // (NV, 16, n_kv, D) at svb/svt/svh
+  const __nv_bfloat16* stg_k;
+  const __nv_bfloat16* pool_v;  // pinned (L, NB, n_kv, 16, D), device view
+  const __nv_bfloat16* pool_k;
+  int64_t svb, svt, svh;
+  const int32_t* p2s;           // (n_kv, NB) this layer
+  const int32_t* vbo;           // (NB,)
+  int t_layer, t_NB, t_S;
 };
 
 AMASS_DEV int unit_pps(int cnt, int split, int pps_min) {
@@ -72,7 +86,7 @@ struct Tile {
 
 AMASS_DEV uint32_t swz(int row, int chunk) { return chunk ^ (row & 7); }
 
-template <int D, int NST>
+template <int D, int NST, bool TIER>
 __global__ void __launch_bounds__(kDecThreads)
 decode_kernel(DecArgs a) {
   grid_dep_wait();     // inputs written by the previous kernel
@@ -159,11 +173,34 @@ decode_kernel(DecArgs a) {
       const int r = u / a.n_kv, kv = u - r * a.n_kv;
       const int pt = a.tab[(int64_t)u * a.MP + cu.j];
       const int64_t blk = a.bt[(int64_t)r * a.bt_stride + pt];
-      const int valid = min(16, a.sl[r] - pt * 16);
+      const int seq = a.sl[r];
+      const int valid = min(16, seq - pt * 16);
       if (lane == 0) my_meta[slot] = valid;
       const uint32_t sbase = smem_u32(my_stages + slot * T::kStageBytes);
       const __nv_bfloat16* kp = a.k + blk * a.k_sb + kv * a.k_sh;
       const __nv_bfloat16* vp = a.v + blk * a.v_sb + kv * a.v_sh;
+      int64_t kst = a.k_st, vst = a.v_st;
+      if constexpr (TIER) {
+        // one source decision per page, on the address (same bytes, so the
+        // math matches the resident decode bit for bit)
+        const int hslot = a.p2s[(int64_t)kv * a.t_NB + blk];
+        const int vb = a.vbo[blk];
+        const bool use_hot = (pt + 1) * 16 <= seq && hslot >= 0;
+        int64_t off;
+        const __nv_bfloat16 *hv, *hk;
+        if (use_hot) {
+          off = ((int64_t)kv * a.t_S + hslot) * (16 * D);
+          hv = a.hot_v; hk = a.hot_k; vst = D;
+        } else if (vb >= 0) {
+          off = vb * a.svb + kv * a.svh;
+          hv = a.stg_v; hk = a.stg_k; vst = a.svt;
+        } else {
+          off = (((int64_t)a.t_layer * a.t_NB + blk) * a.n_kv + kv) * (16 * D);
+          hv = a.pool_v; hk = a.pool_k; vst = D;
+        }
+        vp = hv + off;
+        if (a.hot_k) { kp = hk + off; kst = vst; }
+      }
 #pragma unroll
       for (int i = 0; i < (16 * T::kChunks) / 32; ++i) {
         const int id = lane + 32 * i;
@@ -171,8 +208,8 @@ decode_kernel(DecArgs a) {
         const bool ok = row < valid;
         const uint32_t doff = row * T::kRowBytes + swz(row, ch) * 16;
         const int rr = ok ? row : 0;
-        cp_async16(sbase + doff, kp + rr * a.k_st + ch * 8, ok);
-        cp_async16(sbase + T::kTileBytes + doff, vp + rr * a.v_st + ch * 8, ok);
+        cp_async16(sbase + doff, kp + rr * kst + ch * 8, ok);
+        cp_async16(sbase + T::kTileBytes + doff, vp + rr * vst + ch * 8, ok);
       }
       cu.j += kDecWarps;
     }
@@ -410,11 +447,11 @@ size_t decode_smem(int G, int units) {
          (size_t)kDecWarps * NST * sizeof(int) + (size_t)(units + 1) * sizeof(int);
 }
 
-template <int D, int NST>
+template <int D, int NST, bool TIER>
 int launch_decode(const DecArgs& a, cudaStream_t st) {
   const size_t smem = decode_smem<D, NST>(a.G, a.units);
   if (smem > 220 * 1024) return AMASS_ERR_UNSUPPORTED;
-  auto kern = decode_kernel<D, NST>;
+  auto kern = decode_kernel<D, NST, TIER>;
   static int configured = 0;
   if (!configured) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -476,9 +513,81 @@ extern "C" int amass_sparse_decode(
   a.split = split; a.pps_min = pps_min;
   a.n_req = n_req; a.n_kv = n_kv; a.G = G; a.MP = max_pages;
   a.units = n_req * n_kv;
+  a.hot_v = a.hot_k = a.stg_v = a.stg_k = a.pool_v = a.pool_k = nullptr;
+  a.svb = a.svt = a.svh = 0;
+  a.p2s = a.vbo = nullptr;
+  a.t_layer = a.t_NB = a.t_S = 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (head_dim == 128) return launch_decode<128, 2>(a, st);
-  if (head_dim == 64) return launch_decode<64, 3>(a, st);
+  if (head_dim == 128) return launch_decode<128, 2, false>(a, st);
+  if (head_dim == 64) return launch_decode<64, 3, false>(a, st);
+  return AMASS_ERR_UNSUPPORTED;
+}
+
+extern "C" int amass_tier_decode(
+    const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k,
+    int64_t k_sb, int64_t k_st, int64_t k_sh, const void* hot_v,
+    const void* hot_k, const void* stg_v, const void* stg_k, int64_t svb,
+    int64_t svt, int64_t svh, const void* pool_v, const void* pool_k,
+    const int32_t* page2slot, const int32_t* vbo, int layer, int num_blocks,
+    int hot_slots, const int32_t* block_table, int64_t bt_stride,
+    const int32_t* page_table, const int32_t* page_cnt,
+    const int32_t* seq_lens, float* m_part, float* l_part, float* acc_part,
+    int split, int pps_min, void* out, int64_t o_stride_t, int64_t o_stride_h,
+    float scale, int n_req, int n_kv, int G, int head_dim, int page,
+    int max_pages, void* stream) {
+  using namespace amass;
+  if (n_req < 0 || n_kv <= 0 || G <= 0 || split <= 0 || pps_min <= 0 ||
+      max_pages <= 0 || layer < 0 || num_blocks <= 0 || hot_slots <= 0)
+    return AMASS_ERR_ARG;
+  if (n_req == 0) return AMASS_OK;
+  const bool k_tier = hot_k != nullptr;
+  if (!q || !hot_v || !stg_v || !pool_v || !page2slot || !vbo ||
+      !block_table || !page_table || !page_cnt || !seq_lens || !m_part ||
+      !l_part || !acc_part || !out)
+    return AMASS_ERR_ARG;
+  if (k_tier ? (!stg_k || !pool_k) : !k) return AMASS_ERR_ARG;
+  if (G > 8 || page != 16) return AMASS_ERR_UNSUPPORTED;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(hot_v) |
+                       reinterpret_cast<uintptr_t>(stg_v) |
+                       reinterpret_cast<uintptr_t>(pool_v) |
+                       reinterpret_cast<uintptr_t>(hot_k) |
+                       reinterpret_cast<uintptr_t>(stg_k) |
+                       reinterpret_cast<uintptr_t>(pool_k) |
+                       (k_tier ? 0 : reinterpret_cast<uintptr_t>(k));
+  if ((al & 15) || (svb % 8) || (svt % 8) || (svh % 8) ||
+      (!k_tier && ((k_st % 8) || (k_sb % 8) || (k_sh % 8))) ||
+      (q_stride_h % 2) || (q_stride_t % 2) || (o_stride_h % 2) ||
+      (o_stride_t % 2))
+    return AMASS_ERR_ARG;
+  DecArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.q_st = q_stride_t; a.q_sh = q_stride_h;
+  a.k = static_cast<const __nv_bfloat16*>(k_tier ? hot_k : k);
+  a.k_sb = k_tier ? 0 : k_sb; a.k_st = k_tier ? head_dim : k_st;
+  a.k_sh = k_tier ? 0 : k_sh;
+  a.v = static_cast<const __nv_bfloat16*>(hot_v);
+  a.v_sb = 0; a.v_st = head_dim; a.v_sh = 0;
+  a.bt = block_table; a.bt_stride = bt_stride;
+  a.tab = page_table; a.cnt = page_cnt; a.sl = seq_lens;
+  a.m_part = m_part; a.l_part = l_part; a.acc_part = acc_part;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.o_st = o_stride_t; a.o_sh = o_stride_h;
+  a.scale_log2 = scale * kLog2e;
+  a.split = split; a.pps_min = pps_min;
+  a.n_req = n_req; a.n_kv = n_kv; a.G = G; a.MP = max_pages;
+  a.units = n_req * n_kv;
+  a.hot_v = static_cast<const __nv_bfloat16*>(hot_v);
+  a.hot_k = static_cast<const __nv_bfloat16*>(hot_k);
+  a.stg_v = static_cast<const __nv_bfloat16*>(stg_v);
+  a.stg_k = static_cast<const __nv_bfloat16*>(stg_k);
+  a.pool_v = static_cast<const __nv_bfloat16*>(pool_v);
+  a.pool_k = static_cast<const __nv_bfloat16*>(pool_k);
+  a.svb = svb; a.svt = svt; a.svh = svh;
+  a.p2s = page2slot; a.vbo = vbo;
+  a.t_layer = layer; a.t_NB = num_blocks; a.t_S = hot_slots;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (head_dim == 128) return launch_decode<128, 2, true>(a, st);
+  if (head_dim == 64) return launch_decode<64, 3, true>(a, st);
   return AMASS_ERR_UNSUPPORTED;
 }
 

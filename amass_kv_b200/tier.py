@@ -1,0 +1,352 @@
+"""mem-v / mem-kv DRAM tier -- host side of the sm_100a tier kernels.
+
+Mirrors the reference's ``amass.tier`` surface for the decode hot path:
+
+  MappedHostVPool          tier/pool.py:104-151
+  Staging (V/K pools+vbo)  tier/staging.py:235-310 (buffers only)
+  Residency                tier/residency.py:281-575
+  Tier                     tier/tier.py:37-180 (step / bytes_report)
+  mem_decode_ptrsel        tier/decode_mem.py:169-222
+  mem_dynamic_decode       tier/decode_mem.py:225-274
+
+V (and K under mem-kv) of every page lives in a pinned, device-mapped host
+pool (L, NB, n_kv, page, d); each (layer, kv-head) keeps a VRAM hot buffer of
+S page slots filled by exact LRU; pages written this step and not yet flushed
+sit in the VRAM staging pool addressed by ``vbo``.  Every step of one layer is
+three launches: plan (hits/misses/victims), fetch (host link -> hot), and the
+ptr-select decode that reads each page from hot | staging | pinned.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import ptr
+from .attention import ensure_stage_b_buffers, pps_min_for, split_kv
+
+_FETCH_MODES = ("kernel", "off")
+
+
+def host_device_pointer(host_tensor: torch.Tensor) -> int:
+    """Device address of a pinned host tensor (UVA zero-copy); raises if the
+    memory is not pinned and mapped (reference tier/pool.py:65-80)."""
+    if not host_tensor.is_pinned():
+        raise ValueError("pool tensor must be pinned (pin_memory=True)")
+    dev = ctypes.c_void_p(0)
+    _lib.call("amass_host_device_pointer", ctypes.c_void_p(host_tensor.data_ptr()),
+              ctypes.byref(dev))
+    return int(dev.value)
+
+
+class DevPtrTensor:
+    """A device address without a torch.Tensor wrapper (``data_ptr()``,
+    ``dtype``, ``shape``) -- the pinned pool's device view."""
+
+    __slots__ = ("_ptr", "dtype", "device", "shape")
+
+    def __init__(self, p: int, dtype, device, shape=()):
+        self._ptr, self.dtype, self.device, self.shape = int(p), dtype, device, shape
+
+    def data_ptr(self) -> int:
+        return self._ptr
+
+
+class MappedHostVPool:
+    """Pinned host pool (L, NB, n_kv, page, d) + its device view.  The page of
+    (layer, block, kv-head) starts at element ((l*NB + blk)*n_kv + kv)*page*d
+    (reference tier/pool.py:104-147)."""
+
+    def __init__(self, *, num_layers: int, num_blocks: int, n_kv: int,
+                 page: int, d: int, dtype=torch.bfloat16, device=None,
+                 max_pool_gb: float = 256.0):
+        if dtype not in (torch.bfloat16, torch.float16):
+            raise ValueError(f"pool dtype must be bf16/fp16, got {dtype}")
+        self.L, self.NB, self.n_kv = num_layers, num_blocks, n_kv
+        self.page, self.d, self.dtype = page, d, dtype
+        pool_bytes = num_layers * num_blocks * n_kv * page * d * 2
+        if pool_bytes > max_pool_gb * (1 << 30):
+            raise RuntimeError(
+                f"pinned V pool would be {pool_bytes / 2**30:.1f} GiB "
+                f"(> max_pool_gb={max_pool_gb}); reduce num_blocks or raise "
+                "max_pool_gb (host DRAM, not VRAM)")
+        dev = torch.device(device) if device is not None else \
+            torch.device("cuda", torch.cuda.current_device())
+        self.host = torch.zeros((num_layers, num_blocks, n_kv, page, d),
+                                dtype=dtype, pin_memory=True)
+        self.dev_view = DevPtrTensor(host_device_pointer(self.host),
+                                     torch.int16, dev, tuple(self.host.shape))
+        self.pool_gib = pool_bytes / 2**30
+        self.device = dev
+
+    def page_offset(self, layer: int, blk: int, kv: int) -> int:
+        return ((layer * self.NB + blk) * self.n_kv + kv) * self.page * self.d
+
+    def vram_note(self) -> str:
+        return (f"host_pool={self.pool_gib:.2f}GiB (DRAM, keyed by NB={self.NB}; "
+                "VRAM hot/staging bounded to the working set)")
+
+
+class Staging:
+    """VRAM staging pools for pages written but not yet flushed:
+    v_pool (L, NV, page, n_kv, d), k_pool likewise under mem-kv, and
+    vbo (NB,) = staging row of a block or -1 (reference tier/staging.py:
+    238-310).  The write/flush lifecycle stays with the caller."""
+
+    def __init__(self, *, num_layers: int, num_blocks: int, n_kv: int,
+                 page: int, d: int, n_vslots: int, dtype=torch.bfloat16,
+                 device="cuda", offload_k: bool = False):
+        self.L, self.NB, self.NV = num_layers, num_blocks, n_vslots
+        self.v_pool = torch.zeros((num_layers, n_vslots, page, n_kv, d),
+                                  dtype=dtype, device=device)
+        self.k_pool = (torch.zeros_like(self.v_pool) if offload_k else None)
+        self.vbo = torch.full((num_blocks,), -1, dtype=torch.int32,
+                              device=device)
+
+
+class Residency:
+    """Exact-LRU hot-buffer residency of every (layer, kv-head)
+    (reference tier/residency.py:281-348).
+
+    State (device, allocated once): hot (L, n_kv, S, page, d) [+ hot_k under
+    mem-kv], page2slot (L, n_kv, NB), slot2page / lru_clock (L, n_kv, S),
+    pool_valid (L, n_kv, NB) int8, clock int32[2] (clock, CTA ticket; starts
+    at 1 like the reference), overflow (1,), and per-call scratch
+    fetch_list (n_kv, S, 2) / fetch_cnt (n_kv,)."""
+
+    def __init__(self, *, num_layers: int, num_blocks: int, n_kv: int,
+                 hot_slots: int, page: int, d: int, max_reqs: int,
+                 max_pages: int, dtype=torch.bfloat16, device="cuda",
+                 offload_k: bool = False):
+        self.L, self.NB, self.n_kv = num_layers, num_blocks, n_kv
+        self.S, self.page, self.d = hot_slots, page, d
+        self.R, self.MP = max_reqs, max_pages
+        self.dtype, self.offload_k = dtype, offload_k
+        dev = torch.device(device)
+        self.device = dev
+        i32, i8 = torch.int32, torch.int8
+        self.hot = torch.zeros((num_layers, n_kv, hot_slots, page, d),
+                               dtype=dtype, device=dev)
+        self.hot_i16 = self.hot.view(torch.int16)
+        self.hot_k = torch.zeros_like(self.hot) if offload_k else None
+        self.hot_k_i16 = self.hot_k.view(torch.int16) if offload_k else None
+        self.page2slot = torch.full((num_layers, n_kv, num_blocks), -1,
+                                    dtype=i32, device=dev)
+        self.slot2page = torch.full((num_layers, n_kv, hot_slots), -1,
+                                    dtype=i32, device=dev)
+        self.lru_clock = torch.zeros((num_layers, n_kv, hot_slots), dtype=i32,
+                                     device=dev)
+        self.pool_valid = torch.zeros((num_layers, n_kv, num_blocks),
+                                      dtype=i8, device=dev)
+        self.clock = torch.tensor([1, 0], dtype=i32, device=dev)
+        self.overflow = torch.zeros((1,), dtype=i32, device=dev)
+        self.fetch_list = torch.zeros((n_kv, hot_slots, 2), dtype=i32,
+                                      device=dev)
+        self.fetch_cnt = torch.zeros((n_kv,), dtype=i32, device=dev)
+        self.plan_capacity = _lib.load().amass_tier_plan_capacity(hot_slots)
+        if self.plan_capacity <= 0:
+            raise ValueError(f"hot_slots={hot_slots} outside (0, 8192]")
+        elem = self.hot.element_size()
+        hot_n = self.hot.numel() * (2 if offload_k else 1)
+        self.hot_gib = hot_n * elem / 2**30
+        self.maps_gib = sum(t.numel() * t.element_size() for t in (
+            self.page2slot, self.slot2page, self.lru_clock, self.pool_valid,
+            self.fetch_list, self.fetch_cnt)) / 2**30
+
+    # -- per step ------------------------------------------------------------
+    def invalidate_written(self, block_table, seq_lens, query_start_loc) -> None:
+        """Drop residency and pool validity of every page (re)written this
+        step, all layers (reference residency.py:352-367)."""
+        n_req = seq_lens.shape[0]
+        _lib.call("amass_tier_invalidate", ptr(block_table),
+                  block_table.stride(0), ptr(seq_lens), ptr(query_start_loc),
+                  ptr(self.page2slot), ptr(self.slot2page),
+                  ptr(self.pool_valid), int(n_req), self.L, self.n_kv,
+                  self.NB, self.S, self.page, _lib.stream_of(self.device))
+
+    def gather_plan(self, layer, page_table, page_cnt, block_table, seq_lens,
+                    n_req) -> None:
+        """Hits touch the LRU, misses take exact-LRU victims (clock advances
+        by one); the installed misses land in fetch_list/fetch_cnt
+        (reference residency.py:385-407)."""
+        l = int(layer)
+        _lib.call("amass_tier_plan", ptr(page_table), ptr(page_cnt),
+                  ptr(block_table), block_table.stride(0), ptr(seq_lens),
+                  ptr(self.page2slot[l]), ptr(self.slot2page[l]),
+                  ptr(self.lru_clock[l]), ptr(self.clock), ptr(self.overflow),
+                  ptr(self.fetch_list), ptr(self.fetch_cnt), int(n_req),
+                  self.n_kv, int(page_table.shape[-1]), self.page, self.NB,
+                  self.S, _lib.stream_of(self.device))
+
+    def gather_fetch(self, layer, staging, pool, n_req=None, stream=None,
+                     poolk=None) -> None:
+        """Copy the planned misses into their hot slots: pinned pool when
+        flushed, else staging with write-through (reference residency.py:
+        409-436).  ``pool``/``poolk`` are device views (``dev_view``)."""
+        l = int(layer)
+        vp = staging.v_pool[l]
+        has_k = self.hot_k_i16 is not None
+        if has_k and (poolk is None or staging.k_pool is None):
+            raise ValueError("mem-kv residency needs poolk and staging.k_pool")
+        kp = staging.k_pool[l] if has_k else None
+        st = (stream.cuda_stream if stream is not None
+              else _lib.stream_of(self.device))
+        _lib.call("amass_tier_fetch", ptr(self.fetch_list), ptr(self.fetch_cnt),
+                  ptr(self.hot_i16[l]), pool.data_ptr(), ptr(self.pool_valid[l]),
+                  ptr(staging.vbo), ptr(vp), vp.stride(0), vp.stride(1),
+                  vp.stride(2), ptr(self.hot_k_i16[l]) if has_k else 0,
+                  poolk.data_ptr() if has_k else 0, ptr(kp) if has_k else 0,
+                  l, self.NB, self.n_kv, self.S, self.page, self.d, st)
+
+    def gather(self, layer, page_table, page_cnt, block_table, seq_lens,
+               n_req, staging, pool, poolk=None) -> None:
+        """plan + fetch (reference residency.py:369-383)."""
+        self.gather_plan(layer, page_table, page_cnt, block_table, seq_lens,
+                         n_req)
+        self.gather_fetch(layer, staging, pool, n_req, poolk=poolk)
+
+    # -- debug / reporting (host sync) ---------------------------------------
+    def assert_maps_inverse(self, layer: int | None = None) -> None:
+        """page2slot and slot2page are mutual inverses (reference
+        residency.py:550-572)."""
+        layers = range(self.L) if layer is None else [layer]
+        for l in layers:
+            p2s, s2p = self.page2slot[l].cpu(), self.slot2page[l].cpu()
+            for kv in range(self.n_kv):
+                for s, blk in enumerate(s2p[kv].tolist()):
+                    if blk >= 0 and int(p2s[kv, blk]) != s:
+                        raise AssertionError(
+                            f"slot2page[{l},{kv},{s}]={blk} but page2slot="
+                            f"{int(p2s[kv, blk])}")
+                res = (p2s[kv] >= 0).nonzero().flatten().tolist()
+                for blk in res:
+                    s = int(p2s[kv, blk])
+                    if int(s2p[kv, s]) != blk:
+                        raise AssertionError(
+                            f"page2slot[{l},{kv},{blk}]={s} but slot2page="
+                            f"{int(s2p[kv, s])}")
+
+    def misses_last_call(self) -> int:
+        return int(self.fetch_cnt.sum())
+
+    def bytes_report(self) -> str:
+        return (f"hot={self.hot_gib:.3f}GiB maps={self.maps_gib:.4f}GiB "
+                f"(S={self.S} slots x {self.n_kv} kv x {self.L} layers)")
+
+
+class Tier:
+    """pool (+ pool_k) + staging + residency (reference tier/tier.py:37-180)."""
+
+    def __init__(self, *, num_layers: int, num_blocks: int, n_kv: int,
+                 page: int, d: int, hot_slots: int, max_reqs: int,
+                 max_pages: int, n_vslots: int, offload_k: bool = False,
+                 dtype=torch.bfloat16, device="cuda",
+                 max_pool_gb: float = 256.0):
+        kw = dict(num_layers=num_layers, num_blocks=num_blocks, n_kv=n_kv,
+                  page=page, d=d)
+        self.offload_k = offload_k
+        self.pool = MappedHostVPool(**kw, dtype=dtype, device=device,
+                                    max_pool_gb=max_pool_gb)
+        self.pool_k = (MappedHostVPool(**kw, dtype=dtype, device=device,
+                                       max_pool_gb=max_pool_gb)
+                       if offload_k else None)
+        self.staging = Staging(**kw, n_vslots=n_vslots, dtype=dtype,
+                               device=device, offload_k=offload_k)
+        self.residency = Residency(**kw, hot_slots=hot_slots,
+                                   max_reqs=max_reqs, max_pages=max_pages,
+                                   dtype=dtype, device=device,
+                                   offload_k=offload_k)
+
+    @classmethod
+    def from_config(cls, cfg, *, num_layers, num_blocks, n_kv, page, d,
+                    max_reqs, max_pages, n_vslots, device="cuda"):
+        """Hot slots = cfg.hot_frac of max_pages (at least 1), mem-kv when
+        cfg.mem_mode == "mem-kv" (reference tier/tier.py:70-84)."""
+        frac = float(getattr(cfg, "hot_frac", 0.1))
+        S = max(1, int(round(frac * max_pages)))
+        return cls(num_layers=num_layers, num_blocks=num_blocks, n_kv=n_kv,
+                   page=page, d=d, hot_slots=S, max_reqs=max_reqs,
+                   max_pages=max_pages, n_vslots=n_vslots,
+                   offload_k=getattr(cfg, "mem_mode", "mem-v") == "mem-kv",
+                   device=device,
+                   max_pool_gb=float(getattr(cfg, "max_pool_gb", 256.0)))
+
+    def step(self, lidx, page_table, page_cnt, block_table, seq_lens,
+             n_req) -> None:
+        self.residency.gather(lidx, page_table, page_cnt, block_table,
+                              seq_lens, n_req, self.staging,
+                              self.pool.dev_view,
+                              poolk=self.pool_k.dev_view if self.pool_k
+                              else None)
+
+    def bytes_report(self) -> str:
+        return (f"{self.pool.vram_note()}; {self.residency.bytes_report()}; "
+                f"staging={self.staging.v_pool.numel() * 2 / 2**30:.3f}GiB")
+
+
+def mem_decode_ptrsel(q, kv_cache, block_table, seq_lens, st, out, tier,
+                      lidx: int, *, scale=None, pps_min=None) -> None:
+    """ptr-select tiered split-K decode + merge into ``out[:n_req]`` (bf16):
+    per page V (and K under mem-kv) from hot | staging | pinned
+    (reference tier/decode_mem.py:169-222).  Bitwise equal to the resident
+    decode on the same bytes."""
+    if scale is None:
+        # the state's softmax scale, else 1/sqrt(head_dim)
+        scale = getattr(st, "scale", None) or q.shape[-1] ** -0.5
+    n_req = seq_lens.shape[0]
+    r5, stg = tier.residency, tier.staging
+    l = int(lidx)
+    if getattr(st, "m_part", None) is None:
+        ensure_stage_b_buffers(st, q.device)
+    if pps_min is None:
+        pps_min = pps_min_for(n_req)
+    vp = stg.v_pool[l]
+    if tier.offload_k:
+        kres, skb, skt, skh = None, 0, 0, 0
+        stg_k = stg.k_pool[l]
+        pool_k = tier.pool_k.dev_view.data_ptr()
+    else:
+        kres, _ = split_kv(kv_cache)
+        skb, skt, skh = kres.stride(0), kres.stride(1), kres.stride(2)
+        stg_k = None
+        pool_k = 0
+    if q.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
+        raise ValueError("q and out must be bf16")
+    _lib.call("amass_tier_decode", ptr(q), q.stride(0), q.stride(1),
+              ptr(kres), skb, skt, skh,
+              ptr(r5.hot[l]), ptr(r5.hot_k[l]) if tier.offload_k else 0,
+              ptr(vp), ptr(stg_k), vp.stride(0), vp.stride(1), vp.stride(2),
+              tier.pool.dev_view.data_ptr(), pool_k,
+              ptr(r5.page2slot[l]), ptr(stg.vbo), l, r5.NB, r5.S,
+              ptr(block_table), block_table.stride(0), ptr(st.page_table),
+              ptr(st.page_cnt), ptr(seq_lens), ptr(st.m_part), ptr(st.l_part),
+              ptr(st.acc_part), int(st.split), int(pps_min), ptr(out),
+              out.stride(0), out.stride(1), float(scale), int(n_req),
+              r5.n_kv, int(st.G), r5.d, r5.page, int(st.max_pages),
+              _lib.stream_of(q.device))
+
+
+def mem_dynamic_decode(q, kv_cache, block_table, seq_lens, st, out, tier,
+                       lidx: int, *, scale=None, fetch: str = "kernel",
+                       impl: str = "ptrsel") -> None:
+    """One layer of the tiered decode: residency step (plan + fetch) of the
+    layer's selection, then the ptr-select decode (reference
+    tier/decode_mem.py:225-274).  ``fetch="off"`` decodes from the current
+    residency without a step.  The reference's ``fetch="dma"`` (copy-engine
+    runs planned on the host) and its ``impl`` variants are not provided:
+    the kernel fetch is graph-capturable and the decode has one path."""
+    if fetch not in _FETCH_MODES:
+        raise ValueError(f"fetch must be one of {_FETCH_MODES}, got {fetch!r}")
+    if impl not in ("ptrsel", "cuda"):
+        raise ValueError(f"impl must be 'ptrsel' (or its alias 'cuda'), got {impl!r}")
+    n_req = seq_lens.shape[0]
+    if fetch == "kernel":
+        tier.step(lidx, st.page_table, st.page_cnt, block_table, seq_lens,
+                  n_req)
+    mem_decode_ptrsel(q, kv_cache, block_table, seq_lens, st, out, tier, lidx,
+                      scale=scale)
+
+
+__all__ = ["DevPtrTensor", "MappedHostVPool", "Residency", "Staging", "Tier",
+           "host_device_pointer", "mem_decode_ptrsel", "mem_dynamic_decode"]

@@ -186,6 +186,92 @@ int amass_sparse_decode_noalloc(
     int64_t o_stride_t, int64_t o_stride_h, float scale, int n_req, int n_kv,
     int G, int head_dim, int page, int max_pages, void* stream);
 
+/* ------------------------------------------------------------------------
+ * mem-v / mem-kv DRAM tier (reference tier/pool.py, tier/residency.py,
+ * tier/decode_mem.py).  Per layer the tier keeps a VRAM hot buffer of S page
+ * slots per kv-head; V (and K under mem-kv) of every page lives in a pinned,
+ * device-mapped host pool (L, NB, n_kv, page, d) bf16, and pages not yet
+ * flushed there sit in a VRAM staging pool addressed through vbo.
+ * ------------------------------------------------------------------------ */
+
+/* Device address of pinned, mapped host memory -- replaces
+ * tier/pool.py:65-80 (host_device_pointer). */
+int amass_host_device_pointer(void* host, void** dev);
+
+/* Largest number of misses per kv-head one amass_tier_plan call lists
+ * (beyond it the misses stay non-resident and overflow is set); 0 when
+ * hot_slots is outside (0, 8192]. */
+int amass_tier_plan_capacity(int hot_slots);
+
+/* Residency plan of one layer -- replaces Residency.gather_plan
+ * tier/residency.py:385-407 (kernels :45-139).  Exact LRU:
+ *   clock[0] advances by one (clock is int32[2]; clock[1] is a CTA ticket
+ *   that must be 0 before the first call and is left 0);
+ *   hits (selected, complete, page2slot >= 0) set lru = clock;
+ *   misses, per kv-head in (request, page-table) order and deduplicated,
+ *   take the slot of smallest (lru, index) among slots with lru < clock,
+ *   evict its page and are written to fetch_list (n_kv, hot_slots, 2) as
+ *   (block, slot) with fetch_cnt[kv] entries (fetch_cnt is int32[n_kv]).
+ * A miss without an eligible slot (or beyond amass_tier_plan_capacity)
+ * stays non-resident and sets overflow[0] = 1.
+ * page2slot (n_kv, NB), slot2page / lru_clock (n_kv, hot_slots) are this
+ * layer's rows.  hot_slots <= 8192. */
+int amass_tier_plan(const int32_t* page_table, const int32_t* page_cnt,
+                    const int32_t* block_table, int64_t bt_stride,
+                    const int32_t* seq_lens, int32_t* page2slot,
+                    int32_t* slot2page, int32_t* lru_clock, int32_t* clock,
+                    int32_t* overflow, int32_t* fetch_list, int32_t* fetch_cnt,
+                    int n_req, int n_kv, int max_pages, int page,
+                    int num_blocks, int hot_slots, void* stream);
+
+/* Miss fetch -- replaces Residency.gather_fetch tier/residency.py:409-436
+ * (kernel :196-248).  For each planned (block, slot): hot[kv, slot] <- pinned
+ * pool page when pool_valid[kv, block]; else, when vbo[block] >= 0, the
+ * staging page v_pool + vbo*svb + kv*svh (token stride svt), written through
+ * to the pinned pool with pool_valid = 1; else the pinned pool page.  Bit
+ * copies of 16-bit elements.  hot (n_kv, S, page, d) of this layer; pool_dev
+ * is the device view of the whole (L, NB, n_kv, page, d) pool; pool_valid
+ * (n_kv, NB) of this layer.  hot_k / pool_k_dev / k_pool: the K tier under
+ * mem-kv (all three null under mem-v).  page = 16, head_dim in {64, 128}. */
+int amass_tier_fetch(const int32_t* fetch_list, const int32_t* fetch_cnt,
+                     void* hot, void* pool_dev, int8_t* pool_valid,
+                     const int32_t* vbo, const void* v_pool, int64_t svb,
+                     int64_t svt, int64_t svh, void* hot_k, void* pool_k_dev,
+                     const void* k_pool, int layer, int num_blocks, int n_kv,
+                     int hot_slots, int page, int head_dim, void* stream);
+
+/* Drop residency and pool validity of the pages (re)written this step in all
+ * layers -- replaces Residency.invalidate_written tier/residency.py:352-367
+ * (kernel :251-282).  query_start_loc (n_req+1,); page2slot (L, n_kv, NB),
+ * slot2page (L, n_kv, S), pool_valid (L, n_kv, NB). */
+int amass_tier_invalidate(const int32_t* block_table, int64_t bt_stride,
+                          const int32_t* seq_lens,
+                          const int32_t* query_start_loc, int32_t* page2slot,
+                          int32_t* slot2page, int8_t* pool_valid, int n_req,
+                          int num_layers, int n_kv, int num_blocks,
+                          int hot_slots, int page, void* stream);
+
+/* Tiered split-K decode (ptr-select) -- replaces mem_decode_ptrsel
+ * tier/decode_mem.py:169-222 (kernel :78-166).  As amass_sparse_decode,
+ * but per selected page the V tile (and the K tile when hot_k != NULL,
+ * mem-kv) is read from hot (complete page with page2slot >= 0), else the
+ * staging pool (vbo >= 0; stg_* at svb/svt/svh), else the pinned pool
+ * (pool_* device views).  Under mem-v (hot_k == NULL) K comes from the
+ * resident cache k at k_sb/k_st/k_sh.  Output is bitwise equal to
+ * amass_sparse_decode on the same bytes. */
+int amass_tier_decode(
+    const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k,
+    int64_t k_sb, int64_t k_st, int64_t k_sh, const void* hot_v,
+    const void* hot_k, const void* stg_v, const void* stg_k, int64_t svb,
+    int64_t svt, int64_t svh, const void* pool_v, const void* pool_k,
+    const int32_t* page2slot, const int32_t* vbo, int layer, int num_blocks,
+    int hot_slots, const int32_t* block_table, int64_t bt_stride,
+    const int32_t* page_table, const int32_t* page_cnt,
+    const int32_t* seq_lens, float* m_part, float* l_part, float* acc_part,
+    int split, int pps_min, void* out, int64_t o_stride_t, int64_t o_stride_h,
+    float scale, int n_req, int n_kv, int G, int head_dim, int page,
+    int max_pages, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -473,6 +473,29 @@ def residency_fetch(flist, *, hot, pool, pool_valid, vbo, v_pool, layer: int):
             hot[kv, slot] = pool[layer, blk, kv]
 
 
+def invalidate_written(block_table, seq_lens, query_start_loc, *, page: int,
+                       page2slot, slot2page, pool_valid):
+    """Drop residency and pool validity of every page a request (re)wrote
+    this step -- its pages (sl - ql)//page .. (sl - 1)//page -- in all layers
+    and kv-heads (``residency.py:251-282``).  page2slot/pool_valid
+    (L, n_kv, NB), slot2page (L, n_kv, S), mutated in place."""
+    L, n_kv, _ = page2slot.shape
+    for r in range(len(seq_lens)):
+        sl = int(seq_lens[r])
+        if sl <= 0:
+            continue
+        ql = int(query_start_loc[r + 1]) - int(query_start_loc[r])
+        for p in range(max((sl - ql) // page, 0), (sl - 1) // page + 1):
+            blk = int(block_table[r, p])
+            for l in range(L):
+                for kv in range(n_kv):
+                    pool_valid[l, kv, blk] = 0
+                    s = int(page2slot[l, kv, blk])
+                    if s >= 0:
+                        page2slot[l, kv, blk] = -1
+                        slot2page[l, kv, s] = -1
+
+
 def tier_decode(q, K, block_table, seq_lens, page_table, page_cnt, *, scale,
                 G, hot, page2slot, vbo, v_pool, pool, layer: int):
     """mem-v ptr-select decode (``tier/decode_mem.py:78-166``): each selected

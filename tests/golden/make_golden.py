@@ -262,6 +262,43 @@ def gen_tier(name, case, *, budget, hot_slots=10, steps=3, seed=5):
                         **rec)
 
 
+def gen_invalidate(name, *, seed=9, L=2, n_kv=2, NB=40, S=12, page=16):
+    """Residency.invalidate_written on a populated residency: random maps
+    and validity, requests that appended 1 or several tokens (chunked
+    prefill), one empty request."""
+    rng = np.random.default_rng(seed)
+    res = Residency(num_layers=L, num_blocks=NB, n_kv=n_kv, hot_slots=S,
+                    page=page, d=64, max_reqs=4, max_pages=8,
+                    dtype=torch.bfloat16, device="cpu")
+    for l in range(L):
+        for kv in range(n_kv):
+            blks = rng.choice(NB, S, replace=False)
+            for s_, b in enumerate(blks):
+                if rng.random() < 0.8:
+                    res.page2slot[l, kv, b] = s_
+                    res.slot2page[l, kv, s_] = b
+    res.pool_valid.copy_(torch.from_numpy(
+        (rng.random((L, n_kv, NB)) < 0.7).astype(np.int8)))
+    bt = torch.from_numpy(rng.permutation(NB)[:32].reshape(4, 8)
+                          .astype(np.int32))
+    sl = torch.tensor([100, 33, 0, 128], dtype=torch.int32)
+    qsl = torch.tensor([0, 1, 21, 21, 61], dtype=torch.int32)
+    p2s0 = res.page2slot.numpy().copy()
+    s2p0 = res.slot2page.numpy().copy()
+    v0 = res.pool_valid.numpy().copy()
+    res.invalidate_written(bt, sl, qsl)
+    np.savez_compressed(os.path.join(HERE, name + ".npz"),
+                        block_table=bt.numpy(), seq_lens=sl.numpy(),
+                        query_start_loc=qsl.numpy(), page=np.array([page]),
+                        page2slot_init=p2s0, slot2page_init=s2p0,
+                        pool_valid_init=v0,
+                        page2slot=res.page2slot.numpy(),
+                        slot2page=res.slot2page.numpy(),
+                        pool_valid=res.pool_valid.numpy())
+    print(name, "cleared", int((p2s0 >= 0).sum() - (res.page2slot >= 0).sum()
+                              .item()))
+
+
 def main():
     torch.manual_seed(0)
     # C1: B=2, 8 q / 2 kv heads, d=64, ctx 2048, r'=8 int8 V, budget 0.10, nrm
@@ -291,6 +328,7 @@ def main():
                        r=2, v_bits=8, heavy=3, shift=2.5)
     gen_tier("tier_lru", t, budget=0.25, hot_slots=24, steps=3)
     gen_tier("tier_overflow", t, budget=0.25, hot_slots=10, steps=1)
+    gen_invalidate("tier_invalidate")
 
 
 if __name__ == "__main__":

@@ -182,3 +182,16 @@ def test_selection_tie_band():
     cnt = np.array([[4]], np.int32)
     assert O.selection_diff_ok(tie, cnt, ref, cnt, sc)
     assert not O.selection_diff_ok(gap, cnt, ref, cnt, sc)
+
+
+def test_invalidate_written():
+    z = load_golden("tier_invalidate")
+    p2s = z["page2slot_init"].copy()
+    s2p = z["slot2page_init"].copy()
+    valid = z["pool_valid_init"].copy()
+    O.invalidate_written(z["block_table"], z["seq_lens"],
+                         z["query_start_loc"], page=int(z["page"][0]),
+                         page2slot=p2s, slot2page=s2p, pool_valid=valid)
+    assert np.array_equal(p2s, z["page2slot"])
+    assert np.array_equal(s2p, z["slot2page"])
+    assert np.array_equal(valid, z["pool_valid"])
