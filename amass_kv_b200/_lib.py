@@ -40,8 +40,8 @@ _SIGS = {
                                     _L, _F, _I, _I, _I, _I, _I, _I, _P],
     "amass_host_device_pointer": [_P, _P],
     "amass_tier_plan_capacity": [_I],
-    "amass_tier_plan": [_P, _P, _P, _L, _P, _P, _P, _P, _P, _P, _P, _P, _I,
-                        _I, _I, _I, _I, _I, _P],
+    "amass_tier_plan": [_P, _P, _P, _L, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                        _I, _I, _I, _I, _I, _I, _P],
     "amass_tier_fetch": [_P, _P, _P, _P, _P, _P, _P, _L, _L, _L, _P, _P, _P,
                          _I, _I, _I, _I, _I, _I, _P],
     "amass_tier_invalidate": [_P, _L, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I,

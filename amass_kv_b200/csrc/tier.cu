@@ -14,14 +14,21 @@
 //   slot left the miss stays non-resident and the overflow flag is set (the
 //   decode then reads that page from the staging or pinned pool).
 //
-// Parallel form.  The reference walks the misses one at a time.  Here one CTA
-// per kv-head (1) touches hits and lists its misses in order in shared
-// memory, (2) dedups them with an atomicMin claim on page2slot (the first
-// occurrence wins), (3) sorts the slots by (lru, index) with a bitonic sort,
-// ineligible slots last, and (4) gives the k-th unique miss the k-th sorted
-// slot.  This picks the same victims as the sequential walk: an install makes
-// its slot ineligible, so the k-th install of the walk takes the k-th
-// smallest eligible key, and evicted pages are never misses of the same call.
+// Parallel form.  The reference walks the misses one at a time.  Here a
+// classification kernel over the whole GPU touches the hits and marks the
+// misses entry by entry (the gathers behind it are random and would
+// serialise on one SM), then one CTA per kv-head (1) lists its misses in
+// order in shared memory (each thread reads a contiguous range of the
+// flattened (request, page-table entry) list; one block scan orders them),
+// (2) dedups them with an atomicMin claim on page2slot (the first occurrence
+// wins), (3) finds the `take` = min(unique misses, eligible slots) smallest
+// (lru, index) keys: a radix select on the lru clock gives the take-th
+// smallest value T, the fewer-than-take slots with lru < T are sorted, and
+// slots with lru == T follow in index order, and (4) gives the k-th unique
+// miss the k-th victim.  This picks the same victims as the sequential walk:
+// an install makes its slot ineligible, so the k-th install of the walk takes
+// the k-th smallest eligible key, and evicted pages are never misses of the
+// same call.
 #include <algorithm>
 
 #include "common.cuh"
@@ -32,7 +39,21 @@ namespace {
 constexpr int kPlanThreads = 1024;
 constexpr int kPlanWarps = kPlanThreads / 32;
 constexpr int kPlanMaxSlots = 8192;
+constexpr int kPlanMaxReq = 4096;
+constexpr int kPer = 4;                 // entries per thread per round
 constexpr size_t kPlanSmem = 200 * 1024;
+
+#ifdef AMASS_PLAN_PROBE
+__device__ unsigned long long g_plan_probe[64 * 16];
+#define PLAN_PROBE(k)                                                       \
+  if (threadIdx.x == 0) {                                                   \
+    unsigned long long t_;                                                  \
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                  \
+    g_plan_probe[blockIdx.x * 16 + (k)] = t_;                               \
+  }
+#else
+#define PLAN_PROBE(k)
+#endif
 
 struct PlanArgs {
   const int32_t* tab;     // (R, n_kv, MP)
@@ -47,28 +68,107 @@ struct PlanArgs {
   int32_t* overflow;      // (1,)
   int32_t* flist;         // (n_kv, S, 2): (blk, slot)
   int32_t* fcnt;          // (n_kv,)
+  int32_t* mpage;         // (R, n_kv, MP): miss block per entry, else -1
   int n_req, n_kv, MP, page, NB, S, max_miss;
 };
 
-// Ordered block-wide append of one flag per thread: returns this thread's
-// position (meaningful when flag) and advances *base by the block total.
-AMASS_DEV int block_append(bool flag, int* wcnt, int* base) {
+// Block-wide exclusive scan of one int per thread (kPlanThreads threads);
+// *total receives the block sum.  Ends with a barrier, so wtot can be reused.
+AMASS_DEV int block_scan_excl(int v, int* wtot, int* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const unsigned bal = __ballot_sync(0xffffffffu, flag);
-  if (lane == 0) wcnt[warp] = __popc(bal);
-  __syncthreads();
-  int off = *base, tot = 0;
-#pragma unroll 4
-  for (int w = 0; w < kPlanWarps; ++w) {
-    const int c = wcnt[w];
-    off += w < warp ? c : 0;
-    tot += c;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
   }
-  const int pos = off + __popc(bal & ((1u << lane) - 1u));
+  if (lane == 31) wtot[warp] = incl;
   __syncthreads();
-  if (threadIdx.x == 0) *base += tot;
+  if (warp == 0) {
+    int x = wtot[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += t;
+    }
+    wtot[lane] = x;
+  }
   __syncthreads();
-  return pos;
+  const int base = warp ? wtot[warp - 1] : 0;
+  *total = wtot[kPlanWarps - 1];
+  __syncthreads();
+  return base + incl - v;
+}
+
+// Hit/miss classification of every selected entry (reference
+// residency.py:45-82), spread over the whole GPU: the gathers it needs
+// (page table -> block table -> page2slot) are random, and one SM's L1 would
+// serialise them.  One warp per chunk of 32*kClsPer consecutive entries of a
+// (request, kv-head) unit; a hit touches its slot (lru = clock + 1), and
+// mpage[entry] = block for a miss of a complete page, else -1.
+constexpr int kClsPer = 4;
+constexpr int kClsChunk = 32 * kClsPer;
+
+__global__ void __launch_bounds__(256)
+tier_classify_kernel(PlanArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int lane = threadIdx.x & 31;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  const int chunks = (a.MP + kClsChunk - 1) / kClsChunk;
+  const int items = a.n_req * a.n_kv * chunks;
+  const int clk = a.clock[0] + 1;
+  for (int it = gw; it < items; it += nw) {
+    const int u = it / chunks, ch = it - u * chunks;
+    const int c = __ldg(a.cnt + u);
+    const int j0 = ch * kClsChunk + lane * kClsPer;
+    if (ch * kClsChunk >= c) continue;
+    const int r = u / a.n_kv, kv = u - r * a.n_kv;
+    const int sl = __ldg(a.sl + r);
+    const int32_t* tr = a.tab + (int64_t)u * a.MP;
+    const int32_t* br = a.bt + (int64_t)r * a.bt_stride;
+    int32_t* p2s = a.p2s + (int64_t)kv * a.NB;
+    int pt[kClsPer], bk[kClsPer], slot[kClsPer];
+#pragma unroll
+    for (int i = 0; i < kClsPer; ++i)
+      pt[i] = j0 + i < c ? __ldg(tr + j0 + i) : -1;
+#pragma unroll
+    for (int i = 0; i < kClsPer; ++i) {
+      const bool comp = pt[i] >= 0 && (pt[i] + 1) * a.page <= sl;
+      bk[i] = comp ? __ldg(br + pt[i]) : -1;
+    }
+#pragma unroll
+    for (int i = 0; i < kClsPer; ++i) slot[i] = bk[i] >= 0 ? p2s[bk[i]] : -1;
+#pragma unroll
+    for (int i = 0; i < kClsPer; ++i) {
+      if (j0 + i >= c) continue;
+      const bool hit = bk[i] >= 0 && slot[i] >= 0;
+      if (hit) a.lru[(int64_t)kv * a.S + slot[i]] = clk;
+      a.mpage[(int64_t)u * a.MP + j0 + i] = (bk[i] >= 0 && !hit) ? bk[i] : -1;
+    }
+  }
+}
+
+// Dynamic shared memory of the plan kernel: request offsets, the sort keys of
+// the victims older than the threshold clock, the ordered victim slots, a copy
+// of the lru clocks and the ordered miss list.
+struct PlanSmem {
+  int* reqoff;       // kPlanMaxReq + 1
+  uint64_t* keys;    // S2
+  int* victim;       // S
+  int* lru;          // S: this kv-head's lru clocks after the hit touches
+  int* mblk;         // max_miss
+};
+
+AMASS_DEV PlanSmem plan_smem(uint8_t* base, int S, int S2) {
+  PlanSmem p;
+  p.keys = reinterpret_cast<uint64_t*>(base);
+  p.reqoff = reinterpret_cast<int*>(p.keys + S2);
+  p.victim = p.reqoff + kPlanMaxReq + 1;
+  p.lru = p.victim + S;
+  p.mblk = p.lru + S;
+  return p;
 }
 
 __global__ void __launch_bounds__(kPlanThreads)
@@ -78,117 +178,248 @@ tier_plan_kernel(PlanArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   int S2 = 1;
   while (S2 < a.S) S2 <<= 1;
-  uint64_t* keys = reinterpret_cast<uint64_t*>(smem);   // S2 (lru, slot) keys
-  int* mblk = reinterpret_cast<int*>(keys + S2);        // misses, in order
-  __shared__ int wcnt[kPlanWarps];
-  __shared__ int nmiss, nuniq, neligible, dropped;
+  const PlanSmem sm = plan_smem(smem, a.S, S2);
+  __shared__ int wtot[kPlanWarps];
+  __shared__ unsigned wred[kPlanWarps], wred2[kPlanWarps], wred3[kPlanWarps];
+  __shared__ int hist[2048];
+  __shared__ int sel_bin, sel_below, nT, dropped;
+  const int tid = threadIdx.x;
   const int kv = blockIdx.x;
   const int clk = a.clock[0] + 1;
   int32_t* p2s = a.p2s + (int64_t)kv * a.NB;
   int32_t* s2p = a.s2p + (int64_t)kv * a.S;
   int32_t* lru = a.lru + (int64_t)kv * a.S;
-  if (threadIdx.x == 0) { nmiss = 0; nuniq = 0; dropped = 0; }
-  __syncthreads();
+  if (tid == 0) { dropped = 0; nT = 0; }
+  PLAN_PROBE(0);
 
-  // (1) hits touch their slot; misses of complete pages are listed in
-  //     (request, page-table) order
-  for (int r = 0; r < a.n_req; ++r) {
-    const int c = a.cnt[(int64_t)r * a.n_kv + kv];
-    const int sl = a.sl[r];
-    const int32_t* tr = a.tab + ((int64_t)r * a.n_kv + kv) * a.MP;
-    const int32_t* btr = a.bt + (int64_t)r * a.bt_stride;
-    for (int j0 = 0; j0 < c; j0 += kPlanThreads) {
-      const int j = j0 + threadIdx.x;
-      bool miss = false;
-      int blk = 0;
-      if (j < c) {
-        const int pt = tr[j];
-        if ((pt + 1) * a.page <= sl) {
-          blk = btr[pt];
-          const int slot = p2s[blk];
-          if (slot >= 0) lru[slot] = clk;
-          else miss = true;
+  // ---- request offsets of this kv-head's selected pages ------------------
+  int total;
+  {
+    const int per = (a.n_req + kPlanThreads - 1) / kPlanThreads;
+    const int r0 = tid * per, r1 = min(r0 + per, a.n_req);
+    int loc = 0;
+    for (int r = r0; r < r1; ++r) loc += a.cnt[(int64_t)r * a.n_kv + kv];
+    int run = block_scan_excl(loc, wtot, &total);
+    for (int r = r0; r < r1; ++r) {
+      sm.reqoff[r] = run;
+      run += a.cnt[(int64_t)r * a.n_kv + kv];
+    }
+    if (tid == 0) sm.reqoff[a.n_req] = total;
+    __syncthreads();
+  }
+
+  PLAN_PROBE(1);
+  // ---- (1) misses in (request, entry) order: each thread reads kPer
+  //      consecutive entries of the classified list; one block scan per
+  //      round orders the appends.  (Hits were touched by the classifier.)
+  int mtot = 0;
+  for (int base = 0; base < total; base += kPlanThreads * kPer) {
+    const int f0 = base + tid * kPer;
+    int blk[kPer];
+    int nm = 0;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) blk[i] = -1;
+    if (f0 < total) {
+      int lo = 0, hi = a.n_req - 1;          // last r with reqoff[r] <= f0
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (sm.reqoff[mid] <= f0) lo = mid; else hi = mid - 1;
+      }
+      int r = lo;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int f = f0 + i;
+        if (f < total) {
+          while (f >= sm.reqoff[r + 1]) ++r;
+          blk[i] = a.mpage[((int64_t)r * a.n_kv + kv) * a.MP + (f - sm.reqoff[r])];
+          nm += blk[i] >= 0 ? 1 : 0;
         }
       }
-      const int pos = block_append(miss, wcnt, &nmiss);
-      if (miss) {
-        if (pos < a.max_miss) mblk[pos] = blk;
-        else dropped = 1;
+    }
+    int rtot;
+    int pos = mtot + block_scan_excl(nm, wtot, &rtot);
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      if (blk[i] < 0) continue;
+      if (pos < a.max_miss) sm.mblk[pos] = blk[i];
+      else dropped = 1;
+      ++pos;
+    }
+    mtot += rtot;
+  }
+  __syncthreads();
+  const int M = min(mtot, a.max_miss);
+
+  PLAN_PROBE(2);
+  // ---- (2) dedup: the first occurrence of a block claims page2slot -------
+  for (int i = tid; i < M; i += kPlanThreads)
+    atomicMin(&p2s[sm.mblk[i]], INT_MIN + i);
+  __syncthreads();
+  const int mper = (M + kPlanThreads - 1) / kPlanThreads;
+  const int i0 = min(tid * mper, M), i1 = min(i0 + mper, M);
+  int nu = 0;
+  for (int i = i0; i < i1; ++i) {
+    const int blk = sm.mblk[i];
+    if (p2s[blk] == INT_MIN + i) ++nu;
+    else sm.mblk[i] = blk | INT_MIN;                  // duplicate
+  }
+  int U;
+  const int ubase = block_scan_excl(nu, wtot, &U);
+  PLAN_PROBE(3);
+
+  // ---- (3) victims: the `take` smallest (lru, slot) among slots with
+  //      lru < clk, in order.  Radix-select the take-th smallest lru T
+  //      (11-bit digits of lru - min), sort the fewer-than-take slots with
+  //      lru < T, then append slots with lru == T in index order. ---------
+  unsigned vmin = 0xffffffffu, vmax = 0u, ne = 0u;
+  for (int s = tid; s < a.S; s += kPlanThreads) {
+    const int l = lru[s];
+    sm.lru[s] = l;
+    if (l < clk) {
+      const unsigned u = (unsigned)l ^ 0x80000000u;
+      vmin = min(vmin, u);
+      vmax = max(vmax, u);
+      ++ne;
+    }
+  }
+  {
+    const int lane = tid & 31, warp = tid >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      vmin = min(vmin, __shfl_xor_sync(0xffffffffu, vmin, o));
+      vmax = max(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
+      ne += __shfl_xor_sync(0xffffffffu, ne, o);
+    }
+    if (lane == 0) { wred[warp] = vmin; wred2[warp] = vmax; wred3[warp] = ne; }
+    __syncthreads();
+    if (warp == 0) {
+      vmin = wred[lane]; vmax = wred2[lane]; ne = wred3[lane];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        vmin = min(vmin, __shfl_xor_sync(0xffffffffu, vmin, o));
+        vmax = max(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
+        ne += __shfl_xor_sync(0xffffffffu, ne, o);
       }
+      if (lane == 0) { wred[0] = vmin; wred2[0] = vmax; wred3[0] = ne; }
     }
+    __syncthreads();
+    vmin = wred[0]; vmax = wred2[0]; ne = wred3[0];
   }
-  __syncthreads();
-  const int M = min(nmiss, a.max_miss);
-  // (2) dedup: the first occurrence of a block claims page2slot
-  for (int i = threadIdx.x; i < M; i += kPlanThreads)
-    atomicMin(&p2s[mblk[i]], INT_MIN + i);
-  // (3) slot keys: (lru biased to unsigned, index); slots touched this call
-  //     get the top band and sort last
-  for (int s = threadIdx.x; s < S2; s += kPlanThreads) {
-    uint64_t k = ~0ull;
-    if (s < a.S) {
-      const int l = lru[s];
-      const uint32_t hi = l >= clk ? 0xffffffffu
-                                   : (uint32_t)l ^ 0x80000000u;
-      k = ((uint64_t)hi << 32) | (uint32_t)s;
-    }
-    keys[s] = k;
-  }
-  __syncthreads();
-  for (int size = 2; size <= S2; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = threadIdx.x; i < S2 / 2; i += kPlanThreads) {
-        const int lo = 2 * i - (i & (stride - 1));
-        const int hi = lo + stride;
-        const bool up = (lo & size) == 0;
-        const uint64_t x = keys[lo], y = keys[hi];
-        if ((x > y) == up) { keys[lo] = y; keys[hi] = x; }
+  const int E = (int)ne;
+  const int take = min(U, E);
+  PLAN_PROBE(4);
+  if (take > 0) {
+    const unsigned range = vmax - vmin;
+    const int nbits = range ? 32 - __clz(range) : 0;
+    unsigned prefix = 0, pmask = 0;
+    int need = take, below = 0;
+    for (int shift = nbits > 0 ? ((nbits + 10) / 11 - 1) * 11 : -1; shift >= 0;
+         shift -= 11) {
+      for (int b = tid; b < 2048; b += kPlanThreads) hist[b] = 0;
+      __syncthreads();
+      for (int s = tid; s < a.S; s += kPlanThreads) {
+        const int l = sm.lru[s];
+        const unsigned v = ((unsigned)l ^ 0x80000000u) - vmin;
+        if (l < clk && (v & pmask) == prefix)
+          atomicAdd(&hist[(v >> shift) & 2047], 1);
       }
       __syncthreads();
+      const int h0 = hist[2 * tid], h1 = hist[2 * tid + 1];
+      int tot;
+      const int ex = block_scan_excl(h0 + h1, wtot, &tot);
+      if (ex < need && need <= ex + h0) { sel_bin = 2 * tid; sel_below = ex; }
+      else if (ex + h0 < need && need <= ex + h0 + h1) {
+        sel_bin = 2 * tid + 1; sel_below = ex + h0;
+      }
+      __syncthreads();
+      prefix |= (unsigned)sel_bin << shift;
+      pmask |= 2047u << shift;
+      need -= sel_below;
+      below += sel_below;
+      __syncthreads();
     }
-  }
-  // eligible slots = keys below the top band (sorted: binary search)
-  if (threadIdx.x == 0) {
-    int lo = 0, hi = a.S;
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if ((uint32_t)(keys[mid] >> 32) != 0xffffffffu) lo = mid + 1; else hi = mid;
+  PLAN_PROBE(5);
+    const unsigned T = vmin + prefix;           // biased lru of the threshold
+    const int c = below;                        // slots with lru < T
+    // keys of the slots older than T (unordered), then sorted
+    int P2 = 1;
+    while (P2 < c) P2 <<= 1;
+    if (c > 0) {
+      if (tid == 0) nT = 0;
+      __syncthreads();
+      for (int s = tid; s < a.S; s += kPlanThreads) {
+        const int l = sm.lru[s];
+        const unsigned u = (unsigned)l ^ 0x80000000u;
+        if (l < clk && u < T) {
+          const int k = atomicAdd(&nT, 1);
+          sm.keys[k] = ((uint64_t)u << 32) | (uint32_t)s;
+        }
+      }
+      __syncthreads();
+      for (int k = c + tid; k < P2; k += kPlanThreads) sm.keys[k] = ~0ull;
+      __syncthreads();
+      for (int size = 2; size <= P2; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+          for (int i = tid; i < P2 / 2; i += kPlanThreads) {
+            const int lo = 2 * i - (i & (stride - 1));
+            const int hi = lo + stride;
+            const bool up = (lo & size) == 0;
+            const uint64_t x = sm.keys[lo], y = sm.keys[hi];
+            if ((x > y) == up) { sm.keys[lo] = y; sm.keys[hi] = x; }
+          }
+          __syncthreads();
+        }
+      }
+      for (int k = tid; k < c; k += kPlanThreads)
+        sm.victim[k] = (int)(sm.keys[k] & 0xffffffffu);
     }
-    neligible = lo;
-  }
-  __syncthreads();
-  // (4) install: the k-th unique miss takes the k-th eligible slot.  A later
-  //     duplicate of an installed block reads a slot (>= 0), not its claim.
-  const int E = neligible;
-  int32_t* fl = a.flist + (int64_t)kv * a.S * 2;
-  for (int i0 = 0; i0 < M; i0 += kPlanThreads) {
-    const int i = i0 + threadIdx.x;
-    int blk = 0;
-    bool u = false;
-    if (i < M) {
-      blk = mblk[i];
-      u = p2s[blk] == INT_MIN + i;
-    }
-    const int k = block_append(u, wcnt, &nuniq);
-    if (u) {
-      if (k >= E) {
-        p2s[blk] = -1;
-        dropped = 1;
-      } else {
-        const int slot = (int)(keys[k] & 0xffffffffu);
-        const int old = s2p[slot];
-        if (old >= 0) p2s[old] = -1;
-        p2s[blk] = slot;
-        s2p[slot] = blk;
-        lru[slot] = clk;
-        fl[2 * k] = blk;
-        fl[2 * k + 1] = slot;
+  PLAN_PROBE(6);
+    // slots with lru == T in index order fill victims [c, take): each
+    // thread scans a contiguous run of slots, one block scan orders them
+    {
+      const int sper = (a.S + kPlanThreads - 1) / kPlanThreads;
+      const int s0 = min(tid * sper, a.S), s1 = min(s0 + sper, a.S);
+      int ne2 = 0;
+      for (int s = s0; s < s1; ++s) {
+        const int l = sm.lru[s];
+        ne2 += (l < clk && ((unsigned)l ^ 0x80000000u) == T) ? 1 : 0;
+      }
+      int got;
+      int pos = c + block_scan_excl(ne2, wtot, &got);
+      for (int s = s0; s < s1 && pos < take; ++s) {
+        const int l = sm.lru[s];
+        if (l < clk && ((unsigned)l ^ 0x80000000u) == T) sm.victim[pos++] = s;
       }
     }
+    __syncthreads();
+  }
+
+  PLAN_PROBE(7);
+  // ---- (4) install: the k-th unique miss takes victim k -----------------
+  int32_t* fl = a.flist + (int64_t)kv * a.S * 2;
+  int k = ubase;
+  for (int i = i0; i < i1; ++i) {
+    const int blk = sm.mblk[i];
+    if (blk < 0) continue;                       // duplicate
+    if (k >= take) {
+      p2s[blk] = -1;
+      dropped = 1;
+    } else {
+      const int slot = sm.victim[k];
+      const int old = s2p[slot];
+      if (old >= 0) p2s[old] = -1;
+      p2s[blk] = slot;
+      s2p[slot] = blk;
+      lru[slot] = clk;
+      fl[2 * k] = blk;
+      fl[2 * k + 1] = slot;
+    }
+    ++k;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    a.fcnt[kv] = min(nuniq, E);
+  PLAN_PROBE(8);
+  if (tid == 0) {
+    a.fcnt[kv] = take;
     if (dropped) atomicExch(a.overflow, 1);
     // the last CTA to finish commits the advanced clock; every CTA read the
     // clock before taking its ticket
@@ -324,7 +555,8 @@ extern "C" int amass_tier_plan_capacity(int hot_slots) {
   if (hot_slots <= 0 || hot_slots > amass::kPlanMaxSlots) return 0;
   int S2 = 1;
   while (S2 < hot_slots) S2 <<= 1;
-  const long long room = (long long)amass::kPlanSmem - 8LL * S2;
+  const long long room = (long long)amass::kPlanSmem - 8LL * S2 -
+                         8LL * hot_slots - 4LL * (amass::kPlanMaxReq + 1);
   return room > 0 ? (int)(room / 4) : 0;
 }
 
@@ -335,21 +567,24 @@ extern "C" int amass_tier_plan(const int32_t* page_table,
                                int32_t* slot2page, int32_t* lru_clock,
                                int32_t* clock, int32_t* overflow,
                                int32_t* fetch_list, int32_t* fetch_cnt,
-                               int n_req, int n_kv, int max_pages, int page,
-                               int num_blocks, int hot_slots, void* stream) {
+                               int32_t* miss_pages, int n_req, int n_kv,
+                               int max_pages, int page, int num_blocks,
+                               int hot_slots, void* stream) {
   using namespace amass;
   if (n_req < 0 || n_kv <= 0 || max_pages <= 0 || num_blocks <= 0 ||
       hot_slots <= 0 || page <= 0)
     return AMASS_ERR_ARG;
   if (!page_table || !page_cnt || !block_table || !seq_lens || !page2slot ||
       !slot2page || !lru_clock || !clock || !overflow || !fetch_list ||
-      !fetch_cnt)
+      !fetch_cnt || !miss_pages)
     return AMASS_ERR_ARG;
-  if (hot_slots > kPlanMaxSlots) return AMASS_ERR_UNSUPPORTED;
+  if (hot_slots > kPlanMaxSlots || n_req > kPlanMaxReq)
+    return AMASS_ERR_UNSUPPORTED;
   int S2 = 1;
   while (S2 < hot_slots) S2 <<= 1;
   const int max_miss = amass_tier_plan_capacity(hot_slots);
-  const size_t smem = (size_t)S2 * 8 + (size_t)max_miss * 4;
+  const size_t smem = (size_t)S2 * 8 + (size_t)hot_slots * 8 +
+                      (size_t)(kPlanMaxReq + 1) * 4 + (size_t)max_miss * 4;
   PlanArgs a;
   a.tab = page_table; a.cnt = page_cnt; a.bt = block_table;
   a.bt_stride = bt_stride; a.sl = seq_lens; a.p2s = page2slot;
@@ -357,6 +592,16 @@ extern "C" int amass_tier_plan(const int32_t* page_table,
   a.flist = fetch_list; a.fcnt = fetch_cnt; a.n_req = n_req; a.n_kv = n_kv;
   a.MP = max_pages; a.page = page; a.NB = num_blocks; a.S = hot_slots;
   a.max_miss = max_miss;
+  a.mpage = miss_pages;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  {
+    const int chunks = (max_pages + kClsChunk - 1) / kClsChunk;
+    const long long warps = (long long)n_req * n_kv * chunks;
+    const int grid = (int)std::min<long long>((warps + 7) / 8, num_sms() * 8LL);
+    if (int rc = launch_pdl(tier_classify_kernel, dim3(grid), dim3(256), 0, st,
+                            a))
+      return rc;
+  }
   static int configured = 0;
   if (!configured) {
     cudaFuncSetAttribute(tier_plan_kernel,
@@ -365,7 +610,7 @@ extern "C" int amass_tier_plan(const int32_t* page_table,
     configured = 1;
   }
   if (int rc = launch_pdl(tier_plan_kernel, dim3(n_kv), dim3(kPlanThreads),
-                          smem, static_cast<cudaStream_t>(stream), a))
+                          smem, st, a))
     return rc;
   return launch_status();
 }

@@ -113,7 +113,7 @@ class Residency:
     mem-kv], page2slot (L, n_kv, NB), slot2page / lru_clock (L, n_kv, S),
     pool_valid (L, n_kv, NB) int8, clock int32[2] (clock, CTA ticket; starts
     at 1 like the reference), overflow (1,), and per-call scratch
-    fetch_list (n_kv, S, 2) / fetch_cnt (n_kv,)."""
+    fetch_list (n_kv, S, 2) / fetch_cnt (n_kv,) / miss_pages (R, n_kv, MP)."""
 
     def __init__(self, *, num_layers: int, num_blocks: int, n_kv: int,
                  hot_slots: int, page: int, d: int, max_reqs: int,
@@ -144,6 +144,8 @@ class Residency:
         self.fetch_list = torch.zeros((n_kv, hot_slots, 2), dtype=i32,
                                       device=dev)
         self.fetch_cnt = torch.zeros((n_kv,), dtype=i32, device=dev)
+        self.miss_pages = torch.zeros((max_reqs, n_kv, max_pages), dtype=i32,
+                                      device=dev)
         self.plan_capacity = _lib.load().amass_tier_plan_capacity(hot_slots)
         if self.plan_capacity <= 0:
             raise ValueError(f"hot_slots={hot_slots} outside (0, 8192]")
@@ -152,7 +154,7 @@ class Residency:
         self.hot_gib = hot_n * elem / 2**30
         self.maps_gib = sum(t.numel() * t.element_size() for t in (
             self.page2slot, self.slot2page, self.lru_clock, self.pool_valid,
-            self.fetch_list, self.fetch_cnt)) / 2**30
+            self.fetch_list, self.fetch_cnt, self.miss_pages)) / 2**30
 
     # -- per step ------------------------------------------------------------
     def invalidate_written(self, block_table, seq_lens, query_start_loc) -> None:
@@ -171,11 +173,17 @@ class Residency:
         by one); the installed misses land in fetch_list/fetch_cnt
         (reference residency.py:385-407)."""
         l = int(layer)
+        if page_table.shape[-1] > self.MP or n_req > self.R:
+            raise ValueError(f"selection ({n_req} requests x "
+                             f"{page_table.shape[-1]} pages) exceeds the "
+                             f"residency's max_reqs={self.R} / "
+                             f"max_pages={self.MP}")
         _lib.call("amass_tier_plan", ptr(page_table), ptr(page_cnt),
                   ptr(block_table), block_table.stride(0), ptr(seq_lens),
                   ptr(self.page2slot[l]), ptr(self.slot2page[l]),
                   ptr(self.lru_clock[l]), ptr(self.clock), ptr(self.overflow),
-                  ptr(self.fetch_list), ptr(self.fetch_cnt), int(n_req),
+                  ptr(self.fetch_list), ptr(self.fetch_cnt),
+                  ptr(self.miss_pages), int(n_req),
                   self.n_kv, int(page_table.shape[-1]), self.page, self.NB,
                   self.S, _lib.stream_of(self.device))
 

@@ -488,6 +488,177 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------- #
+# C5: mem-v tiered decode (V in the pinned host pool, exact-LRU hot buffer)  #
+# --------------------------------------------------------------------------- #
+C5_REQ, C5_KV, C5_G = 16, 8, 8
+
+
+def run_c5(args):
+    """BASELINE C5: Llama-3.1-70B attention (64 q / 8 kv heads, d 128), B=16,
+    contexts uniform on [32K, 128K], V of every page in the pinned mapped host
+    pool, K and summaries in HBM, hot buffer of 10% of the pages per kv-head
+    (capped at 8192 slots), budget 0.05, q rotating slowly so the selection
+    drifts.  A step = derive + quad score + select + residency plan + miss
+    fetch + ptr-select decode + merge for one layer; it is timed stage by
+    stage (CUDA graphs, events between them) after `--warmup` steps that
+    bring the hot buffer to its steady hit rate."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    from amass_kv_b200 import attention as A
+    from amass_kv_b200 import selection as S
+    from amass_kv_b200 import tier as T
+    from amass_kv_b200.attention import ensure_stage_b_buffers
+    from amass_kv_b200.selection import QuadState
+    from amass_kv_b200.workloads import make_quad_case_gpu
+    rng = np.random.default_rng(5000 + rank)
+    ctxs = rng.integers(32768, 131072 + 1, C5_REQ)
+    b = make_quad_case_gpu(dev, seed=5000 + rank, ctxs=ctxs, n_kv=C5_KV,
+                           G=C5_G, d=D, page=PAGE, r=RANK_Q, v_bits=V_BITS,
+                           layers=1)
+    NB, MP = b["NB"], b["MP"]
+    kv, bt, sl = b["kv_cache"][0], b["block_table"], b["seq_lens"]
+    st = QuadState(dev, num_layers=1, num_blocks=1, n_kv=C5_KV, G=C5_G,
+                   head_dim=D, page=PAGE, max_reqs=C5_REQ, max_pages=MP,
+                   rank=RANK_Q, budget=BUDGET, v_bits=V_BITS, combine=COMBINE)
+    st.quad_mu, st.mu_scale = b["quad_mu"], b["mu_scale"]
+    st.quad_V, st.V_scale, st.quad_sig2 = (b["quad_V"], b["V_scale"],
+                                           b["quad_sig2"])
+    ensure_stage_b_buffers(st, dev, 128)
+    hot_slots = min(8192, max(1, int(round(0.10 * NB))))
+    n_vslots = 2 * C5_REQ
+    tier = T.Tier(num_layers=1, num_blocks=NB, n_kv=C5_KV, page=PAGE, d=D,
+                  hot_slots=hot_slots, max_reqs=C5_REQ, max_pages=MP,
+                  n_vslots=n_vslots, device=dev)
+    # every page flushed to the pinned pool; the resident V half stays only
+    # for the resident-decode comparison
+    vt = kv[:, 1].permute(0, 2, 1, 3).contiguous()
+    tier.pool.host[0].copy_(vt.cpu())
+    del vt
+    tier.residency.pool_valid.fill_(1)
+    kv_k_only = kv[:, :1]                     # K-only (nb, 1, page, kv, d)
+    scale = 1.0 / math.sqrt(D)
+    q0 = b["q"][0].float()
+    q1 = torch.randn_like(q0)
+    qbuf = torch.empty_like(b["q"][0])
+    out = torch.empty_like(qbuf)
+    out_res = torch.empty_like(qbuf)
+
+    def set_q(i):
+        th = 0.02 * i
+        qbuf.copy_((q0 * math.cos(th) + q1 * math.sin(th)).to(torch.bfloat16))
+
+    r5 = tier.residency
+
+    def stage(k):
+        if k == 0:
+            S.derive_page_params(st, sl, C5_REQ)
+            S._score_launch(st, 0, qbuf, bt, C5_REQ, scale, COMBINE == "nrm")
+            S.select_pages(st, C5_REQ, from_score_h=COMBINE == "nrm")
+        elif k == 1:
+            r5.gather_plan(0, st.page_table, st.page_cnt, bt, sl, C5_REQ)
+        elif k == 2:
+            r5.gather_fetch(0, tier.staging, tier.pool.dev_view)
+        elif k == 3:
+            T.mem_decode_ptrsel(qbuf, kv_k_only, bt, sl, st, out, tier, 0,
+                                scale=scale)
+        else:
+            A.sparse_paged_decode_batched_cuda(qbuf, kv, bt, sl, st, out_res,
+                                               scale=scale)
+
+    NS = 5
+    set_q(0)
+    for k in range(NS):                  # eager first use (attributes)
+        stage(k)
+    torch.cuda.synchronize()
+    graphs = []
+    for k in range(NS):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            stage(k)
+        graphs.append(g)
+    torch.cuda.synchronize()
+    page_bytes = PAGE * D * 2
+    warm = max(args.warmup, 10)
+    for i in range(1, warm + 1):
+        set_q(i)
+        for g in graphs[:4]:
+            g.replay()
+    torch.cuda.synchronize()
+    steps = max(args.steps, 20) if args.steps else 20
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(NS + 1)]
+          for _ in range(steps)]
+    misses, selected, equal = [], [], True
+    with ClockSampler(local) as clk:
+        for i in range(steps):
+            set_q(warm + 1 + i)
+            ev[i][0].record()
+            for k in range(NS):
+                graphs[k].replay()
+                ev[i][k + 1].record()
+            torch.cuda.synchronize()
+            misses.append(int(r5.fetch_cnt.sum()))
+            cnt = st.page_cnt.cpu().numpy()
+            selected.append(int(cnt.sum()))
+            equal = equal and bool(torch.equal(out, out_res))
+    t = np.array([[e[k].elapsed_time(e[k + 1]) for k in range(NS)]
+                  for e in ev]) * 1e3                          # us
+    t_sel, t_plan, t_fetch, t_dec, t_res = t.mean(0)
+    tier_step = t_sel + t_plan + t_fetch + t_dec
+    miss_b = np.array(misses) * page_bytes
+    link = float(miss_b.sum() / (t[:, 2].sum() * 1e-6) / 1e9) \
+        if miss_b.sum() else 0.0
+    if world > 1:
+        x = torch.tensor([tier_step], device=dev)
+        dist.all_reduce(x, op=dist.ReduceOp.MAX)
+        tier_step = float(x.item())
+    n_pages_tot = NB
+    kb = n_pages_tot * C5_KV * page_bytes
+    summ = n_pages_tot * C5_KV * B_SUM
+    hot_b = C5_KV * hot_slots * page_bytes
+    stg_b = n_vslots * C5_KV * page_bytes
+    saved = 1.0 - (kb + summ + hot_b + stg_b) / (2 * kb + summ)
+    if rank == 0:
+        hbm, kind = _peaks()
+        line = {
+            "metric": "mem-v tiered sparse decode us/layer/step (C5)",
+            "value": round(float(tier_step), 2), "unit": UNIT,
+            "n_gpus": world, "steps": steps, "warmup": warm,
+            "higher_is_better": False, "scaling": "weak", "dtype": "bf16",
+            "data": "synthetic (seeded; BASELINE C5 shapes)",
+            "config": {"workload": "C5: B=16, ctx U(32K,128K) (realized mean "
+                       f"{float(np.mean(ctxs)):.0f}), Llama-3.1-70B attn "
+                       "(64q/8kv, d128), V in pinned host pool, hot = 10% of "
+                       f"pages ({hot_slots} slots/kv-head), budget 0.05, "
+                       "quad r'=2 int4-V nrm, q rotating 0.02 rad/step",
+                       "NB": NB},
+            "stage_us": {"derive+score+select": round(float(t_sel), 2),
+                         "residency_plan": round(float(t_plan), 2),
+                         "miss_fetch": round(float(t_fetch), 2),
+                         "tiered_decode+merge": round(float(t_dec), 2),
+                         "resident_decode+merge": round(float(t_res), 2)},
+            "hit_rate": round(1.0 - float(np.sum(misses)) /
+                              max(1, float(np.sum(selected))), 4),
+            "miss_pages_per_step": round(float(np.mean(misses)), 1),
+            "selected_pages_per_step": round(float(np.mean(selected)), 1),
+            "host_link_gbs": round(link, 2),
+            "vram_saved_frac": round(saved, 4),
+            "tiered_equals_resident": equal,
+            "hbm_peak_gbs": hbm, "peak_kind": kind,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -500,6 +671,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--pps-min", type=int, default=None,
                     help="decode pages-per-chunk floor (default: by batch)")
+    ap.add_argument("--workload", default="c3", choices=["c3", "c5"],
+                    help="c3 = the headline resident decode (default); c5 = "
+                         "the mem-v tiered decode")
     ap.add_argument("--requests", type=int, default=N_REQ,
                     help="batch size per GPU (64 = BASELINE C3; smaller only "
                          "for profiling captures)")
@@ -508,6 +682,8 @@ def main():
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "c5":
+        run_c5(args)
     else:
         run_gpu(args)
 

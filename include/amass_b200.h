@@ -215,14 +215,17 @@ int amass_tier_plan_capacity(int hot_slots);
  * A miss without an eligible slot (or beyond amass_tier_plan_capacity)
  * stays non-resident and sets overflow[0] = 1.
  * page2slot (n_kv, NB), slot2page / lru_clock (n_kv, hot_slots) are this
- * layer's rows.  hot_slots <= 8192. */
+ * layer's rows.  miss_pages (n_req, n_kv, max_pages) int32 is scratch (the
+ * classified entries: the block of a miss, else -1).  Two launches: the
+ * classification over the whole GPU, then one CTA per kv-head.
+ * hot_slots <= 8192, n_req <= 4096. */
 int amass_tier_plan(const int32_t* page_table, const int32_t* page_cnt,
                     const int32_t* block_table, int64_t bt_stride,
                     const int32_t* seq_lens, int32_t* page2slot,
                     int32_t* slot2page, int32_t* lru_clock, int32_t* clock,
                     int32_t* overflow, int32_t* fetch_list, int32_t* fetch_cnt,
-                    int n_req, int n_kv, int max_pages, int page,
-                    int num_blocks, int hot_slots, void* stream);
+                    int32_t* miss_pages, int n_req, int n_kv, int max_pages,
+                    int page, int num_blocks, int hot_slots, void* stream);
 
 /* Miss fetch -- replaces Residency.gather_fetch tier/residency.py:409-436
  * (kernel :196-248).  For each planned (block, slot): hot[kv, slot] <- pinned
