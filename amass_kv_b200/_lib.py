@@ -47,7 +47,7 @@ _SIGS = {
     "amass_tier_invalidate": [_P, _L, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I,
                               _I, _P],
     "amass_tier_decode": [_P, _L, _L, _P, _L, _L, _L, _P, _P, _P, _P, _L, _L,
-                          _L, _P, _P, _P, _P, _I, _I, _I, _P, _L, _P, _P, _P,
+                          _L, _P, _P, _P, _P, _P, _I, _I, _I, _P, _L, _P, _P, _P,
                           _P, _P, _P, _I, _I, _P, _L, _L, _F, _I, _I, _I, _I,
                           _I, _I, _P],
 }

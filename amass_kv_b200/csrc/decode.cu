@@ -62,6 +62,7 @@ struct DecArgs {
   int64_t svb, svt, svh;
   const int32_t* p2s;           // (n_kv, NB) this layer
   const int32_t* vbo;           // (NB,)
+  const int32_t* eslot;         // (R, n_kv, MP) classified entries or null
   int t_layer, t_NB, t_S;
 };
 
@@ -172,6 +173,8 @@ decode_kernel(DecArgs a) {
       const int u = cu.unit;
       const int r = u / a.n_kv, kv = u - r * a.n_kv;
       const int pt = a.tab[(int64_t)u * a.MP + cu.j];
+      // hot slot of a classified hit (-(slot + 2)), loaded beside pt
+      const int ev = (TIER && a.eslot) ? a.eslot[(int64_t)u * a.MP + cu.j] : -1;
       const int64_t blk = a.bt[(int64_t)r * a.bt_stride + pt];
       const int seq = a.sl[r];
       const int valid = min(16, seq - pt * 16);
@@ -183,9 +186,9 @@ decode_kernel(DecArgs a) {
       if constexpr (TIER) {
         // one source decision per page, on the address (same bytes, so the
         // math matches the resident decode bit for bit)
-        const int hslot = a.p2s[(int64_t)kv * a.t_NB + blk];
-        const int vb = a.vbo[blk];
-        const bool use_hot = (pt + 1) * 16 <= seq && hslot >= 0;
+        const int hslot = ev <= -2 ? -ev - 2 : a.p2s[(int64_t)kv * a.t_NB + blk];
+        const bool use_hot = ev <= -2 || ((pt + 1) * 16 <= seq && hslot >= 0);
+        const int vb = use_hot ? -1 : a.vbo[blk];
         int64_t off;
         const __nv_bfloat16 *hv, *hk;
         if (use_hot) {
@@ -515,7 +518,7 @@ extern "C" int amass_sparse_decode(
   a.units = n_req * n_kv;
   a.hot_v = a.hot_k = a.stg_v = a.stg_k = a.pool_v = a.pool_k = nullptr;
   a.svb = a.svt = a.svh = 0;
-  a.p2s = a.vbo = nullptr;
+  a.p2s = a.vbo = a.eslot = nullptr;
   a.t_layer = a.t_NB = a.t_S = 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (head_dim == 128) return launch_decode<128, 2, false>(a, st);
@@ -528,9 +531,9 @@ extern "C" int amass_tier_decode(
     int64_t k_sb, int64_t k_st, int64_t k_sh, const void* hot_v,
     const void* hot_k, const void* stg_v, const void* stg_k, int64_t svb,
     int64_t svt, int64_t svh, const void* pool_v, const void* pool_k,
-    const int32_t* page2slot, const int32_t* vbo, int layer, int num_blocks,
-    int hot_slots, const int32_t* block_table, int64_t bt_stride,
-    const int32_t* page_table, const int32_t* page_cnt,
+    const int32_t* page2slot, const int32_t* vbo, const int32_t* entry_slots,
+    int layer, int num_blocks, int hot_slots, const int32_t* block_table,
+    int64_t bt_stride, const int32_t* page_table, const int32_t* page_cnt,
     const int32_t* seq_lens, float* m_part, float* l_part, float* acc_part,
     int split, int pps_min, void* out, int64_t o_stride_t, int64_t o_stride_h,
     float scale, int n_req, int n_kv, int G, int head_dim, int page,
@@ -583,7 +586,7 @@ extern "C" int amass_tier_decode(
   a.pool_v = static_cast<const __nv_bfloat16*>(pool_v);
   a.pool_k = static_cast<const __nv_bfloat16*>(pool_k);
   a.svb = svb; a.svt = svt; a.svh = svh;
-  a.p2s = page2slot; a.vbo = vbo;
+  a.p2s = page2slot; a.vbo = vbo; a.eslot = entry_slots;
   a.t_layer = layer; a.t_NB = num_blocks; a.t_S = hot_slots;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (head_dim == 128) return launch_decode<128, 2, true>(a, st);

@@ -68,7 +68,7 @@ struct PlanArgs {
   int32_t* overflow;      // (1,)
   int32_t* flist;         // (n_kv, S, 2): (blk, slot)
   int32_t* fcnt;          // (n_kv,)
-  int32_t* mpage;         // (R, n_kv, MP): miss block per entry, else -1
+  int32_t* mpage;         // (R, n_kv, MP): miss block | -(hit slot + 2) | -1
   int n_req, n_kv, MP, page, NB, S, max_miss;
 };
 
@@ -104,8 +104,10 @@ AMASS_DEV int block_scan_excl(int v, int* wtot, int* total) {
 // residency.py:45-82), spread over the whole GPU: the gathers it needs
 // (page table -> block table -> page2slot) are random, and one SM's L1 would
 // serialise them.  One warp per chunk of 32*kClsPer consecutive entries of a
-// (request, kv-head) unit; a hit touches its slot (lru = clock + 1), and
-// mpage[entry] = block for a miss of a complete page, else -1.
+// (request, kv-head) unit; a hit touches its slot (lru = clock + 1).
+// mpage[entry] = block (>= 0) for a miss of a complete page, -(slot + 2) for
+// a hit (its slot cannot be evicted by this call: it now holds the newest
+// clock), -1 for a page that is not complete.
 constexpr int kClsPer = 4;
 constexpr int kClsChunk = 32 * kClsPer;
 
@@ -145,7 +147,8 @@ tier_classify_kernel(PlanArgs a) {
       if (j0 + i >= c) continue;
       const bool hit = bk[i] >= 0 && slot[i] >= 0;
       if (hit) a.lru[(int64_t)kv * a.S + slot[i]] = clk;
-      a.mpage[(int64_t)u * a.MP + j0 + i] = (bk[i] >= 0 && !hit) ? bk[i] : -1;
+      a.mpage[(int64_t)u * a.MP + j0 + i] =
+          hit ? -(slot[i] + 2) : (bk[i] >= 0 ? bk[i] : -1);
     }
   }
 }
@@ -232,7 +235,7 @@ tier_plan_kernel(PlanArgs a) {
         if (f < total) {
           while (f >= sm.reqoff[r + 1]) ++r;
           blk[i] = a.mpage[((int64_t)r * a.n_kv + kv) * a.MP + (f - sm.reqoff[r])];
-          nm += blk[i] >= 0 ? 1 : 0;
+          if (blk[i] >= 0) ++nm; else blk[i] = -1;
         }
       }
     }

@@ -294,11 +294,14 @@ class Tier:
 
 
 def mem_decode_ptrsel(q, kv_cache, block_table, seq_lens, st, out, tier,
-                      lidx: int, *, scale=None, pps_min=None) -> None:
+                      lidx: int, *, scale=None, pps_min=None,
+                      entry_slots=None) -> None:
     """ptr-select tiered split-K decode + merge into ``out[:n_req]`` (bf16):
     per page V (and K under mem-kv) from hot | staging | pinned
     (reference tier/decode_mem.py:169-222).  Bitwise equal to the resident
-    decode on the same bytes."""
+    decode on the same bytes.  ``entry_slots``: the residency's
+    ``miss_pages`` right after its plan for this same selection (hits then
+    skip the page2slot lookup), else None."""
     if scale is None:
         # the state's softmax scale, else 1/sqrt(head_dim)
         scale = getattr(st, "scale", None) or q.shape[-1] ** -0.5
@@ -326,7 +329,8 @@ def mem_decode_ptrsel(q, kv_cache, block_table, seq_lens, st, out, tier,
               ptr(r5.hot[l]), ptr(r5.hot_k[l]) if tier.offload_k else 0,
               ptr(vp), ptr(stg_k), vp.stride(0), vp.stride(1), vp.stride(2),
               tier.pool.dev_view.data_ptr(), pool_k,
-              ptr(r5.page2slot[l]), ptr(stg.vbo), l, r5.NB, r5.S,
+              ptr(r5.page2slot[l]), ptr(stg.vbo), ptr(entry_slots), l, r5.NB,
+              r5.S,
               ptr(block_table), block_table.stride(0), ptr(st.page_table),
               ptr(st.page_cnt), ptr(seq_lens), ptr(st.m_part), ptr(st.l_part),
               ptr(st.acc_part), int(st.split), int(pps_min), ptr(out),
@@ -349,11 +353,14 @@ def mem_dynamic_decode(q, kv_cache, block_table, seq_lens, st, out, tier,
     if impl not in ("ptrsel", "cuda"):
         raise ValueError(f"impl must be 'ptrsel' (or its alias 'cuda'), got {impl!r}")
     n_req = seq_lens.shape[0]
+    es = None
     if fetch == "kernel":
         tier.step(lidx, st.page_table, st.page_cnt, block_table, seq_lens,
                   n_req)
+        if st.page_table.shape[-1] == tier.residency.MP:
+            es = tier.residency.miss_pages
     mem_decode_ptrsel(q, kv_cache, block_table, seq_lens, st, out, tier, lidx,
-                      scale=scale)
+                      scale=scale, entry_slots=es)
 
 
 __all__ = ["DevPtrTensor", "MappedHostVPool", "Residency", "Staging", "Tier",

@@ -568,7 +568,7 @@ def run_c5(args):
             r5.gather_fetch(0, tier.staging, tier.pool.dev_view)
         elif k == 3:
             T.mem_decode_ptrsel(qbuf, kv_k_only, bt, sl, st, out, tier, 0,
-                                scale=scale)
+                                scale=scale, entry_slots=r5.miss_pages)
         else:
             A.sparse_paged_decode_batched_cuda(qbuf, kv, bt, sl, st, out_res,
                                                scale=scale)

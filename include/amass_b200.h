@@ -215,8 +215,9 @@ int amass_tier_plan_capacity(int hot_slots);
  * A miss without an eligible slot (or beyond amass_tier_plan_capacity)
  * stays non-resident and sets overflow[0] = 1.
  * page2slot (n_kv, NB), slot2page / lru_clock (n_kv, hot_slots) are this
- * layer's rows.  miss_pages (n_req, n_kv, max_pages) int32 is scratch (the
- * classified entries: the block of a miss, else -1).  Two launches: the
+ * layer's rows.  miss_pages (n_req, n_kv, max_pages) int32 receives the
+ * classified entries: the block of a miss (>= 0), -(slot + 2) for a hit, -1
+ * for a page that is not complete.  Two launches: the
  * classification over the whole GPU, then one CTA per kv-head.
  * hot_slots <= 8192, n_req <= 4096. */
 int amass_tier_plan(const int32_t* page_table, const int32_t* page_cnt,
@@ -260,16 +261,20 @@ int amass_tier_invalidate(const int32_t* block_table, int64_t bt_stride,
  * mem-kv) is read from hot (complete page with page2slot >= 0), else the
  * staging pool (vbo >= 0; stg_* at svb/svt/svh), else the pinned pool
  * (pool_* device views).  Under mem-v (hot_k == NULL) K comes from the
- * resident cache k at k_sb/k_st/k_sh.  Output is bitwise equal to
- * amass_sparse_decode on the same bytes. */
+ * resident cache k at k_sb/k_st/k_sh.  entry_slots: NULL, or the
+ * miss_pages of the amass_tier_plan call made for this same page_table on
+ * this layer (entries that were hits carry their hot slot there, which
+ * saves the page2slot lookup); with any other array the result is
+ * undefined.  Output is bitwise equal to amass_sparse_decode on the same
+ * bytes. */
 int amass_tier_decode(
     const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k,
     int64_t k_sb, int64_t k_st, int64_t k_sh, const void* hot_v,
     const void* hot_k, const void* stg_v, const void* stg_k, int64_t svb,
     int64_t svt, int64_t svh, const void* pool_v, const void* pool_k,
-    const int32_t* page2slot, const int32_t* vbo, int layer, int num_blocks,
-    int hot_slots, const int32_t* block_table, int64_t bt_stride,
-    const int32_t* page_table, const int32_t* page_cnt,
+    const int32_t* page2slot, const int32_t* vbo, const int32_t* entry_slots,
+    int layer, int num_blocks, int hot_slots, const int32_t* block_table,
+    int64_t bt_stride, const int32_t* page_table, const int32_t* page_cnt,
     const int32_t* seq_lens, float* m_part, float* l_part, float* acc_part,
     int split, int pps_min, void* out, int64_t o_stride_t, int64_t o_stride_h,
     float scale, int n_req, int n_kv, int G, int head_dim, int page,

@@ -215,7 +215,12 @@ def test_tier_random_vs_oracle(seed, n_req, n_kv, G, d, S, mem_kv, inval, dev):
         res = torch.zeros_like(out)
         A.sparse_paged_decode_batched_cuda(q, kv_true, bt, sl, st, res,
                                            scale=d ** -0.5)
+        # the same decode without the plan's entry slots (page2slot lookups)
+        out2 = torch.zeros_like(out)
+        T.mem_decode_ptrsel(q, kv_dev, bt, sl, st, out2, tier, layer,
+                            scale=d ** -0.5)
         torch.cuda.synchronize()
+        assert torch.equal(out, out2), s
         clock += 1
         fl, ovf = O.residency_step(tab, cnt, c["bt"], c["ctx"], page=page,
                                    page2slot=o_p2s[layer], slot2page=o_s2p[layer],
