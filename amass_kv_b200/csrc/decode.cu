@@ -27,6 +27,7 @@ namespace amass {
 namespace {
 
 constexpr int kDecWarps = 4;
+constexpr int kMaxPeers = 8;
 constexpr int kDecThreads = kDecWarps * 32;
 
 struct DecArgs {
@@ -64,6 +65,11 @@ struct DecArgs {
   const int32_t* vbo;           // (NB,)
   const int32_t* eslot;         // (R, n_kv, MP) classified entries or null
   int t_layer, t_NB, t_S;
+  // merged rows go to n_out buffers (this GPU's `out` alone, or every
+  // rank's output under kv-head sharding: peer addresses over NVLink), at
+  // global head head_off + local head
+  __nv_bfloat16* outs[kMaxPeers];
+  int n_out, head_off;
 };
 
 AMASS_DEV int unit_pps(int cnt, int split, int pps_min) {
@@ -434,11 +440,18 @@ merge_kernel(DecArgs a) {
     }
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
-  __nv_bfloat16* op = a.out + (int64_t)r * a.o_st + (int64_t)h * a.o_sh + lane * PER;
+  uint32_t w[PER / 2];
 #pragma unroll
-  for (int i = 0; i < PER; i += 2) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(acc[i] * inv, acc[i + 1] * inv);
-    *reinterpret_cast<__nv_bfloat162*>(op + i) = v;
+  for (int i = 0; i < PER; i += 2) w[i / 2] = pack_bf2(acc[i] * inv, acc[i + 1] * inv);
+  const int64_t off = (int64_t)r * a.o_st + (int64_t)(a.head_off + h) * a.o_sh + lane * PER;
+  for (int p = 0; p < a.n_out; ++p) {
+    __nv_bfloat16* op = a.outs[p] + off;
+    if constexpr (PER == 4) {
+      *reinterpret_cast<uint2*>(op) = make_uint2(w[0], w[1]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < PER / 2; ++i) reinterpret_cast<uint32_t*>(op)[i] = w[i];
+    }
   }
 }
 
@@ -476,16 +489,27 @@ int launch_decode(const DecArgs& a, cudaStream_t st) {
 }  // namespace
 }  // namespace amass
 
-extern "C" int amass_sparse_decode(
+namespace amass {
+namespace {
+
+// Resident decode into n_out output buffers (outs[0] = out for the plain
+// call); rows of this call's heads land at global head head_off + h.
+int resident_decode(
     const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k,
     int64_t k_sb, int64_t k_st, int64_t k_sh, const void* v, int64_t v_sb,
     int64_t v_st, int64_t v_sh, const int32_t* block_table, int64_t bt_stride,
     const int32_t* page_table, const int32_t* page_cnt,
     const int32_t* seq_lens, float* m_part, float* l_part, float* acc_part,
-    int split, int pps_min, void* out, int64_t o_stride_t, int64_t o_stride_h,
-    float scale, int n_req, int n_kv, int G, int head_dim, int page,
-    int max_pages, void* stream) {
-  using namespace amass;
+    int split, int pps_min, void* const* outs, int n_out, int head_off,
+    int64_t o_stride_t, int64_t o_stride_h, float scale, int n_req, int n_kv,
+    int G, int head_dim, int page, int max_pages, void* stream) {
+  void* out = n_out > 0 ? outs[0] : nullptr;
+  if (n_out < 1 || n_out > kMaxPeers || head_off < 0) return AMASS_ERR_ARG;
+  for (int p = 0; p < n_out; ++p)
+    if (!outs[p] || (head_dim == 128 && (reinterpret_cast<uintptr_t>(outs[p]) & 7)))
+      return AMASS_ERR_ARG;
+  if (head_dim == 128 && ((o_stride_t % 4) || (o_stride_h % 4)))
+    return AMASS_ERR_ARG;
   if (n_req < 0 || n_kv <= 0 || G <= 0 || split <= 0 || pps_min <= 0 ||
       max_pages <= 0)
     return AMASS_ERR_ARG;
@@ -512,6 +536,8 @@ extern "C" int amass_sparse_decode(
   a.m_part = m_part; a.l_part = l_part; a.acc_part = acc_part;
   a.out = static_cast<__nv_bfloat16*>(out);
   a.o_st = o_stride_t; a.o_sh = o_stride_h;
+  for (int p = 0; p < n_out; ++p) a.outs[p] = static_cast<__nv_bfloat16*>(outs[p]);
+  a.n_out = n_out; a.head_off = head_off;
   a.scale_log2 = scale * kLog2e;
   a.split = split; a.pps_min = pps_min;
   a.n_req = n_req; a.n_kv = n_kv; a.G = G; a.MP = max_pages;
@@ -524,6 +550,44 @@ extern "C" int amass_sparse_decode(
   if (head_dim == 128) return launch_decode<128, 2, false>(a, st);
   if (head_dim == 64) return launch_decode<64, 3, false>(a, st);
   return AMASS_ERR_UNSUPPORTED;
+}
+
+}  // namespace
+}  // namespace amass
+
+extern "C" int amass_sparse_decode(
+    const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k,
+    int64_t k_sb, int64_t k_st, int64_t k_sh, const void* v, int64_t v_sb,
+    int64_t v_st, int64_t v_sh, const int32_t* block_table, int64_t bt_stride,
+    const int32_t* page_table, const int32_t* page_cnt,
+    const int32_t* seq_lens, float* m_part, float* l_part, float* acc_part,
+    int split, int pps_min, void* out, int64_t o_stride_t, int64_t o_stride_h,
+    float scale, int n_req, int n_kv, int G, int head_dim, int page,
+    int max_pages, void* stream) {
+  void* outs[1] = {out};
+  return amass::resident_decode(
+      q, q_stride_t, q_stride_h, k, k_sb, k_st, k_sh, v, v_sb, v_st, v_sh,
+      block_table, bt_stride, page_table, page_cnt, seq_lens, m_part, l_part,
+      acc_part, split, pps_min, outs, 1, 0, o_stride_t, o_stride_h, scale,
+      n_req, n_kv, G, head_dim, page, max_pages, stream);
+}
+
+extern "C" int amass_sparse_decode_gather(
+    const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k,
+    int64_t k_sb, int64_t k_st, int64_t k_sh, const void* v, int64_t v_sb,
+    int64_t v_st, int64_t v_sh, const int32_t* block_table, int64_t bt_stride,
+    const int32_t* page_table, const int32_t* page_cnt,
+    const int32_t* seq_lens, float* m_part, float* l_part, float* acc_part,
+    int split, int pps_min, void* const* out_peers, int n_peers,
+    int head_offset, int64_t o_stride_t, int64_t o_stride_h, float scale,
+    int n_req, int n_kv, int G, int head_dim, int page, int max_pages,
+    void* stream) {
+  if (!out_peers) return AMASS_ERR_ARG;
+  return amass::resident_decode(
+      q, q_stride_t, q_stride_h, k, k_sb, k_st, k_sh, v, v_sb, v_st, v_sh,
+      block_table, bt_stride, page_table, page_cnt, seq_lens, m_part, l_part,
+      acc_part, split, pps_min, out_peers, n_peers, head_offset, o_stride_t,
+      o_stride_h, scale, n_req, n_kv, G, head_dim, page, max_pages, stream);
 }
 
 extern "C" int amass_tier_decode(
@@ -575,6 +639,10 @@ extern "C" int amass_tier_decode(
   a.m_part = m_part; a.l_part = l_part; a.acc_part = acc_part;
   a.out = static_cast<__nv_bfloat16*>(out);
   a.o_st = o_stride_t; a.o_sh = o_stride_h;
+  a.outs[0] = a.out; a.n_out = 1; a.head_off = 0;
+  if (head_dim == 128 && ((o_stride_t % 4) || (o_stride_h % 4) ||
+                          (reinterpret_cast<uintptr_t>(out) & 7)))
+    return AMASS_ERR_ARG;
   a.scale_log2 = scale * kLog2e;
   a.split = split; a.pps_min = pps_min;
   a.n_req = n_req; a.n_kv = n_kv; a.G = G; a.MP = max_pages;

@@ -121,19 +121,21 @@ class ClockSampler:
 # the hot path over one layer (public API)                                    #
 # --------------------------------------------------------------------------- #
 class Batch:
-    def __init__(self, dev, seed, layers):
+    def __init__(self, dev, seed, layers, n_kv=None, gather=None):
         import torch
         from amass_kv_b200.attention import ensure_stage_b_buffers
         from amass_kv_b200.selection import QuadState
         from amass_kv_b200.workloads import c3_contexts, make_quad_case_gpu
+        n_kv = n_kv or N_KV
+        self.n_kv, self.gather = n_kv, gather
         self.ctxs = c3_contexts(seed, N_REQ)
-        b = make_quad_case_gpu(dev, seed=seed, ctxs=self.ctxs, n_kv=N_KV, G=G,
+        b = make_quad_case_gpu(dev, seed=seed, ctxs=self.ctxs, n_kv=n_kv, G=G,
                                d=D, page=PAGE, r=RANK_Q, v_bits=V_BITS,
                                layers=layers)
         self.kv, self.q = b["kv_cache"], b["q"]
         self.bt, self.sl = b["block_table"], b["seq_lens"]
         self.MP, self.NB, self.layers = b["MP"], b["NB"], layers
-        st = QuadState(dev, num_layers=1, num_blocks=1, n_kv=N_KV, G=G,
+        st = QuadState(dev, num_layers=1, num_blocks=1, n_kv=n_kv, G=G,
                        head_dim=D, page=PAGE, max_reqs=N_REQ, max_pages=self.MP,
                        rank=RANK_Q, budget=BUDGET, v_bits=V_BITS,
                        combine=COMBINE)
@@ -144,7 +146,7 @@ class Batch:
         ensure_stage_b_buffers(st, dev, 128)
         self.st = st
         self.scale = 1.0 / math.sqrt(D)
-        self.out = torch.empty(N_REQ, N_KV * G, D, dtype=torch.bfloat16,
+        self.out = torch.empty(N_REQ, n_kv * G, D, dtype=torch.bfloat16,
                                device=dev)
         # derive, q-limbs, score, select, decode, merge
         self.launches_per_step = 6
@@ -163,6 +165,11 @@ class Batch:
             S._score_launch(st, l, q, self.bt, N_REQ, self.scale, nrm)
         elif k == 1:
             S.select_pages(st, N_REQ, from_score_h=nrm)
+        elif self.gather is not None:
+            from amass_kv_b200 import sharding as SH
+            self.out_full = SH.sparse_paged_decode_kvsharded(
+                q, self.kv[l], self.bt, self.sl, st, self.gather,
+                scale=self.scale, pps_min=self.pps_min)
         else:
             A.sparse_paged_decode_batched_cuda(q, self.kv[l], self.bt, self.sl,
                                                st, self.out, scale=self.scale,
@@ -180,8 +187,8 @@ class Batch:
         torch.cuda.synchronize()
         nsh = np.maximum(self.st.n_sel_hi.cpu().numpy().astype(np.int64), 0)
         cnt = self.st.page_cnt.cpu().numpy().astype(np.int64)
-        qo = N_REQ * N_KV * G * D * 2
-        score_b = int((N_KV * nsh * B_SUM + 4 * nsh).sum()) + qo // 2
+        qo = N_REQ * self.n_kv * G * D * 2
+        score_b = int((self.n_kv * nsh * B_SUM + 4 * nsh).sum()) + qo // 2
         kv_b = int(cnt.sum()) * 2 * PAGE * D * 2
         decode_b = kv_b + qo
         return dict(score=score_b, decode=decode_b,
@@ -201,7 +208,16 @@ def run_gpu(args):
         dist.init_process_group("nccl", device_id=dev)
     from amass_kv_b200 import _lib
     _lib.load()
-    batch = Batch(dev, seed=1000 + rank, layers=args.layers)
+    kvmode = args.shard == "kv"
+    if kvmode:
+        from amass_kv_b200 import sharding as SH
+        gather = SH.HeadGather(N_REQ, N_KV * G, D, device=dev,
+                               mode=args.gather)
+        # every rank holds the same requests and its N_KV/world kv heads
+        batch = Batch(dev, seed=1000, layers=args.layers,
+                      n_kv=N_KV // world, gather=gather)
+    else:
+        batch = Batch(dev, seed=1000 + rank, layers=args.layers)
     batch.pps_min = args.pps_min
     L = args.layers
     alg = [batch.algorithmic_bytes(l) for l in range(L)]
@@ -285,8 +301,8 @@ def run_gpu(args):
                      pin_memory=True)
     qh.copy_(batch.q.cpu())
     slh = batch.sl.cpu().pin_memory()
-    outh = torch.empty(tuple(batch.out.shape), dtype=torch.bfloat16,
-                       pin_memory=True)
+    out_shape = (N_REQ, N_KV * G, D) if kvmode else tuple(batch.out.shape)
+    outh = torch.empty(out_shape, dtype=torch.bfloat16, pin_memory=True)
     qd = torch.empty_like(batch.q[0])
     h2d = qd.numel() * 2 + slh.numel() * 4
     d2h = outh.numel() * 2
@@ -294,7 +310,7 @@ def run_gpu(args):
         qd.copy_(qh[i % L], non_blocking=True)
         batch.sl.copy_(slh, non_blocking=True)
         batch.step(i % L, q=qd)
-        outh.copy_(batch.out, non_blocking=True)
+        outh.copy_(batch.out_full if kvmode else batch.out, non_blocking=True)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -305,7 +321,7 @@ def run_gpu(args):
         qd.copy_(qh[i % L], non_blocking=True)
         batch.sl.copy_(slh, non_blocking=True)
         batch.step(i % L, q=qd)
-        outh.copy_(batch.out, non_blocking=True)
+        outh.copy_(batch.out_full if kvmode else batch.out, non_blocking=True)
     x1.record()
     torch.cuda.synchronize()
     e2e_ms = x0.elapsed_time(x1)
@@ -336,16 +352,21 @@ def run_gpu(args):
             "metric": METRIC, "value": round(ms_step * 1e3, 2), "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms_step, 5), "higher_is_better": False,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "strong" if kvmode else "weak", "vs_baseline": None,
+            "dtype": "bf16",
             "data": "synthetic (seeded; BASELINE C3 shapes)",
             "config": {
                 "workload": "C3: ragged B=64 decode, ctx log-uniform 4K-64K "
                             f"(realized mean {alg[0]['mean_ctx']:.0f}), "
                             "Llama-3.1-8B attn (32q/8kv, d128, bf16, page 16),"
                             " quad r'=2 int4-V nrm, budget 0.05",
-                "batch_per_gpu": N_REQ, "requests_per_step": N_REQ * world,
-                "parallelism": f"sequence-sharded x{world}" if world > 1
-                else "single GPU",
+                "batch_per_gpu": N_REQ,
+                "requests_per_step": N_REQ if kvmode else N_REQ * world,
+                "parallelism": (f"kv-head-sharded x{world} ({N_KV // world} kv "
+                                f"heads/GPU, {args.gather} output gather)"
+                                if kvmode else
+                                f"sequence-sharded x{world}" if world > 1
+                                else "single GPU"),
                 "l2": f"inputs larger than L2: {L} layer slabs rotated "
                       f"(~{a_total / 1e6:.0f} MB algorithmic bytes each)",
                 "cuda_graph": not args.no_graph,
@@ -671,6 +692,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--pps-min", type=int, default=None,
                     help="decode pages-per-chunk floor (default: by batch)")
+    ap.add_argument("--shard", default="seq", choices=["seq", "kv"],
+                    help="multi-GPU layout: seq = each rank its own batch "
+                         "(weak scaling, no collective); kv = one batch, kv "
+                         "heads split across ranks + output gather")
+    ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
+                    help="kv mode output exchange: merge kernel stores to "
+                         "every rank over NVLink, or NCCL all-gather")
     ap.add_argument("--workload", default="c3", choices=["c3", "c5"],
                     help="c3 = the headline resident decode (default); c5 = "
                          "the mem-v tiered decode")

@@ -186,6 +186,38 @@ int amass_sparse_decode_noalloc(
     int64_t o_stride_t, int64_t o_stride_h, float scale, int n_req, int n_kv,
     int G, int head_dim, int page, int max_pages, void* stream);
 
+/* KV-head-sharded decode with the all-gather fused into the merge.  As
+ * amass_sparse_decode over this rank's kv heads (q, k, v, page_table,
+ * page_cnt and the partials hold n_kv local heads), but every merged output
+ * row is stored into each of the n_peers buffers out_peers[0..n_peers)
+ * (this GPU's and the peers' output tensors, mapped into this GPU's address
+ * space, all (T, H, d) with strides o_stride_t / o_stride_h) at global head
+ * head_offset + local head.  n_peers <= 8.  The stores are plain peer
+ * stores over NVLink; the caller orders them before any reader with a
+ * cross-GPU barrier after the call.  Replaces the reference's decode
+ * (attention/decode_cuda.py:1376-1465) followed by the all-gather of a
+ * head-sharded attention output. */
+int amass_sparse_decode_gather(
+    const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k,
+    int64_t k_sb, int64_t k_st, int64_t k_sh, const void* v, int64_t v_sb,
+    int64_t v_st, int64_t v_sh, const int32_t* block_table, int64_t bt_stride,
+    const int32_t* page_table, const int32_t* page_cnt,
+    const int32_t* seq_lens, float* m_part, float* l_part, float* acc_part,
+    int split, int pps_min, void* const* out_peers, int n_peers,
+    int head_offset, int64_t o_stride_t, int64_t o_stride_h, float scale,
+    int n_req, int n_kv, int G, int head_dim, int page, int max_pages,
+    void* stream);
+
+/* Cross-GPU barrier for amass_sparse_decode_gather: peer_flags[i] is rank
+ * i's int32[n_ranks] flag array mapped into this GPU (zeroed once before the
+ * first call); epoch is this rank's int32 call counter (device, zeroed
+ * once).  Makes the stream's earlier peer stores visible, signals every
+ * rank, and waits (bounded, about a second) until every rank has signalled
+ * this call; on timeout err[0] becomes 1 + the missing rank and the kernel
+ * returns.  One launch; CUDA-graph capturable.  n_ranks <= 8. */
+int amass_peer_barrier(int32_t* const* peer_flags, int n_ranks, int rank,
+                       int32_t* epoch, int32_t* err, void* stream);
+
 /* ------------------------------------------------------------------------
  * mem-v / mem-kv DRAM tier (reference tier/pool.py, tier/residency.py,
  * tier/decode_mem.py).  Per layer the tier keeps a VRAM hot buffer of S page
