@@ -221,6 +221,11 @@ def run_gpu(args):
     batch.pps_min = args.pps_min
     L = args.layers
     alg = [batch.algorithmic_bytes(l) for l in range(L)]
+    # NCCL in a captured graph: the process group's watchdog thread keeps
+    # querying events while this thread captures, which the default global
+    # capture mode forbids
+    cap_mode = "thread_local" if (kvmode and args.gather == "nccl") \
+        else "global"
 
     # ---- CUDA-graph the per-layer step (the serving configuration) --------
     graphs = []
@@ -234,7 +239,7 @@ def run_gpu(args):
     if not args.no_graph:
         for l in range(L):
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
+            with torch.cuda.graph(g, capture_error_mode=cap_mode):
                 batch.step(l)
             graphs.append(g)
         torch.cuda.synchronize()
@@ -275,7 +280,7 @@ def run_gpu(args):
         gs = []
         for k in range(3):
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
+            with torch.cuda.graph(g, capture_error_mode=cap_mode):
                 batch.stage(l, k)
             gs.append(g)
         stage_graphs.append(gs)
