@@ -260,3 +260,166 @@ def make_quad_case_gpu(device, *, seed, ctxs, n_kv=8, G=4, d=128, page=16,
                 seq_lens=torch.as_tensor(np.asarray(ctxs), dtype=torch.int32,
                                          device=dev),
                 NB=NB, MP=MP, **st)
+
+
+def _quant_t(x, dim, bits):
+    """torch twin of ``quantize``: symmetric codes along ``dim`` (int or
+    tuple), scale = max(amax / lvl, 1e-8)."""
+    import torch
+    lvl = float((1 << (bits - 1)) - 1)
+    amax = x.abs().amax(dim=dim, keepdim=True)
+    s = torch.clamp(amax / lvl, min=1e-8)
+    code = torch.clamp(torch.round(x / s), -lvl, lvl).to(torch.int8)
+    return code, s
+
+
+def _pack_int4_t(code):
+    import torch
+    c = code.to(torch.int32) & 0xF
+    return (c[..., 0::2] | (c[..., 1::2] << 4)).to(torch.uint8).view(torch.int8)
+
+
+def make_planted_gpu(device, *, seed, ctxs, n_kv=8, G=4, d=128, page=16,
+                     heavy_frac=0.05, shift=None, target_mass=None,
+                     outlier_frac=0.0, outlier_mult=8.0, r_quad=2, v_bits=4,
+                     r8=8, c_bits=8, slack=64, chunk=2048):
+    """Decode batch with planted heavy pages and BOTH summary kinds, built on
+    the GPU from the actual keys (one layer).
+
+    K, V ~ N(0, 1) bf16 in the (NB, 2, page, n_kv, d) cache; optionally a
+    seeded ``outlier_frac`` of each head's channels scaled by
+    ``outlier_mult``.  ``heavy_frac`` of each (request, kv-head)'s selectable
+    pages get ``shift * q_hat`` added to their keys (q_hat = the unit mean of
+    the head group's queries); with ``target_mass`` the shift is found by
+    bisection so the planted tokens carry that share of the exact softmax
+    mass (mean over query heads).  Quad summaries: page mean and the top
+    ``r_quad`` principal directions of the page's centred keys (eigen-
+    decomposition of the 16 x 16 token Gram matrix) with their eigenvalues
+    as sigma^2.  r8 summaries: a seeded per-head orthonormal rank-``r8``
+    basis, the page's centred coordinates in it quantised with one scale per
+    (block, head)."""
+    import torch
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    npg = [(int(c) + page - 1) // page for c in ctxs]
+    NB = sum(npg) + slack
+    MP = max(npg)
+    perm = torch.randperm(NB, generator=g).to(torch.int32)
+    bt = torch.zeros(len(ctxs), MP, dtype=torch.int32)
+    o = 0
+    for i, n in enumerate(npg):
+        bt[i, :n] = perm[o:o + n]
+        o += n
+    dev = torch.device(device)
+    gd = torch.Generator(device=dev).manual_seed(seed + 1)
+    H = n_kv * G
+    q = torch.randn((len(ctxs), H, d), generator=gd, device=dev)
+    q = q.to(torch.bfloat16).float()
+    K = torch.randn((NB, page, n_kv, d), generator=gd, device=dev)
+    if outlier_frac > 0:
+        n_out = max(1, int(round(outlier_frac * d)))
+        for kv in range(n_kv):
+            ch = torch.randperm(d, generator=g)[:n_out].to(dev)
+            K[:, :, kv, ch] *= outlier_mult
+    V = torch.randn((NB, page, n_kv, d), generator=gd, device=dev)
+    # planted pages (sink page 0 and the window/tail excluded)
+    btd = bt.to(dev)
+    planted = torch.zeros((len(ctxs), n_kv, MP), dtype=torch.bool, device=dev)
+    heavy_blk, heavy_kv, heavy_dir = [], [], []
+    qhat = q.view(len(ctxs), n_kv, G, d).mean(2)
+    qhat = qhat / qhat.norm(dim=-1, keepdim=True).clamp_min(1e-12)
+    for i, n in enumerate(npg):
+        nsel = n - 2
+        nh = int(round(heavy_frac * nsel))
+        if nh < 1:
+            continue
+        for kv in range(n_kv):
+            pages = 1 + torch.randperm(nsel, generator=g)[:nh]
+            planted[i, kv, pages.to(dev)] = True
+            heavy_blk.append(bt[i, pages].to(dev).long())
+            heavy_kv.append(torch.full((nh,), kv, device=dev, dtype=torch.long))
+            heavy_dir.append(qhat[i, kv].expand(nh, d))
+    K0 = K
+    if heavy_blk:
+        hb, hk, hd = (torch.cat(heavy_blk), torch.cat(heavy_kv),
+                      torch.cat(heavy_dir))
+
+        def apply(a):
+            Kx = K0.clone()
+            Kx[hb, :, hk, :] += a * hd[:, None, :]
+            return Kx.to(torch.bfloat16).float()
+
+        def mass(Kx):
+            tot = 0.0
+            for i, n in enumerate(npg):
+                blks = btd[i, :n].long()
+                Ki = Kx[blks].reshape(n * page, n_kv, d)[:int(ctxs[i])]
+                lg = torch.einsum("kgd,tkd->kgt", q[i].view(n_kv, G, d),
+                                  Ki) / math.sqrt(d)
+                p = torch.softmax(lg, dim=-1)
+                pm = planted[i, :, :n].repeat_interleave(page, dim=1)
+                pm = pm[:, :int(ctxs[i])]
+                tot += float((p * pm[:, None, :]).sum(-1).mean())
+            return tot / len(npg)
+
+        if target_mass is not None:
+            lo, hi = 0.0, 64.0
+            for _ in range(24):
+                mid = 0.5 * (lo + hi)
+                if mass(apply(mid)) < target_mass:
+                    lo = mid
+                else:
+                    hi = mid
+            shift = 0.5 * (lo + hi)
+        K = apply(float(shift or 0.0))
+    else:
+        K = K.to(torch.bfloat16).float()
+    V = V.to(torch.bfloat16).float()
+    realized = mass(K) if heavy_blk else 0.0
+    kv_cache = torch.stack([K, V], dim=1).to(torch.bfloat16).contiguous()
+    # ---- summaries, chunk by chunk of blocks ----------------------------
+    rv = r_quad // 2 if v_bits == 4 else r_quad
+    quad_mu = torch.empty((NB, n_kv, d), dtype=torch.int8, device=dev)
+    mu_scale = torch.empty((NB, n_kv), dtype=torch.float16, device=dev)
+    quad_V = torch.empty((NB, n_kv, d, rv), dtype=torch.int8, device=dev)
+    V_scale = torch.empty((NB, n_kv, r_quad), dtype=torch.float16, device=dev)
+    quad_sig2 = torch.empty((NB, n_kv, r_quad), dtype=torch.float16, device=dev)
+    basis = torch.linalg.qr(torch.randn((n_kv, d, r8), generator=gd,
+                                        device=dev))[0]          # (kv, d, r8)
+    r8_Vk = torch.empty((NB, n_kv, d, r8), dtype=torch.int8, device=dev)
+    Vk_scale = torch.empty((NB, n_kv, r8), dtype=torch.float16, device=dev)
+    r8_c = torch.empty((NB, n_kv, page, r8), dtype=torch.int8, device=dev)
+    c_scale = torch.empty((NB, n_kv, page), dtype=torch.float16, device=dev)
+    vk_code, vk_s = _quant_t(basis, -2, 8)                       # per column
+    r8_Vk[:] = vk_code[None]
+    Vk_scale[:] = vk_s[:, 0, :][None].half()
+    for b0 in range(0, NB, chunk):
+        Kc = kv_cache[b0:b0 + chunk, 0].float()                  # (b, t, kv, d)
+        mu = Kc.mean(1)                                          # (b, kv, d)
+        code, s = _quant_t(mu, -1, 8)
+        quad_mu[b0:b0 + chunk] = code
+        mu_scale[b0:b0 + chunk] = s[..., 0].half()
+        X = (Kc - mu[:, None]).permute(0, 2, 1, 3)               # (b, kv, t, d)
+        gram = X @ X.transpose(-1, -2)                           # (b, kv, t, t)
+        ev, U = torch.linalg.eigh(gram.double())
+        ev = ev.flip(-1)[..., :r_quad].clamp_min(0).float()
+        U = U.flip(-1)[..., :r_quad].float()                     # (b, kv, t, r)
+        Vdir = X.transpose(-1, -2) @ U                           # (b, kv, d, r)
+        Vdir = Vdir / Vdir.norm(dim=-2, keepdim=True).clamp_min(1e-12)
+        vc, vs = _quant_t(Vdir, -2, v_bits)
+        quad_V[b0:b0 + chunk] = _pack_int4_t(vc) if v_bits == 4 else vc
+        V_scale[b0:b0 + chunk] = vs[:, :, 0, :].half()
+        quad_sig2[b0:b0 + chunk] = ev.half()
+        coords = torch.einsum("bktd,kdr->bktr", X, basis)
+        cc, cs = _quant_t(coords, (-2, -1), c_bits)
+        r8_c[b0:b0 + chunk] = cc
+        c_scale[b0:b0 + chunk] = cs[..., 0, 0][..., None].expand(-1, -1, page).half()
+    return dict(kv_cache=kv_cache, q=q.to(torch.bfloat16), block_table=btd,
+                seq_lens=torch.as_tensor(np.asarray(ctxs), dtype=torch.int32,
+                                         device=dev),
+                NB=NB, MP=MP, planted=planted, shift=float(shift or 0.0),
+                planted_mass=realized,
+                quad_mu=quad_mu[None], mu_scale=mu_scale[None],
+                quad_V=quad_V[None], V_scale=V_scale[None],
+                quad_sig2=quad_sig2[None], r8_mu=quad_mu[None],
+                r8_Vk=r8_Vk[None], Vk_scale=Vk_scale[None], r8_c=r8_c[None],
+                c_scale=c_scale[None])

@@ -685,6 +685,174 @@ def run_c5(args):
         dist.destroy_process_group()
 
 
+# --------------------------------------------------------------------------- #
+# C2 (B=1 coverage) and C4 (r8 scorer + Jaccard vs quad): secondary lines     #
+# --------------------------------------------------------------------------- #
+def run_select_workload(args):
+    """C2: Llama-3.1-8B geometry, batch 1, context 32768, 2% outlier
+    channels x8, 5% planted pages carrying 90% of the exact softmax mass,
+    quad r'=2 int4-V nrm summaries built from the keys, per-head coverage
+    0.95.  C4: batch 32, context 65536, r8 scorer (per-head rank-8 basis,
+    int8 coordinates with one scale per (block, head), token-max page
+    score), coverage 0.95, and the quad selection of the same inputs for the
+    Jaccard overlap.  A step = derive + score + coverage select + decode +
+    merge of one layer, CUDA-graph replayed; per-stage graphs give the
+    split."""
+    import torch
+    from amass_kv_b200 import attention as A
+    from amass_kv_b200 import selection as S
+    from amass_kv_b200.attention import ensure_stage_b_buffers
+    from amass_kv_b200.selection import QuadState, R8State
+    from amass_kv_b200.workloads import make_planted_gpu
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    c4 = args.workload == "c4"
+    ctxs = [65536] * 32 if c4 else [32768]
+    b = make_planted_gpu(dev, seed=2024 + (4 if c4 else 2), ctxs=ctxs,
+                         n_kv=N_KV, G=G, d=D, page=PAGE, heavy_frac=0.05,
+                         target_mass=0.9, outlier_frac=0.0 if c4 else 0.02,
+                         r_quad=RANK_Q, v_bits=V_BITS, r8=8, c_bits=8)
+    n_req, MP = len(ctxs), b["MP"]
+    kv, q, bt, sl = b["kv_cache"], b["q"], b["block_table"], b["seq_lens"]
+    scale = 1.0 / math.sqrt(D)
+    cov = 0.95
+    stq = QuadState(dev, num_layers=1, num_blocks=1, n_kv=N_KV, G=G,
+                    head_dim=D, page=PAGE, max_reqs=n_req, max_pages=MP,
+                    rank=RANK_Q, budget=BUDGET, v_bits=V_BITS, combine=COMBINE,
+                    coverage=cov)
+    stq.quad_mu, stq.mu_scale = b["quad_mu"], b["mu_scale"]
+    stq.quad_V, stq.V_scale, stq.quad_sig2 = (b["quad_V"], b["V_scale"],
+                                              b["quad_sig2"])
+    ensure_stage_b_buffers(stq, dev, 128)
+    out = torch.empty_like(q)
+    st = stq
+    if c4:
+        st8 = R8State(dev, num_layers=1, num_blocks=1, n_kv=N_KV, G=G,
+                      head_dim=D, page=PAGE, max_reqs=n_req, max_pages=MP,
+                      rank=8, budget=BUDGET, coverage=cov, vk_bits=8, c_bits=8,
+                      c_grain="tensor")
+        st8.r8_mu, st8.mu_scale = b["r8_mu"], b["mu_scale"]
+        st8.r8_Vk, st8.Vk_scale = b["r8_Vk"], b["Vk_scale"]
+        st8.r8_c, st8.c_scale = b["r8_c"], b["c_scale"]
+        ensure_stage_b_buffers(st8, dev, 128)
+        st = st8
+
+    def stage(k, which=None):
+        s_ = which or st
+        if k == 0:
+            S.derive_page_params(s_, sl, n_req)
+            if s_ is stq:
+                S._score_launch(s_, 0, q, bt, n_req, scale, COMBINE == "nrm")
+            else:
+                S.r8_score_cuda(s_, 0, q, bt, sl, n_req, scale,
+                                token_agg="tokmax")
+        elif k == 1:
+            S.select_pages(s_, n_req, coverage=cov,
+                           from_score_h=(s_ is stq and COMBINE == "nrm"))
+        else:
+            A.sparse_paged_decode_batched_cuda(q, kv, bt, sl, s_, out,
+                                               scale=scale)
+
+    for k in range(3):
+        stage(k)
+    torch.cuda.synchronize()
+    full = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(full):
+        for k in range(3):
+            stage(k)
+    parts = []
+    for k in range(3):
+        g_ = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_):
+            stage(k)
+        parts.append(g_)
+    torch.cuda.synchronize()
+    steps, warm = args.steps, max(args.warmup, 3)
+    for _ in range(warm):
+        full.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(
+        enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record()
+        for _ in range(steps):
+            full.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    us_step = e0.elapsed_time(e1) / steps * 1e3
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)]
+          for _ in range(steps)]
+    for i in range(steps):
+        ev[i][0].record()
+        for k in range(3):
+            parts[k].replay()
+            ev[i][k + 1].record()
+    torch.cuda.synchronize()
+    t = np.array([[e[k].elapsed_time(e[k + 1]) for k in range(3)]
+                  for e in ev]).mean(0) * 1e3
+    cnt = st.page_cnt.cpu().numpy().astype(np.int64)
+    nsh = np.maximum(st.n_sel_hi.cpu().numpy().astype(np.int64), 0)
+    b_sum = (D + 2 + D * 8 + 16 + PAGE * 8 + 2 * PAGE) if c4 else B_SUM
+    alg = int((N_KV * nsh * b_sum + 4 * nsh).sum()) + int(cnt.sum()) * 2 * \
+        PAGE * D * 2 + n_req * N_KV * G * D * 4
+    hbm, kind = _peaks()
+    line = {
+        "metric": ("r8 scorer + coverage sparse decode us/layer/step (C4)"
+                   if c4 else "coverage sparse decode us/layer/step (C2)"),
+        "value": round(us_step, 2), "unit": UNIT, "n_gpus": 1,
+        "steps": steps, "warmup": warm, "higher_is_better": False,
+        "dtype": "bf16", "data": "synthetic (seeded; BASELINE C4 shapes)"
+        if c4 else "synthetic (seeded; BASELINE C2 shapes)",
+        "config": {"workload": (
+            "C4: B=32, ctx 65536, Llama-3.1-8B attn, r8 (rank 8 per-head "
+            "basis, int8 coords, one scale per (block, head), token-max), "
+            "coverage 0.95" if c4 else
+            "C2: B=1, ctx 32768, Llama-3.1-8B attn, 2% outlier channels x8, "
+            "quad r'=2 int4-V nrm from the keys, coverage 0.95"),
+            "planted_heavy_frac": 0.05,
+            "planted_mass": round(b["planted_mass"], 4)},
+        "stage_us": {"derive+score": round(float(t[0]), 2),
+                     "coverage_select": round(float(t[1]), 2),
+                     "sparse_decode+merge": round(float(t[2]), 2)},
+        "selected_pages_per_step": int(cnt.sum()),
+        "mean_pages_per_unit": round(float(cnt.mean()), 1),
+        "step_roofline": {"bound": "hbm", "alg_bytes": alg,
+                          "achieved": round(alg / (us_step * 1e-6) / 1e9, 1),
+                          "peak": hbm, "unit": "GB/s",
+                          "frac": round(alg / (us_step * 1e-6) / 1e9 / hbm, 4),
+                          "peak_kind": kind},
+        "clocks": clk.summary(),
+    }
+    # planted recall: share of planted (request, kv, page) kept
+    tab = st.page_table.cpu().numpy()
+    planted = b["planted"].cpu().numpy()
+    hit = tot = 0
+    for r in range(n_req):
+        for k in range(N_KV):
+            sel = set(tab[r, k, :cnt[r, k]].tolist())
+            pp = np.nonzero(planted[r, k])[0]
+            tot += len(pp)
+            hit += sum(1 for p in pp if p in sel)
+    line["planted_recall"] = round(hit / max(tot, 1), 4)
+    if c4:
+        # quad selection of the same inputs (coverage 0.95) vs r8's
+        for k in range(2):
+            stage(k, stq)
+        torch.cuda.synchronize()
+        tq = stq.page_table.cpu().numpy()
+        cq = stq.page_cnt.cpu().numpy()
+        jac = []
+        for r in range(n_req):
+            for k in range(N_KV):
+                a_ = set(tab[r, k, :cnt[r, k]].tolist())
+                b_ = set(tq[r, k, :cq[r, k]].tolist())
+                jac.append(len(a_ & b_) / max(len(a_ | b_), 1))
+        line["jaccard_r8_vs_quad"] = round(float(np.mean(jac)), 4)
+        line["quad_selected_pages"] = int(cq.sum())
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -704,9 +872,11 @@ def main():
     ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
                     help="kv mode output exchange: merge kernel stores to "
                          "every rank over NVLink, or NCCL all-gather")
-    ap.add_argument("--workload", default="c3", choices=["c3", "c5"],
-                    help="c3 = the headline resident decode (default); c5 = "
-                         "the mem-v tiered decode")
+    ap.add_argument("--workload", default="c3",
+                    choices=["c3", "c2", "c4", "c5"],
+                    help="c3 = the headline resident decode (default); c2 = "
+                         "batch-1 coverage; c4 = r8 scorer + Jaccard vs quad; "
+                         "c5 = the mem-v tiered decode")
     ap.add_argument("--requests", type=int, default=N_REQ,
                     help="batch size per GPU (64 = BASELINE C3; smaller only "
                          "for profiling captures)")
@@ -717,6 +887,8 @@ def main():
         run_reference(args)
     elif args.workload == "c5":
         run_c5(args)
+    elif args.workload in ("c2", "c4"):
+        run_select_workload(args)
     else:
         run_gpu(args)
 
