@@ -544,24 +544,25 @@ def run_c5(args):
     from amass_kv_b200.attention import ensure_stage_b_buffers
     from amass_kv_b200.selection import QuadState
     from amass_kv_b200.workloads import make_quad_case_gpu
+    n5 = args.batch or C5_REQ
     rng = np.random.default_rng(5000 + rank)
-    ctxs = rng.integers(32768, 131072 + 1, C5_REQ)
+    ctxs = rng.integers(32768, 131072 + 1, n5)
     b = make_quad_case_gpu(dev, seed=5000 + rank, ctxs=ctxs, n_kv=C5_KV,
                            G=C5_G, d=D, page=PAGE, r=RANK_Q, v_bits=V_BITS,
                            layers=1)
     NB, MP = b["NB"], b["MP"]
     kv, bt, sl = b["kv_cache"][0], b["block_table"], b["seq_lens"]
     st = QuadState(dev, num_layers=1, num_blocks=1, n_kv=C5_KV, G=C5_G,
-                   head_dim=D, page=PAGE, max_reqs=C5_REQ, max_pages=MP,
+                   head_dim=D, page=PAGE, max_reqs=n5, max_pages=MP,
                    rank=RANK_Q, budget=BUDGET, v_bits=V_BITS, combine=COMBINE)
     st.quad_mu, st.mu_scale = b["quad_mu"], b["mu_scale"]
     st.quad_V, st.V_scale, st.quad_sig2 = (b["quad_V"], b["V_scale"],
                                            b["quad_sig2"])
     ensure_stage_b_buffers(st, dev, 128)
     hot_slots = min(8192, max(1, int(round(0.10 * NB))))
-    n_vslots = 2 * C5_REQ
+    n_vslots = 2 * n5
     tier = T.Tier(num_layers=1, num_blocks=NB, n_kv=C5_KV, page=PAGE, d=D,
-                  hot_slots=hot_slots, max_reqs=C5_REQ, max_pages=MP,
+                  hot_slots=hot_slots, max_reqs=n5, max_pages=MP,
                   n_vslots=n_vslots, device=dev)
     # every page flushed to the pinned pool; the resident V half stays only
     # for the resident-decode comparison
@@ -585,11 +586,11 @@ def run_c5(args):
 
     def stage(k):
         if k == 0:
-            S.derive_page_params(st, sl, C5_REQ)
-            S._score_launch(st, 0, qbuf, bt, C5_REQ, scale, COMBINE == "nrm")
-            S.select_pages(st, C5_REQ, from_score_h=COMBINE == "nrm")
+            S.derive_page_params(st, sl, n5)
+            S._score_launch(st, 0, qbuf, bt, n5, scale, COMBINE == "nrm")
+            S.select_pages(st, n5, from_score_h=COMBINE == "nrm")
         elif k == 1:
-            r5.gather_plan(0, st.page_table, st.page_cnt, bt, sl, C5_REQ)
+            r5.gather_plan(0, st.page_table, st.page_cnt, bt, sl, n5)
         elif k == 2:
             r5.gather_fetch(0, tier.staging, tier.pool.dev_view)
         elif k == 3:
@@ -708,7 +709,7 @@ def run_select_workload(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     c4 = args.workload == "c4"
-    ctxs = [65536] * 32 if c4 else [32768]
+    ctxs = [65536] * (args.batch or 32) if c4 else [32768] * (args.batch or 1)
     b = make_planted_gpu(dev, seed=2024 + (4 if c4 else 2), ctxs=ctxs,
                          n_kv=N_KV, G=G, d=D, page=PAGE, heavy_frac=0.05,
                          target_mass=0.9, outlier_frac=0.0 if c4 else 0.02,
@@ -877,6 +878,9 @@ def main():
                     help="c3 = the headline resident decode (default); c2 = "
                          "batch-1 coverage; c4 = r8 scorer + Jaccard vs quad; "
                          "c5 = the mem-v tiered decode")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="batch size of the c2/c4/c5 workloads (default: the "
+                         "config's; smaller only for profiling captures)")
     ap.add_argument("--requests", type=int, default=N_REQ,
                     help="batch size per GPU (64 = BASELINE C3; smaller only "
                          "for profiling captures)")
