@@ -143,6 +143,12 @@ AMASS_DEV void ldsm_x4(uint32_t* r, uint32_t saddr) {
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(saddr));
 }
+// transpose of the 8x8 b16 matrix held as one fragment register per lane
+AMASS_DEV uint32_t movmatrix_t(uint32_t x) {
+  uint32_t r;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(r) : "r"(x));
+  return r;
+}
 AMASS_DEV void ldsm_x4_t(uint32_t* r, uint32_t saddr) {
   asm volatile(
       "ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"

@@ -13,9 +13,11 @@
 // copies into an XOR-swizzled [token][d] tile, zero-filled beyond seq_len) and
 // the ring runs across item boundaries.
 //
-// Per page a warp computes S = Q K^T (m16n8k16 bf16 MMAs: rows = the G query
-// heads of the group, cols = 16 tokens), an online softmax in the log2
-// domain, and O += P V (P in bf16, V via ldmatrix.trans).  At the end of an
+// Per page a warp computes the transposed products: S^T = K Q^T
+// (m16n8k16 bf16 MMAs, rows = the 16 tokens from ldmatrix, cols = the G query
+// heads of the group), an online softmax per head in the log2 domain, and
+// O^T += V^T P^T (V^T via ldmatrix.trans, P^T moved into the B operand with
+// movmatrix) -- D/16 MMAs for each product, half of the head-major form.  At the end of an
 // item the four warp states are merged through shared memory and written as
 // one (m, l, acc) partial; a second kernel merges the partials of each
 // (request, query head) and writes bf16 output.
@@ -254,10 +256,12 @@ decode_kernel(DecArgs a) {
         qa[s][1] = gv ? w1 : 0u;
       }
     }
-    float m_i = -INFINITY, l_i = 0.f;
-    float o[D / 8][2];
+    // per thread: query heads h0 = 2*c4, h1 = 2*c4 + 1 (columns of the
+    // transposed tiles); l holds this lane's partial sums until the end
+    float m_i[2] = {-INFINITY, -INFINITY}, l_i[2] = {0.f, 0.f};
+    float o[D / 16][4];   // O^T fragments: rows d = 16*dt + g (+8), cols h0, h1
 #pragma unroll
-    for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = 0.f;
+    for (int i = 0; i < D / 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 
     for (; cc.j < cc.j1; cc.j += kDecWarps) {
       issue(ic, slot_i);
@@ -268,73 +272,83 @@ decode_kernel(DecArgs a) {
       const uint32_t vbase = kbase + T::kTileBytes;
       const int valid = my_meta[slot_c];
 
-      // S = Q K^T  (two n-tiles of 8 tokens)
-      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      // S^T = K Q^T: rows = the 16 tokens, cols = the query heads; A = K
+      // from shared memory (ldmatrix), B = the q fragment; two accumulators
+      // (even / odd k-steps) halve the dependent MMA chain
+      float st0[4] = {0.f, 0.f, 0.f, 0.f}, st1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
         const int mat = lane >> 3, rin = lane & 7;
-        const int tok = (mat >> 1) * 8 + rin;
-        const int ch = 2 * ks + (mat & 1);
-        uint32_t b[4];
-        ldsm_x4(b, kbase + tok * T::kRowBytes + swz(tok, ch) * 16);
-        const uint32_t afr[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
-        mma_bf16(s[0], afr, b[0], b[1]);
-        mma_bf16(s[1], afr, b[2], b[3]);
-      }
-      // online softmax (log2 domain), row g; tokens 8nt + 2c4 + {0,1}
-      float x[4];
-      x[0] = (2 * c4 < valid) ? s[0][0] * a.scale_log2 : -INFINITY;
-      x[1] = (2 * c4 + 1 < valid) ? s[0][1] * a.scale_log2 : -INFINITY;
-      x[2] = (8 + 2 * c4 < valid) ? s[1][0] * a.scale_log2 : -INFINITY;
-      x[3] = (9 + 2 * c4 < valid) ? s[1][1] * a.scale_log2 : -INFINITY;
-      float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float m_new = fmaxf(m_i, mx);
-      const float alpha = exp2f(m_i - m_new);
-      float p[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) p[i] = exp2f(x[i] - m_new);
-      l_i = l_i * alpha + (p[0] + p[1] + p[2] + p[3]);
-      m_i = m_new;
-#pragma unroll
-      for (int i = 0; i < D / 8; ++i) {
-        o[i][0] *= alpha;
-        o[i][1] *= alpha;
-      }
-      const uint32_t pa[4] = {pack_bf2(p[0], p[1]), 0u, pack_bf2(p[2], p[3]), 0u};
-      // O += P V
-#pragma unroll
-      for (int dt = 0; dt < D / 8; dt += 2) {
-        const int mat = lane >> 3, rin = lane & 7;
         const int tok = (mat & 1) * 8 + rin;
-        const int ch = dt + (mat >> 1);
-        uint32_t b[4];
-        ldsm_x4_t(b, vbase + tok * T::kRowBytes + swz(tok, ch) * 16);
-        float c0[4] = {o[dt][0], o[dt][1], 0.f, 0.f};
-        float c1[4] = {o[dt + 1][0], o[dt + 1][1], 0.f, 0.f};
-        mma_bf16(c0, pa, b[0], b[1]);
-        mma_bf16(c1, pa, b[2], b[3]);
-        o[dt][0] = c0[0]; o[dt][1] = c0[1];
-        o[dt + 1][0] = c1[0]; o[dt + 1][1] = c1[1];
+        const int ch = 2 * ks + (mat >> 1);
+        uint32_t ka[4];
+        ldsm_x4(ka, kbase + tok * T::kRowBytes + swz(tok, ch) * 16);
+        mma_bf16((ks & 1) ? st1 : st0, ka, qa[ks][0], qa[ks][1]);
+      }
+      // online softmax per head (log2 domain): this lane holds tokens g and
+      // g + 8 of heads h0, h1; the column max spans the 8 lanes of equal c4
+      float x[4];
+      x[0] = (g < valid) ? (st0[0] + st1[0]) * a.scale_log2 : -INFINITY;
+      x[1] = (g < valid) ? (st0[1] + st1[1]) * a.scale_log2 : -INFINITY;
+      x[2] = (g + 8 < valid) ? (st0[2] + st1[2]) * a.scale_log2 : -INFINITY;
+      x[3] = (g + 8 < valid) ? (st0[3] + st1[3]) * a.scale_log2 : -INFINITY;
+      float mx0 = fmaxf(x[0], x[2]), mx1 = fmaxf(x[1], x[3]);
+#pragma unroll
+      for (int o_ = 4; o_ < 32; o_ <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o_));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o_));
+      }
+      const float mn0 = fmaxf(m_i[0], mx0), mn1 = fmaxf(m_i[1], mx1);
+      const float al0 = exp2f(m_i[0] - mn0), al1 = exp2f(m_i[1] - mn1);
+      const float p0 = exp2f(x[0] - mn0), p1 = exp2f(x[1] - mn1);
+      const float p2 = exp2f(x[2] - mn0), p3 = exp2f(x[3] - mn1);
+      l_i[0] = l_i[0] * al0 + (p0 + p2);
+      l_i[1] = l_i[1] * al1 + (p1 + p3);
+      m_i[0] = mn0;
+      m_i[1] = mn1;
+#pragma unroll
+      for (int i = 0; i < D / 16; ++i) {
+        o[i][0] *= al0; o[i][2] *= al0;
+        o[i][1] *= al1; o[i][3] *= al1;
+      }
+      // P^T (tokens x heads) as the B operand: each 8x8 bf16 block of the
+      // C fragment transposed in registers
+      const uint32_t pb0 = movmatrix_t(pack_bf2(p0, p1));
+      const uint32_t pb1 = movmatrix_t(pack_bf2(p2, p3));
+      // O^T += V^T P^T: A = V^T tiles (ldmatrix.trans of the V rows)
+#pragma unroll
+      for (int dt = 0; dt < D / 16; ++dt) {
+        const int mat = lane >> 3, rin = lane & 7;
+        const int tok = (mat >> 1) * 8 + rin;
+        const int ch = 2 * dt + (mat & 1);
+        uint32_t va[4];
+        ldsm_x4_t(va, vbase + tok * T::kRowBytes + swz(tok, ch) * 16);
+        mma_bf16(o[dt], va, pb0, pb1);
       }
       __syncwarp();
       slot_c = (slot_c + 1 == NST) ? 0 : slot_c + 1;
     }
 
     // ---- merge the 4 warp states of this item and write one partial ------
-    l_i += __shfl_xor_sync(0xffffffffu, l_i, 1);
-    l_i += __shfl_xor_sync(0xffffffffu, l_i, 2);
-    if (g < a.G) {
-      if (c4 == 0) {
-        mbuf[warp * 8 + g] = m_i;
-        lbuf[warp * 8 + g] = l_i;
-      }
-      float* ab = abuf + (warp * a.G + g) * D;
 #pragma unroll
-      for (int dt = 0; dt < D / 8; ++dt) {
-        ab[8 * dt + 2 * c4] = o[dt][0];
-        ab[8 * dt + 2 * c4 + 1] = o[dt][1];
+    for (int o_ = 4; o_ < 32; o_ <<= 1) {
+      l_i[0] += __shfl_xor_sync(0xffffffffu, l_i[0], o_);
+      l_i[1] += __shfl_xor_sync(0xffffffffu, l_i[1], o_);
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int hh = 2 * c4 + j;
+      if (hh < a.G) {
+        if (g == 0) {
+          mbuf[warp * 8 + hh] = m_i[j];
+          lbuf[warp * 8 + hh] = l_i[j];
+        }
+        float* ab = abuf + (warp * a.G + hh) * D;
+#pragma unroll
+        for (int dt = 0; dt < D / 16; ++dt) {
+          ab[16 * dt + g] = o[dt][j];
+          ab[16 * dt + g + 8] = o[dt][2 + j];
+        }
       }
     }
     __syncthreads();
