@@ -398,7 +398,16 @@ def run_gpu(args):
             line["cpu_baseline"] = cpu_baseline(batch.ctxs)
         print(json.dumps(line), flush=True)
     if world > 1:
-        dist.destroy_process_group()
+        # graphs that captured NCCL collectives keep the communicator busy at
+        # teardown: release them, line the ranks up, then leave without the
+        # communicator destroy (the driver frees everything at process exit)
+        graphs.clear()
+        stage_graphs.clear()
+        torch.cuda.synchronize()
+        dist.barrier()
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(0)
 
 
 # --------------------------------------------------------------------------- #
