@@ -28,6 +28,7 @@
 // With the nrm combine the kernel also max-accumulates the per-head page
 // maximum into hmax[r, h, g]; the fold (nrm_combine / select_pages) consumes
 // it and resets it to -inf, so the fold is a single pass.
+#include <algorithm>
 #include <type_traits>
 
 #include "common.cuh"
@@ -62,6 +63,12 @@ struct QuadArgs {
   const __half* cs;  // (NB, n_kv, page) fp16 per-token scale
   const int32_t* sl; // (n_req,) seq_lens
   int page, tokmax;
+  // CLSE (quad geometry + per-key coordinates) only
+  const __half* resid;  // (NB, n_kv) residual scatter energy, or null
+  float* qsq;           // (n_req, H) |q_g|^2 written by the q prologue
+  float iso_coef;       // s^2 / (2 P (d - r))
+  int ctok;             // coordinate scales per token (1) or per page (0)
+  int write_h;          // per-head scores + hmax (nrm) instead of the max
 };
 
 AMASS_DEV void atomic_max_float(float* addr, float v) {
@@ -112,6 +119,14 @@ __global__ void __launch_bounds__(256) q_limbs_kernel(QuadArgs a) {
     lo[lane * PER + i] = (int8_t)(qi - 128 * h8);         // |lo| <= 64
   }
   if (lane == 0) a.qs[idx] = sq;
+  if (a.qsq) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) ss += v[i] * v[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) a.qsq[idx] = ss;
+  }
 }
 
 // 4 code bytes (d0..d0+3) of byte-column KB from a step's V words, RB bytes/d
@@ -574,15 +589,31 @@ r8_score_kernel(QuadArgs a) {
       }
       *reinterpret_cast<uint4*>(cb + e * 16) = v;
     }
-    for (int e = lane; e < kSBytes / 16; e += 32) {
-      const int pg = e / (PG * 2 / 16), off = e - pg * (PG * 2 / 16);
-      const int p = it.p0 + pg;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (p < nsh) {
-        const int64_t blk = __ldg(btr + p);
-        v = __ldg(reinterpret_cast<const uint4*>(a.cs + (blk * a.n_kv + h) * PG) + off);
+    if (a.ctok) {
+      for (int e = lane; e < kSBytes / 16; e += 32) {
+        const int pg = e / (PG * 2 / 16), off = e - pg * (PG * 2 / 16);
+        const int p = it.p0 + pg;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (p < nsh) {
+          const int64_t blk = __ldg(btr + p);
+          v = __ldg(reinterpret_cast<const uint4*>(a.cs + (blk * a.n_kv + h) * PG) + off);
+        }
+        *reinterpret_cast<uint4*>(cb + kCBytes + e * 16) = v;
       }
-      *reinterpret_cast<uint4*>(cb + kCBytes + e * 16) = v;
+    } else {
+      // one scale per (block, head): broadcast over the page's tokens
+      for (int e = lane; e < kSBytes / 16; e += 32) {
+        const int pg = e / (PG * 2 / 16);
+        const int p = it.p0 + pg;
+        uint32_t w = 0;
+        if (p < nsh) {
+          const int64_t blk = __ldg(btr + p);
+          const uint32_t hb = __ldg(reinterpret_cast<const unsigned short*>(a.cs) +
+                                    blk * a.n_kv + h);
+          w = hb | (hb << 16);
+        }
+        *reinterpret_cast<uint4*>(cb + kCBytes + e * 16) = make_uint4(w, w, w, w);
+      }
     }
     int acc[1 + R][2][4];
     item_dots(it, qf, a, lane, acc);
@@ -590,6 +621,14 @@ r8_score_kernel(QuadArgs a) {
     const int sl_r = __ldg(a.sl + it.r);
     constexpr float vdiv = (VB == 8) ? 1.f : 1.f / 16.f;
     float best[2] = {-INFINITY, -INFINITY};
+    float Sv[2][2];
+    float qsqv[2] = {0.f, 0.f};
+    if (a.resid) {
+      const int H = a.n_kv * a.G;
+      const float* qr_ = a.qsq + (int64_t)it.r * H + h * a.G;
+      qsqv[0] = __ldg(qr_ + min(2 * c, a.G - 1));
+      qsqv[1] = __ldg(qr_ + min(2 * c + 1, a.G - 1));
+    }
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int pl = m + 8 * half;                 // page within the tile
@@ -638,31 +677,59 @@ r8_score_kernel(QuadArgs a) {
           }
         }
       }
+      // CLSE: the out-of-subspace energy (|q|^2 - |q~|^2) * resid * coef
+      const float res = a.resid ? __half2float(a.resid[half ? it.rowb : it.rowa]) : 0.f;
 #pragma unroll
       for (int jj = 0; jj < 2; ++jj) {
         const int idx = 2 * half + jj;
         const float qmu = (float)(128 * acc[0][0][idx] + acc[0][1][idx]) * qf.sq[jj] *
                           mus * a.scale;
         const float agg = a.tokmax ? mx[jj] : mx[jj] + logf(sm[jj]);
-        const float S = qmu + agg;
+        float S = qmu + agg;
+        if (a.resid) {
+          float qh = 0.f;
+#pragma unroll
+          for (int k = 0; k < R; ++k) qh += qt[jj][k] * qt[jj][k];
+          S += fmaxf(qsqv[jj] - qh, 0.f) * res * a.iso_coef;
+        }
+        Sv[half][jj] = S;
         if (2 * c + jj < a.G) best[half] = fmaxf(best[half], S);
       }
     }
+    if (a.write_h) {
+      // per-head scores and the per-head page maximum (the nrm fold's hmax)
+      float* base = a.score_h + ((int64_t)it.r * a.n_kv + h) * a.G * a.SHS;
+      const int pa = it.p0 + m, pb = pa + 8;
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      float v = best[half];
-      v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
-      v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
-      const bool pv = half ? it.vb : it.va;
-      if (pv && c == 0)
-        a.score[((int64_t)it.r * a.n_kv + h) * a.MP + it.p0 + m + 8 * half] = v;
+      for (int jj = 0; jj < 2; ++jj) {
+        const int g = 2 * c + jj;
+        float mxh = -INFINITY;
+        if (g < a.G) {
+          if (it.va) { base[(int64_t)g * a.SHS + pa] = Sv[0][jj]; mxh = Sv[0][jj]; }
+          if (it.vb) { base[(int64_t)g * a.SHS + pb] = Sv[1][jj]; mxh = fmaxf(mxh, Sv[1][jj]); }
+        }
+        mxh = fmaxf(mxh, __shfl_xor_sync(0xffffffffu, mxh, 4));
+        mxh = fmaxf(mxh, __shfl_xor_sync(0xffffffffu, mxh, 8));
+        mxh = fmaxf(mxh, __shfl_xor_sync(0xffffffffu, mxh, 16));
+        if (m == 0 && g < a.G && mxh > -INFINITY)
+          atomic_max_float(a.hmax + ((int64_t)it.r * a.n_kv + h) * a.G + g, mxh);
+      }
+    } else {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float v = best[half];
+        v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+        v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+        const bool pv = half ? it.vb : it.va;
+        if (pv && c == 0)
+          a.score[((int64_t)it.r * a.n_kv + h) * a.MP + it.p0 + m + 8 * half] = v;
+      }
     }
   }
 }
 
-template <int D, int CB, int VB>
+template <int D, int CB, int VB, int R = 8>
 int launch_r8(const QuadArgs& a, cudaStream_t st) {
-  constexpr int R = 8;
   auto k = r8_score_kernel<D, R, VB, CB>;
   static int ps = 0;
   if (ps == 0) {
@@ -831,6 +898,7 @@ extern "C" int amass_r8_score(const void* q, int64_t q_stride_t,
   a.MP = max_pages;
   a.page = page;
   a.tokmax = token_agg == AMASS_R8_TOKMAX ? 1 : 0;
+  a.ctok = 1;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto go = [&](auto d) -> int {
     constexpr int D = decltype(d)::value;
@@ -841,5 +909,87 @@ extern "C" int amass_r8_score(const void* q, int64_t q_stride_t,
   };
   if (head_dim == 128) return go(std::integral_constant<int, 128>{});
   if (head_dim == 64) return go(std::integral_constant<int, 64>{});
+  return AMASS_ERR_UNSUPPORTED;
+}
+
+extern "C" int amass_clse_score(
+    const void* q, int64_t q_stride_t, int64_t q_stride_h, const int8_t* mu,
+    const void* mu_scale, const int8_t* V, const void* V_scale,
+    const int8_t* c, const void* c_scale, int c_token_grain,
+    const void* resid, const int32_t* block_table, int64_t bt_stride,
+    const int32_t* seq_lens, const int32_t* n_sel_hi, float* score,
+    float* score_h, int64_t sh_stride, float* hmax, int8_t* q8_ws,
+    float* qs_ws, float* qsq_ws, float scale, int n_req, int n_kv, int G,
+    int head_dim, int page, int rank, int v_bits, int c_bits, int max_pages,
+    int write_h, void* stream) {
+  using namespace amass;
+  if (n_req < 0 || n_kv <= 0 || G <= 0 || max_pages <= 0) return AMASS_ERR_ARG;
+  if (n_req == 0) return AMASS_OK;
+  if (!q || !mu || !mu_scale || !V || !V_scale || !c || !c_scale || !resid ||
+      !block_table || !seq_lens || !n_sel_hi || !q8_ws || !qs_ws || !qsq_ws)
+    return AMASS_ERR_ARG;
+  if (write_h ? (!score_h || !hmax || sh_stride < max_pages) : !score)
+    return AMASS_ERR_ARG;
+  if (G > 8 || page != 16 || n_req > kR8MaxReq ||
+      (rank != 2 && rank != 4 && rank != 8) || (v_bits != 8 && v_bits != 4) ||
+      (c_bits != 8 && c_bits != 4))
+    return AMASS_ERR_UNSUPPORTED;
+  if ((q_stride_h % 2) || (q_stride_t % 2) ||
+      (reinterpret_cast<uintptr_t>(mu) & 15) ||
+      (reinterpret_cast<uintptr_t>(V) & 15) ||
+      (reinterpret_cast<uintptr_t>(c) & 15) ||
+      (c_token_grain && (reinterpret_cast<uintptr_t>(c_scale) & 15)) ||
+      (reinterpret_cast<uintptr_t>(V_scale) & 3) ||
+      (reinterpret_cast<uintptr_t>(q8_ws) & 15))
+    return AMASS_ERR_ARG;
+  QuadArgs a{};
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.q_st = q_stride_t;
+  a.q_sh = q_stride_h;
+  a.mu = mu;
+  a.mus = static_cast<const __half*>(mu_scale);
+  a.V = V;
+  a.Vs = static_cast<const __half*>(V_scale);
+  a.sig2 = static_cast<const __half*>(V_scale);   // unused here
+  a.c = c;
+  a.cs = static_cast<const __half*>(c_scale);
+  a.sl = seq_lens;
+  a.bt = block_table;
+  a.bt_stride = bt_stride;
+  a.nsh = n_sel_hi;
+  a.score = score;
+  a.score_h = score_h;
+  a.SHS = sh_stride;
+  a.hmax = hmax;
+  a.q8 = q8_ws;
+  a.qs = qs_ws;
+  a.qsq = qsq_ws;
+  a.resid = static_cast<const __half*>(resid);
+  a.scale = scale;
+  a.iso_coef = scale * scale / (2.f * page * (float)std::max(head_dim - rank, 1));
+  a.ctok = c_token_grain ? 1 : 0;
+  a.write_h = write_h ? 1 : 0;
+  a.n_req = n_req;
+  a.n_kv = n_kv;
+  a.G = G;
+  a.MP = max_pages;
+  a.page = page;
+  a.tokmax = 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto go = [&](auto d, auto r) -> int {
+    constexpr int D = decltype(d)::value;
+    constexpr int R = decltype(r)::value;
+    if (v_bits == 8 && c_bits == 8) return launch_r8<D, 8, 8, R>(a, st);
+    if (v_bits == 8 && c_bits == 4) return launch_r8<D, 4, 8, R>(a, st);
+    if (v_bits == 4 && c_bits == 8) return launch_r8<D, 8, 4, R>(a, st);
+    return launch_r8<D, 4, 4, R>(a, st);
+  };
+  auto by_rank = [&](auto d) -> int {
+    if (rank == 2) return go(d, std::integral_constant<int, 2>{});
+    if (rank == 4) return go(d, std::integral_constant<int, 4>{});
+    return go(d, std::integral_constant<int, 8>{});
+  };
+  if (head_dim == 128) return by_rank(std::integral_constant<int, 128>{});
+  if (head_dim == 64) return by_rank(std::integral_constant<int, 64>{});
   return AMASS_ERR_UNSUPPORTED;
 }

@@ -58,8 +58,12 @@ class QuadState:
             raise ValueError("int4 V packs two nibbles per byte: rank even")
         if combine not in COMBINE:
             raise ValueError(f"combine must be 'max' or 'nrm', got {combine!r}")
-        if coords != "none":
-            raise NotImplementedError("CLSE coords are outside this build")
+        if coords not in ("none", "lse"):
+            raise ValueError(f"coords must be 'none' or 'lse', got {coords!r}")
+        if coords == "lse" and c_bits == 4 and rank % 2:
+            raise ValueError("int4 coords pack two nibbles per byte: rank even")
+        if c_grain not in ("token", "page"):
+            raise ValueError(f"c_grain must be 'token' or 'page', got {c_grain!r}")
         L, NB, D, r, MP, R = (num_layers, num_blocks, head_dim, rank,
                               max_pages, max_reqs)
         self.L, self.NB, self.n_kv, self.G, self.d = L, NB, n_kv, G, D
@@ -81,7 +85,21 @@ class QuadState:
         self.quad_sig2 = torch.zeros(L, NB, n_kv, r, dtype=torch.float16, **kw)
         self.quad_tag = torch.full((L, NB, n_kv, tagw), float("nan"),
                                    dtype=torch.bfloat16, **kw)
-        self.quad_c = self.c_scale = self.quad_resid = None
+        self.c_bits, self.c_grain = int(c_bits), c_grain
+        if coords == "lse":
+            # CLSE: per-key rank-r' coordinates, their scales (per token or
+            # per page) and the out-of-subspace scatter energy
+            rc = r // 2 if self.c_bits == 4 else r
+            self.quad_c = torch.zeros(L, NB, n_kv, page, rc, dtype=torch.int8,
+                                      **kw)
+            cs_shape = (L, NB, n_kv, page) if c_grain == "token" else \
+                (L, NB, n_kv)
+            self.c_scale = torch.zeros(cs_shape, dtype=torch.float16, **kw)
+            self.quad_resid = torch.zeros(L, NB, n_kv, dtype=torch.float16,
+                                          **kw)
+            self.qsq = torch.zeros(R, n_kv * G, dtype=torch.float32, **kw)
+        else:
+            self.quad_c = self.c_scale = self.quad_resid = self.qsq = None
         self.score = torch.empty(R, n_kv, MP, dtype=torch.float32, **kw)
         self.page_table = torch.empty(R, n_kv, MP, dtype=torch.int32, **kw)
         self.page_cnt = torch.zeros(R, n_kv, dtype=torch.int32, **kw)
@@ -233,6 +251,56 @@ def select_pages_quad(st, layer: int, q, block_table, seq_lens, n_req: int,
         derive_page_params(st, seq_lens, n_req)
     nrm = getattr(st, "combine", "max") == "nrm"
     _score_launch(st, layer, q, block_table, n_req, scale, nrm)
+    select_pages(st, n_req, coverage=coverage, from_score_h=nrm)
+
+
+# --------------------------------------------------------------------------- #
+# CLSE scorer: quad geometry + per-key coordinates + residual energy          #
+# --------------------------------------------------------------------------- #
+def clse_score_cuda(st, layer: int, q, block_table, seq_lens, n_req: int,
+                    scale: float) -> None:
+    """Drop-in for the reference ``clse_score`` / ``clse_score_cuda``
+    (``selection/quad_score.py:318-374``, ``quad_score_cuda.py:1797``):
+    S_g = s*mu.q_g + logsumexp_t(s * c_t . V^T q_g) + iso_g per page; writes
+    ``st.score`` (combine "max") or ``st.score_h`` + ``st.hmax`` for the nrm
+    fold (combine "nrm"; ``select_pages`` folds)."""
+    if getattr(st, "quad_c", None) is None:
+        raise ValueError("CLSE needs a state built with coords='lse'")
+    nrm = getattr(st, "combine", "max") == "nrm"
+    _prepare(st, q.device, nrm)
+    _check_q(q, st)
+    if getattr(st, "qsq", None) is None:
+        st.qsq = torch.zeros(st.max_reqs, st.n_kv * st.G, dtype=torch.float32,
+                             device=q.device)
+    mu, mu_s, V, V_s = (st.quad_mu[layer], st.mu_scale[layer],
+                        st.quad_V[layer], st.V_scale[layer])
+    c, c_s, res = st.quad_c[layer], st.c_scale[layer], st.quad_resid[layer]
+    _lib.call("amass_clse_score", ptr(q), q.stride(0), q.stride(1), ptr(mu),
+              ptr(mu_s), ptr(V), ptr(V_s), ptr(c), ptr(c_s),
+              1 if getattr(st, "c_grain", "token") == "token" else 0,
+              ptr(res), ptr(block_table), block_table.stride(0),
+              ptr(seq_lens), ptr(st.n_sel_hi), ptr(st.score),
+              ptr(st.score_h) if nrm else 0,
+              st.score_h.stride(2) if nrm else 0,
+              ptr(st.hmax) if nrm else 0, ptr(st.q8), ptr(st.qs), ptr(st.qsq),
+              float(scale), int(n_req), int(st.n_kv), int(st.G), int(st.d),
+              int(st.page), int(st.r), int(getattr(st, "v_bits", 8)),
+              int(st.c_bits), int(st.max_pages), 1 if nrm else 0,
+              _lib.stream_of(q.device))
+
+
+clse_score = clse_score_cuda
+
+
+def select_pages_clse(st, layer: int, q, block_table, seq_lens, n_req: int,
+                      scale: float, *, derive: bool = True,
+                      coverage=None) -> None:
+    """One-call Stage A (CLSE): (derive) + score + fused fold/select
+    (reference ``selection/quad_score.py`` select_pages_clse)."""
+    if derive:
+        derive_page_params(st, seq_lens, n_req)
+    clse_score_cuda(st, layer, q, block_table, seq_lens, n_req, scale)
+    nrm = getattr(st, "combine", "max") == "nrm"
     select_pages(st, n_req, coverage=coverage, from_score_h=nrm)
 
 

@@ -209,6 +209,36 @@ def make_r8_case(seed=0, *, n_req=2, n_kv=2, G=4, d=64, page=16,
                   c_bits=c_bits, page=page, MP=base.MP, scale=base.scale)
 
 
+def make_clse_case(seed=0, *, n_req=2, n_kv=2, G=4, d=64, page=16,
+                   ctxs=(700, 333), r=2, v_bits=8, c_bits=8,
+                   c_grain="token", heavy=3, shift=2.5):
+    """Quad case plus the CLSE extras of the same keys: per-token coordinates
+    in the page basis (quantised per token or per page), and the residual
+    scatter energy resid = trace - sum_k sig2_k."""
+    base = make_quad_case(seed, n_req=n_req, n_kv=n_kv, G=G, d=d, page=page,
+                          ctxs=ctxs, r=r, v_bits=v_bits, heavy=heavy,
+                          shift=shift)
+    K = base.K.astype(np.float64)
+    basis = base.extra["basis"]                                   # (kv, d, r)
+    mu = K.mean(axis=1)
+    Kc = K - mu[:, None]
+    coords = np.einsum("btkd,kdr->bktr", Kc, basis)               # (NB,kv,t,r)
+    trace = (Kc ** 2).sum(axis=(1, 3))                            # (NB, kv)
+    sig2 = (coords ** 2).sum(axis=2)                              # (NB, kv, r)
+    resid = np.maximum(trace - sig2.sum(-1), 0.0).astype(np.float16)
+    if c_grain == "token":
+        c_code, c_sc = quantize(coords.astype(np.float32), -1, c_bits)
+        c_sc = c_sc[..., 0]                                       # (NB,kv,t)
+    else:
+        c_code, c_sc = quantize(coords.astype(np.float32), (-2, -1), c_bits)
+        c_sc = c_sc[..., 0, 0]                                    # (NB,kv)
+    if c_bits == 4:
+        c_code = pack_int4(c_code)
+    base.extra.update(c=c_code, c_s=c_sc.astype(np.float16), resid=resid,
+                      c_bits=c_bits, c_grain=c_grain)
+    return base
+
+
 # --------------------------------------------------------------------------- #
 # full-size GPU batches (benchmark)                                           #
 # --------------------------------------------------------------------------- #

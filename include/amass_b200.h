@@ -142,6 +142,29 @@ int amass_r8_score(const void* q, int64_t q_stride_t, int64_t q_stride_h,
                    int rank, int vk_bits, int c_bits, int max_pages,
                    int token_agg, void* stream);
 
+/* clse_score -- replaces selection/quad_score_cuda.py:1797 (Triton golden
+ * selection/quad_score.py:156-374).  The quad geometry plus rank-r' per-key
+ * coordinates c (NB, n_kv, page, rc) int8 (rc = rank, or rank/2 packed int4)
+ * with fp16 scales per token (c_token_grain = 1: (NB, n_kv, page)) or per
+ * page (0: (NB, n_kv)), and resid (NB, n_kv) fp16 = trace - sum sig2:
+ *   S_g = s*mu.q_g + logsumexp_{t < seq_len} (s * c_t . V^T q_g)
+ *         + max(|q_g|^2 - |V^T q_g|^2, 0) * resid * s^2 / (2P(d - rank)).
+ * write_h = 0: score = max_g S_g; write_h = 1: score_h / hmax as in
+ * amass_quad_score (the nrm fold follows).  qsq_ws (n_req, H) fp32 scratch
+ * receives |q_g|^2.  rank in {2, 4, 8}, v_bits / c_bits in {4, 8},
+ * head_dim in {64, 128}, G <= 8, page = 16, n_req <= 2048. */
+int amass_clse_score(const void* q, int64_t q_stride_t, int64_t q_stride_h,
+                     const int8_t* mu, const void* mu_scale, const int8_t* V,
+                     const void* V_scale, const int8_t* c, const void* c_scale,
+                     int c_token_grain, const void* resid,
+                     const int32_t* block_table, int64_t bt_stride,
+                     const int32_t* seq_lens, const int32_t* n_sel_hi,
+                     float* score, float* score_h, int64_t sh_stride,
+                     float* hmax, int8_t* q8_ws, float* qs_ws, float* qsq_ws,
+                     float scale, int n_req, int n_kv, int G, int head_dim,
+                     int page, int rank, int v_bits, int c_bits, int max_pages,
+                     int write_h, void* stream);
+
 /* sparse_paged_decode -- replaces attention/decode_cuda.py:1376-1465
  * (Triton golden attention/decode.py:247-304 + merge.py:21-50).
  * K/V tiles are addressed as base + blk*s_b + tok*s_t + kv*s_h (elements,

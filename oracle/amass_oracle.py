@@ -401,6 +401,55 @@ def r8_score(q, mu, mu_s, Vk, Vk_s, c, c_s, block_table, seq_lens, n_sel_hi,
 
 
 # --------------------------------------------------------------------------- #
+# CLSE page score (selection/quad_score.py:156-273)                           #
+# --------------------------------------------------------------------------- #
+def clse_score_h(q, mu, mu_s, V, V_s, c, c_s, resid, block_table, seq_lens,
+                 n_sel_hi, *, scale: float, page: int, G: int, r: int,
+                 v_bits: int, c_bits: int, token_grain: bool, MP: int):
+    """Per-head CLSE score S[g] for every scored page p < n_sel_hi:
+
+        q~    = V^T q_g                       V = V_code * V_scale (per column)
+        tok_t = s * c_t . q~                   c = c_code * c_scale (token or page)
+        iso   = max(|q_g|^2 - |q~|^2, 0) * resid * s^2 / (2 P (d - r))
+        S_g   = s * mu.q_g + logsumexp_{t: tok < seq_len} tok_t + iso
+
+    (``selection/quad_score.py:156-273``).  Returns (R, n_kv, G, MP) float32,
+    NaN where no score is written."""
+    n_req = block_table.shape[0]
+    n_kv, d = mu.shape[1], mu.shape[2]
+    out = np.full((n_req, n_kv, G, MP), np.nan, dtype=F32)
+    iso_coef = F32(scale * scale / (2.0 * page * max(d - r, 1)))
+    for rq in range(n_req):
+        nsh = int(n_sel_hi[rq])
+        if nsh <= 0:
+            continue
+        sl = int(seq_lens[rq])
+        blks = block_table[rq, :nsh].astype(np.int64)
+        qg = q[rq].reshape(n_kv, G, d).astype(F32)
+        qsq = np.sum(qg * qg, axis=-1, dtype=F32)                      # (kv,G)
+        mu_f = mu[blks].astype(F32) * mu_s[blks].astype(F32)[..., None]
+        Vf = unpack_codes(V[blks], r, v_bits) * \
+            V_s[blks].astype(F32)[:, :, None, :]                       # (P,kv,d,r)
+        cs = c_s[blks].astype(F32)
+        if not token_grain:
+            cs = np.broadcast_to(cs[..., None], cs.shape + (page,))
+        cc = unpack_codes(c[blks], r, c_bits) * cs[..., None]           # (P,kv,t,r)
+        qt = np.einsum("kgd,pkdr->pkgr", qg, Vf, dtype=F32)
+        tok = np.einsum("pkgr,pktr->pkgt", qt, cc, dtype=F32) * F32(scale)
+        tpos = np.arange(nsh)[:, None] * page + np.arange(page)[None, :]
+        tok = np.where((tpos < sl)[:, None, None, :], tok, -np.inf)
+        m = tok.max(axis=-1)
+        lse = m + np.log(np.exp(tok - m[..., None]).sum(-1))
+        qhsq = np.sum(qt * qt, axis=-1, dtype=F32)
+        iso = np.maximum(qsq[None] - qhsq, 0) * \
+            resid[blks].astype(F32)[:, :, None] * iso_coef
+        qmu = np.einsum("kgd,pkd->pkg", qg, mu_f, dtype=F32) * F32(scale)
+        S = (qmu + lse + iso).astype(F32)                               # (P,kv,G)
+        out[rq, :, :, :nsh] = S.transpose(1, 2, 0)
+    return out
+
+
+# --------------------------------------------------------------------------- #
 # a10/a11: exact-LRU residency plan + miss fetch                              #
 #          tier/residency.py:45-139 (plan), :196-248 (fetch)                  #
 # --------------------------------------------------------------------------- #

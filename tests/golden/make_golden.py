@@ -34,10 +34,11 @@ sys.path.insert(0, REF)
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-from amass_kv_b200.workloads import make_quad_case, make_r8_case  # noqa: E402
+from amass_kv_b200.workloads import (make_clse_case, make_quad_case,  # noqa: E402
+                                     make_r8_case)
 
 from amass.selection import (QuadState, R8State, derive_page_params,  # noqa
-                             quad_score, r8_score, topb_select)
+                             quad_score, r8_score, topb_select, clse_score)
 from amass.attention.decode import (ResidentVSource,  # noqa: E402
                                     ensure_stage_b_buffers,
                                     sparse_paged_decode_batched)
@@ -190,6 +191,50 @@ def gen_r8(name, case, *, budget):
     print(name, "cnt", st.page_cnt.tolist())
 
 
+def gen_clse(name, case, *, budget, combine):
+    """The reference CLSE scorer (its default r'=2 path is the block-sweep
+    kernel) + top-b on a quad case with per-token coordinates and resid."""
+    n_req = case.block_table.shape[0]
+    NB = case.K.shape[0]
+    x = case.extra
+    st = QuadState("cpu", num_layers=1, num_blocks=NB, n_kv=case.n_kv,
+                   G=case.G, head_dim=case.d, page=case.page, max_reqs=n_req,
+                   max_pages=case.MP, rank=case.r, budget=budget,
+                   v_bits=case.v_bits, combine=combine, coords="lse",
+                   c_bits=x["c_bits"], c_grain=x["c_grain"])
+    st.quad_mu[0].copy_(torch.from_numpy(case.mu))
+    st.mu_scale[0].copy_(torch.from_numpy(case.mu_s))
+    st.quad_V[0].copy_(torch.from_numpy(case.Vq))
+    st.V_scale[0].copy_(torch.from_numpy(case.V_s))
+    st.quad_sig2[0].copy_(torch.from_numpy(case.sig2))
+    st.quad_c[0].copy_(torch.from_numpy(x["c"]))
+    st.c_scale[0].copy_(torch.from_numpy(x["c_s"]))
+    st.quad_resid[0].copy_(torch.from_numpy(x["resid"]))
+    st.score.fill_(float("nan"))
+    if combine == "nrm":
+        st.score_h.fill_(float("nan"))
+    q = t_bf16(case.q)
+    bt = torch.from_numpy(case.block_table)
+    sl = torch.from_numpy(case.seq_lens)
+    derive_page_params(st, sl, n_req)
+    clse_score(st, 0, q, bt, sl, n_req, case.scale)
+    topb_select(st, n_req)
+    extra = {}
+    if combine == "nrm":
+        extra["score_h"] = st.score_h.numpy()
+    np.savez_compressed(
+        os.path.join(HERE, name + ".npz"), **quad_inputs(case),
+        c=x["c"], c_s=x["c_s"], resid=x["resid"],
+        cmeta=np.array([x["c_bits"], 1 if x["c_grain"] == "token" else 0],
+                       np.int64),
+        combine=np.array([combine]), budget=np.array([budget]),
+        n_sel_hi=st.n_sel_hi.numpy(), n_pages=st.n_pages.numpy(),
+        b_fix=st.b_fix.numpy(), score=st.score.numpy(),
+        page_table=st.page_table.numpy(), page_cnt=st.page_cnt.numpy(),
+        **extra)
+    print(name, "cnt", st.page_cnt.tolist())
+
+
 def gen_tier(name, case, *, budget, hot_slots=10, steps=3, seed=5):
     """Residency gather over several steps with forced eviction, staged and
     flushed sources, then the ptr-select tiered decode."""
@@ -329,6 +374,15 @@ def main():
     gen_tier("tier_lru", t, budget=0.25, hot_slots=24, steps=3)
     gen_tier("tier_overflow", t, budget=0.25, hot_slots=10, steps=1)
     gen_invalidate("tier_invalidate")
+    cl1 = make_clse_case(7, n_req=2, n_kv=2, G=4, d=64, ctxs=(700, 333), r=2,
+                         v_bits=4, c_bits=4, c_grain="token")
+    gen_clse("clse_i4_tok_nrm", cl1, budget=0.1, combine="nrm")
+    cl2 = make_clse_case(8, n_req=3, n_kv=2, G=8, d=128, ctxs=(900, 260, 40),
+                         r=2, v_bits=8, c_bits=8, c_grain="page")
+    gen_clse("clse_i8_page_max", cl2, budget=0.1, combine="max")
+    cl3 = make_clse_case(9, n_req=2, n_kv=2, G=4, d=128, ctxs=(500, 377),
+                         r=4, v_bits=8, c_bits=8, c_grain="token")
+    gen_clse("clse_r4_i8_tok_max", cl3, budget=0.1, combine="max")
 
 
 if __name__ == "__main__":

@@ -195,3 +195,47 @@ def test_invalidate_written():
     assert np.array_equal(p2s, z["page2slot"])
     assert np.array_equal(s2p, z["slot2page"])
     assert np.array_equal(valid, z["pool_valid"])
+
+
+CLSE = ["clse_i4_tok_nrm", "clse_i8_page_max", "clse_r4_i8_tok_max"]
+
+
+def clse_h(z):
+    g = _quad(z)
+    c_bits, tok = [int(x) for x in z["cmeta"]]
+    return O.clse_score_h(g["q"], z["mu"], z["mu_s"], z["Vq"], z["V_s"],
+                          z["c"], z["c_s"], z["resid"], z["block_table"],
+                          z["seq_lens"], z["n_sel_hi"], scale=g["scale"],
+                          page=g["page"], G=g["G"], r=g["r"],
+                          v_bits=g["v_bits"], c_bits=c_bits,
+                          token_grain=bool(tok), MP=g["MP"])
+
+
+@pytest.mark.parametrize("name", CLSE)
+def test_clse_score(name):
+    """The CLSE restatement against the reference's own clse_score
+    (block-sweep kernel at r'=2, generic kernel at r'=4)."""
+    z = load_golden(name)
+    sh = clse_h(z)
+    comb = str(z["combine"][0])
+    nsh = z["n_sel_hi"]
+    if comb == "nrm":
+        for rq in range(sh.shape[0]):
+            n = int(nsh[rq])
+            np.testing.assert_allclose(sh[rq, :, :, :n],
+                                       z["score_h"][rq, :, :, :n],
+                                       rtol=2e-4, atol=2e-4)
+        sc = O.combine_nrm(sh, nsh)
+    else:
+        sc = O.combine_max(sh, nsh)
+    for rq in range(sh.shape[0]):
+        n = int(nsh[rq])
+        np.testing.assert_allclose(sc[rq, :, :n], z["score"][rq, :, :n],
+                                   rtol=2e-4, atol=2e-4)
+    # the reference's top-b of its own scores is the threshold rule
+    MP = int(z["meta"][4])
+    scm = np.where(np.isnan(z["score"]), -np.inf, z["score"]).astype(np.float32)
+    tab, cnt = O.topb_select(scm, z["n_pages"], z["n_sel_hi"], z["b_fix"],
+                             sink=1, MP=MP)
+    assert np.array_equal(tab, z["page_table"])
+    assert np.array_equal(cnt, z["page_cnt"])
