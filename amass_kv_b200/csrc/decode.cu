@@ -538,7 +538,7 @@ int resident_decode(
       (reinterpret_cast<uintptr_t>(v) & 15) || (q_stride_h % 2) ||
       (q_stride_t % 2) || (o_stride_h % 2) || (o_stride_t % 2))
     return AMASS_ERR_ARG;
-  DecArgs a;
+  DecArgs a{};
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.q_st = q_stride_t; a.q_sh = q_stride_h;
   a.k = static_cast<const __nv_bfloat16*>(k);
@@ -640,7 +640,7 @@ extern "C" int amass_tier_decode(
       (q_stride_h % 2) || (q_stride_t % 2) || (o_stride_h % 2) ||
       (o_stride_t % 2))
     return AMASS_ERR_ARG;
-  DecArgs a;
+  DecArgs a{};
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.q_st = q_stride_t; a.q_sh = q_stride_h;
   a.k = static_cast<const __nv_bfloat16*>(k_tier ? hot_k : k);

@@ -68,7 +68,7 @@ extern "C" int amass_peer_barrier(int32_t* const* peer_flags, int n_ranks,
   if (!peer_flags || !epoch || !err || n_ranks < 1 || n_ranks > kMaxRanks ||
       rank < 0 || rank >= n_ranks)
     return AMASS_ERR_ARG;
-  BarrierArgs a;
+  BarrierArgs a{};
   for (int i = 0; i < kMaxRanks; ++i)
     a.flags[i] = i < n_ranks ? peer_flags[i] : nullptr;
   for (int i = 0; i < n_ranks; ++i)

@@ -512,6 +512,37 @@ struct R8Tok {
   static constexpr int RC = (CB == 8) ? R : R / 2;   // code bytes per token
 };
 
+// Coordinate staging of one tile: 16-byte cp.async pieces into the warp's
+// buffer, page-major codes then (token grain) the per-token scales.  Lane
+// (m, c) stages the pieces of its own pages m and m+8 (their rows are known
+// to it), lanes c = 0..3 interleaved; pages past n_sel_hi are zero-filled.
+template <int D, int R, int VB, int CB>
+AMASS_DEV void stage_coords(const Item<D, R, VB>& it, const QuadArgs& a,
+                            int lane, uint32_t cbase) {
+  constexpr int RC = R8Tok<R, CB>::RC;
+  constexpr int PG = 16;
+  constexpr int kCBytes = 16 * PG * RC;
+  constexpr int NPC = PG * RC / 16;                 // code pieces per page
+  const int NP = NPC + (a.ctok ? 2 : 0);            // pieces per page
+  const int m = lane >> 2, c = lane & 3;
+  for (int i = c; i < 2 * NP; i += 4) {
+    const int half = i >= NP;
+    const int k = i - half * NP;
+    const int pl = m + 8 * half;
+    const int row = half ? it.rowb : it.rowa;
+    const bool ok = half ? it.vb : it.va;
+    if (k < NPC) {
+      cp_async16(cbase + pl * PG * RC + k * 16,
+                 a.c + (int64_t)row * PG * RC + k * 16, ok);
+    } else {
+      const int k2 = k - NPC;
+      cp_async16(cbase + kCBytes + pl * PG * 2 + k2 * 16,
+                 reinterpret_cast<const uint8_t*>(a.cs) + (int64_t)row * PG * 2 + k2 * 16,
+                 ok);
+    }
+  }
+}
+
 template <int D, int R, int VB, int CB>
 __global__ void __launch_bounds__(kQuadWarps * 32, 1)
 r8_score_kernel(QuadArgs a) {
@@ -521,9 +552,10 @@ r8_score_kernel(QuadArgs a) {
   constexpr int PG = 16;                                    // tokens per page
   constexpr int kCBytes = 16 * PG * RC;                     // 16 pages of codes
   constexpr int kSBytes = 16 * PG * 2;                      // their scales
+  constexpr int kBuf = kCBytes + kSBytes;
   __shared__ int prefix[kR8MaxReq + 1];
   __shared__ int nshs[kR8MaxReq];
-  __shared__ __align__(16) uint8_t cbuf[kQuadWarps][kCBytes + kSBytes];
+  extern __shared__ __align__(16) uint8_t r8dyn[];          // warps x 2 x kBuf
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0) {
     int run = 0;
@@ -562,78 +594,63 @@ r8_score_kernel(QuadArgs a) {
     rh = lo;
   }
   const int m = lane >> 2, c = lane & 3;
-  uint8_t* cb = cbuf[warp];
-  const __half* csb = reinterpret_cast<const __half*>(cb + kCBytes);
+  uint8_t* wbuf = r8dyn + warp * 2 * kBuf;
+  const uint32_t wbuf_s = smem_u32(wbuf);
   QFrag<D> qf;
   int qr = -1;
-  Item<D, R, VB> it;
-  for (int t = t_lo; t < t_hi; ++t) {
-    load_idx(it, a, prefix, nshs, t * a.n_kv + h, lane, &rh);
-    // block ids of all 16 pages of the tile (for the coordinate staging)
-    const int32_t* btr = a.bt + (int64_t)it.r * a.bt_stride;
-    const int nsh = nshs[it.r];
-    load_data(it, a, lane);
-    if (it.r != qr) {
-      load_qfrag(qf, a, it.r, h, lane);
-      qr = it.r;
+  // three-deep pipeline as the quad scorer (block ids two tiles ahead,
+  // summary registers and the coordinate copies one tile ahead)
+  Item<D, R, VB> cur, nxt, nn;
+  __half2 csp_cur, csp_nxt;                 // page-grain coordinate scales
+  auto page_scales = [&](const Item<D, R, VB>& x) {
+    __half2 v;
+    v.x = x.va ? a.cs[x.rowa] : __ushort_as_half(0);
+    v.y = x.vb ? a.cs[x.rowb] : __ushort_as_half(0);
+    return v;
+  };
+  int t = t_lo;
+  load_idx(cur, a, prefix, nshs, t * a.n_kv + h, lane, &rh);
+  load_data(cur, a, lane);
+  stage_coords<D, R, VB, CB>(cur, a, lane, wbuf_s);
+  cp_async_commit();
+  if (!a.ctok) csp_cur = page_scales(cur);
+  if (t + 1 < t_hi) load_idx(nxt, a, prefix, nshs, (t + 1) * a.n_kv + h, lane, &rh);
+  constexpr float kL2e = 1.4426950408889634f, kLn2 = 0.6931471805599453f;
+  while (true) {
+    const bool more = t + 1 < t_hi;
+    if (t + 2 < t_hi) load_idx(nn, a, prefix, nshs, (t + 2) * a.n_kv + h, lane, &rh);
+    if (more) {
+      load_data(nxt, a, lane);
+      stage_coords<D, R, VB, CB>(nxt, a, lane, wbuf_s + ((t + 1 - t_lo) & 1) * kBuf);
+      if (!a.ctok) csp_nxt = page_scales(nxt);
     }
-    // stage codes + scales: 16-byte pieces, page-major
-    __syncwarp();
-    for (int e = lane; e < kCBytes / 16; e += 32) {
-      const int pg = e / (PG * RC / 16), off = e - pg * (PG * RC / 16);
-      const int p = it.p0 + pg;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (p < nsh) {
-        const int64_t blk = __ldg(btr + p);
-        v = __ldg(reinterpret_cast<const uint4*>(a.c + ((blk * a.n_kv + h) * PG) * RC) + off);
-      }
-      *reinterpret_cast<uint4*>(cb + e * 16) = v;
-    }
-    if (a.ctok) {
-      for (int e = lane; e < kSBytes / 16; e += 32) {
-        const int pg = e / (PG * 2 / 16), off = e - pg * (PG * 2 / 16);
-        const int p = it.p0 + pg;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (p < nsh) {
-          const int64_t blk = __ldg(btr + p);
-          v = __ldg(reinterpret_cast<const uint4*>(a.cs + (blk * a.n_kv + h) * PG) + off);
-        }
-        *reinterpret_cast<uint4*>(cb + kCBytes + e * 16) = v;
-      }
-    } else {
-      // one scale per (block, head): broadcast over the page's tokens
-      for (int e = lane; e < kSBytes / 16; e += 32) {
-        const int pg = e / (PG * 2 / 16);
-        const int p = it.p0 + pg;
-        uint32_t w = 0;
-        if (p < nsh) {
-          const int64_t blk = __ldg(btr + p);
-          const uint32_t hb = __ldg(reinterpret_cast<const unsigned short*>(a.cs) +
-                                    blk * a.n_kv + h);
-          w = hb | (hb << 16);
-        }
-        *reinterpret_cast<uint4*>(cb + kCBytes + e * 16) = make_uint4(w, w, w, w);
-      }
+    cp_async_commit();
+    if (cur.r != qr) {
+      load_qfrag(qf, a, cur.r, h, lane);
+      qr = cur.r;
     }
     int acc[1 + R][2][4];
-    item_dots(it, qf, a, lane, acc);
+    item_dots(cur, qf, a, lane, acc);
+    cp_async_wait<1>();                    // this tile's coordinates landed
     __syncwarp();
-    const int sl_r = __ldg(a.sl + it.r);
+    const uint8_t* cb = wbuf + ((t - t_lo) & 1) * kBuf;
+    const __half* csb = reinterpret_cast<const __half*>(cb + kCBytes);
+    const int sl_r = __ldg(a.sl + cur.r);
     constexpr float vdiv = (VB == 8) ? 1.f : 1.f / 16.f;
     float best[2] = {-INFINITY, -INFINITY};
     float Sv[2][2];
     float qsqv[2] = {0.f, 0.f};
     if (a.resid) {
       const int H = a.n_kv * a.G;
-      const float* qr_ = a.qsq + (int64_t)it.r * H + h * a.G;
+      const float* qr_ = a.qsq + (int64_t)cur.r * H + h * a.G;
       qsqv[0] = __ldg(qr_ + min(2 * c, a.G - 1));
       qsqv[1] = __ldg(qr_ + min(2 * c + 1, a.G - 1));
     }
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int pl = m + 8 * half;                 // page within the tile
-      const int p = it.p0 + pl;
-      const float mus = half ? __high2float(it.mus) : __low2float(it.mus);
+      const int p = cur.p0 + pl;
+      const float mus = half ? __high2float(cur.mus) : __low2float(cur.mus);
       float qt[2][R];
 #pragma unroll
       for (int jj = 0; jj < 2; ++jj) {
@@ -641,10 +658,12 @@ r8_score_kernel(QuadArgs a) {
 #pragma unroll
         for (int k = 0; k < R; ++k)
           qt[jj][k] = (float)(128 * acc[1 + k][0][idx] + acc[1 + k][1][idx]) *
-                      (qf.sq[jj] * vdiv) * it.vsf(half, k);
+                      (qf.sq[jj] * vdiv) * cur.vsf(half, k);
       }
-      float mx[2] = {-INFINITY, -INFINITY}, sm[2] = {0.f, 0.f};
-#pragma unroll 4
+      const float csp = half ? __high2float(csp_cur) : __low2float(csp_cur);
+      // token logits in the log2 domain: two passes (max, then sum)
+      float tk2[2][PG];
+#pragma unroll
       for (int tk = 0; tk < PG; ++tk) {
         const bool tv = p * PG + tk < sl_r;
         const uint8_t* row = cb + (pl * PG + tk) * RC;
@@ -660,31 +679,34 @@ r8_score_kernel(QuadArgs a) {
             code[k + 1] = (float)(b >> 4);
           }
         }
-        const float cs = __half2float(csb[pl * PG + tk]) * a.scale;
+        const float cs = (a.ctok ? __half2float(csb[pl * PG + tk]) : csp) * a.scale;
 #pragma unroll
         for (int jj = 0; jj < 2; ++jj) {
           float d = 0.f;
 #pragma unroll
           for (int k = 0; k < R; ++k) d += code[k] * qt[jj][k];
-          const float tok = tv ? d * cs : -INFINITY;
-          if (a.tokmax) {
-            mx[jj] = fmaxf(mx[jj], tok);
-          } else if (tok > mx[jj]) {
-            sm[jj] = sm[jj] * expf(mx[jj] - tok) + 1.f;
-            mx[jj] = tok;
-          } else if (tok > -INFINITY) {
-            sm[jj] += expf(tok - mx[jj]);
-          }
+          tk2[jj][tk] = tv ? d * cs * kL2e : -INFINITY;
         }
       }
       // CLSE: the out-of-subspace energy (|q|^2 - |q~|^2) * resid * coef
-      const float res = a.resid ? __half2float(a.resid[half ? it.rowb : it.rowa]) : 0.f;
+      const float res = a.resid ? __half2float(a.resid[half ? cur.rowb : cur.rowa]) : 0.f;
 #pragma unroll
       for (int jj = 0; jj < 2; ++jj) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int tk = 0; tk < PG; ++tk) mx = fmaxf(mx, tk2[jj][tk]);
+        float agg;
+        if (a.tokmax) {
+          agg = mx * kLn2;
+        } else {
+          float sm = 0.f;
+#pragma unroll
+          for (int tk = 0; tk < PG; ++tk) sm += exp2f(tk2[jj][tk] - mx);
+          agg = (mx + log2f(sm)) * kLn2;
+        }
         const int idx = 2 * half + jj;
         const float qmu = (float)(128 * acc[0][0][idx] + acc[0][1][idx]) * qf.sq[jj] *
                           mus * a.scale;
-        const float agg = a.tokmax ? mx[jj] : mx[jj] + logf(sm[jj]);
         float S = qmu + agg;
         if (a.resid) {
           float qh = 0.f;
@@ -698,21 +720,21 @@ r8_score_kernel(QuadArgs a) {
     }
     if (a.write_h) {
       // per-head scores and the per-head page maximum (the nrm fold's hmax)
-      float* base = a.score_h + ((int64_t)it.r * a.n_kv + h) * a.G * a.SHS;
-      const int pa = it.p0 + m, pb = pa + 8;
+      float* base = a.score_h + ((int64_t)cur.r * a.n_kv + h) * a.G * a.SHS;
+      const int pa = cur.p0 + m, pb = pa + 8;
 #pragma unroll
       for (int jj = 0; jj < 2; ++jj) {
         const int g = 2 * c + jj;
         float mxh = -INFINITY;
         if (g < a.G) {
-          if (it.va) { base[(int64_t)g * a.SHS + pa] = Sv[0][jj]; mxh = Sv[0][jj]; }
-          if (it.vb) { base[(int64_t)g * a.SHS + pb] = Sv[1][jj]; mxh = fmaxf(mxh, Sv[1][jj]); }
+          if (cur.va) { base[(int64_t)g * a.SHS + pa] = Sv[0][jj]; mxh = Sv[0][jj]; }
+          if (cur.vb) { base[(int64_t)g * a.SHS + pb] = Sv[1][jj]; mxh = fmaxf(mxh, Sv[1][jj]); }
         }
         mxh = fmaxf(mxh, __shfl_xor_sync(0xffffffffu, mxh, 4));
         mxh = fmaxf(mxh, __shfl_xor_sync(0xffffffffu, mxh, 8));
         mxh = fmaxf(mxh, __shfl_xor_sync(0xffffffffu, mxh, 16));
         if (m == 0 && g < a.G && mxh > -INFINITY)
-          atomic_max_float(a.hmax + ((int64_t)it.r * a.n_kv + h) * a.G + g, mxh);
+          atomic_max_float(a.hmax + ((int64_t)cur.r * a.n_kv + h) * a.G + g, mxh);
       }
     } else {
 #pragma unroll
@@ -720,20 +742,30 @@ r8_score_kernel(QuadArgs a) {
         float v = best[half];
         v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
         v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
-        const bool pv = half ? it.vb : it.va;
+        const bool pv = half ? cur.vb : cur.va;
         if (pv && c == 0)
-          a.score[((int64_t)it.r * a.n_kv + h) * a.MP + it.p0 + m + 8 * half] = v;
+          a.score[((int64_t)cur.r * a.n_kv + h) * a.MP + cur.p0 + m + 8 * half] = v;
       }
     }
+    __syncwarp();                          // buffer reused two tiles later
+    if (!more) break;
+    cur = nxt;
+    nxt = nn;
+    csp_cur = csp_nxt;
+    ++t;
   }
+  cp_async_wait<0>();
 }
 
 template <int D, int CB, int VB, int R = 8>
 int launch_r8(const QuadArgs& a, cudaStream_t st) {
   auto k = r8_score_kernel<D, R, VB, CB>;
+  constexpr int RC = R8Tok<R, CB>::RC;
+  const size_t smem = (size_t)kQuadWarps * 2 * (16 * 16 * RC + 16 * 16 * 2);
   static int ps = 0;
   if (ps == 0) {
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ps, k, kQuadWarps * 32, 0);
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ps, k, kQuadWarps * 32, smem);
     if (ps < 1) ps = 1;
   }
   const int heads = a.n_req * a.n_kv * a.G;
@@ -741,7 +773,7 @@ int launch_r8(const QuadArgs& a, cudaStream_t st) {
   int grid = num_sms() * ps;
   const int per = a.n_kv > kQuadWarps ? a.n_kv / kQuadWarps : 1;
   grid = (grid / per) * per;
-  if (int rc = launch_pdl(k, dim3(grid), dim3(kQuadWarps * 32), 0, st, a)) return rc;
+  if (int rc = launch_pdl(k, dim3(grid), dim3(kQuadWarps * 32), smem, st, a)) return rc;
   return launch_status();
 }
 
@@ -814,7 +846,7 @@ extern "C" int amass_quad_score(const void* q, int64_t q_stride_t,
       (reinterpret_cast<uintptr_t>(V) & 15) ||
       (reinterpret_cast<uintptr_t>(q8_ws) & 15))
     return AMASS_ERR_ARG;
-  QuadArgs a;
+  QuadArgs a{};
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.q_st = q_stride_t;
   a.q_sh = q_stride_h;

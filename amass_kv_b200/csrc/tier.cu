@@ -588,7 +588,7 @@ extern "C" int amass_tier_plan(const int32_t* page_table,
   const int max_miss = amass_tier_plan_capacity(hot_slots);
   const size_t smem = (size_t)S2 * 8 + (size_t)hot_slots * 8 +
                       (size_t)(kPlanMaxReq + 1) * 4 + (size_t)max_miss * 4;
-  PlanArgs a;
+  PlanArgs a{};
   a.tab = page_table; a.cnt = page_cnt; a.bt = block_table;
   a.bt_stride = bt_stride; a.sl = seq_lens; a.p2s = page2slot;
   a.s2p = slot2page; a.lru = lru_clock; a.clock = clock; a.overflow = overflow;
@@ -643,7 +643,7 @@ extern "C" int amass_tier_fetch(const int32_t* fetch_list,
                        reinterpret_cast<uintptr_t>(pool_k_dev) |
                        reinterpret_cast<uintptr_t>(k_pool);
   if ((al & 15) || (svb % 8) || (svt % 8) || (svh % 8)) return AMASS_ERR_ARG;
-  FetchArgs a;
+  FetchArgs a{};
   a.flist = fetch_list; a.fcnt = fetch_cnt;
   a.hot = static_cast<int16_t*>(hot); a.pool = static_cast<int16_t*>(pool_dev);
   a.valid = pool_valid; a.vbo = vbo;
@@ -683,7 +683,7 @@ extern "C" int amass_tier_invalidate(const int32_t* block_table,
   if (!block_table || !seq_lens || !query_start_loc || !page2slot ||
       !slot2page || !pool_valid)
     return AMASS_ERR_ARG;
-  InvalArgs a;
+  InvalArgs a{};
   a.bt = block_table; a.bt_stride = bt_stride; a.sl = seq_lens;
   a.qsl = query_start_loc; a.p2s = page2slot; a.s2p = slot2page;
   a.valid = pool_valid; a.n_req = n_req; a.L = num_layers; a.n_kv = n_kv;

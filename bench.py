@@ -37,6 +37,7 @@ METRIC = "sparse decode µs/layer/step & HBM TB/s frac, B=64 ctx=32K " \
 UNIT = "us/layer/step"
 N_REQ, N_KV, G, D, PAGE = 64, 8, 4, 128, 16
 RANK_Q, V_BITS, BUDGET, COMBINE = 2, 4, 0.05, "nrm"
+SCORER = "quad"                     # --scorer: quad (headline) or clse
 B_SUM = D + 2 + D * RANK_Q // 2 + 2 * RANK_Q + 2 * RANK_Q     # 266 B
 
 
@@ -143,6 +144,20 @@ class Batch:
         st.quad_mu, st.mu_scale = b["quad_mu"], b["mu_scale"]
         st.quad_V, st.V_scale, st.quad_sig2 = (b["quad_V"], b["V_scale"],
                                                b["quad_sig2"])
+        self.clse = SCORER == "clse"
+        if self.clse:
+            # CLSE extras of the same blocks: int4 rank-2 token coordinates
+            # (one byte per token), per-token fp16 scales, residual energy
+            gd = torch.Generator(device=dev).manual_seed(seed + 7)
+            Lx, NBx = b["quad_mu"].shape[0], b["quad_mu"].shape[1]
+            st.quad_c = torch.randint(-128, 128, (Lx, NBx, n_kv, PAGE, 1),
+                                      generator=gd, device=dev,
+                                      dtype=torch.int8)
+            st.c_scale = (torch.rand((Lx, NBx, n_kv, PAGE), generator=gd,
+                                     device=dev) * 0.05 + 0.01).half()
+            st.quad_resid = (torch.rand((Lx, NBx, n_kv), generator=gd,
+                                        device=dev) * 50 + 10).half()
+            st.c_bits, st.c_grain = 4, "token"
         ensure_stage_b_buffers(st, dev, 128)
         self.st = st
         self.scale = 1.0 / math.sqrt(D)
@@ -162,7 +177,11 @@ class Batch:
         nrm = COMBINE == "nrm"
         if k == 0:
             S.derive_page_params(st, self.sl, N_REQ)
-            S._score_launch(st, l, q, self.bt, N_REQ, self.scale, nrm)
+            if self.clse:
+                S.clse_score_cuda(st, l, q, self.bt, self.sl, N_REQ,
+                                  self.scale)
+            else:
+                S._score_launch(st, l, q, self.bt, N_REQ, self.scale, nrm)
         elif k == 1:
             S.select_pages(st, N_REQ, from_score_h=nrm)
         elif self.gather is not None:
@@ -188,7 +207,8 @@ class Batch:
         nsh = np.maximum(self.st.n_sel_hi.cpu().numpy().astype(np.int64), 0)
         cnt = self.st.page_cnt.cpu().numpy().astype(np.int64)
         qo = N_REQ * self.n_kv * G * D * 2
-        score_b = int((self.n_kv * nsh * B_SUM + 4 * nsh).sum()) + qo // 2
+        b_sum = B_SUM + (PAGE * 1 + 2 * PAGE + 2 if self.clse else 0)
+        score_b = int((self.n_kv * nsh * b_sum + 4 * nsh).sum()) + qo // 2
         kv_b = int(cnt.sum()) * 2 * PAGE * D * 2
         decode_b = kv_b + qo
         return dict(score=score_b, decode=decode_b,
@@ -364,7 +384,9 @@ def run_gpu(args):
                 "workload": "C3: ragged B=64 decode, ctx log-uniform 4K-64K "
                             f"(realized mean {alg[0]['mean_ctx']:.0f}), "
                             "Llama-3.1-8B attn (32q/8kv, d128, bf16, page 16),"
-                            " quad r'=2 int4-V nrm, budget 0.05",
+                            + (" clse r'=2 int4-V int4 token coords nrm"
+                               if SCORER == "clse" else " quad r'=2 int4-V nrm")
+                            + ", budget 0.05",
                 "batch_per_gpu": N_REQ,
                 "requests_per_step": N_REQ if kvmode else N_REQ * world,
                 "parallelism": (f"kv-head-sharded x{world} ({N_KV // world} kv "
@@ -875,6 +897,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--pps-min", type=int, default=None,
                     help="decode pages-per-chunk floor (default: by batch)")
+    ap.add_argument("--scorer", default="quad", choices=["quad", "clse"],
+                    help="Stage-A scorer of the c3 step: quad (the headline) "
+                         "or clse (the reference config's default score)")
     ap.add_argument("--shard", default="seq", choices=["seq", "kv"],
                     help="multi-GPU layout: seq = each rank its own batch "
                          "(weak scaling, no collective); kv = one batch, kv "
@@ -895,6 +920,7 @@ def main():
                          "for profiling captures)")
     args = ap.parse_args()
     globals()["N_REQ"] = args.requests
+    globals()["SCORER"] = args.scorer
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         run_reference(args)
