@@ -31,6 +31,9 @@ _SIGS = {
     "amass_clse_score": [_P, _L, _L, _P, _P, _P, _P, _P, _P, _I, _P, _P, _L,
                          _P, _P, _P, _P, _L, _P, _P, _P, _P, _F, _I, _I, _I,
                          _I, _I, _I, _I, _I, _I, _I, _P],
+    "amass_summarize_pages": [_P, _I, _L, _L, _L, _P, _I, _I, _I, _I, _I, _I,
+                              _I, _P, _P, _P, _P, _I, _I, _P, _P, _I, _P, _P,
+                              _I, _I, _P, _P],
     "amass_nrm_combine": [_P, _L, _P, _P, _P, _I, _I, _I, _I, _P],
     "amass_topb_select": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "amass_select_pages": [_P, _L, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I,

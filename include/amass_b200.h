@@ -165,6 +165,33 @@ int amass_clse_score(const void* q, int64_t q_stride_t, int64_t q_stride_h,
                      int page, int rank, int v_bits, int c_bits, int max_pages,
                      int write_h, void* stream);
 
+/* Page summary build -- replaces the page-finalize summarizers
+ * selection/build.py:396-452 (_page_eigh, _r8_write) and
+ * selection/quad_build.py:37-84 (_quad_write): for every layer l of
+ * k_layers[0..n_layers) (each a key cache addressed as
+ * base + block*k_sb + token*k_st + head*k_sh, bf16) and every block in
+ * blocks[0..n_blocks), per kv-head: page mean, the top `rank` eigenpairs of
+ * the 16 x 16 Gram of the centred keys (ascending order, eigenvalues clamped
+ * >= 1e-10), Vk = dc^T U / sqrt(lambda), quantised and written at slab layer
+ * layer0 + l:  mu (NB, n_kv, d) int8 + mu_scale fp16; V (NB, n_kv, d, rv)
+ * int8 or packed int4 + V_scale (NB, n_kv, rank) per column (v_tensor = 0)
+ * or one scale (1); sig2 (NB, n_kv, rank) fp16 or NULL; tag (NB, n_kv,
+ * tagw) bf16 or NULL.  With c != NULL also the coordinates c = U sqrt(lambda)
+ * (NB, n_kv, 16, rc) and c_scale: c_mode 0 = per token (.., 16), 1 = one
+ * scale per page repeated over (.., 16), 2 = one per page (..); resid
+ * (NB, n_kv) fp16 = sum K^2 - 16 |mu|^2 - sum lambda, or NULL.  Slabs are the
+ * whole layer-major arrays (first layer at index 0).  Eigenvectors are
+ * unique up to sign.  head_dim in {64, 128}, page = 16, rank <= 8,
+ * n_layers <= 128. */
+int amass_summarize_pages(const void* const* k_layers, int n_layers,
+                          int64_t k_sb, int64_t k_st, int64_t k_sh,
+                          const int32_t* blocks, int n_blocks, int layer0,
+                          int num_blocks, int n_kv, int head_dim, int page,
+                          int rank, int8_t* mu, void* mu_scale, int8_t* V,
+                          void* V_scale, int v_bits, int v_tensor, void* sig2,
+                          void* tag, int tagw, int8_t* c, void* c_scale,
+                          int c_bits, int c_mode, void* resid, void* stream);
+
 /* sparse_paged_decode -- replaces attention/decode_cuda.py:1376-1465
  * (Triton golden attention/decode.py:247-304 + merge.py:21-50).
  * K/V tiles are addressed as base + blk*s_b + tok*s_t + kv*s_h (elements,

@@ -401,6 +401,74 @@ def r8_score(q, mu, mu_s, Vk, Vk_s, c, c_s, block_table, seq_lens, n_sel_hi,
 
 
 # --------------------------------------------------------------------------- #
+# page summary build (selection/build.py:297-452, quad_build.py:37-84)        #
+# --------------------------------------------------------------------------- #
+def _quant_np(x, axis, bits):
+    """code = round_half_even(x / s), s = max(amax(|x|)/lvl, 1e-8) in fp32
+    (``build.py:297-302``)."""
+    lvl = F32((1 << (bits - 1)) - 1)
+    s = np.maximum(np.abs(x).max(axis=axis, keepdims=True) / lvl, F32(1e-8))
+    s = s.astype(F32)
+    code = np.clip(np.rint(x / s), -lvl, lvl).astype(np.int8)
+    return code, s
+
+
+def page_summary(Kp, r: int, *, v_bits: int = 8, v_grain: str = "col",
+                 coords: str = "none", c_bits: int = 8,
+                 c_grain: str = "token", tagw: int = 8):
+    """Summary of finalized pages Kp (N, page, n_kv, d) (float32 holding
+    bf16 values), per (page, kv-head) (``build.py:396-452`` _page_eigh +
+    ``quad_build.py:56-84`` _quad_write):
+
+        mu = mean_t K;  dc = K - mu;  Gm = dc dc^T (page x page);  eigh(Gm)
+        S2r = top-r eigenvalues (ascending order, clamped >= 1e-10)
+        U8 = their eigenvectors;  Vk = dc^T U8 / sqrt(S2r)        (d, r)
+        c = U8 * sqrt(S2r)  (page, r);  resid = trace - sum S2r  (CLSE)
+
+    Eigenvectors are unique up to sign; this restatement uses numpy's fp64
+    eigh, so compare sign-invariant quantities.  Returns a dict of quantised
+    slabs (reference layouts) and the fp32 factors."""
+    N, page, n_kv, d = Kp.shape
+    K = Kp.transpose(0, 2, 1, 3).astype(F32)                   # (N,kv,t,d)
+    mu = K.mean(axis=2)
+    dc = K - mu[:, :, None, :]
+    Gm = np.einsum("nktd,nksd->nkts", dc.astype(np.float64),
+                   dc.astype(np.float64))
+    S2, U = np.linalg.eigh(Gm)                                 # ascending
+    S2r = np.maximum(S2[..., -r:], 1e-10).astype(F32)
+    U8 = U[..., -r:].astype(F32)
+    S8 = np.sqrt(S2r)
+    Vk = np.einsum("nktd,nktr->nkdr", dc, U8) / S8[:, :, None, :]
+    out = {}
+    out["mu_code"], s = _quant_np(mu, -1, 8)
+    out["mu_s"] = s[..., 0].astype(np.float16)
+    if v_grain == "col":
+        vc, vs = _quant_np(Vk, -2, v_bits)
+        vs = vs[:, :, 0, :]
+    else:
+        vc, vs = _quant_np(Vk, (-2, -1), v_bits)
+        vs = np.broadcast_to(vs[:, :, 0, :], Vk.shape[:2] + (r,))
+    out["V_code"] = pack_int4(vc) if v_bits == 4 else vc
+    out["V_s"] = vs.astype(np.float16)
+    out["sig2"] = S2r.astype(np.float16)
+    out["tag"] = Kp[:, page - 1, :, :tagw]
+    out["factors"] = dict(mu=mu, S2r=S2r, Vk=Vk, U8=U8)
+    if coords != "none":
+        c = U8 * S8[:, :, None, :]                             # (N,kv,t,r)
+        if c_grain == "token":
+            cc, cs = _quant_np(c, -1, c_bits)
+            cs = cs[..., 0]                                    # (N,kv,t)
+        else:
+            cc, cs = _quant_np(c, (-2, -1), c_bits)
+            cs = cs[..., 0, 0]                                 # (N,kv)
+        out["c_code"] = pack_int4(cc) if c_bits == 4 else cc
+        out["c_s"] = cs.astype(np.float16)
+        trace = (K * K).sum(axis=(2, 3)) - page * (mu * mu).sum(-1)
+        out["resid"] = np.maximum(trace - S2r.sum(-1), 0).astype(np.float16)
+    return out
+
+
+# --------------------------------------------------------------------------- #
 # CLSE page score (selection/quad_score.py:156-273)                           #
 # --------------------------------------------------------------------------- #
 def clse_score_h(q, mu, mu_s, V, V_s, c, c_s, resid, block_table, seq_lens,

@@ -44,6 +44,7 @@ from amass.attention.decode import (ResidentVSource,  # noqa: E402
                                     sparse_paged_decode_batched)
 from amass.backend._selection_bridge import _nucleus_b  # noqa: E402
 from amass.tier.residency import Residency  # noqa: E402
+from amass.selection.quad_build import quad_build_tail  # noqa: E402
 from amass.tier.decode_mem import mem_decode_ptrsel  # noqa: E402
 
 
@@ -235,6 +236,47 @@ def gen_clse(name, case, *, budget, combine):
     print(name, "cnt", st.page_cnt.tolist())
 
 
+def gen_build(name, *, seed, n_req, n_kv, d, ctxs, L, r, v_bits, coords,
+              c_bits=4, c_grain="token"):
+    """The reference's batched tail rebuild (quad_build_tail: the last
+    finalized page of every request, every layer) on seeded K caches."""
+    rng = np.random.default_rng(seed)
+    page = 16
+    npg = [(c + page - 1) // page for c in ctxs]
+    NB = sum(npg) + 4
+    perm = rng.permutation(NB).astype(np.int32)
+    MP = max(npg)
+    bt = np.zeros((n_req, MP), np.int32)
+    o = 0
+    for i, n in enumerate(npg):
+        bt[i, :n] = perm[o:o + n]
+        o += n
+    K = rng.standard_normal((L, NB, page, n_kv, d)).astype(np.float32)
+    K[:, :, :, :, :3] *= 4.0                                  # anisotropy
+    Kb = t_bf16(K)
+    st = QuadState("cpu", num_layers=L, num_blocks=NB, n_kv=n_kv, G=4,
+                   head_dim=d, page=page, max_reqs=n_req, max_pages=MP,
+                   rank=r, budget=0.1, v_bits=v_bits, coords=coords,
+                   c_bits=c_bits, c_grain=c_grain)
+    sl = torch.tensor(ctxs, dtype=torch.int32)
+    n = quad_build_tail(st, [Kb[l] for l in range(L)],
+                        torch.from_numpy(bt), sl, n_req)
+    extra = {}
+    if coords == "lse":
+        extra = dict(c=st.quad_c.numpy(), c_s=st.c_scale.numpy(),
+                     resid=st.quad_resid.numpy())
+    np.savez_compressed(
+        os.path.join(HERE, name + ".npz"), K=bf16_bits(Kb), block_table=bt,
+        seq_lens=np.asarray(ctxs, np.int32),
+        meta=np.array([L, NB, n_kv, d, r, v_bits, c_bits,
+                       1 if c_grain == "token" else 0,
+                       1 if coords == "lse" else 0], np.int64),
+        mu=st.quad_mu.numpy(), mu_s=st.mu_scale.numpy(),
+        V=st.quad_V.numpy(), V_s=st.V_scale.numpy(),
+        sig2=st.quad_sig2.numpy(), tag=bf16_bits(st.quad_tag), **extra)
+    print(name, "pages built", n)
+
+
 def gen_tier(name, case, *, budget, hot_slots=10, steps=3, seed=5):
     """Residency gather over several steps with forced eviction, staged and
     flushed sources, then the ptr-select tiered decode."""
@@ -383,6 +425,11 @@ def main():
     cl3 = make_clse_case(9, n_req=2, n_kv=2, G=4, d=128, ctxs=(500, 377),
                          r=4, v_bits=8, c_bits=8, c_grain="token")
     gen_clse("clse_r4_i8_tok_max", cl3, budget=0.1, combine="max")
+    gen_build("build_quad_i4", seed=21, n_req=3, n_kv=2, d=128,
+              ctxs=[100, 257, 16], L=2, r=2, v_bits=4, coords="none")
+    gen_build("build_clse_i8", seed=22, n_req=2, n_kv=2, d=64,
+              ctxs=[300, 48], L=2, r=4, v_bits=8, coords="lse", c_bits=8,
+              c_grain="page")
 
 
 if __name__ == "__main__":

@@ -239,3 +239,75 @@ def test_clse_score(name):
                              sink=1, MP=MP)
     assert np.array_equal(tab, z["page_table"])
     assert np.array_equal(cnt, z["page_cnt"])
+
+
+def _tail_pages(z):
+    L, NB, n_kv, d, r, vb, cb, ctok, lse = [int(x) for x in z["meta"]]
+    sl = z["seq_lens"]
+    fin1 = np.maximum(sl // 16 - 1, 0)
+    blocks = z["block_table"][np.arange(len(sl)), fin1]
+    return (L, NB, n_kv, d, r, vb, cb, ctok, lse), blocks
+
+
+def _deq_cols(code, s, r, bits):
+    """(..., d, rv) codes + (..., r) scales -> (..., d, r) float32"""
+    return O.unpack_codes(code, r, bits) * s.astype(np.float32)[..., None, :]
+
+
+def check_summary(z, got, l, blocks):
+    """Sign-invariant comparison of one layer's built summaries (``got``:
+    dict of the build's slabs for that layer) with the reference's."""
+    (L, NB, n_kv, d, r, vb, cb, ctok, lse), _ = _tail_pages(z)
+    for b in blocks:
+        assert np.abs(got["mu"][b].astype(int) - z["mu"][l, b].astype(int)).max() <= 1
+        np.testing.assert_allclose(got["mu_s"][b].astype(np.float32),
+                                   z["mu_s"][l, b].astype(np.float32), rtol=2e-3)
+        np.testing.assert_allclose(got["sig2"][b].astype(np.float32),
+                                   z["sig2"][l, b].astype(np.float32),
+                                   rtol=5e-3, atol=1e-2)
+        vr = _deq_cols(z["V"][l, b], z["V_s"][l, b], r, vb)       # (kv,d,r)
+        vg = _deq_cols(got["V"][b], got["V_s"][b], r, vb)
+        sgn = np.sign((vr * vg).sum(axis=1, keepdims=True))
+        lvl = 7.0 if vb == 4 else 127.0
+        tol = 1.5 * z["V_s"][l, b].astype(np.float32).max() + 1e-3
+        assert np.abs(vr - sgn * vg).max() <= tol, (l, b)
+        assert np.array_equal(got["tag"][b], z["tag"][l, b])
+        if lse:
+            cr = O.unpack_codes(z["c"][l, b], r, cb).astype(np.float32)
+            cg = O.unpack_codes(got["c"][b], r, cb).astype(np.float32)
+            csr = z["c_s"][l, b].astype(np.float32)
+            csg = got["c_s"][b].astype(np.float32)
+            if not ctok:
+                csr, csg = csr[..., None], csg[..., None]
+            cr, cg = cr * csr[..., None], cg * csg[..., None]      # (kv,t,r)
+            sgc = np.sign((cr * cg).sum(axis=1, keepdims=True))
+            assert np.abs(cr - sgc * cg).max() <= 1.5 * csr.max() + 1e-3
+            np.testing.assert_allclose(got["resid"][b].astype(np.float32),
+                                       z["resid"][l, b].astype(np.float32),
+                                       rtol=5e-3, atol=5e-2)
+
+
+@pytest.mark.parametrize("name", ["build_quad_i4", "build_clse_i8"])
+def test_page_summary_vs_reference_build(name):
+    z = load_golden(name)
+    meta, blocks = _tail_pages(z)
+    L, NB, n_kv, d, r, vb, cb, ctok, lse = meta
+    K = bits_to_f32(z["K"])                                       # (L,NB,t,kv,d)
+    for l in range(L):
+        s = O.page_summary(K[l][blocks], r, v_bits=vb,
+                           coords="lse" if lse else "none", c_bits=cb,
+                           c_grain="token" if ctok else "page")
+        got = {"mu": {}, "mu_s": {}, "sig2": {}, "V": {}, "V_s": {},
+               "tag": {}, "c": {}, "c_s": {}, "resid": {}}
+        for i, b in enumerate(blocks):
+            got["mu"][b] = s["mu_code"][i]
+            got["mu_s"][b] = s["mu_s"][i]
+            got["sig2"][b] = s["sig2"][i]
+            got["V"][b] = s["V_code"][i]
+            got["V_s"][b] = s["V_s"][i]
+            got["tag"][b] = (s["tag"][i].view(np.uint32) >> 16).astype(np.uint16).view(np.int16)
+            if lse:
+                got["c"][b] = s["c_code"][i]
+                got["c_s"][b] = s["c_s"][i]
+                got["resid"][b] = s["resid"][i]
+        check_summary(z, got, l, blocks)
