@@ -885,6 +885,81 @@ def run_select_workload(args):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------- #
+# summary build (page finalize): the C3 batch, Llama-3.1-8B's 32 layers       #
+# --------------------------------------------------------------------------- #
+def run_build(args):
+    """Timing of the page-finalize summary build at the C3 batch: the tail
+    rebuild (every request's last finalized page, all 32 layers, one launch)
+    and the bulk build of every finalized page of one layer (the prefill
+    case), quad r'=2 int4-V; CUDA events around CUDA-graph replays."""
+    import torch
+    from amass_kv_b200 import summaries as SU
+    from amass_kv_b200.selection import QuadState
+    from amass_kv_b200.workloads import c3_contexts
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    L = 32
+    ctxs = c3_contexts(1000, N_REQ)
+    npg = [(int(c) + PAGE - 1) // PAGE for c in ctxs]
+    NB = sum(npg) + 64
+    MP = max(npg)
+    g = torch.Generator(device="cpu").manual_seed(3)
+    perm = torch.randperm(NB, generator=g).to(torch.int32)
+    bt = torch.zeros(N_REQ, MP, dtype=torch.int32)
+    o = 0
+    for i, n in enumerate(npg):
+        bt[i, :n] = perm[o:o + n]
+        o += n
+    bt = bt.to(dev)
+    sl = torch.as_tensor(np.asarray(ctxs), dtype=torch.int32, device=dev)
+    # one shared random key cache viewed as 32 layers (summaries depend only
+    # on the page bytes; distinct layers would only cost memory)
+    K = torch.randn((NB, PAGE, N_KV, D), device=dev).to(torch.bfloat16)
+    st = QuadState(dev, num_layers=L, num_blocks=NB, n_kv=N_KV, G=G,
+                   head_dim=D, page=PAGE, max_reqs=N_REQ, max_pages=MP,
+                   rank=RANK_Q, budget=BUDGET, v_bits=V_BITS, combine=COMBINE)
+    Ks = [K] * L
+    stb = QuadState(dev, num_layers=1, num_blocks=NB, n_kv=N_KV, G=G,
+                    head_dim=D, page=PAGE, max_reqs=N_REQ, max_pages=MP,
+                    rank=RANK_Q, budget=BUDGET, v_bits=V_BITS, combine=COMBINE)
+    res = {}
+    for name, fn in (("tail_all_layers", lambda: SU.quad_build_tail(
+                          st, Ks, bt, sl, N_REQ)),
+                     ("bulk_one_layer", lambda: SU.quad_build_bulk(
+                          stb, [K], bt, sl, N_REQ, MP))):
+        fn()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            fn()
+        for _ in range(3):
+            gr.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(
+            enable_timing=True)
+        n = max(args.steps // 10, 5)
+        e0.record()
+        for _ in range(n):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        res[name] = round(e0.elapsed_time(e1) / n * 1e3, 2)
+    fin = sum(int(c) // PAGE for c in ctxs)
+    line = {"metric": "page summary build us (C3 batch)",
+            "value": res["tail_all_layers"], "unit": "us/finalize-step",
+            "higher_is_better": False, "dtype": "f32 (eigh), int8/int4 out",
+            "data": "synthetic (seeded; BASELINE C3 shapes)",
+            "config": {"workload": "quad r'=2 int4-V summaries; tail = last "
+                       "finalized page of 64 requests x 8 kv-heads x 32 "
+                       f"layers ({N_REQ * N_KV * L} page-heads); bulk = all "
+                       f"{fin} finalized pages x 8 kv-heads of one layer"},
+            "bulk_one_layer_us": res["bulk_one_layer"],
+            "page_heads_per_s_bulk": round(fin * N_KV / (res["bulk_one_layer"]
+                                                         * 1e-6), 0)}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -908,7 +983,7 @@ def main():
                     help="kv mode output exchange: merge kernel stores to "
                          "every rank over NVLink, or NCCL all-gather")
     ap.add_argument("--workload", default="c3",
-                    choices=["c3", "c2", "c4", "c5"],
+                    choices=["c3", "c2", "c4", "c5", "build"],
                     help="c3 = the headline resident decode (default); c2 = "
                          "batch-1 coverage; c4 = r8 scorer + Jaccard vs quad; "
                          "c5 = the mem-v tiered decode")
@@ -928,6 +1003,8 @@ def main():
         run_c5(args)
     elif args.workload in ("c2", "c4"):
         run_select_workload(args)
+    elif args.workload == "build":
+        run_build(args)
     else:
         run_gpu(args)
 
