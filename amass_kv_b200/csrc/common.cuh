@@ -50,6 +50,17 @@ inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block,
              : AMASS_ERR_CUDA;
 }
 
+// Kernel attributes are per device: true the first time this is called for
+// the current device with this mask (one bit per device id).
+inline bool first_on_device(unsigned long long& mask) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (mask & bit) return false;
+  mask |= bit;
+  return true;
+}
+
 inline int num_sms() {
   static int sms = 0;
   if (sms == 0) {

@@ -482,11 +482,10 @@ int launch_decode(const DecArgs& a, cudaStream_t st) {
   const size_t smem = decode_smem<D, NST>(a.G, a.units);
   if (smem > 220 * 1024) return AMASS_ERR_UNSUPPORTED;
   auto kern = decode_kernel<D, NST, TIER>;
-  static int configured = 0;
-  if (!configured) {
+  static unsigned long long configured = 0;
+  if (first_on_device(configured)) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          220 * 1024);
-    configured = 1;
   }
   int per_sm = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecThreads, smem);

@@ -763,8 +763,10 @@ int launch_r8(const QuadArgs& a, cudaStream_t st) {
   constexpr int RC = R8Tok<R, CB>::RC;
   const size_t smem = (size_t)kQuadWarps * 2 * (16 * 16 * RC + 16 * 16 * 2);
   static int ps = 0;
-  if (ps == 0) {
+  static unsigned long long attr = 0;
+  if (first_on_device(attr))
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (ps == 0) {
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ps, k, kQuadWarps * 32, smem);
     if (ps < 1) ps = 1;
   }

@@ -516,11 +516,10 @@ template <bool FOLD, bool LIN, bool COV>
 int launch_select(const SelArgs& a, int units, cudaStream_t st) {
   const size_t smem = (size_t)a.MP * sizeof(float);
   auto k = select_kernel<FOLD, LIN, COV>;
-  static int configured = 0;
-  if (!configured) {
+  static unsigned long long configured = 0;
+  if (first_on_device(configured)) {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          kMaxSmem);
-    configured = 1;
   }
   if (int rc = launch_pdl(k, dim3(units), dim3(kSelThreads), smem, st, a)) return rc;
   return launch_status();
@@ -576,11 +575,10 @@ extern "C" int amass_nrm_combine(const float* score_h, int64_t sh_stride,
   a.G = G;
   a.MP = max_pages;
   const size_t smem = (size_t)max_pages * sizeof(float);
-  static int configured = 0;
-  if (!configured) {
+  static unsigned long long configured = 0;
+  if (first_on_device(configured)) {
     cudaFuncSetAttribute(nrm_combine_kernel,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
-    configured = 1;
   }
   if (int rc = launch_pdl(nrm_combine_kernel, dim3(n_req * n_kv),
                           dim3(kSelThreads), smem,

@@ -398,13 +398,12 @@ extern "C" int amass_summarize_pages(
   const int grid = (int)std::min<long long>((items + kSumWarps - 1) / kSumWarps,
                                             (long long)num_sms() * 8);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  static int conf = 0;                 // both variants, set once
-  if (!conf) {
+  static unsigned long long conf = 0;  // both variants, once per device
+  if (first_on_device(conf)) {
     cudaFuncSetAttribute(summary_kernel<128>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaFuncSetAttribute(summary_kernel<64>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    conf = 1;
   }
   auto kern = head_dim == 128 ? summary_kernel<128> : summary_kernel<64>;
   if (int rc = launch_pdl(kern, dim3(grid), dim3(kSumWarps * 32), smem, st, a))

@@ -605,12 +605,11 @@ extern "C" int amass_tier_plan(const int32_t* page_table,
                             a))
       return rc;
   }
-  static int configured = 0;
-  if (!configured) {
+  static unsigned long long configured = 0;
+  if (first_on_device(configured)) {
     cudaFuncSetAttribute(tier_plan_kernel,
                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)kPlanSmem);
-    configured = 1;
   }
   if (int rc = launch_pdl(tier_plan_kernel, dim3(n_kv), dim3(kPlanThreads),
                           smem, st, a))
