@@ -63,15 +63,12 @@ def ensure_stage_b_buffers(st, device, split: int = DEFAULT_SPLIT) -> None:
 
 
 def pps_min_for(n_req: int) -> int:
-    """Minimum pages per chunk: small for tiny batches (more chunks in
-    flight), larger once the batch fills the machine (fewer chunk epilogues
-    and partials; measured on B200 at the C3 batch: 8 -> 88 us, 16 -> 73 us,
-    32 -> 65 us for decode + merge)."""
-    if n_req <= 2:
-        return 4
-    if n_req < 16:
-        return 8
-    return 32 if n_req >= 32 else 16
+    """Minimum pages per chunk.  32 at every batch size measured on B200:
+    at the C3 batch (64 requests) 8 -> 88 us, 16 -> 73 us, 32 -> 65 us for
+    decode + merge; at batch 1 with coverage 0.95 (~830 pages per unit)
+    4 -> 44.3 us, 16 -> 34.9 us, 32 -> 28.6 us, 64 -> 28.7 us (fewer chunk
+    epilogues and partials to merge)."""
+    return 32
 
 
 def sparse_paged_decode_batched_cuda(q, kv_cache, block_table, seq_lens, st,

@@ -784,7 +784,8 @@ def run_select_workload(args):
                            from_score_h=(s_ is stq and COMBINE == "nrm"))
         else:
             A.sparse_paged_decode_batched_cuda(q, kv, bt, sl, s_, out,
-                                               scale=scale)
+                                               scale=scale,
+                                               pps_min=args.pps_min)
 
     for k in range(3):
         stage(k)
