@@ -49,6 +49,11 @@ _SIGS = {
                                    _I, _P, _I, _I, _L, _L, _F, _I, _I, _I,
                                    _I, _I, _I, _P],
     "amass_peer_barrier": [_P, _I, _I, _P, _P, _P],
+    "amass_staging_begin_step": [_P, _L, _P, _P, _I, _I, _I, _P, _P, _P, _P,
+                                 _P, _P, _P, _P, _I, _P, _P, _L, _L, _L, _L,
+                                 _P, _P, _P, _I, _I, _I, _I, _I, _P],
+    "amass_staging_scatter": [_P, _L, _L, _P, _L, _L, _P, _P, _P, _L, _L, _L,
+                              _I, _I, _I, _I, _P],
     "amass_host_device_pointer": [_P, _P],
     "amass_tier_plan_capacity": [_I],
     "amass_tier_plan": [_P, _P, _P, _L, _P, _P, _P, _P, _P, _P, _P, _P, _P,

@@ -700,3 +700,337 @@ extern "C" int amass_host_device_pointer(void* host, void** dev) {
   return cudaHostGetDevicePointer(dev, host, 0) == cudaSuccess ? AMASS_OK
                                                                : AMASS_ERR_CUDA;
 }
+
+// ===========================================================================
+// Staging lifecycle of the tier's write side (reference tier/staging.py:
+// 51-232, begin_step :312-346, scatter_kv :348-367).  Under mem-v the V of
+// the tokens written each step lands in a bounded VRAM staging pool
+// v_pool (L, NV, page, n_kv, d); once a page is complete its V is flushed to
+// the pinned pool and the staging block recycled through a free stack.
+// begin_step runs, in this order (flush-before-reuse):
+//   1. v_slot_mapping[:n_tokens] = -1
+//   2. vflush_clear  pages written this step lose their flushed latch
+//   3. collect       complete pages written by earlier steps that hold a
+//                    staging block: claim the flushed latch (first claim
+//                    enters the flush list (blk, vb), at most max_flush) and
+//                    free the staging block (pushed on the free stack)
+//   4. flush copy    v_pool[l, vb] -> pinned pool[l, blk] for every layer and
+//                    kv-head, pool_valid = 1 (bit copies)
+//   5. valloc        a staging block for every page written this step that
+//                    has none (pop the free stack; underflow sets overflow)
+//   6. vslot         v_slot_mapping[token] = vb * page + pos % page, or -1
+// Requests with seq_len <= 0 or no new tokens are skipped throughout.
+// ===========================================================================
+namespace amass {
+namespace {
+
+struct StgArgs {
+  const int32_t* bt;
+  int64_t bt_stride;
+  const int32_t* sl;
+  const int32_t* qsl;     // (n_req + 1,)
+  int n_req, n_tokens, page;
+  int64_t* vslot;         // (max_tokens,)
+  int32_t* vbo;           // (NB,)
+  int32_t* vfl;           // (NB,) flushed latch
+  int32_t* stack;         // (NV,)
+  int32_t* top;           // (1,)
+  int32_t* flist;         // (MAXF, 2)
+  int32_t* fcnt;          // (1,)
+  int32_t* ovf;           // (1,)
+  int MAXF;
+  const int16_t* vpool;   // (L, NV, page, n_kv, d) at svl/svb/svt/svh
+  const int16_t* kpool;   // mem-kv (or null)
+  int64_t svl, svb, svt, svh;
+  int16_t* pool;          // pinned (L, NB, n_kv, page, d) device view
+  int16_t* poolk;
+  int8_t* valid;          // (L, n_kv, NB)
+  int L, NB, n_kv;
+};
+
+AMASS_DEV void req_span(const StgArgs& a, int r, int& sl, int& ql) {
+  sl = a.sl[r];
+  ql = a.qsl[r + 1] - a.qsl[r];
+}
+
+__global__ void stg_vflush_clear_kernel(StgArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int r = blockIdx.x;
+  int sl, ql;
+  req_span(a, r, sl, ql);
+  if (sl <= 0 || ql <= 0) return;
+  const int p0 = (sl - ql) / a.page, p1 = (sl - 1) / a.page;
+  for (int p = p0 + (int)threadIdx.x; p <= p1; p += blockDim.x)
+    a.vfl[a.bt[(int64_t)r * a.bt_stride + p]] = 0;
+}
+
+constexpr int kStgThreads = 1024;
+
+// Block-wide exclusive scan of a 0/1 flag (kStgThreads threads); *tot gets
+// the block count.  Ends with a barrier.
+AMASS_DEV int stg_scan(int v, int* wsum, int* tot) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned bal = __ballot_sync(0xffffffffu, v != 0);
+  if (lane == 0) wsum[warp] = __popc(bal);
+  __syncthreads();
+  int off = 0, t = 0;
+  for (int w = 0; w < kStgThreads / 32; ++w) {
+    off += w < warp ? wsum[w] : 0;
+    t += wsum[w];
+  }
+  __syncthreads();
+  *tot = t;
+  return off + __popc(bal & ((1u << lane) - 1u));
+}
+
+__global__ void __launch_bounds__(kStgThreads)
+stg_collect_kernel(StgArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
+  __shared__ int wsum[kStgThreads / 32];
+  __shared__ int s_fcnt, s_top;
+  if (threadIdx.x == 0) { s_fcnt = 0; s_top = *a.top; }
+  __syncthreads();
+  for (int r = 0; r < a.n_req; ++r) {
+    int sl, ql;
+    req_span(a, r, sl, ql);
+    if (sl <= 0 || ql <= 0) continue;
+    const int np_ctx = (sl - ql) / a.page;
+    for (int p0 = 0; p0 < np_ctx; p0 += kStgThreads) {
+      const int p = p0 + threadIdx.x;
+      int blk = 0, vb = -1, fl = 1;
+      if (p < np_ctx) {
+        blk = a.bt[(int64_t)r * a.bt_stride + p];
+        vb = a.vbo[blk];
+        if (vb >= 0) fl = atomicExch(a.vfl + blk, 1);
+      }
+      const bool act = vb >= 0;
+      const bool nw = act && fl == 0;
+      int nnew;
+      const int i = s_fcnt + stg_scan(nw, wsum, &nnew);
+      const bool ok = nw && i < a.MAXF;
+      if (ok) {
+        a.flist[2 * i] = blk;
+        a.flist[2 * i + 1] = vb;
+      }
+      const bool over = nw && !ok;
+      if (over) a.vfl[blk] = 0;
+      int old = -1;
+      if (act && !over) old = atomicExch(a.vbo + blk, -1);
+      const bool dofree = old >= 0;
+      int nfree;
+      const int j = s_top + stg_scan(dofree, wsum, &nfree);
+      if (dofree) a.stack[j] = old;
+      if (threadIdx.x == 0) {
+        s_fcnt = min(s_fcnt + nnew, a.MAXF);
+        s_top += nfree;
+      }
+      __syncthreads();
+    }
+  }
+  if (threadIdx.x == 0) {
+    *a.fcnt = s_fcnt;
+    *a.top = s_top;
+  }
+}
+
+// one warp per (flush entry, layer, kv-head) tile
+template <int D>
+__global__ void __launch_bounds__(256)
+stg_flush_copy_kernel(StgArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int lane = threadIdx.x & 31;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  const int n = min(*a.fcnt, a.MAXF);
+  const int total = n * a.L * a.n_kv;
+  constexpr int64_t kTile = 16 * D;
+  for (int it = gw; it < total; it += nw) {
+    const int e = it / (a.L * a.n_kv);
+    const int rem = it - e * a.L * a.n_kv;
+    const int l = rem / a.n_kv, kv = rem - l * a.n_kv;
+    const int64_t blk = a.flist[2 * e], vb = a.flist[2 * e + 1];
+    const int64_t src = l * a.svl + vb * a.svb + kv * a.svh;
+    const int64_t dst = (((int64_t)l * a.NB + blk) * a.n_kv + kv) * kTile;
+    copy_tile<D>(a.pool + dst, a.vpool + src, a.svt, lane);
+    if (a.kpool) copy_tile<D>(a.poolk + dst, a.kpool + src, a.svt, lane);
+    if (lane == 0) a.valid[((int64_t)l * a.n_kv + kv) * a.NB + blk] = 1;
+  }
+}
+
+// ordered single-thread pass: the free stack is a shared LIFO
+__global__ void stg_valloc_kernel(StgArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
+  if (threadIdx.x != 0) return;
+  int top = *a.top;
+  for (int r = 0; r < a.n_req; ++r) {
+    int sl, ql;
+    req_span(a, r, sl, ql);
+    if (sl <= 0 || ql <= 0) continue;
+    const int p0 = (sl - ql) / a.page, p1 = (sl - 1) / a.page;
+    for (int p = p0; p <= p1; ++p) {
+      const int blk = a.bt[(int64_t)r * a.bt_stride + p];
+      if (a.vbo[blk] >= 0) continue;
+      if (top <= 0) {
+        *a.ovf = 1;
+        continue;
+      }
+      a.vbo[blk] = a.stack[--top];
+    }
+  }
+  *a.top = top;
+}
+
+__global__ void stg_vslot_kernel(StgArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int r = blockIdx.y;
+  int sl, ql;
+  req_span(a, r, sl, ql);
+  if (sl <= 0 || ql <= 0) return;
+  const int q0 = a.qsl[r];
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ql;
+       i += gridDim.x * blockDim.x) {
+    const int pos = sl - ql + i;
+    const int blk = a.bt[(int64_t)r * a.bt_stride + pos / a.page];
+    const int vb = a.vbo[blk];
+    a.vslot[q0 + i] = vb >= 0 ? (int64_t)vb * a.page + pos % a.page : -1;
+  }
+}
+
+struct ScatArgs {
+  const int16_t* v;       // (n_tokens, n_kv, d) at svt/svh
+  const int16_t* k;       // mem-kv (or null)
+  int64_t vt, vh, kt, kh;
+  const int64_t* vslot;
+  int16_t* vp;            // this layer (NV, page, n_kv, d) at pb/pt/ph
+  int16_t* kp;
+  int64_t pb, pt, ph;
+  int n_tokens, n_kv, d, page;
+};
+
+// one warp per token: its n_kv rows of d 16-bit values, 16-byte pieces
+__global__ void __launch_bounds__(256) stg_scatter_kernel(ScatArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int lane = threadIdx.x & 31;
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (t >= a.n_tokens) return;
+  const int64_t vs = a.vslot[t];
+  if (vs < 0) return;
+  const int64_t vb = vs / a.page, off = vs % a.page;
+  const int per = a.d / 8;
+  for (int e = lane; e < a.n_kv * per; e += 32) {
+    const int kv = e / per, ch = e - kv * per;
+    const int64_t dst = vb * a.pb + off * a.pt + kv * a.ph + ch * 8;
+    *reinterpret_cast<uint4*>(a.vp + dst) =
+        *reinterpret_cast<const uint4*>(a.v + t * a.vt + kv * a.vh + ch * 8);
+    if (a.k)
+      *reinterpret_cast<uint4*>(a.kp + dst) =
+          *reinterpret_cast<const uint4*>(a.k + t * a.kt + kv * a.kh + ch * 8);
+  }
+}
+
+}  // namespace
+}  // namespace amass
+
+extern "C" int amass_staging_begin_step(
+    const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+    const int32_t* query_start_loc, int n_req, int n_tokens, int max_query_len,
+    int64_t* v_slot_mapping, int32_t* vbo, int32_t* v_flushed,
+    int32_t* free_stack, int32_t* free_top, int32_t* flush_list,
+    int32_t* flush_cnt, int32_t* overflow, int max_flush, const void* v_pool,
+    const void* k_pool, int64_t svl, int64_t svb, int64_t svt, int64_t svh,
+    void* pool_dev, void* pool_k_dev, int8_t* pool_valid, int num_layers,
+    int num_blocks, int n_kv, int head_dim, int page, void* stream) {
+  using namespace amass;
+  if (n_req < 0 || n_tokens < 0 || num_layers <= 0 || num_blocks <= 0 ||
+      n_kv <= 0 || max_flush <= 0)
+    return AMASS_ERR_ARG;
+  if (!v_slot_mapping || !vbo || !v_flushed || !free_stack || !free_top ||
+      !flush_list || !flush_cnt || !overflow || !v_pool || !pool_dev ||
+      !pool_valid || (n_req > 0 && (!block_table || !seq_lens || !query_start_loc)))
+    return AMASS_ERR_ARG;
+  if ((k_pool != nullptr) != (pool_k_dev != nullptr)) return AMASS_ERR_ARG;
+  if (page != 16 || (head_dim != 64 && head_dim != 128)) return AMASS_ERR_UNSUPPORTED;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(v_pool) |
+                       reinterpret_cast<uintptr_t>(k_pool) |
+                       reinterpret_cast<uintptr_t>(pool_dev) |
+                       reinterpret_cast<uintptr_t>(pool_k_dev);
+  if ((al & 15) || (svl % 8) || (svb % 8) || (svt % 8) || (svh % 8))
+    return AMASS_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n_tokens > 0 &&
+      cudaMemsetAsync(v_slot_mapping, 0xff, sizeof(int64_t) * n_tokens, st) !=
+          cudaSuccess)
+    return AMASS_ERR_CUDA;
+  if (n_req == 0) return AMASS_OK;
+  StgArgs a{};
+  a.bt = block_table; a.bt_stride = bt_stride; a.sl = seq_lens;
+  a.qsl = query_start_loc; a.n_req = n_req; a.n_tokens = n_tokens;
+  a.page = page; a.vslot = v_slot_mapping; a.vbo = vbo; a.vfl = v_flushed;
+  a.stack = free_stack; a.top = free_top; a.flist = flush_list;
+  a.fcnt = flush_cnt; a.ovf = overflow; a.MAXF = max_flush;
+  a.vpool = static_cast<const int16_t*>(v_pool);
+  a.kpool = static_cast<const int16_t*>(k_pool);
+  a.svl = svl; a.svb = svb; a.svt = svt; a.svh = svh;
+  a.pool = static_cast<int16_t*>(pool_dev);
+  a.poolk = static_cast<int16_t*>(pool_k_dev);
+  a.valid = pool_valid; a.L = num_layers; a.NB = num_blocks; a.n_kv = n_kv;
+  int rc;
+  if ((rc = launch_pdl(stg_vflush_clear_kernel, dim3(n_req), dim3(32), 0, st, a))) return rc;
+  if ((rc = launch_pdl(stg_collect_kernel, dim3(1), dim3(kStgThreads), 0, st, a))) return rc;
+  {
+    const long long warps = (long long)max_flush * num_layers * n_kv;
+    const int grid = (int)std::min<long long>((warps + 7) / 8, num_sms() * 8LL);
+    rc = head_dim == 128
+             ? launch_pdl(stg_flush_copy_kernel<128>, dim3(grid), dim3(256), 0, st, a)
+             : launch_pdl(stg_flush_copy_kernel<64>, dim3(grid), dim3(256), 0, st, a);
+    if (rc) return rc;
+  }
+  if ((rc = launch_pdl(stg_valloc_kernel, dim3(1), dim3(32), 0, st, a))) return rc;
+  {
+    const int bx = std::max(1, std::min((max_query_len + 127) / 128, 64));
+    if ((rc = launch_pdl(stg_vslot_kernel, dim3(bx, n_req), dim3(128), 0, st, a)))
+      return rc;
+  }
+  return launch_status();
+}
+
+extern "C" int amass_staging_scatter(const void* value, int64_t v_st,
+                                     int64_t v_sh, const void* key,
+                                     int64_t k_st, int64_t k_sh,
+                                     const int64_t* v_slot_mapping,
+                                     void* v_pool_layer, void* k_pool_layer,
+                                     int64_t pb, int64_t pt, int64_t ph,
+                                     int n_tokens, int n_kv, int head_dim,
+                                     int page, void* stream) {
+  using namespace amass;
+  if (n_tokens < 0 || n_kv <= 0 || head_dim <= 0 || page <= 0) return AMASS_ERR_ARG;
+  if (n_tokens == 0) return AMASS_OK;
+  if (!value || !v_slot_mapping || !v_pool_layer) return AMASS_ERR_ARG;
+  if ((key != nullptr) != (k_pool_layer != nullptr)) return AMASS_ERR_ARG;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(value) |
+                       reinterpret_cast<uintptr_t>(key) |
+                       reinterpret_cast<uintptr_t>(v_pool_layer) |
+                       reinterpret_cast<uintptr_t>(k_pool_layer);
+  if ((al & 15) || (head_dim % 8) || (v_st % 8) || (v_sh % 8) ||
+      (key && ((k_st % 8) || (k_sh % 8))) || (pb % 8) || (pt % 8) || (ph % 8))
+    return AMASS_ERR_ARG;
+  ScatArgs a{};
+  a.v = static_cast<const int16_t*>(value);
+  a.k = static_cast<const int16_t*>(key);
+  a.vt = v_st; a.vh = v_sh; a.kt = k_st; a.kh = k_sh;
+  a.vslot = v_slot_mapping;
+  a.vp = static_cast<int16_t*>(v_pool_layer);
+  a.kp = static_cast<int16_t*>(k_pool_layer);
+  a.pb = pb; a.pt = pt; a.ph = ph;
+  a.n_tokens = n_tokens; a.n_kv = n_kv; a.d = head_dim; a.page = page;
+  if (int rc = launch_pdl(stg_scatter_kernel, dim3((n_tokens + 7) / 8), dim3(256),
+                          0, static_cast<cudaStream_t>(stream), a))
+    return rc;
+  return launch_status();
+}

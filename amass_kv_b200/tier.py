@@ -89,20 +89,135 @@ class MappedHostVPool:
 
 
 class Staging:
-    """VRAM staging pools for pages written but not yet flushed:
-    v_pool (L, NV, page, n_kv, d), k_pool likewise under mem-kv, and
-    vbo (NB,) = staging row of a block or -1 (reference tier/staging.py:
-    238-310).  The write/flush lifecycle stays with the caller."""
+    """VRAM staging pools for pages written but not yet flushed, and their
+    per-step lifecycle (reference tier/staging.py:235-520).
+
+    v_pool (L, NV, page, n_kv, d) [+ k_pool under mem-kv]; vbo (NB,) = staging
+    block of an engine block or -1; v_flushed (NB,) latch; a free stack of
+    staging blocks (v_free_stack, v_free_top); v_slot_mapping (max_tokens,)
+    int64; the per-step flush list (max_flush, 2) + flush_cnt; overflow latch.
+    NV defaults to the working-set bound 2*ceil(max_tokens/page) + 4*max_reqs
+    (reference :251-274); ``n_vslots`` is accepted as a synonym of v_blocks."""
 
     def __init__(self, *, num_layers: int, num_blocks: int, n_kv: int,
-                 page: int, d: int, n_vslots: int, dtype=torch.bfloat16,
-                 device="cuda", offload_k: bool = False):
-        self.L, self.NB, self.NV = num_layers, num_blocks, n_vslots
-        self.v_pool = torch.zeros((num_layers, n_vslots, page, n_kv, d),
-                                  dtype=dtype, device=device)
-        self.k_pool = (torch.zeros_like(self.v_pool) if offload_k else None)
-        self.vbo = torch.full((num_blocks,), -1, dtype=torch.int32,
-                              device=device)
+                 page: int, d: int, max_reqs: int = 1, max_pages: int = 1,
+                 max_tokens: int = 1, dtype=torch.bfloat16, device="cuda",
+                 v_blocks: int | None = None, max_flush: int | None = None,
+                 offload_k: bool = False, n_vslots: int | None = None):
+        self.L, self.NB, self.n_kv = num_layers, num_blocks, n_kv
+        self.page, self.d = page, d
+        self.R, self.MP, self.max_tokens = max_reqs, max_pages, max_tokens
+        self.offload_k = offload_k
+        dev = torch.device(device)
+        self.device = dev
+        chunk_pages = (max_tokens + page - 1) // page
+        if v_blocks is None:
+            v_blocks = n_vslots
+        if v_blocks is None or v_blocks <= 0:
+            v_blocks = 2 * chunk_pages + 4 * max_reqs
+        if max_flush is None or max_flush <= 0:
+            max_flush = chunk_pages + 2 * max_reqs + 64
+        self.NV, self.MAXF, self.chunk_pages = v_blocks, max_flush, chunk_pages
+        i32 = torch.int32
+        self.v_pool = torch.zeros((num_layers, v_blocks, page, n_kv, d),
+                                  dtype=dtype, device=dev)
+        self.k_pool = torch.zeros_like(self.v_pool) if offload_k else None
+        self.vbo = torch.full((num_blocks,), -1, dtype=i32, device=dev)
+        self.v_flushed = torch.zeros((num_blocks,), dtype=i32, device=dev)
+        self.v_free_stack = torch.arange(v_blocks, dtype=i32, device=dev)
+        self.v_free_top = torch.full((1,), v_blocks, dtype=i32, device=dev)
+        self.v_slot_mapping = torch.full((max(max_tokens, 1),), -1,
+                                         dtype=torch.int64, device=dev)
+        self.flush_list = torch.zeros((max_flush, 2), dtype=i32, device=dev)
+        self.flush_cnt = torch.zeros((1,), dtype=i32, device=dev)
+        self.overflow = torch.zeros((1,), dtype=i32, device=dev)
+        pools = self.v_pool.numel() * (2 if offload_k else 1)
+        self.vpool_gib = pools * self.v_pool.element_size() / 2**30
+
+    # the ordered per-step lifecycle (outside or inside a graph: no sync)
+    def begin_step(self, block_table, seq_lens, query_start_loc,
+                   max_query_len: int, n_tokens: int, pool, pool_valid,
+                   capture: bool = False, poolk=None) -> None:
+        """Reset this step's slots; clear the flushed latch of rewritten
+        pages; collect + free complete staged pages; copy them to the pinned
+        pool (pool_valid = 1); allocate staging blocks for this step's pages;
+        fill v_slot_mapping (reference staging.py:312-346).  ``pool`` /
+        ``poolk`` are the pinned pools' device views."""
+        if n_tokens > self.v_slot_mapping.numel():
+            raise RuntimeError(f"{n_tokens} tokens > v_slot_mapping capacity "
+                               f"{self.v_slot_mapping.numel()}")
+        n_req = seq_lens.shape[0]
+        if capture:
+            self.v_slot_mapping[:n_tokens].fill_(-1)
+            return
+        vp = self.v_pool
+        has_k = self.k_pool is not None
+        _lib.call("amass_staging_begin_step", ptr(block_table),
+                  block_table.stride(0), ptr(seq_lens), ptr(query_start_loc),
+                  int(n_req), int(n_tokens), int(max_query_len),
+                  ptr(self.v_slot_mapping), ptr(self.vbo), ptr(self.v_flushed),
+                  ptr(self.v_free_stack), ptr(self.v_free_top),
+                  ptr(self.flush_list), ptr(self.flush_cnt),
+                  ptr(self.overflow), self.MAXF, ptr(vp),
+                  ptr(self.k_pool) if has_k else 0, vp.stride(0),
+                  vp.stride(1), vp.stride(2), vp.stride(3), pool.data_ptr(),
+                  poolk.data_ptr() if has_k else 0, ptr(pool_valid), self.L,
+                  self.NB, self.n_kv, self.d, self.page,
+                  _lib.stream_of(self.device))
+
+    def scatter_kv(self, lidx: int, key, value, n_tokens: int) -> None:
+        """Write path: this step's V (and K under mem-kv) (n_tokens, n_kv, d)
+        into layer ``lidx``'s staging pool(s) at v_slot_mapping (reference
+        staging.py:348-367)."""
+        vp = self.v_pool[lidx]
+        has_k = self.k_pool is not None
+        kp = self.k_pool[lidx] if has_k else None
+        _lib.call("amass_staging_scatter", ptr(value), value.stride(0),
+                  value.stride(1), ptr(key) if has_k else 0,
+                  key.stride(0) if has_k else 0, key.stride(1) if has_k else 0,
+                  ptr(self.v_slot_mapping), ptr(vp), ptr(kp) if has_k else 0,
+                  vp.stride(0), vp.stride(1), vp.stride(2), int(n_tokens),
+                  self.n_kv, self.d, self.page, _lib.stream_of(self.device))
+
+    # invariant checks (host sync; debug)
+    def assert_free_partition(self) -> None:
+        """Assigned (vbo >= 0) and free (v_free_stack[:top]) staging blocks
+        partition [0, NV) (reference staging.py:454-470)."""
+        top = int(self.v_free_top.item())
+        if not 0 <= top <= self.NV:
+            raise AssertionError(f"free_top={top} out of [0, {self.NV}]")
+        assigned = self.vbo[self.vbo >= 0]
+        free = self.v_free_stack[:top]
+        both = torch.cat([assigned, free])
+        if both.numel() != self.NV or int(torch.unique(both).numel()) != self.NV:
+            raise AssertionError("staging blocks: assigned + free do not "
+                                 f"partition [0, {self.NV})")
+
+    def assert_no_lost_v(self, block_table, seq_lens, query_start_loc,
+                         pool_valid) -> None:
+        """Every complete page written by earlier steps is staged or flushed
+        in every layer and kv-head (reference staging.py:472-486)."""
+        sl = seq_lens.tolist()
+        qsl = query_start_loc.tolist()
+        vbo = self.vbo.cpu()
+        pv = pool_valid.cpu()
+        for r in range(len(sl)):
+            ql = qsl[r + 1] - qsl[r]
+            if sl[r] <= 0 or ql <= 0:
+                continue
+            for p in range((sl[r] - ql) // self.page):
+                blk = int(block_table[r, p])
+                if int(vbo[blk]) < 0 and not bool((pv[:, :, blk] == 1).all()):
+                    raise AssertionError(f"request {r} block {blk}: complete "
+                                         "page neither staged nor flushed")
+
+    def assert_capacity(self) -> None:
+        floor = self.chunk_pages + self.R
+        if self.NV < floor:
+            raise AssertionError(f"v_blocks NV={self.NV} < floor {floor}")
+
+    def bytes_report(self) -> str:
+        return f"v_pool={self.vpool_gib:.3f}GiB (NV={self.NV} blocks)"
 
 
 class Residency:
@@ -248,9 +363,10 @@ class Tier:
 
     def __init__(self, *, num_layers: int, num_blocks: int, n_kv: int,
                  page: int, d: int, hot_slots: int, max_reqs: int,
-                 max_pages: int, n_vslots: int, offload_k: bool = False,
-                 dtype=torch.bfloat16, device="cuda",
-                 max_pool_gb: float = 256.0):
+                 max_pages: int, n_vslots: int | None = None,
+                 offload_k: bool = False, dtype=torch.bfloat16, device="cuda",
+                 max_pool_gb: float = 256.0, max_tokens: int | None = None,
+                 v_blocks: int | None = None):
         kw = dict(num_layers=num_layers, num_blocks=num_blocks, n_kv=n_kv,
                   page=page, d=d)
         self.offload_k = offload_k
@@ -259,7 +375,9 @@ class Tier:
         self.pool_k = (MappedHostVPool(**kw, dtype=dtype, device=device,
                                        max_pool_gb=max_pool_gb)
                        if offload_k else None)
-        self.staging = Staging(**kw, n_vslots=n_vslots, dtype=dtype,
+        self.staging = Staging(**kw, max_reqs=max_reqs, max_pages=max_pages,
+                               max_tokens=max_tokens or max_reqs,
+                               v_blocks=v_blocks or n_vslots, dtype=dtype,
                                device=device, offload_k=offload_k)
         self.residency = Residency(**kw, hot_slots=hot_slots,
                                    max_reqs=max_reqs, max_pages=max_pages,
@@ -279,6 +397,34 @@ class Tier:
                    offload_k=getattr(cfg, "mem_mode", "mem-v") == "mem-kv",
                    device=device,
                    max_pool_gb=float(getattr(cfg, "max_pool_gb", 256.0)))
+
+    def begin_step(self, block_table, seq_lens, query_start_loc,
+                   max_query_len: int, n_tokens: int,
+                   capture: bool = False) -> None:
+        """Residency invalidation of the rewritten pages, then the staging
+        lifecycle (reference tier/tier.py:86-104); capture batches mutate
+        nothing."""
+        if not capture:
+            self.residency.invalidate_written(block_table, seq_lens,
+                                              query_start_loc)
+        self.staging.begin_step(block_table, seq_lens, query_start_loc,
+                                max_query_len, n_tokens, self.pool.dev_view,
+                                self.residency.pool_valid, capture=capture,
+                                poolk=self.pool_k.dev_view if self.pool_k
+                                else None)
+
+    def write_kv(self, lidx, value, n_tokens, key=None) -> None:
+        """In-graph write path: this step's V (and K, mem-kv) into staging
+        (reference tier/tier.py:125-130)."""
+        self.staging.scatter_kv(lidx, key, value, n_tokens)
+
+    def assert_invariants(self, block_table, seq_lens, query_start_loc) -> None:
+        if int(self.staging.overflow.item()) != 0:
+            raise AssertionError("staging free stack underflowed")
+        self.staging.assert_free_partition()
+        self.residency.assert_maps_inverse()
+        self.staging.assert_no_lost_v(block_table, seq_lens, query_start_loc,
+                                      self.residency.pool_valid)
 
     def step(self, lidx, page_table, page_cnt, block_table, seq_lens,
              n_req) -> None:

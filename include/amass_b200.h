@@ -337,6 +337,41 @@ int amass_tier_invalidate(const int32_t* block_table, int64_t bt_stride,
                           int num_layers, int n_kv, int num_blocks,
                           int hot_slots, int page, void* stream);
 
+/* Staging lifecycle of one step (write side of the tier) -- replaces
+ * Staging.begin_step tier/staging.py:312-346 (kernels :51-232).  In order:
+ * v_slot_mapping[:n_tokens] = -1; clear the flushed latch of the pages
+ * written this step; collect the complete pages written by earlier steps
+ * that hold a staging block (requests in order): the first claim of the
+ * latch enters flush_list (blk, vb) (at most max_flush entries, flush_cnt),
+ * and the staging block is freed onto free_stack (free_top); copy every
+ * flushed page v_pool[l, vb] -> the pinned pool [l, blk] for all layers and
+ * kv-heads (and k_pool -> pool_k under mem-kv) and set pool_valid; allocate
+ * a staging block (pop) for every page written this step without one
+ * (underflow sets overflow[0]); fill v_slot_mapping (int64) for this step's
+ * tokens (vb * page + pos % page, or -1).  v_pool (L, NV, page, n_kv, d) at
+ * element strides svl/svb/svt/svh; pool_valid (L, n_kv, NB).  Requests with
+ * seq_len <= 0 or no new tokens are skipped. */
+int amass_staging_begin_step(
+    const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+    const int32_t* query_start_loc, int n_req, int n_tokens, int max_query_len,
+    int64_t* v_slot_mapping, int32_t* vbo, int32_t* v_flushed,
+    int32_t* free_stack, int32_t* free_top, int32_t* flush_list,
+    int32_t* flush_cnt, int32_t* overflow, int max_flush, const void* v_pool,
+    const void* k_pool, int64_t svl, int64_t svb, int64_t svt, int64_t svh,
+    void* pool_dev, void* pool_k_dev, int8_t* pool_valid, int num_layers,
+    int num_blocks, int n_kv, int head_dim, int page, void* stream);
+
+/* Write path: scatter this step's V (and K under mem-kv) (n_tokens, n_kv, d)
+ * 16-bit into one layer's staging pool(s) (NV, page, n_kv, d) at
+ * v_slot_mapping (-1 skips) -- replaces Staging.scatter_kv
+ * tier/staging.py:348-367 (kernel :51-77).  Bit copies. */
+int amass_staging_scatter(const void* value, int64_t v_st, int64_t v_sh,
+                          const void* key, int64_t k_st, int64_t k_sh,
+                          const int64_t* v_slot_mapping, void* v_pool_layer,
+                          void* k_pool_layer, int64_t pb, int64_t pt,
+                          int64_t ph, int n_tokens, int n_kv, int head_dim,
+                          int page, void* stream);
+
 /* Tiered split-K decode (ptr-select) -- replaces mem_decode_ptrsel
  * tier/decode_mem.py:169-222 (kernel :78-166).  As amass_sparse_decode,
  * but per selected page the V tile (and the K tile when hot_k != NULL,

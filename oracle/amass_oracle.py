@@ -613,6 +613,82 @@ def invalidate_written(block_table, seq_lens, query_start_loc, *, page: int,
                         slot2page[l, kv, s] = -1
 
 
+def staging_begin_step(st, block_table, seq_lens, query_start_loc, n_tokens,
+                       *, page: int, pool, pool_valid):
+    """One Staging.begin_step (``tier/staging.py:312-346``, kernels
+    :80-232), sequential semantics.  ``st`` holds numpy arrays vbo, vfl,
+    stack, top (int), flist, fcnt (int), ovf (int), vslot, v_pool (L, NV,
+    page, n_kv, d) int16, MAXF; pool (L, NB, n_kv, page, d) int16 and
+    pool_valid (L, n_kv, NB) are updated in place."""
+    n_req = len(seq_lens)
+    sl = [int(x) for x in seq_lens]
+    ql = [int(query_start_loc[r + 1] - query_start_loc[r]) for r in range(n_req)]
+    st["vslot"][:n_tokens] = -1
+    for r in range(n_req):                                   # vflush_clear
+        if sl[r] > 0 and ql[r] > 0:
+            for p in range((sl[r] - ql[r]) // page, (sl[r] - 1) // page + 1):
+                st["vfl"][block_table[r, p]] = 0
+    st["fcnt"] = 0                                           # collect
+    for r in range(n_req):
+        if sl[r] <= 0 or ql[r] <= 0:
+            continue
+        for p in range((sl[r] - ql[r]) // page):
+            blk = int(block_table[r, p])
+            vb = int(st["vbo"][blk])
+            if vb < 0:
+                continue
+            over = False
+            if st["vfl"][blk] == 0:
+                st["vfl"][blk] = 1
+                if st["fcnt"] < st["MAXF"]:
+                    st["flist"][st["fcnt"]] = (blk, vb)
+                    st["fcnt"] += 1
+                else:
+                    st["vfl"][blk] = 0
+                    over = True
+            if not over:
+                old = int(st["vbo"][blk])
+                st["vbo"][blk] = -1
+                if old >= 0:
+                    st["stack"][st["top"]] = old
+                    st["top"] += 1
+    L = pool.shape[0]                                        # flush copy
+    for i in range(st["fcnt"]):
+        blk, vb = (int(x) for x in st["flist"][i])
+        for l in range(L):
+            pool[l, blk] = st["v_pool"][l, vb].transpose(1, 0, 2)
+            pool_valid[l, :, blk] = 1
+    for r in range(n_req):                                   # valloc
+        if sl[r] <= 0 or ql[r] <= 0:
+            continue
+        for p in range((sl[r] - ql[r]) // page, (sl[r] - 1) // page + 1):
+            blk = int(block_table[r, p])
+            if st["vbo"][blk] >= 0:
+                continue
+            if st["top"] <= 0:
+                st["ovf"] = 1
+                continue
+            st["top"] -= 1
+            st["vbo"][blk] = st["stack"][st["top"]]
+    q0 = 0                                                   # vslot
+    for r in range(n_req):
+        if sl[r] > 0 and ql[r] > 0:
+            for i in range(ql[r]):
+                pos = sl[r] - ql[r] + i
+                vb = int(st["vbo"][block_table[r, pos // page]])
+                st["vslot"][q0 + i] = vb * page + pos % page if vb >= 0 else -1
+        q0 += max(ql[r], 0)
+
+
+def staging_scatter(st, layer: int, values, n_tokens: int, *, page: int):
+    """Staging.scatter_kv (``tier/staging.py:51-77``): values (n_tokens,
+    n_kv, d) int16 into v_pool[layer] at vslot."""
+    for t in range(n_tokens):
+        vs = int(st["vslot"][t])
+        if vs >= 0:
+            st["v_pool"][layer, vs // page, vs % page] = values[t]
+
+
 def tier_decode(q, K, block_table, seq_lens, page_table, page_cnt, *, scale,
                 G, hot, page2slot, vbo, v_pool, pool, layer: int):
     """mem-v ptr-select decode (``tier/decode_mem.py:78-166``): each selected

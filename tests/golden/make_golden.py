@@ -45,6 +45,7 @@ from amass.attention.decode import (ResidentVSource,  # noqa: E402
 from amass.backend._selection_bridge import _nucleus_b  # noqa: E402
 from amass.tier.residency import Residency  # noqa: E402
 from amass.selection.quad_build import quad_build_tail  # noqa: E402
+from amass.tier.staging import Staging  # noqa: E402
 from amass.tier.decode_mem import mem_decode_ptrsel  # noqa: E402
 
 
@@ -277,6 +278,63 @@ def gen_build(name, *, seed, n_req, n_kv, d, ctxs, L, r, v_bits, coords,
     print(name, "pages built", n)
 
 
+STAGING_STEPS = [
+    # (seq_lens after the step, new tokens per request) for 3 requests
+    ([40, 20, 0], [40, 20, 0]),        # two prefills
+    ([41, 35, 0], [1, 15, 0]),         # decode + second prefill chunk
+    ([42, 36, 18], [1, 1, 18]),        # decodes + a new prefill
+    ([48, 37, 19], [6, 1, 1]),         # a 6-token step crossing a page
+    ([49, 48, 20], [1, 11, 1]),        # completes pages of request 1
+]
+
+
+def gen_staging(name, *, seed=31, L=2, NB=40, n_kv=2, d=64, page=16,
+                v_blocks=12, max_flush=6):
+    """The reference Staging.begin_step + scatter_kv over STAGING_STEPS."""
+    rng = np.random.default_rng(seed)
+    R = 3
+    MP = 4
+    bt = np.zeros((R, MP), np.int32)
+    perm = rng.permutation(NB).astype(np.int32)
+    bt[:] = perm[:R * MP].reshape(R, MP)
+    stg = Staging(num_layers=L, num_blocks=NB, n_kv=n_kv, page=page, d=d,
+                  max_reqs=R, max_pages=MP, max_tokens=64,
+                  dtype=torch.bfloat16, device="cpu", v_blocks=v_blocks,
+                  max_flush=max_flush)
+    pool = torch.zeros((L, NB, n_kv, page, d), dtype=torch.int16)
+    pool_valid = torch.zeros((L, n_kv, NB), dtype=torch.int8)
+    rec = {}
+    for s_, (sl, ql) in enumerate(STAGING_STEPS):
+        qsl = np.concatenate([[0], np.cumsum(ql)]).astype(np.int32)
+        n_tok = int(qsl[-1])
+        slt = torch.tensor(sl, dtype=torch.int32)
+        qslt = torch.from_numpy(qsl)
+        stg.begin_step(torch.from_numpy(bt), slt, qslt, max(ql), n_tok,
+                       pool=pool.view(-1), pool_valid=pool_valid)
+        vals = t_bf16(rng.standard_normal((L, n_tok, n_kv, d)))
+        for l in range(L):
+            stg.scatter_kv(l, None, vals[l], n_tok)
+        rec[f"vals_{s_}"] = bf16_bits(vals)
+        rec[f"vbo_{s_}"] = stg.vbo.numpy().copy()
+        rec[f"vfl_{s_}"] = stg.v_flushed.numpy().copy()
+        rec[f"top_{s_}"] = stg.v_free_top.numpy().copy()
+        rec[f"stack_{s_}"] = stg.v_free_stack.numpy().copy()
+        rec[f"fcnt_{s_}"] = stg.flush_cnt.numpy().copy()
+        rec[f"flist_{s_}"] = stg.flush_list.numpy().copy()
+        rec[f"vslot_{s_}"] = stg.v_slot_mapping[:n_tok].numpy().copy()
+        rec[f"pool_{s_}"] = pool.numpy().copy()
+        rec[f"valid_{s_}"] = pool_valid.numpy().copy()
+        rec[f"vpool_{s_}"] = bf16_bits(stg.v_pool).copy()
+        rec[f"ovf_{s_}"] = stg.overflow.numpy().copy()
+    np.savez_compressed(
+        os.path.join(HERE, name + ".npz"), block_table=bt,
+        meta=np.array([L, NB, n_kv, d, page, v_blocks, max_flush,
+                       len(STAGING_STEPS)], np.int64),
+        steps_sl=np.array([x[0] for x in STAGING_STEPS], np.int32),
+        steps_ql=np.array([x[1] for x in STAGING_STEPS], np.int32), **rec)
+    print(name, "final top", int(stg.v_free_top), "ovf", int(stg.overflow))
+
+
 def gen_tier(name, case, *, budget, hot_slots=10, steps=3, seed=5):
     """Residency gather over several steps with forced eviction, staged and
     flushed sources, then the ptr-select tiered decode."""
@@ -425,6 +483,7 @@ def main():
     cl3 = make_clse_case(9, n_req=2, n_kv=2, G=4, d=128, ctxs=(500, 377),
                          r=4, v_bits=8, c_bits=8, c_grain="token")
     gen_clse("clse_r4_i8_tok_max", cl3, budget=0.1, combine="max")
+    gen_staging("tier_staging")
     gen_build("build_quad_i4", seed=21, n_req=3, n_kv=2, d=128,
               ctxs=[100, 257, 16], L=2, r=2, v_bits=4, coords="none")
     gen_build("build_clse_i8", seed=22, n_req=2, n_kv=2, d=64,

@@ -311,3 +311,38 @@ def test_page_summary_vs_reference_build(name):
                 got["c_s"][b] = s["c_s"][i]
                 got["resid"][b] = s["resid"][i]
         check_summary(z, got, l, blocks)
+
+
+def test_staging_lifecycle_vs_reference():
+    z = load_golden("tier_staging")
+    L, NB, n_kv, d, page, NV, MAXF, steps = [int(x) for x in z["meta"]]
+    st = dict(vbo=np.full(NB, -1, np.int32), vfl=np.zeros(NB, np.int32),
+              stack=np.arange(NV, dtype=np.int32), top=NV,
+              flist=np.zeros((MAXF, 2), np.int32), fcnt=0, ovf=0,
+              vslot=np.full(64, -1, np.int64),
+              v_pool=np.zeros((L, NV, page, n_kv, d), np.int16), MAXF=MAXF)
+    pool = np.zeros((L, NB, n_kv, page, d), np.int16)
+    valid = np.zeros((L, n_kv, NB), np.int8)
+    bt = z["block_table"]
+    for s in range(steps):
+        sl, ql = z["steps_sl"][s], z["steps_ql"][s]
+        qsl = np.concatenate([[0], np.cumsum(ql)])
+        n_tok = int(qsl[-1])
+        O.staging_begin_step(st, bt, sl, qsl, n_tok, page=page, pool=pool,
+                             pool_valid=valid)
+        vals = z[f"vals_{s}"]
+        for l in range(L):
+            O.staging_scatter(st, l, vals[l], n_tok, page=page)
+        assert np.array_equal(st["vbo"], z[f"vbo_{s}"]), s
+        assert np.array_equal(st["vfl"], z[f"vfl_{s}"]), s
+        assert st["top"] == int(z[f"top_{s}"][0]), s
+        assert np.array_equal(st["stack"][:st["top"]],
+                              z[f"stack_{s}"][:st["top"]]), s
+        assert st["fcnt"] == int(z[f"fcnt_{s}"][0]), s
+        assert np.array_equal(st["flist"][:st["fcnt"]],
+                              z[f"flist_{s}"][:st["fcnt"]]), s
+        assert np.array_equal(st["vslot"][:n_tok], z[f"vslot_{s}"]), s
+        assert np.array_equal(pool, z[f"pool_{s}"]), s
+        assert np.array_equal(valid, z[f"valid_{s}"]), s
+        assert np.array_equal(st["v_pool"], z[f"vpool_{s}"]), s
+        assert st["ovf"] == int(z[f"ovf_{s}"][0]), s
