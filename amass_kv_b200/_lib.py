@@ -17,6 +17,16 @@ _P = ctypes.c_void_p
 _I = ctypes.c_int
 _L = ctypes.c_int64
 _F = ctypes.c_float
+_U = ctypes.c_uint64
+
+
+class DmaRun(ctypes.Structure):
+    """AmassDmaRun: one copy-engine copy (rows of a strided 2-D copy)."""
+    _fields_ = [("dst", ctypes.c_uint64), ("src", ctypes.c_uint64),
+                ("dst_k", ctypes.c_uint64), ("src_k", ctypes.c_uint64),
+                ("dpitch", ctypes.c_int64), ("spitch", ctypes.c_int64),
+                ("width", ctypes.c_int64), ("height", ctypes.c_int64)]
+
 
 # name -> argtypes (restype is int status for every compute entry point)
 _SIGS = {
@@ -51,7 +61,8 @@ _SIGS = {
     "amass_peer_barrier": [_P, _I, _I, _P, _P, _P],
     "amass_staging_begin_step": [_P, _L, _P, _P, _I, _I, _I, _P, _P, _P, _P,
                                  _P, _P, _P, _P, _I, _P, _P, _L, _L, _L, _L,
-                                 _P, _P, _P, _I, _I, _I, _I, _I, _P],
+                                 _P, _P, _P, _I, _I, _I, _I, _I, _P, _I,
+                                 _P],
     "amass_staging_scatter": [_P, _L, _L, _P, _L, _L, _P, _P, _P, _L, _L, _L,
                               _I, _I, _I, _I, _P],
     "amass_host_device_pointer": [_P, _P],
@@ -60,6 +71,11 @@ _SIGS = {
                         _I, _I, _I, _I, _I, _I, _P],
     "amass_tier_fetch": [_P, _P, _P, _P, _P, _P, _P, _L, _L, _L, _P, _P, _P,
                          _I, _I, _I, _I, _I, _I, _P],
+    "amass_tier_fetch_staged": [_P, _P, _P, _P, _P, _P, _P, _L, _L, _L, _P,
+                                _P, _P, _I, _I, _I, _I, _I, _I, _P],
+    "amass_tier_dma_plan": [_P, _P, _P, _I, _I, _I, _I, _I, _I, _U, _U, _U,
+                            _U, _P, _I, _P, _P],
+    "amass_dma_issue": [_P, _I, _P],
     "amass_tier_invalidate": [_P, _L, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I,
                               _I, _P],
     "amass_tier_decode": [_P, _L, _L, _P, _L, _L, _L, _P, _P, _P, _P, _L, _L,

@@ -30,6 +30,7 @@
 // the k-th smallest eligible key, and evicted pages are never misses of the
 // same call.
 #include <algorithm>
+#include <climits>
 
 #include "common.cuh"
 
@@ -448,6 +449,7 @@ struct FetchArgs {
   int16_t* pool_k;
   const int16_t* kpool;
   int layer, NB, n_kv, S;
+  int staged_only;        // copy only the installs whose page is not flushed
 };
 
 // One warp copies one (16 x D) tile of 16-bit elements: all loads first
@@ -496,6 +498,7 @@ tier_fetch_kernel(FetchArgs a) {
         (((int64_t)a.layer * a.NB + blk) * a.n_kv + kv) * kTile;
     const bool vld = a.valid[(int64_t)kv * a.NB + blk] > 0;
     const int vb = a.vbo[blk];
+    if (a.staged_only && vld) continue;
     if (vld || vb < 0) {
       copy_tile<D>(a.hot + hot_off, a.pool + pool_off, D, lane);
       if (a.hot_k) copy_tile<D>(a.hot_k + hot_off, a.pool_k + pool_off, D, lane);
@@ -617,16 +620,15 @@ extern "C" int amass_tier_plan(const int32_t* page_table,
   return launch_status();
 }
 
-extern "C" int amass_tier_fetch(const int32_t* fetch_list,
-                                const int32_t* fetch_cnt, void* hot,
-                                void* pool_dev, int8_t* pool_valid,
-                                const int32_t* vbo, const void* v_pool,
-                                int64_t svb, int64_t svt, int64_t svh,
-                                void* hot_k, void* pool_k_dev,
-                                const void* k_pool, int layer, int num_blocks,
-                                int n_kv, int hot_slots, int page, int head_dim,
-                                void* stream) {
-  using namespace amass;
+namespace amass {
+namespace {
+int tier_fetch_impl(const int32_t* fetch_list, const int32_t* fetch_cnt,
+                    void* hot, void* pool_dev, int8_t* pool_valid,
+                    const int32_t* vbo, const void* v_pool, int64_t svb,
+                    int64_t svt, int64_t svh, void* hot_k, void* pool_k_dev,
+                    const void* k_pool, int layer, int num_blocks, int n_kv,
+                    int hot_slots, int page, int head_dim, void* stream,
+                    bool staged_only) {
   if (!fetch_list || !fetch_cnt || !hot || !pool_dev || !pool_valid || !vbo ||
       !v_pool || num_blocks <= 0 || n_kv <= 0 || hot_slots <= 0 || layer < 0)
     return AMASS_ERR_ARG;
@@ -652,6 +654,7 @@ extern "C" int amass_tier_fetch(const int32_t* fetch_list,
   a.pool_k = static_cast<int16_t*>(pool_k_dev);
   a.kpool = static_cast<const int16_t*>(k_pool);
   a.layer = layer; a.NB = num_blocks; a.n_kv = n_kv; a.S = hot_slots;
+  a.staged_only = staged_only ? 1 : 0;
   const long long warps = (long long)n_kv * hot_slots;
   const int grid = (int)std::min<long long>((warps + 7) / 8, num_sms() * 8LL);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -664,6 +667,35 @@ extern "C" int amass_tier_fetch(const int32_t* fetch_list,
     return AMASS_ERR_UNSUPPORTED;
   if (rc) return rc;
   return launch_status();
+}
+}  // namespace
+}  // namespace amass
+
+extern "C" int amass_tier_fetch(const int32_t* fetch_list,
+                                const int32_t* fetch_cnt, void* hot,
+                                void* pool_dev, int8_t* pool_valid,
+                                const int32_t* vbo, const void* v_pool,
+                                int64_t svb, int64_t svt, int64_t svh,
+                                void* hot_k, void* pool_k_dev,
+                                const void* k_pool, int layer, int num_blocks,
+                                int n_kv, int hot_slots, int page, int head_dim,
+                                void* stream) {
+  return amass::tier_fetch_impl(fetch_list, fetch_cnt, hot, pool_dev,
+                                pool_valid, vbo, v_pool, svb, svt, svh, hot_k,
+                                pool_k_dev, k_pool, layer, num_blocks, n_kv,
+                                hot_slots, page, head_dim, stream, false);
+}
+
+extern "C" int amass_tier_fetch_staged(
+    const int32_t* fetch_list, const int32_t* fetch_cnt, void* hot,
+    void* pool_dev, int8_t* pool_valid, const int32_t* vbo, const void* v_pool,
+    int64_t svb, int64_t svt, int64_t svh, void* hot_k, void* pool_k_dev,
+    const void* k_pool, int layer, int num_blocks, int n_kv, int hot_slots,
+    int page, int head_dim, void* stream) {
+  return amass::tier_fetch_impl(fetch_list, fetch_cnt, hot, pool_dev,
+                                pool_valid, vbo, v_pool, svb, svt, svh, hot_k,
+                                pool_k_dev, k_pool, layer, num_blocks, n_kv,
+                                hot_slots, page, head_dim, stream, true);
 }
 
 extern "C" int amass_tier_invalidate(const int32_t* block_table,
@@ -746,6 +778,8 @@ struct StgArgs {
   int16_t* poolk;
   int8_t* valid;          // (L, n_kv, NB)
   int L, NB, n_kv;
+  int32_t* cand;          // [0] = count, [1..cap] = keys r * bt_stride + p
+  int cand_cap;           // 0: collect walks every complete page itself
 };
 
 AMASS_DEV void req_span(const StgArgs& a, int r, int& sl, int& ql) {
@@ -759,10 +793,33 @@ __global__ void stg_vflush_clear_kernel(StgArgs a) {
   const int r = blockIdx.x;
   int sl, ql;
   req_span(a, r, sl, ql);
+  if (r == 0 && threadIdx.x == 0 && a.cand) a.cand[0] = 0;
   if (sl <= 0 || ql <= 0) return;
   const int p0 = (sl - ql) / a.page, p1 = (sl - 1) / a.page;
   for (int p = p0 + (int)threadIdx.x; p <= p1; p += blockDim.x)
     a.vfl[a.bt[(int64_t)r * a.bt_stride + p]] = 0;
+}
+
+// Whole-GPU pre-pass of collect: the complete settled pages whose block is
+// staged (vbo >= 0) -- a handful among all context pages -- appended in any
+// order as keys r * bt_stride + p.  grid (x, n_req).
+__global__ void __launch_bounds__(256) stg_cand_kernel(StgArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int r = blockIdx.y;
+  int sl, ql;
+  req_span(a, r, sl, ql);
+  if (sl <= 0 || ql <= 0) return;
+  const int np_ctx = (sl - ql) / a.page;
+  const int64_t row = (int64_t)r * a.bt_stride;
+  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < np_ctx;
+       p += gridDim.x * blockDim.x) {
+    const int blk = __ldg(a.bt + row + p);
+    if (a.vbo[blk] >= 0) {
+      const int i = atomicAdd(a.cand, 1);
+      if (i < a.cand_cap) a.cand[1 + i] = (int)(row + p);
+    }
+  }
 }
 
 constexpr int kStgThreads = 1024;
@@ -784,49 +841,93 @@ AMASS_DEV int stg_scan(int v, int* wsum, int* tot) {
   return off + __popc(bal & ((1u << lane) - 1u));
 }
 
+constexpr int kStgCandCap = 4096;
+
+// One ordered chunk of collect: thread t holds the t-th page of the chunk
+// (vb < 0: nothing to do).  A staged page whose latch was clear enters the
+// flush list (past max_flush the latch is undone and the page stays staged);
+// every staged page that leaves staging frees its block onto the stack.  The
+// two block scans keep list slots and pushes in chunk order.
+AMASS_DEV void stg_collect_chunk(const StgArgs& a, int blk, int vb, int* wsum,
+                                 int& s_fcnt, int& s_top) {
+  int fl = 1;
+  if (vb >= 0) fl = atomicExch(a.vfl + blk, 1);
+  const bool act = vb >= 0;
+  const bool nw = act && fl == 0;
+  int nnew;
+  const int i = s_fcnt + stg_scan(nw, wsum, &nnew);
+  const bool ok = nw && i < a.MAXF;
+  if (ok) {
+    a.flist[2 * i] = blk;
+    a.flist[2 * i + 1] = vb;
+  }
+  const bool over = nw && !ok;
+  if (over) a.vfl[blk] = 0;
+  int old = -1;
+  if (act && !over) old = atomicExch(a.vbo + blk, -1);
+  const bool dofree = old >= 0;
+  int nfree;
+  const int j = s_top + stg_scan(dofree, wsum, &nfree);
+  if (dofree) a.stack[j] = old;
+  if (threadIdx.x == 0) {
+    s_fcnt = min(s_fcnt + nnew, a.MAXF);
+    s_top += nfree;
+  }
+  __syncthreads();
+}
+
 __global__ void __launch_bounds__(kStgThreads)
 stg_collect_kernel(StgArgs a) {
   grid_dep_wait();
   grid_dep_launch();
   __shared__ int wsum[kStgThreads / 32];
   __shared__ int s_fcnt, s_top;
+  __shared__ int keys[kStgCandCap];
   if (threadIdx.x == 0) { s_fcnt = 0; s_top = *a.top; }
+  const int ncand = a.cand_cap > 0 ? *a.cand : 0;
   __syncthreads();
-  for (int r = 0; r < a.n_req; ++r) {
+  if (a.cand_cap > 0 && ncand <= a.cand_cap) {
+    // ascending keys = (request, page) order: bitonic sort in shared memory
+    int n2 = 1;
+    while (n2 < ncand) n2 <<= 1;
+    for (int i = threadIdx.x; i < n2; i += kStgThreads)
+      keys[i] = i < ncand ? a.cand[1 + i] : INT_MAX;
+    __syncthreads();
+    for (int k = 2; k <= n2; k <<= 1)
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int i = threadIdx.x; i < n2; i += kStgThreads) {
+          const int x = i ^ j;
+          if (x > i) {
+            const int u = keys[i], w = keys[x];
+            if (((i & k) == 0) == (u > w)) { keys[i] = w; keys[x] = u; }
+          }
+        }
+        __syncthreads();
+      }
+    for (int c0 = 0; c0 < ncand; c0 += kStgThreads) {
+      const int c = c0 + threadIdx.x;
+      int blk = 0, vb = -1;
+      if (c < ncand) {
+        blk = a.bt[keys[c]];
+        vb = a.vbo[blk];
+      }
+      stg_collect_chunk(a, blk, vb, wsum, s_fcnt, s_top);
+    }
+  } else {
+    for (int r = 0; r < a.n_req; ++r) {
     int sl, ql;
     req_span(a, r, sl, ql);
     if (sl <= 0 || ql <= 0) continue;
-    const int np_ctx = (sl - ql) / a.page;
-    for (int p0 = 0; p0 < np_ctx; p0 += kStgThreads) {
-      const int p = p0 + threadIdx.x;
-      int blk = 0, vb = -1, fl = 1;
-      if (p < np_ctx) {
-        blk = a.bt[(int64_t)r * a.bt_stride + p];
-        vb = a.vbo[blk];
-        if (vb >= 0) fl = atomicExch(a.vfl + blk, 1);
+      const int np_ctx = (sl - ql) / a.page;
+      for (int p0 = 0; p0 < np_ctx; p0 += kStgThreads) {
+        const int p = p0 + threadIdx.x;
+        int blk = 0, vb = -1;
+        if (p < np_ctx) {
+          blk = a.bt[(int64_t)r * a.bt_stride + p];
+          vb = a.vbo[blk];
+        }
+        stg_collect_chunk(a, blk, vb, wsum, s_fcnt, s_top);
       }
-      const bool act = vb >= 0;
-      const bool nw = act && fl == 0;
-      int nnew;
-      const int i = s_fcnt + stg_scan(nw, wsum, &nnew);
-      const bool ok = nw && i < a.MAXF;
-      if (ok) {
-        a.flist[2 * i] = blk;
-        a.flist[2 * i + 1] = vb;
-      }
-      const bool over = nw && !ok;
-      if (over) a.vfl[blk] = 0;
-      int old = -1;
-      if (act && !over) old = atomicExch(a.vbo + blk, -1);
-      const bool dofree = old >= 0;
-      int nfree;
-      const int j = s_top + stg_scan(dofree, wsum, &nfree);
-      if (dofree) a.stack[j] = old;
-      if (threadIdx.x == 0) {
-        s_fcnt = min(s_fcnt + nnew, a.MAXF);
-        s_top += nfree;
-      }
-      __syncthreads();
     }
   }
   if (threadIdx.x == 0) {
@@ -860,28 +961,89 @@ stg_flush_copy_kernel(StgArgs a) {
   }
 }
 
-// ordered single-thread pass: the free stack is a shared LIFO
-__global__ void stg_valloc_kernel(StgArgs a) {
+// Block-wide exclusive scan of an int (kStgThreads threads); *tot gets the
+// block sum.  Ends with a barrier.
+AMASS_DEV int stg_scan_int(int v, int* wsum, int* tot) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[warp] = x;
+  __syncthreads();
+  int off = 0, t = 0;
+  for (int w = 0; w < kStgThreads / 32; ++w) {
+    off += w < warp ? wsum[w] : 0;
+    t += wsum[w];
+  }
+  __syncthreads();
+  *tot = t;
+  return off + x - v;
+}
+
+// Staging blocks for the pages written this step, in (request, page) order
+// off the LIFO free stack: the k-th page without a block takes
+// stack[top - 1 - k]; pages past the stack's depth set the overflow latch.
+// One CTA; the written pages of up to 1024 requests are flattened and their
+// (block table, vbo) loads issued together.  (A block written by two
+// requests in one step -- not a valid engine state -- would get two blocks.)
+__global__ void __launch_bounds__(kStgThreads) stg_valloc_kernel(StgArgs a) {
   grid_dep_wait();
   grid_dep_launch();
-  if (threadIdx.x != 0) return;
-  int top = *a.top;
-  for (int r = 0; r < a.n_req; ++r) {
-    int sl, ql;
-    req_span(a, r, sl, ql);
-    if (sl <= 0 || ql <= 0) continue;
-    const int p0 = (sl - ql) / a.page, p1 = (sl - 1) / a.page;
-    for (int p = p0; p <= p1; ++p) {
-      const int blk = a.bt[(int64_t)r * a.bt_stride + p];
-      if (a.vbo[blk] >= 0) continue;
-      if (top <= 0) {
-        *a.ovf = 1;
-        continue;
+  __shared__ int wsum[kStgThreads / 32];
+  __shared__ int offs[kStgThreads + 1], p0s[kStgThreads];
+  __shared__ int s_top, s_ovf;
+  const int tid = threadIdx.x;
+  if (tid == 0) { s_top = *a.top; s_ovf = 0; }
+  for (int r0 = 0; r0 < a.n_req; r0 += kStgThreads) {
+    int c = 0, p0 = 0;
+    if (r0 + tid < a.n_req) {
+      int sl, ql;
+      req_span(a, r0 + tid, sl, ql);
+      if (sl > 0 && ql > 0) {
+        p0 = (sl - ql) / a.page;
+        c = (sl - 1) / a.page - p0 + 1;
       }
-      a.vbo[blk] = a.stack[--top];
     }
+    int tot;
+    const int ex = stg_scan_int(c, wsum, &tot);
+    offs[tid] = ex;
+    p0s[tid] = p0;
+    if (tid == 0) offs[kStgThreads] = tot;
+    __syncthreads();
+    for (int e0 = 0; e0 < tot; e0 += kStgThreads) {
+      const int e = e0 + tid;
+      int blk = 0;
+      bool need = false;
+      if (e < tot) {
+        int lo = 0, hi = kStgThreads;          // offs[lo] <= e < offs[hi]
+        while (hi - lo > 1) {
+          const int mid = (lo + hi) >> 1;
+          if (offs[mid] <= e) lo = mid; else hi = mid;
+        }
+        const int64_t row = (int64_t)(r0 + lo) * a.bt_stride;
+        blk = a.bt[row + p0s[lo] + (e - offs[lo])];
+        need = a.vbo[blk] < 0;
+      }
+      const int top0 = s_top;
+      int nneed;
+      const int k = stg_scan(need, wsum, &nneed);
+      if (need) {
+        const int idx = top0 - 1 - k;
+        if (idx >= 0) a.vbo[blk] = a.stack[idx];
+        else s_ovf = 1;
+      }
+      if (tid == 0) s_top = max(top0 - nneed, 0);
+      __syncthreads();
+    }
+    __syncthreads();
   }
-  *a.top = top;
+  if (tid == 0) {
+    *a.top = s_top;
+    if (s_ovf) *a.ovf = 1;
+  }
 }
 
 __global__ void stg_vslot_kernel(StgArgs a) {
@@ -945,10 +1107,11 @@ extern "C" int amass_staging_begin_step(
     int32_t* flush_cnt, int32_t* overflow, int max_flush, const void* v_pool,
     const void* k_pool, int64_t svl, int64_t svb, int64_t svt, int64_t svh,
     void* pool_dev, void* pool_k_dev, int8_t* pool_valid, int num_layers,
-    int num_blocks, int n_kv, int head_dim, int page, void* stream) {
+    int num_blocks, int n_kv, int head_dim, int page, int32_t* cand,
+    int cand_cap, void* stream) {
   using namespace amass;
   if (n_req < 0 || n_tokens < 0 || num_layers <= 0 || num_blocks <= 0 ||
-      n_kv <= 0 || max_flush <= 0)
+      n_kv <= 0 || max_flush <= 0 || cand_cap < 0 || (cand_cap > 0 && !cand))
     return AMASS_ERR_ARG;
   if (!v_slot_mapping || !vbo || !v_flushed || !free_stack || !free_top ||
       !flush_list || !flush_cnt || !overflow || !v_pool || !pool_dev ||
@@ -980,8 +1143,17 @@ extern "C" int amass_staging_begin_step(
   a.pool = static_cast<int16_t*>(pool_dev);
   a.poolk = static_cast<int16_t*>(pool_k_dev);
   a.valid = pool_valid; a.L = num_layers; a.NB = num_blocks; a.n_kv = n_kv;
+  // keys must fit int32; otherwise collect walks the pages itself
+  const bool use_cand = cand_cap > 0 && (int64_t)n_req * bt_stride < INT_MAX;
+  a.cand = use_cand ? cand : nullptr;
+  a.cand_cap = use_cand ? std::min(cand_cap, kStgCandCap) : 0;
   int rc;
   if ((rc = launch_pdl(stg_vflush_clear_kernel, dim3(n_req), dim3(32), 0, st, a))) return rc;
+  if (use_cand) {
+    const int gx = (int)std::min<int64_t>((bt_stride + 255) / 256, 64);
+    if ((rc = launch_pdl(stg_cand_kernel, dim3(gx, n_req), dim3(256), 0, st, a)))
+      return rc;
+  }
   if ((rc = launch_pdl(stg_collect_kernel, dim3(1), dim3(kStgThreads), 0, st, a))) return rc;
   {
     const long long warps = (long long)max_flush * num_layers * n_kv;
@@ -991,7 +1163,7 @@ extern "C" int amass_staging_begin_step(
              : launch_pdl(stg_flush_copy_kernel<64>, dim3(grid), dim3(256), 0, st, a);
     if (rc) return rc;
   }
-  if ((rc = launch_pdl(stg_valloc_kernel, dim3(1), dim3(32), 0, st, a))) return rc;
+  if ((rc = launch_pdl(stg_valloc_kernel, dim3(1), dim3(kStgThreads), 0, st, a))) return rc;
   {
     const int bx = std::max(1, std::min((max_query_len + 127) / 128, 64));
     if ((rc = launch_pdl(stg_vslot_kernel, dim3(bx, n_req), dim3(128), 0, st, a)))

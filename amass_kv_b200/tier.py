@@ -26,7 +26,7 @@ from . import _lib
 from ._lib import ptr
 from .attention import ensure_stage_b_buffers, pps_min_for, split_kv
 
-_FETCH_MODES = ("kernel", "off")
+_FETCH_MODES = ("kernel", "dma", "off")
 
 
 def host_device_pointer(host_tensor: torch.Tensor) -> int:
@@ -103,7 +103,8 @@ class Staging:
                  page: int, d: int, max_reqs: int = 1, max_pages: int = 1,
                  max_tokens: int = 1, dtype=torch.bfloat16, device="cuda",
                  v_blocks: int | None = None, max_flush: int | None = None,
-                 offload_k: bool = False, n_vslots: int | None = None):
+                 offload_k: bool = False, n_vslots: int | None = None,
+                 cand_cap: int = 4096):
         self.L, self.NB, self.n_kv = num_layers, num_blocks, n_kv
         self.page, self.d = page, d
         self.R, self.MP, self.max_tokens = max_reqs, max_pages, max_tokens
@@ -131,6 +132,9 @@ class Staging:
         self.flush_list = torch.zeros((max_flush, 2), dtype=i32, device=dev)
         self.flush_cnt = torch.zeros((1,), dtype=i32, device=dev)
         self.overflow = torch.zeros((1,), dtype=i32, device=dev)
+        # scratch of the collect pre-pass (count + staged complete pages)
+        self.cand_cap = max(0, min(int(cand_cap), 4096))
+        self.cand = torch.zeros((1 + self.cand_cap,), dtype=i32, device=dev)
         pools = self.v_pool.numel() * (2 if offload_k else 1)
         self.vpool_gib = pools * self.v_pool.element_size() / 2**30
 
@@ -162,8 +166,8 @@ class Staging:
                   ptr(self.k_pool) if has_k else 0, vp.stride(0),
                   vp.stride(1), vp.stride(2), vp.stride(3), pool.data_ptr(),
                   poolk.data_ptr() if has_k else 0, ptr(pool_valid), self.L,
-                  self.NB, self.n_kv, self.d, self.page,
-                  _lib.stream_of(self.device))
+                  self.NB, self.n_kv, self.d, self.page, ptr(self.cand),
+                  self.cand_cap, _lib.stream_of(self.device))
 
     def scatter_kv(self, lidx: int, key, value, n_tokens: int) -> None:
         """Write path: this step's V (and K under mem-kv) (n_tokens, n_kv, d)
@@ -218,6 +222,58 @@ class Staging:
 
     def bytes_report(self) -> str:
         return f"v_pool={self.vpool_gib:.3f}GiB (NV={self.NV} blocks)"
+
+
+class CopyEngine:
+    """Copy-engine transport on dedicated side streams, double-buffered so a
+    prefetch for step N+1 does not queue behind step N's (reference
+    tier/dma.py:77-140).  ``memcpy_async`` is one contiguous copy,
+    ``memcpy_2d_async`` a strided 2-D copy (one coalesced run); both go
+    through the library's ``amass_dma_issue``.  The reference's scattered
+    one-call batch copy is not provided: this build's fetch is the kernel
+    (graph-capturable) or these run copies."""
+
+    def __init__(self, n_buffers: int = 2, device=None):
+        self.device = torch.device(device) if device is not None else \
+            torch.device("cuda", torch.cuda.current_device())
+        self.streams = [torch.cuda.Stream(self.device)
+                        for _ in range(n_buffers)]
+        self.events = [torch.cuda.Event() for _ in range(n_buffers)]
+        self._i = 0
+        self.has_batch = False
+
+    def next_stream(self):
+        s = self.streams[self._i]
+        self._i = (self._i + 1) % len(self.streams)
+        return s
+
+    def issue(self, runs, stream) -> None:
+        if len(runs):
+            _lib.call("amass_dma_issue", ctypes.cast(runs, ctypes.c_void_p),
+                      len(runs), stream.cuda_stream)
+
+    def memcpy_async(self, dst_ptr: int, src_ptr: int, nbytes: int,
+                     stream) -> None:
+        self.issue((_lib.DmaRun * 1)(_lib.DmaRun(dst_ptr, src_ptr, 0, 0,
+                                                 nbytes, nbytes, nbytes, 1)),
+                   stream)
+
+    def memcpy_2d_async(self, dst_ptr: int, dpitch: int, src_ptr: int,
+                        spitch: int, width_bytes: int, height: int,
+                        stream) -> None:
+        self.issue((_lib.DmaRun * 1)(_lib.DmaRun(dst_ptr, src_ptr, 0, 0,
+                                                 dpitch, spitch, width_bytes,
+                                                 height)), stream)
+
+    def memcpy_batch(self, *args, **kwargs) -> None:
+        raise RuntimeError("the scattered one-call batch copy is not part of "
+                           "this build; use the kernel fetch or run copies")
+
+    def record(self, stream):
+        ev = (self.events[self.streams.index(stream)]
+              if stream in self.streams else torch.cuda.Event())
+        ev.record(stream)
+        return ev
 
 
 class Residency:
@@ -307,20 +363,80 @@ class Residency:
         """Copy the planned misses into their hot slots: pinned pool when
         flushed, else staging with write-through (reference residency.py:
         409-436).  ``pool``/``poolk`` are device views (``dev_view``)."""
+        st = (stream.cuda_stream if stream is not None
+              else _lib.stream_of(self.device))
+        self._fetch("amass_tier_fetch", layer, staging, pool, poolk, st)
+
+    def _fetch(self, entry, layer, staging, pool, poolk, st) -> None:
         l = int(layer)
         vp = staging.v_pool[l]
         has_k = self.hot_k_i16 is not None
         if has_k and (poolk is None or staging.k_pool is None):
             raise ValueError("mem-kv residency needs poolk and staging.k_pool")
         kp = staging.k_pool[l] if has_k else None
-        st = (stream.cuda_stream if stream is not None
-              else _lib.stream_of(self.device))
-        _lib.call("amass_tier_fetch", ptr(self.fetch_list), ptr(self.fetch_cnt),
+        _lib.call(entry, ptr(self.fetch_list), ptr(self.fetch_cnt),
                   ptr(self.hot_i16[l]), pool.data_ptr(), ptr(self.pool_valid[l]),
                   ptr(staging.vbo), ptr(vp), vp.stride(0), vp.stride(1),
                   vp.stride(2), ptr(self.hot_k_i16[l]) if has_k else 0,
                   poolk.data_ptr() if has_k else 0, ptr(kp) if has_k else 0,
                   l, self.NB, self.n_kv, self.S, self.page, self.d, st)
+
+    def gather_fetch_staged(self, layer, staging, pool, n_req=None,
+                            poolk=None) -> None:
+        """The kernel fetch restricted to installs whose page is not flushed
+        (the ones the copy-engine plan leaves out): the device half of the
+        copy-engine fetch (reference residency.py:
+        527-548)."""
+        self._fetch("amass_tier_fetch_staged", layer, staging, pool, poolk,
+                    _lib.stream_of(self.device))
+
+    def build_dma_plan(self, layer, pool, n_req=None, poolk=None):
+        """Copy-engine plan of the last gather_plan's flushed installs (host:
+        reads fetch_list / fetch_cnt / pool_valid back, a device sync):
+        (runs, has_staged), runs a ctypes array of DmaRun.  Each run is one
+        strided 2-D copy of contiguous blocks into contiguous hot slots of
+        one kv-head (reference residency.py:438-492).  For a prefetch, build
+        during the previous step."""
+        l = int(layer)
+        fl = self.fetch_list.cpu().contiguous()
+        fc = self.fetch_cnt.cpu().contiguous()
+        pv = self.pool_valid[l].cpu().contiguous()
+        cap = max(1, int(fc.sum()))
+        runs = (_lib.DmaRun * cap)()
+        n = ctypes.c_int(0)
+        staged = ctypes.c_int(0)
+        has_k = self.hot_k_i16 is not None
+        if has_k and poolk is None:
+            raise ValueError("mem-kv residency needs poolk")
+        _lib.call("amass_tier_dma_plan", fl.data_ptr(), fc.data_ptr(),
+                  pv.data_ptr(), l, self.NB, self.n_kv, self.S, self.page,
+                  self.d, pool.data_ptr(), self.hot_i16[l].data_ptr(),
+                  poolk.data_ptr() if has_k else 0,
+                  self.hot_k_i16[l].data_ptr() if has_k else 0,
+                  ctypes.cast(runs, ctypes.c_void_p), cap, ctypes.byref(n),
+                  ctypes.byref(staged))
+        return (_lib.DmaRun * n.value).from_buffer(runs), bool(staged.value)
+
+    def issue_dma_plan(self, runs, copy_engine, stream) -> None:
+        """Issue a built plan on ``stream`` (copy engines only; reference
+        residency.py:494-509)."""
+        copy_engine.issue(runs, stream)
+
+    def gather_fetch_dma(self, layer, staging, pool, n_req, copy_engine,
+                         poolk=None, stream=None):
+        """Copy-engine fetch (build + issue): flushed installs by the copy
+        engines on a side stream, unflushed installs by the kernel on the
+        current stream.  Returns the side stream's event (reference
+        residency.py:511-525)."""
+        stream = stream if stream is not None else copy_engine.next_stream()
+        runs, has_staged = self.build_dma_plan(layer, pool, n_req, poolk)
+        # victim slots may still be read by work queued before the plan
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        self.issue_dma_plan(runs, copy_engine, stream)
+        ev = copy_engine.record(stream)
+        if has_staged:
+            self.gather_fetch_staged(layer, staging, pool, n_req, poolk)
+        return ev
 
     def gather(self, layer, page_table, page_cnt, block_table, seq_lens,
                n_req, staging, pool, poolk=None) -> None:
@@ -434,6 +550,32 @@ class Tier:
                               poolk=self.pool_k.dev_view if self.pool_k
                               else None)
 
+    @property
+    def copy_engine(self) -> CopyEngine:
+        """Lazily created double-buffered copy engine (reference
+        tier/tier.py:144-152)."""
+        ce = getattr(self, "_copy_engine", None)
+        if ce is None:
+            ce = CopyEngine(device=self.residency.device)
+            self._copy_engine = ce
+        return ce
+
+    def step_dma(self, lidx, page_table, page_cnt, block_table, seq_lens,
+                 n_req, wait: bool = True):
+        """``step`` with the flushed misses moved by the copy engines: plan
+        on the device, build the runs on the host (a sync), issue them on a
+        side stream that first waits for the current stream; staged misses
+        go to the kernel.  Returns the side stream's event; ``wait`` makes
+        the current stream wait on it (reference tier/tier.py:154-169)."""
+        self.residency.gather_plan(lidx, page_table, page_cnt, block_table,
+                                   seq_lens, n_req)
+        ev = self.residency.gather_fetch_dma(
+            lidx, self.staging, self.pool.dev_view, n_req, self.copy_engine,
+            poolk=self.pool_k.dev_view if self.pool_k else None)
+        if wait:
+            torch.cuda.current_stream(self.residency.device).wait_event(ev)
+        return ev
+
     def bytes_report(self) -> str:
         return (f"{self.pool.vram_note()}; {self.residency.bytes_report()}; "
                 f"staging={self.staging.v_pool.numel() * 2 / 2**30:.3f}GiB")
@@ -491,9 +633,9 @@ def mem_dynamic_decode(q, kv_cache, block_table, seq_lens, st, out, tier,
     """One layer of the tiered decode: residency step (plan + fetch) of the
     layer's selection, then the ptr-select decode (reference
     tier/decode_mem.py:225-274).  ``fetch="off"`` decodes from the current
-    residency without a step.  The reference's ``fetch="dma"`` (copy-engine
-    runs planned on the host) and its ``impl`` variants are not provided:
-    the kernel fetch is graph-capturable and the decode has one path."""
+    residency without a step; ``fetch="dma"`` moves the flushed misses with
+    the copy engines (host-planned runs, a host sync).  The reference's
+    ``impl`` variants are one decode path here."""
     if fetch not in _FETCH_MODES:
         raise ValueError(f"fetch must be one of {_FETCH_MODES}, got {fetch!r}")
     if impl not in ("ptrsel", "cuda"):
@@ -505,9 +647,14 @@ def mem_dynamic_decode(q, kv_cache, block_table, seq_lens, st, out, tier,
                   n_req)
         if st.page_table.shape[-1] == tier.residency.MP:
             es = tier.residency.miss_pages
+    elif fetch == "dma":
+        tier.step_dma(lidx, st.page_table, st.page_cnt, block_table, seq_lens,
+                      n_req, wait=True)
+        if st.page_table.shape[-1] == tier.residency.MP:
+            es = tier.residency.miss_pages
     mem_decode_ptrsel(q, kv_cache, block_table, seq_lens, st, out, tier, lidx,
                       scale=scale, entry_slots=es)
 
 
-__all__ = ["DevPtrTensor", "MappedHostVPool", "Residency", "Staging", "Tier",
+__all__ = ["CopyEngine", "DevPtrTensor", "MappedHostVPool", "Residency", "Staging", "Tier",
            "host_device_pointer", "mem_decode_ptrsel", "mem_dynamic_decode"]

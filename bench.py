@@ -677,6 +677,9 @@ def run_c5(args):
         x = torch.tensor([tier_step], device=dev)
         dist.all_reduce(x, op=dist.ReduceOp.MAX)
         tier_step = float(x.item())
+    wp = _c5_write_path(T, tier, kv, bt, sl, n5, NB, MP)
+    wp["begin_step_us_one_cta_walk"] = _c5_write_path(
+        T, tier, kv, bt, sl, n5, NB, MP, cand_cap=0)["begin_step_us_per_step"]
     n_pages_tot = NB
     kb = n_pages_tot * C5_KV * page_bytes
     summ = n_pages_tot * C5_KV * B_SUM
@@ -702,6 +705,7 @@ def run_c5(args):
                          "miss_fetch": round(float(t_fetch), 2),
                          "tiered_decode+merge": round(float(t_dec), 2),
                          "resident_decode+merge": round(float(t_res), 2)},
+            "write_path": wp,
             "hit_rate": round(1.0 - float(np.sum(misses)) /
                               max(1, float(np.sum(selected))), 4),
             "miss_pages_per_step": round(float(np.mean(misses)), 1),
@@ -715,6 +719,83 @@ def run_c5(args):
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def _c5_write_path(T, tier, kv, bt, sl, n5, NB, MP, n_steps=64,
+                   cand_cap=4096):
+    """The tier's write path at C5: a separate Staging replays the last
+    ``n_steps`` decode steps of every request (one prefill step that writes
+    each request's partial page, then one token per request per step) with
+    the true V bytes, so every flush rewrites the bytes the pinned pool
+    already holds.  Times begin_step (once per step, all layers' flushes; one
+    layer here) and scatter_kv (once per layer) as CUDA graphs."""
+    import torch
+    dev = kv.device
+    n_kv, d = kv.shape[3], kv.shape[4]
+    stg = T.Staging(num_layers=1, num_blocks=NB, n_kv=n_kv, page=PAGE, d=d,
+                    max_reqs=n5, max_pages=MP, max_tokens=n5 * PAGE,
+                    device=dev, cand_cap=cand_cap)
+    valid = torch.zeros((1, n_kv, NB), dtype=torch.int8, device=dev)
+    pool = tier.pool.dev_view
+    sl64 = sl[:n5].to(torch.int64)
+    start = sl64 - n_steps
+    ps = (start // PAGE) * PAGE
+    btl = bt[:n5].to(torch.int64)
+
+    def v_at(r_idx, pos):
+        blk = btl[r_idx, pos // PAGE]
+        return kv[blk, 1, pos % PAGE]                      # (n, n_kv, d)
+
+    # prefill step: positions [ps, start) of every request
+    qlp = (start - ps).to(torch.int32)
+    qslp = torch.zeros(n5 + 1, dtype=torch.int32, device=dev)
+    qslp[1:] = torch.cumsum(qlp, 0)
+    r_idx = torch.repeat_interleave(torch.arange(n5, device=dev),
+                                    qlp.to(torch.int64))
+    pos = ps[r_idx] + (torch.arange(r_idx.numel(), device=dev)
+                       - qslp[:-1].to(torch.int64)[r_idx])
+    n_tok = int(r_idx.numel())
+    stg.begin_step(bt, start.to(torch.int32), qslp, max(int(qlp.max()), 1),
+                   n_tok, pool=pool, pool_valid=valid)
+    if n_tok:
+        stg.scatter_kv(0, None, v_at(r_idx, pos).contiguous(), n_tok)
+    # decode timeline: graphs over fixed buffers
+    sl_g = start.to(torch.int32) + 1
+    qsl_g = torch.arange(n5 + 1, dtype=torch.int32, device=dev)
+    ar = torch.arange(n5, device=dev)
+    vals = torch.stack([v_at(ar, start + i) for i in range(n_steps)])
+    val_g = torch.empty_like(vals[0])
+    torch.cuda.synchronize()
+    stg.begin_step(bt, sl_g, qsl_g, 1, n5, pool=pool, pool_valid=valid)
+    val_g.copy_(vals[0])
+    stg.scatter_kv(0, None, val_g, n5)
+    g_bs, g_sc = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_bs):
+        stg.begin_step(bt, sl_g, qsl_g, 1, n5, pool=pool, pool_valid=valid)
+    with torch.cuda.graph(g_sc):
+        stg.scatter_kv(0, None, val_g, n5)
+    t_bs, t_sc, flushes = [], [], 0
+    for i in range(1, n_steps):
+        sl_g.copy_((start + i + 1).to(torch.int32))
+        val_g.copy_(vals[i])
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        e[0].record()
+        g_bs.replay()
+        e[1].record()
+        g_sc.replay()
+        e[2].record()
+        torch.cuda.synchronize()
+        t_bs.append(e[0].elapsed_time(e[1]) * 1e3)
+        t_sc.append(e[1].elapsed_time(e[2]) * 1e3)
+        flushes += int(stg.flush_cnt.item())
+    stg.assert_free_partition()
+    if int(stg.overflow.item()):
+        raise RuntimeError("write path: staging overflow at C5")
+    return {"begin_step_us_per_step": round(float(np.mean(t_bs[2:])), 2),
+            "scatter_us_per_layer": round(float(np.mean(t_sc[2:])), 2),
+            "flushed_pages_per_step": round(flushes / (n_steps - 1), 2),
+            "context_pages_walked_per_step": int((sl64 // PAGE).sum()),
+            "staging_blocks": stg.NV}
 
 
 # --------------------------------------------------------------------------- #

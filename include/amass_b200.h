@@ -326,6 +326,47 @@ int amass_tier_fetch(const int32_t* fetch_list, const int32_t* fetch_cnt,
                      const void* k_pool, int layer, int num_blocks, int n_kv,
                      int hot_slots, int page, int head_dim, void* stream);
 
+/* As amass_tier_fetch, but only the installs whose page is not flushed
+ * (pool_valid 0: staged, or neither staged nor flushed), exactly the ones
+ * amass_tier_dma_plan leaves out: the device half of the copy-engine fetch --
+ * Residency._gather_staged_only tier/residency.py:527-548. */
+int amass_tier_fetch_staged(
+    const int32_t* fetch_list, const int32_t* fetch_cnt, void* hot,
+    void* pool_dev, int8_t* pool_valid, const int32_t* vbo, const void* v_pool,
+    int64_t svb, int64_t svt, int64_t svh, void* hot_k, void* pool_k_dev,
+    const void* k_pool, int layer, int num_blocks, int n_kv, int hot_slots,
+    int page, int head_dim, void* stream);
+
+/* One copy-engine copy: `height` rows of `width` bytes, rows dpitch / spitch
+ * bytes apart (height 1: a plain copy); dst_k / src_k the same rows of the K
+ * tier under mem-kv (0 otherwise).  Addresses are device / UVA pointers. */
+typedef struct AmassDmaRun {
+  uint64_t dst, src, dst_k, src_k;
+  int64_t dpitch, spitch, width, height;
+} AmassDmaRun;
+
+/* HOST function (reads host copies of fetch_list (n_kv, S, 2), fetch_cnt
+ * (n_kv,) and this layer's pool_valid (n_kv, NB)) -- replaces
+ * Residency.build_dma_plan tier/residency.py:438-492.  Coalesces each
+ * kv-head's flushed installs into runs whose blocks and slots both advance
+ * by one; staged installs are skipped and reported in *has_staged.
+ * pool_base / hot_base: the pinned pool (L, NB, n_kv, page, d) and this
+ * layer's hot buffer (n_kv, S, page, d); the _k bases under mem-kv, else 0.
+ * AMASS_ERR_CAPACITY when more than max_runs runs are needed. */
+int amass_tier_dma_plan(const int32_t* fetch_list, const int32_t* fetch_cnt,
+                        const int8_t* pool_valid, int layer, int num_blocks,
+                        int n_kv, int hot_slots, int page, int head_dim,
+                        uint64_t pool_base, uint64_t hot_base,
+                        uint64_t pool_k_base, uint64_t hot_k_base,
+                        AmassDmaRun* runs, int max_runs, int* n_runs,
+                        int* has_staged);
+
+/* Issue a plan's runs on `stream` with the copy engines (cudaMemcpyAsync /
+ * cudaMemcpy2DAsync, one call per run and tier) -- replaces
+ * Residency.issue_dma_plan tier/residency.py:494-509 and CopyEngine
+ * tier/dma.py:77-140. */
+int amass_dma_issue(const AmassDmaRun* runs, int n_runs, void* stream);
+
 /* Drop residency and pool validity of the pages (re)written this step in all
  * layers -- replaces Residency.invalidate_written tier/residency.py:352-367
  * (kernel :251-282).  query_start_loc (n_req+1,); page2slot (L, n_kv, NB),
@@ -350,7 +391,11 @@ int amass_tier_invalidate(const int32_t* block_table, int64_t bt_stride,
  * (underflow sets overflow[0]); fill v_slot_mapping (int64) for this step's
  * tokens (vb * page + pos % page, or -1).  v_pool (L, NV, page, n_kv, d) at
  * element strides svl/svb/svt/svh; pool_valid (L, n_kv, NB).  Requests with
- * seq_len <= 0 or no new tokens are skipped. */
+ * seq_len <= 0 or no new tokens are skipped.  cand (1 + cand_cap int32,
+ * cand_cap <= 4096) is scratch for a whole-GPU pre-pass that lists the
+ * staged complete pages, so the ordered part only visits those; cand_cap 0,
+ * or more staged complete pages than cand_cap, walks every complete page in
+ * one CTA instead (same result). */
 int amass_staging_begin_step(
     const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
     const int32_t* query_start_loc, int n_req, int n_tokens, int max_query_len,
@@ -359,7 +404,8 @@ int amass_staging_begin_step(
     int32_t* flush_cnt, int32_t* overflow, int max_flush, const void* v_pool,
     const void* k_pool, int64_t svl, int64_t svb, int64_t svt, int64_t svh,
     void* pool_dev, void* pool_k_dev, int8_t* pool_valid, int num_layers,
-    int num_blocks, int n_kv, int head_dim, int page, void* stream);
+    int num_blocks, int n_kv, int head_dim, int page, int32_t* cand,
+    int cand_cap, void* stream);
 
 /* Write path: scatter this step's V (and K under mem-kv) (n_tokens, n_kv, d)
  * 16-bit into one layer's staging pool(s) (NV, page, n_kv, d) at

@@ -590,6 +590,38 @@ def residency_fetch(flist, *, hot, pool, pool_valid, vbo, v_pool, layer: int):
             hot[kv, slot] = pool[layer, blk, kv]
 
 
+def dma_plan_runs(fetch_list, fetch_cnt, pool_valid, *, layer: int, NB: int,
+                  page: int, d: int, pool_base: int, hot_base: int):
+    """Copy-engine runs of a fetch list (``residency.py:438-492``): per
+    kv-head, installs in list order; a flushed install starts a run that
+    extends while the next install's block and slot are both one more and
+    its page is flushed too; staged installs are skipped (has_staged).
+    fetch_list (n_kv, S, 2) = (block, slot); pool_valid (n_kv, NB).
+    Returns ([(dst, src, dpitch, spitch, width, height)], has_staged)."""
+    n_kv, S, _ = fetch_list.shape
+    pb = page * d * 2
+    runs, staged = [], False
+    for kv in range(n_kv):
+        m = int(fetch_cnt[kv])
+        i = 0
+        while i < m:
+            blk, slot = (int(x) for x in fetch_list[kv, i])
+            if pool_valid[kv, blk] == 0:
+                staged = True
+                i += 1
+                continue
+            run = 1
+            while (i + run < m and int(fetch_list[kv, i + run, 0]) == blk + run
+                   and int(fetch_list[kv, i + run, 1]) == slot + run
+                   and pool_valid[kv, blk + run] != 0):
+                run += 1
+            runs.append((hot_base + (kv * S + slot) * pb,
+                         pool_base + ((layer * NB + blk) * n_kv + kv) * pb,
+                         pb, n_kv * pb, pb, run))
+            i += run
+    return runs, staged
+
+
 def invalidate_written(block_table, seq_lens, query_start_loc, *, page: int,
                        page2slot, slot2page, pool_valid):
     """Drop residency and pool validity of every page a request (re)wrote

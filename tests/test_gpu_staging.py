@@ -119,20 +119,22 @@ def _random_steps(rng, R, MP, page, n_steps, chunk):
     return out
 
 
-@pytest.mark.parametrize("NV,MAXF,offload_k,d", [
-    (None, None, False, 128),   # default working-set sizing: no overflow
-    (None, None, True, 128),    # mem-kv: K staged and flushed beside V
-    (14, 3, False, 64),         # flush-list overflow (undo) and stack underflow
+@pytest.mark.parametrize("NV,MAXF,offload_k,d,cap", [
+    (None, None, False, 128, 4096),  # default sizing: no overflow
+    (None, None, True, 128, 4096),   # mem-kv: K staged and flushed beside V
+    (14, 3, False, 64, 4096),        # flush-list cap (undo), stack underflow
+    (None, None, False, 64, 0),      # collect walks every page (no pre-pass)
+    (None, None, False, 64, 2),      # pre-pass list overflows on some steps
 ])
-def test_staging_random_vs_oracle(dev, NV, MAXF, offload_k, d):
-    rng = np.random.default_rng(7 + (NV or 0) + d + offload_k)
+def test_staging_random_vs_oracle(dev, NV, MAXF, offload_k, d, cap):
+    rng = np.random.default_rng(7 + (NV or 0) + d + offload_k + cap)
     L, R, MP, page, n_kv, chunk = 3, 6, 12, 16, 4, 40
     NB = R * MP + 9
     max_tokens = R * chunk
     stg = T.Staging(num_layers=L, num_blocks=NB, n_kv=n_kv, page=page, d=d,
                     max_reqs=R, max_pages=MP, max_tokens=max_tokens,
                     device=dev, v_blocks=NV, max_flush=MAXF,
-                    offload_k=offload_k)
+                    offload_k=offload_k, cand_cap=cap)
     NVr, MAXFr = stg.NV, stg.MAXF
     bt_np = rng.permutation(NB)[:R * MP].astype(np.int32).reshape(R, MP)
     bt = torch.from_numpy(bt_np).to(dev)

@@ -138,14 +138,17 @@ def _random_tier_case(seed, *, n_req, n_kv, G, d, S, steps, L=2, layer=1,
                 d=d, S=S, n_req=n_req, mem_kv=mem_kv, invalidate=invalidate)
 
 
-@pytest.mark.parametrize("seed,n_req,n_kv,G,d,S,mem_kv,inval", [
-    (0, 4, 2, 4, 128, 40, False, False),
-    (1, 6, 4, 8, 64, 24, False, True),
-    (2, 3, 2, 4, 128, 6, False, False),       # overflow: S below one step
-    (3, 5, 2, 4, 128, 64, True, True),        # mem-kv
-    (4, 8, 8, 4, 128, 300, False, False),
+@pytest.mark.parametrize("seed,n_req,n_kv,G,d,S,mem_kv,inval,fetch", [
+    (0, 4, 2, 4, 128, 40, False, False, "kernel"),
+    (1, 6, 4, 8, 64, 24, False, True, "kernel"),
+    (2, 3, 2, 4, 128, 6, False, False, "kernel"),  # overflow: S below a step
+    (3, 5, 2, 4, 128, 64, True, True, "kernel"),   # mem-kv
+    (4, 8, 8, 4, 128, 300, False, False, "kernel"),
+    (0, 4, 2, 4, 128, 40, False, False, "dma"),    # copy engines + staged kernel
+    (3, 5, 2, 4, 128, 64, True, True, "dma"),      # mem-kv over copy engines
 ])
-def test_tier_random_vs_oracle(seed, n_req, n_kv, G, d, S, mem_kv, inval, dev):
+def test_tier_random_vs_oracle(seed, n_req, n_kv, G, d, S, mem_kv, inval,
+                               fetch, dev):
     c = _random_tier_case(seed, n_req=n_req, n_kv=n_kv, G=G, d=d, S=S,
                           steps=4, mem_kv=mem_kv, invalidate=inval)
     rng, page, NB, L, layer = c["rng"], c["page"], c["NB"], c["L"], c["layer"]
@@ -211,7 +214,7 @@ def test_tier_random_vs_oracle(seed, n_req, n_kv, G, d, S, mem_kv, inval, dev):
         q = torch.from_numpy(q_all[s]).to(torch.bfloat16).to(dev)
         out = torch.zeros(q.shape, dtype=torch.bfloat16, device=dev)
         T.mem_dynamic_decode(q, kv_dev, bt, sl, st, out, tier, layer,
-                             scale=d ** -0.5)
+                             scale=d ** -0.5, fetch=fetch)
         res = torch.zeros_like(out)
         A.sparse_paged_decode_batched_cuda(q, kv_true, bt, sl, st, res,
                                            scale=d ** -0.5)
@@ -329,3 +332,62 @@ def test_invalidate_golden(dev):
     assert np.array_equal(r5.page2slot.cpu().numpy(), z["page2slot"])
     assert np.array_equal(r5.slot2page.cpu().numpy(), z["slot2page"])
     assert np.array_equal(r5.pool_valid.cpu().numpy(), z["pool_valid"])
+
+
+@pytest.mark.parametrize("mem_kv", [False, True])
+def test_tier_dma_coalesced_runs(mem_kv, dev):
+    """A fresh hot buffer takes victims in slot order, so one request whose
+    blocks are consecutive installs consecutive blocks into consecutive
+    slots: the copy-engine plan coalesces them into a few strided 2-D runs
+    (staged blocks break runs and go to the staged-only kernel), and the hot
+    buffer, pool and validity end bit-equal to the kernel fetch's."""
+    n_kv, G, d, page, S = 2, 4, 128, 16, 64
+    NB, MP = 80, 48
+    res = {}
+    for mode in ("kernel", "dma"):
+        tier = T.Tier(num_layers=1, num_blocks=NB, n_kv=n_kv, page=page, d=d,
+                      hot_slots=S, max_reqs=1, max_pages=MP, n_vslots=8,
+                      offload_k=mem_kv, device=dev)
+        r5, stg = tier.residency, tier.staging
+        g = torch.Generator().manual_seed(5)
+        host = torch.randn(tier.pool.host.shape, generator=g)
+        tier.pool.host.copy_(host.to(torch.bfloat16))
+        if mem_kv:
+            tier.pool_k.host.copy_((-host).to(torch.bfloat16))
+        r5.pool_valid.fill_(1)
+        for i, blk in enumerate((20, 31)):          # staged, not flushed
+            stg.vbo[blk] = i
+            stg.v_pool[0, i].fill_(float(i + 2))
+            if mem_kv:
+                stg.k_pool[0, i].fill_(float(-i - 2))
+            r5.pool_valid[0, :, blk] = 0
+        bt = torch.arange(10, 10 + MP, dtype=torch.int32,
+                          device=dev)[None].contiguous()
+        sl = torch.tensor([MP * page], dtype=torch.int32, device=dev)
+        tab = torch.full((1, n_kv, MP), -1, dtype=torch.int32, device=dev)
+        cnt = torch.tensor([[40, 33]], dtype=torch.int32, device=dev)
+        tab[0, 0, :40] = torch.arange(40, dtype=torch.int32)
+        tab[0, 1, :33] = torch.arange(5, 38, dtype=torch.int32)
+        if mode == "kernel":
+            tier.step(0, tab, cnt, bt, sl, 1)
+        else:
+            r5.gather_plan(0, tab, cnt, bt, sl, 1)
+            runs, staged = r5.build_dma_plan(0, tier.pool.dev_view, 1,
+                                             tier.pool_k.dev_view
+                                             if mem_kv else None)
+            assert staged
+            assert 0 < len(runs) <= 6, len(runs)
+            assert sum(r.height for r in runs) == 40 + 33 - 2 - 2
+            ev = r5.gather_fetch_dma(0, stg, tier.pool.dev_view, 1,
+                                     tier.copy_engine,
+                                     poolk=tier.pool_k.dev_view
+                                     if mem_kv else None)
+            torch.cuda.current_stream(dev).wait_event(ev)
+        torch.cuda.synchronize(dev)
+        res[mode] = (_bits(r5.hot), _bits(r5.hot_k) if mem_kv else None,
+                     tier.pool.host.view(torch.int16).numpy().copy(),
+                     r5.pool_valid.cpu().numpy(),
+                     r5.slot2page.cpu().numpy())
+    for a, b in zip(res["kernel"], res["dma"]):
+        if a is not None:
+            assert np.array_equal(a, b)
