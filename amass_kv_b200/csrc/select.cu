@@ -93,26 +93,29 @@ struct SelArgs {
 
 // nrm fold of one unit (reference quad_score.py:293-315): sc[p] =
 // sum_g exp(S_g[p] - hmax_g) for p < nsh; writes score; resets hmax to -inf.
+// GM: the largest G this instantiation serves (registers hold GM x KQ
+// 16-byte loads per thread, all issued before any use).
+template <int GM = 8, int KQ = 1>
 AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int nsh, float* sc) {
   const float* sh = a.score_h + (int64_t)unit * a.G * a.SHS;
   float* hm_g = a.hmax + (int64_t)unit * a.G;
-  float hm[8];
+  float hm[GM];
 #pragma unroll
-  for (int g = 0; g < 8; ++g) hm[g] = g < a.G ? hm_g[g] : 0.f;
+  for (int g = 0; g < GM; ++g) hm[g] = g < a.G ? hm_g[g] : 0.f;
   float* so = a.score + (int64_t)unit * a.MP;
   // batches of pages per thread: every load of a batch issues before any
   // use, so a long unit costs a few memory round trips, not one per page
   if ((a.SHS & 3) == 0 && (reinterpret_cast<uintptr_t>(a.score_h) & 15) == 0) {
     // 16-byte loads: thread owns page quads tid, tid + kSelThreads, ...
-    constexpr int kQ = 1;
+    constexpr int kQ = KQ;
     const int nq = (nsh + 3) >> 2;
     for (int q0 = threadIdx.x; q0 < nq; q0 += kQ * kSelThreads) {
-      float4 v[kQ][8];
+      float4 v[kQ][GM];
 #pragma unroll
       for (int i = 0; i < kQ; ++i) {
         const int q = q0 + i * kSelThreads;
 #pragma unroll
-        for (int g = 0; g < 8; ++g)
+        for (int g = 0; g < GM; ++g)
           v[i][g] = (g < a.G && q < nq)
                         ? __ldcg(reinterpret_cast<const float4*>(sh + (int64_t)g * a.SHS) + q)
                         : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -123,7 +126,7 @@ AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int nsh, float* sc) {
         if (q < nq) {
           float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int g = 0; g < 8; ++g) {
+          for (int g = 0; g < GM; ++g) {
             if (g < a.G) {
               s4[0] += expf(v[i][g].x - hm[g]);
               s4[1] += expf(v[i][g].y - hm[g]);
@@ -142,12 +145,12 @@ AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int nsh, float* sc) {
   } else {
     constexpr int kB = 8;
     for (int p0 = threadIdx.x; p0 < nsh; p0 += kB * kSelThreads) {
-      float v[kB][8];
+      float v[kB][GM];
 #pragma unroll
       for (int i = 0; i < kB; ++i) {
         const int p = p0 + i * kSelThreads;
 #pragma unroll
-        for (int g = 0; g < 8; ++g)
+        for (int g = 0; g < GM; ++g)
           v[i][g] = (g < a.G && p < nsh) ? __ldcg(sh + (int64_t)g * a.SHS + p) : 0.f;
       }
 #pragma unroll
@@ -156,7 +159,7 @@ AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int nsh, float* sc) {
         if (p < nsh) {
           float s1 = 0.f;
 #pragma unroll
-          for (int g = 0; g < 8; ++g)
+          for (int g = 0; g < GM; ++g)
             if (g < a.G) s1 += expf(v[i][g] - hm[g]);
           sc[p] = s1;
           so[p] = s1;
@@ -371,7 +374,7 @@ AMASS_DEV uint32_t find_tau(const float* sc, int lo_p, int hi_p, int k,
 
 // FOLD: fold score_h (nrm) into score first.  LIN: page mass = score (nrm
 // semantics) instead of exp(score - max) (max semantics).
-template <bool FOLD, bool LIN, bool COVERAGE>
+template <bool FOLD, bool LIN, bool COVERAGE, int GM = 8>
 __global__ void __launch_bounds__(kSelThreads, 4)
 select_kernel(SelArgs a) {
   grid_dep_wait();     // inputs written by the previous kernel
@@ -388,7 +391,7 @@ select_kernel(SelArgs a) {
   SEL_PROBE(0);
   if (nsh > 0) {
     if (FOLD) {
-      nrm_fold(a, unit, nsh, sc);
+      nrm_fold<GM, (GM <= 4 ? 2 : 1)>(a, unit, nsh, sc);
     } else {
       const float* si = a.score + (int64_t)unit * a.MP;
       constexpr int kB = 8;
@@ -515,9 +518,10 @@ constexpr int kMaxSmem = 160 * 1024;
 template <bool FOLD, bool LIN, bool COV>
 int launch_select(const SelArgs& a, int units, cudaStream_t st) {
   const size_t smem = (size_t)a.MP * sizeof(float);
-  auto k = select_kernel<FOLD, LIN, COV>;
-  static unsigned long long configured = 0;
-  if (first_on_device(configured)) {
+  const bool g4 = FOLD && a.G <= 4;
+  auto k = g4 ? select_kernel<FOLD, LIN, COV, 4> : select_kernel<FOLD, LIN, COV, 8>;
+  static unsigned long long configured[2] = {0, 0};
+  if (first_on_device(configured[g4 ? 1 : 0])) {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          kMaxSmem);
   }
