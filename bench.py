@@ -341,13 +341,32 @@ def run_gpu(args):
         dist.barrier()
     x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(
         enable_timing=True)
-    x0.record()
-    for i in range(args.steps):
-        qd.copy_(qh[i % L], non_blocking=True)
-        batch.sl.copy_(slh, non_blocking=True)
-        batch.step(i % L, q=qd)
-        outh.copy_(batch.out_full if kvmode else batch.out, non_blocking=True)
-    x1.record()
+    pipe = None
+    if not kvmode and not batch.clse and not args.no_graph:
+        # the serving form of the public API: captured layer-steps, copies
+        # on their own streams overlapping the neighbouring steps
+        from amass_kv_b200.pipeline import StepPipeline
+        pipe = StepPipeline(batch.st, [batch.kv[l] for l in range(L)],
+                            batch.bt, n_req=N_REQ, scale=batch.scale,
+                            q_shape=tuple(batch.q.shape[1:]), device=dev)
+        for i in range(args.warmup):
+            pipe.submit(i % L, qh[i % L], slh, outh)
+        pipe.synchronize()
+        x0.record()
+        pipe.h2d.wait_stream(torch.cuda.current_stream())
+        for i in range(args.steps):
+            pipe.submit(i % L, qh[i % L], slh, outh)
+        torch.cuda.current_stream().wait_stream(pipe.d2h)
+        x1.record()
+    else:
+        x0.record()
+        for i in range(args.steps):
+            qd.copy_(qh[i % L], non_blocking=True)
+            batch.sl.copy_(slh, non_blocking=True)
+            batch.step(i % L, q=qd)
+            outh.copy_(batch.out_full if kvmode else batch.out,
+                       non_blocking=True)
+        x1.record()
     torch.cuda.synchronize()
     e2e_ms = x0.elapsed_time(x1)
     if world > 1:
