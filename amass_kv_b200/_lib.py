@@ -44,6 +44,8 @@ _SIGS = {
     "amass_summarize_pages": [_P, _I, _L, _L, _L, _P, _I, _I, _I, _I, _I, _I,
                               _I, _P, _P, _P, _P, _I, _I, _P, _P, _I, _P, _P,
                               _I, _I, _P, _P],
+    "amass_tag_stale": [_P, _I, _L, _L, _L, _P, _I, _I, _I, _I, _I, _P, _I,
+                        _P, _P, _P],
     "amass_nrm_combine": [_P, _L, _P, _P, _P, _I, _I, _I, _I, _P],
     "amass_topb_select": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "amass_select_pages": [_P, _L, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I,

@@ -90,6 +90,7 @@ summary_kernel(SumArgs a) {
     const int rem = item - l * per_layer;
     const int bi = rem / a.n_kv, h = rem - bi * a.n_kv;
     const int64_t blk = a.blocks[bi];
+    if (blk < 0) continue;                       // not stale (delta rebuild)
     const __nv_bfloat16* kp = a.k[l] + blk * a.kb + h * a.kh + lane * PER;
     // ---- keys -> registers; mean; centred keys; sum of squares -----------
     float x[kPg][PER];
@@ -407,6 +408,88 @@ extern "C" int amass_summarize_pages(
   }
   auto kern = head_dim == 128 ? summary_kernel<128> : summary_kernel<64>;
   if (int rc = launch_pdl(kern, dim3(grid), dim3(kSumWarps * 32), smem, st, a))
+    return rc;
+  return launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// Content-tag staleness of candidate blocks (reference selection/build.py:
+// 532-545): a block is stale when, in ANY layer and kv-head, its stored tag
+// differs from the leading tagw channels of its page-final key (compared as
+// floats: a NaN-initialised tag is always stale).  One warp per candidate.
+// ---------------------------------------------------------------------------
+namespace amass {
+namespace {
+
+struct TagArgs {
+  const __nv_bfloat16* k[kMaxLayers];
+  int64_t kb, kt, kh;
+  const __nv_bfloat16* tag;   // (Ltot, NB, n_kv, tagw)
+  const int32_t* in;
+  int32_t* out;
+  int32_t* count;
+  int n, n_layers, l0, NB, n_kv, tagw, page;
+};
+
+__global__ void __launch_bounds__(256) tag_stale_kernel(TagArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int lane = threadIdx.x & 31;
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (i >= a.n) return;
+  const int blk = a.in[i];
+  bool stale = false;
+  if (blk >= 0) {
+    const int per = a.n_kv * a.tagw;
+    for (int e = lane; e < a.n_layers * per && !stale; e += 32) {
+      const int l = e / per, rem = e - l * per;
+      const int kv = rem / a.tagw, w = rem - kv * a.tagw;
+      const float cur = __bfloat162float(
+          a.k[l][(int64_t)blk * a.kb + (int64_t)(a.page - 1) * a.kt + kv * a.kh + w]);
+      const float old = __bfloat162float(
+          a.tag[(((int64_t)(a.l0 + l) * a.NB + blk) * a.n_kv + kv) * a.tagw + w]);
+      stale = cur != old;
+    }
+  }
+  stale = __any_sync(0xffffffffu, stale);
+  if (lane == 0) {
+    a.out[i] = stale ? blk : -1;
+    if (stale) atomicAdd(a.count, 1);
+  }
+}
+
+}  // namespace
+}  // namespace amass
+
+extern "C" int amass_tag_stale(const void* const* k_layers, int n_layers,
+                               int64_t k_sb, int64_t k_st, int64_t k_sh,
+                               const void* tag, int layer0, int num_blocks,
+                               int n_kv, int tagw, int page,
+                               const int32_t* blocks_in, int n_blocks,
+                               int32_t* blocks_out, int32_t* count,
+                               void* stream) {
+  using namespace amass;
+  if (!k_layers || n_layers <= 0 || n_layers > kMaxLayers || !tag ||
+      layer0 < 0 || num_blocks <= 0 || n_kv <= 0 || tagw <= 0 || page <= 0 ||
+      n_blocks < 0 || !count)
+    return AMASS_ERR_ARG;
+  if (n_blocks > 0 && (!blocks_in || !blocks_out)) return AMASS_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(count, 0, sizeof(int32_t), st) != cudaSuccess)
+    return AMASS_ERR_CUDA;
+  if (n_blocks == 0) return AMASS_OK;
+  TagArgs a{};
+  for (int l = 0; l < n_layers; ++l) {
+    if (!k_layers[l]) return AMASS_ERR_ARG;
+    a.k[l] = static_cast<const __nv_bfloat16*>(k_layers[l]);
+  }
+  a.kb = k_sb; a.kt = k_st; a.kh = k_sh;
+  a.tag = static_cast<const __nv_bfloat16*>(tag);
+  a.in = blocks_in; a.out = blocks_out; a.count = count;
+  a.n = n_blocks; a.n_layers = n_layers; a.l0 = layer0; a.NB = num_blocks;
+  a.n_kv = n_kv; a.tagw = tagw; a.page = page;
+  if (int rc = launch_pdl(tag_stale_kernel, dim3((n_blocks + 7) / 8), dim3(256),
+                          0, st, a))
     return rc;
   return launch_status();
 }

@@ -125,8 +125,47 @@ def quad_build_bulk(st, K_layers, block_table, seq_lens, n_req: int,
     return len(K_layers) * int(blocks.numel())
 
 
+def delta_blocks(block_table, seq_lens, n_req: int, page: int, max_fin: int):
+    """Blocks of every finalized page p < min(seq_len // page, max_fin) of
+    the first n_req requests, -1 elsewhere (device ops)."""
+    sl = seq_lens[:n_req].to(torch.int64)
+    fin = (sl // page).clamp_(max=max_fin)
+    bt = block_table[:n_req, :max_fin].to(torch.int64)
+    p = torch.arange(max_fin, device=bt.device)[None, :]
+    return torch.where(p < fin[:, None], bt, -1).reshape(-1).to(torch.int32)
+
+
+def quad_build_delta(st, K_layers, block_table, seq_lens, n_req: int,
+                     max_fin: int, chunk_pairs: int = 8192) -> int:
+    """Composition-change rebuild: every finalized block whose content tag
+    (leading tag channels of its page-final key) no longer matches the live
+    keys in some layer is rebuilt in all layers of ``K_layers`` (reference
+    quad_build.py:110-121, build.py:532-545).  One tag kernel and one
+    summary launch; returns layers x stale (request, page) entries rebuilt
+    (a host read, like the reference's count)."""
+    if n_req == 0 or max_fin <= 0:
+        return 0
+    tag = getattr(st, "r8_tag", None) if hasattr(st, "r8_mu") else \
+        getattr(st, "quad_tag", None)
+    if tag is None:
+        raise ValueError("the state has no content tags (tagw = 0)")
+    arr, k0 = _layers_arg(K_layers)
+    cand = delta_blocks(block_table, seq_lens, n_req, st.page, max_fin)
+    stale = torch.empty_like(cand)
+    count = torch.zeros(1, dtype=torch.int32, device=cand.device)
+    _lib.call("amass_tag_stale", ctypes.cast(arr, ctypes.c_void_p), len(arr),
+              k0.stride(0), k0.stride(1), k0.stride(2), ptr(tag), 0,
+              int(tag.shape[1]), int(st.n_kv), int(tag.shape[-1]),
+              int(st.page), ptr(cand), int(cand.numel()), ptr(stale),
+              ptr(count), _lib.stream_of(k0.device))
+    summarize_pages(st, K_layers, stale)
+    return len(K_layers) * int(count.item())
+
+
 r8_build_tail = quad_build_tail
 r8_build_bulk = quad_build_bulk
+r8_build_delta = quad_build_delta
 
-__all__ = ["bulk_blocks", "quad_build_bulk", "quad_build_tail",
+__all__ = ["bulk_blocks", "delta_blocks", "quad_build_bulk", "quad_build_delta",
+           "r8_build_delta", "quad_build_tail",
            "r8_build_bulk", "r8_build_tail", "summarize_pages", "tail_blocks"]

@@ -182,7 +182,7 @@ int amass_clse_score(const void* q, int64_t q_stride_t, int64_t q_stride_h,
  * (NB, n_kv) fp16 = sum K^2 - 16 |mu|^2 - sum lambda, or NULL.  Slabs are the
  * whole layer-major arrays (first layer at index 0).  Eigenvectors are
  * unique up to sign.  head_dim in {64, 128}, page = 16, rank <= 8,
- * n_layers <= 128. */
+ * n_layers <= 128.  Negative entries of `blocks` are skipped. */
 int amass_summarize_pages(const void* const* k_layers, int n_layers,
                           int64_t k_sb, int64_t k_st, int64_t k_sh,
                           const int32_t* blocks, int n_blocks, int layer0,
@@ -191,6 +191,20 @@ int amass_summarize_pages(const void* const* k_layers, int n_layers,
                           void* V_scale, int v_bits, int v_tensor, void* sig2,
                           void* tag, int tagw, int8_t* c, void* c_scale,
                           int c_bits, int c_mode, void* resid, void* stream);
+
+/* Content-tag staleness for the delta rebuild -- replaces the tag pass of
+ * quad_build_delta / r8_build_delta (selection/build.py:532-545,
+ * quad_build.py:110-121): blocks_out[i] = blocks_in[i] when, in any of the
+ * n_layers layers (slab layer layer0 + l) and any kv-head, the stored tag
+ * (Ltot, NB, n_kv, tagw) bf16 differs (as floats; NaN always differs) from
+ * the first tagw channels of the block's last-token key, else -1 (also for
+ * negative inputs); *count = number of stale entries.  Feed blocks_out to
+ * amass_summarize_pages, which skips the -1 entries. */
+int amass_tag_stale(const void* const* k_layers, int n_layers, int64_t k_sb,
+                    int64_t k_st, int64_t k_sh, const void* tag, int layer0,
+                    int num_blocks, int n_kv, int tagw, int page,
+                    const int32_t* blocks_in, int n_blocks, int32_t* blocks_out,
+                    int32_t* count, void* stream);
 
 /* sparse_paged_decode -- replaces attention/decode_cuda.py:1376-1465
  * (Triton golden attention/decode.py:247-304 + merge.py:21-50).

@@ -622,6 +622,24 @@ def dma_plan_runs(fetch_list, fetch_cnt, pool_valid, *, layer: int, NB: int,
     return runs, staged
 
 
+def delta_stale(tag, K, block_table, seq_lens, *, page: int, max_fin: int):
+    """Content-tag staleness (``selection/build.py:532-545``): the blocks of
+    finalized pages p < min(seq_len // page, max_fin), in (request, page)
+    order, whose stored tag (L, NB, n_kv, tagw) differs -- as floats, NaN
+    always -- from the first tagw channels of the page-final key in ANY
+    layer.  K (L, NB, page, n_kv, d) float."""
+    tagw = tag.shape[-1]
+    out = []
+    for r in range(len(seq_lens)):
+        for p in range(min(int(seq_lens[r]) // page, max_fin)):
+            blk = int(block_table[r, p])
+            cur = K[:, blk, page - 1, :, :tagw]
+            with np.errstate(invalid="ignore"):
+                if (cur != tag[:, blk]).any():
+                    out.append(blk)
+    return out
+
+
 def invalidate_written(block_table, seq_lens, query_start_loc, *, page: int,
                        page2slot, slot2page, pool_valid):
     """Drop residency and pool validity of every page a request (re)wrote

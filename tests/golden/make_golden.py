@@ -44,7 +44,8 @@ from amass.attention.decode import (ResidentVSource,  # noqa: E402
                                     sparse_paged_decode_batched)
 from amass.backend._selection_bridge import _nucleus_b  # noqa: E402
 from amass.tier.residency import Residency  # noqa: E402
-from amass.selection.quad_build import quad_build_tail  # noqa: E402
+from amass.selection.quad_build import quad_build_tail, quad_build_bulk  # noqa: E402
+from amass.selection.build import _delta_select  # noqa: E402
 from amass.tier.staging import Staging  # noqa: E402
 from amass.tier.decode_mem import mem_decode_ptrsel  # noqa: E402
 
@@ -335,6 +336,48 @@ def gen_staging(name, *, seed=31, L=2, NB=40, n_kv=2, d=64, page=16,
     print(name, "final top", int(stg.v_free_top), "ovf", int(stg.overflow))
 
 
+def gen_delta(name, *, seed=41, n_req=3, n_kv=2, d=64, L=2):
+    """The reference's content-tag staleness pass (_delta_select) after a
+    bulk build, once the keys of some blocks changed: in a tag channel of
+    the page-final token (stale), in a non-tag channel (not stale), and one
+    tag reset to NaN (stale)."""
+    rng = np.random.default_rng(seed)
+    page, ctxs = 16, [70, 130, 41]
+    npg = [(c + page - 1) // page for c in ctxs]
+    NB = sum(npg) + 3
+    perm = rng.permutation(NB).astype(np.int32)
+    MP = max(npg)
+    bt = np.zeros((n_req, MP), np.int32)
+    o = 0
+    for i, n in enumerate(npg):
+        bt[i, :n] = perm[o:o + n]
+        o += n
+    Kb = t_bf16(rng.standard_normal((L, NB, page, n_kv, d)).astype(np.float32))
+    st = QuadState("cpu", num_layers=L, num_blocks=NB, n_kv=n_kv, G=4,
+                   head_dim=d, page=page, max_reqs=n_req, max_pages=MP,
+                   rank=2, budget=0.1, v_bits=4)
+    sl = torch.tensor(ctxs, dtype=torch.int32)
+    max_fin = max(c // page for c in ctxs)
+    quad_build_bulk(st, [Kb[l] for l in range(L)], torch.from_numpy(bt), sl,
+                    n_req, max_fin)
+    fin = [bt[r, p] for r in range(n_req) for p in range(ctxs[r] // page)]
+    pick = rng.choice(fin, 5, replace=False)
+    Kb[1, pick[0], page - 1, 1, 2] += 1.0        # tag channel, layer 1
+    Kb[0, pick[1], page - 1, 0, 0] += 1.0        # tag channel, layer 0
+    Kb[0, pick[2], page - 1, 0, 40] += 1.0       # not a tag channel
+    Kb[1, pick[3], 3, 1, 1] += 1.0               # not the page-final token
+    st.quad_tag[0, pick[4], 1, 5] = float("nan")
+    stale = _delta_select(st.quad_tag, [Kb[l] for l in range(L)],
+                          torch.from_numpy(bt), sl, n_req, page, max_fin,
+                          st.tagw)
+    np.savez_compressed(
+        os.path.join(HERE, name + ".npz"), K=bf16_bits(Kb),
+        tag=bf16_bits(st.quad_tag), block_table=bt,
+        seq_lens=np.array(ctxs, np.int32), max_fin=np.array([max_fin]),
+        stale=stale.numpy().astype(np.int32))
+    print(name, "stale", stale.tolist(), "picked", pick.tolist())
+
+
 def gen_tier(name, case, *, budget, hot_slots=10, steps=3, seed=5):
     """Residency gather over several steps with forced eviction, staged and
     flushed sources, then the ptr-select tiered decode."""
@@ -484,6 +527,7 @@ def main():
                          r=4, v_bits=8, c_bits=8, c_grain="token")
     gen_clse("clse_r4_i8_tok_max", cl3, budget=0.1, combine="max")
     gen_staging("tier_staging")
+    gen_delta("build_delta_tags")
     gen_build("build_quad_i4", seed=21, n_req=3, n_kv=2, d=128,
               ctxs=[100, 257, 16], L=2, r=2, v_bits=4, coords="none")
     gen_build("build_clse_i8", seed=22, n_req=2, n_kv=2, d=64,

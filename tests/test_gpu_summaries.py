@@ -130,3 +130,73 @@ def test_r8_state_build_matches_oracle(dev):
     cr = s["c_code"].astype(np.float32) * s["c_s"].astype(np.float32)[..., None]
     sg = np.sign((cg * cr).sum(axis=2, keepdims=True))
     assert np.abs(cr - sg * cg).max() <= 1.5 * s["c_s"].astype(np.float32).max()
+
+
+def test_tag_stale_matches_reference(dev):
+    """The staleness kernel marks exactly the blocks the reference's tag
+    pass selects, in order (tag-channel edits and a NaN tag; edits outside
+    the tag channels or the page-final token stay fresh)."""
+    import ctypes
+    from amass_kv_b200 import _lib
+    z = load_golden("build_delta_tags")
+    K = torch.from_numpy(z["K"]).view(torch.bfloat16).to(dev)
+    tag = torch.from_numpy(z["tag"]).view(torch.bfloat16).to(dev)
+    L = K.shape[0]
+    bt = torch.from_numpy(z["block_table"]).to(dev)
+    sl = torch.from_numpy(z["seq_lens"]).to(dev)
+    mf = int(z["max_fin"][0])
+    cand = SU.delta_blocks(bt, sl, bt.shape[0], 16, mf)
+    out = torch.empty_like(cand)
+    cnt = torch.zeros(1, dtype=torch.int32, device=dev)
+    ks = [K[l] for l in range(L)]
+    arr = (ctypes.c_void_p * L)(*[k.data_ptr() for k in ks])
+    _lib.call("amass_tag_stale", ctypes.cast(arr, ctypes.c_void_p), L,
+              ks[0].stride(0), ks[0].stride(1), ks[0].stride(2),
+              tag.data_ptr(), 0, K.shape[1], K.shape[3], tag.shape[-1], 16,
+              cand.data_ptr(), cand.numel(), out.data_ptr(), cnt.data_ptr(),
+              _lib.stream_of(dev))
+    o = out.cpu().numpy()
+    assert o[o >= 0].tolist() == z["stale"].tolist()
+    assert int(cnt.item()) == len(z["stale"])
+
+
+def test_delta_rebuild_equals_bulk(dev):
+    """First delta (NaN tags) rebuilds every finalized block; a second finds
+    nothing; after keys of two blocks change, the delta result equals a
+    bulk rebuild of the changed keys, slab for slab."""
+    rng = np.random.default_rng(9)
+    L, n_kv, d, page = 3, 4, 128, 16
+    ctxs = [300, 517, 64, 129]
+    npg = [(c + page - 1) // page for c in ctxs]
+    NB = sum(npg) + 5
+    perm = rng.permutation(NB).astype(np.int32)
+    MP = max(npg)
+    bt_np = np.zeros((len(ctxs), MP), np.int32)
+    o = 0
+    for i, n in enumerate(npg):
+        bt_np[i, :n] = perm[o:o + n]
+        o += n
+    bt = torch.from_numpy(bt_np).to(dev)
+    sl = torch.tensor(ctxs, dtype=torch.int32, device=dev)
+    K = torch.randn((L, NB, page, n_kv, d), device=dev).to(torch.bfloat16)
+    mk = lambda: QuadState(dev, num_layers=L, num_blocks=NB, n_kv=n_kv, G=4,  # noqa: E731
+                           head_dim=d, page=page, max_reqs=len(ctxs),
+                           max_pages=MP, rank=2, budget=0.1, v_bits=4)
+    st, ref = mk(), mk()
+    mf = max(c // page for c in ctxs)
+    n_fin = sum(c // page for c in ctxs)
+    ks = [K[l] for l in range(L)]
+    assert SU.quad_build_delta(st, ks, bt, sl, len(ctxs), mf) == L * n_fin
+    assert SU.quad_build_delta(st, ks, bt, sl, len(ctxs), mf) == 0
+    K[2, int(bt_np[1, 7]), page - 1, 3, 0] += 2.0
+    K[0, int(bt_np[0, 2]), page - 1, 0, 7] -= 1.0
+    assert SU.quad_build_delta(st, ks, bt, sl, len(ctxs), mf) == 2 * L
+    SU.quad_build_bulk(ref, ks, bt, sl, len(ctxs), mf)
+    torch.cuda.synchronize()
+    fin = [int(bt_np[r, p]) for r in range(len(ctxs))
+           for p in range(ctxs[r] // page)]
+    for name in ("quad_mu", "mu_scale", "quad_V", "V_scale", "quad_sig2",
+                 "quad_tag"):
+        a = getattr(st, name)[:, fin].view(torch.int8)
+        b = getattr(ref, name)[:, fin].view(torch.int8)
+        assert torch.equal(a, b), name

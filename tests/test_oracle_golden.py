@@ -346,3 +346,12 @@ def test_staging_lifecycle_vs_reference():
         assert np.array_equal(valid, z[f"valid_{s}"]), s
         assert np.array_equal(st["v_pool"], z[f"vpool_{s}"]), s
         assert st["ovf"] == int(z[f"ovf_{s}"][0]), s
+
+
+def test_delta_stale_vs_reference():
+    z = load_golden("build_delta_tags")
+    K = bits_to_f32(z["K"])
+    tag = bits_to_f32(z["tag"])
+    got = O.delta_stale(tag, K, z["block_table"], z["seq_lens"], page=16,
+                        max_fin=int(z["max_fin"][0]))
+    assert got == z["stale"].tolist()
