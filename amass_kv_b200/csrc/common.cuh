@@ -205,6 +205,18 @@ AMASS_DEV uint32_t ldg_nc_u32(const void* p) {
 }
 
 // Programmatic dependent launch: wait for the producing grid's memory.
+// PTX ex2.approx / lg2.approx (relative error about 2^-22; 2^-inf = 0)
+AMASS_DEV float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+AMASS_DEV float lg2_approx(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 AMASS_DEV void grid_dep_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }

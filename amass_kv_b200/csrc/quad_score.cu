@@ -29,6 +29,7 @@
 // maximum into hmax[r, h, g]; the fold (nrm_combine / select_pages) consumes
 // it and resets it to -inf, so the fold is a single pass.
 #include <algorithm>
+#include <cstdlib>
 #include <type_traits>
 
 #include "common.cuh"
@@ -543,8 +544,8 @@ AMASS_DEV void stage_coords(const Item<D, R, VB>& it, const QuadArgs& a,
   }
 }
 
-template <int D, int R, int VB, int CB>
-__global__ void __launch_bounds__(kQuadWarps * 32, 1)
+template <int D, int R, int VB, int CB, bool TS = false>
+__global__ void __launch_bounds__(kQuadWarps * 32, TS ? 2 : 1)
 r8_score_kernel(QuadArgs a) {
   grid_dep_wait();
   grid_dep_launch();
@@ -646,76 +647,195 @@ r8_score_kernel(QuadArgs a) {
       qsqv[0] = __ldg(qr_ + min(2 * c, a.G - 1));
       qsqv[1] = __ldg(qr_ + min(2 * c + 1, a.G - 1));
     }
+    if constexpr (TS) {
+      // token split (G <= 4, rank <= 4): lane c evaluates tokens 4c..4c+3
+      // of its two pages for all four head slots, so each token's code is
+      // decoded once per quad of lanes instead of four times and no logits
+      // are spent on head slots >= 4; the per-(page, head) log-sum-exp is
+      // then combined across the quad's lanes
+      float qtl[2][2][R];
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int pl = m + 8 * half;                 // page within the tile
-      const int p = cur.p0 + pl;
-      const float mus = half ? __high2float(cur.mus) : __low2float(cur.mus);
-      float qt[2][R];
-#pragma unroll
-      for (int jj = 0; jj < 2; ++jj) {
-        const int idx = 2 * half + jj;
-#pragma unroll
-        for (int k = 0; k < R; ++k)
-          qt[jj][k] = (float)(128 * acc[1 + k][0][idx] + acc[1 + k][1][idx]) *
-                      (qf.sq[jj] * vdiv) * cur.vsf(half, k);
-      }
-      const float csp = half ? __high2float(csp_cur) : __low2float(csp_cur);
-      // token logits in the log2 domain: two passes (max, then sum)
-      float tk2[2][PG];
-#pragma unroll
-      for (int tk = 0; tk < PG; ++tk) {
-        const bool tv = p * PG + tk < sl_r;
-        const uint8_t* row = cb + (pl * PG + tk) * RC;
-        float code[R];
-        if constexpr (CB == 8) {
-#pragma unroll
-          for (int k = 0; k < R; ++k) code[k] = (float)(int8_t)row[k];
-        } else {
-#pragma unroll
-          for (int k = 0; k < R; k += 2) {
-            const int b = (int8_t)row[k / 2];
-            code[k] = (float)((b << 28) >> 28);
-            code[k + 1] = (float)(b >> 4);
-          }
-        }
-        const float cs = (a.ctok ? __half2float(csb[pl * PG + tk]) : csp) * a.scale;
+      for (int half = 0; half < 2; ++half)
 #pragma unroll
         for (int jj = 0; jj < 2; ++jj) {
-          float d = 0.f;
+          const int idx = 2 * half + jj;
 #pragma unroll
-          for (int k = 0; k < R; ++k) d += code[k] * qt[jj][k];
-          tk2[jj][tk] = tv ? d * cs * kL2e : -INFINITY;
+          for (int k = 0; k < R; ++k)
+            qtl[half][jj][k] = (float)(128 * acc[1 + k][0][idx] + acc[1 + k][1][idx]) *
+                               (qf.sq[jj] * vdiv) * cur.vsf(half, k);
+        }
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int pl = m + 8 * half;
+        const int p = cur.p0 + pl;
+        float qa[4][R];
+#pragma unroll
+        for (int g = 0; g < 4; ++g)
+#pragma unroll
+          for (int k = 0; k < R; ++k)
+            qa[g][k] = __shfl_sync(0xffffffffu, qtl[half][g & 1][k],
+                                   (lane & ~3) | (g >> 1));
+        constexpr int RCT = R8Tok<R, CB>::RC;
+        const uint8_t* rowp = cb + (pl * PG + 4 * c) * RCT;
+        uint32_t cw[RCT];
+        if constexpr (RCT == 1) {
+          cw[0] = *reinterpret_cast<const uint32_t*>(rowp);
+        } else if constexpr (RCT == 2) {
+          const uint2 x = *reinterpret_cast<const uint2*>(rowp);
+          cw[0] = x.x; cw[1] = x.y;
+        } else {
+          const uint4 x = *reinterpret_cast<const uint4*>(rowp);
+          cw[0] = x.x; cw[1] = x.y; cw[2] = x.z; cw[3] = x.w;
+        }
+        float csv[4];
+        if (a.ctok) {
+          const uint2 sw = *reinterpret_cast<const uint2*>(csb + pl * PG + 4 * c);
+          csv[0] = __half2float(__ushort_as_half((uint16_t)(sw.x & 0xffffu)));
+          csv[1] = __half2float(__ushort_as_half((uint16_t)(sw.x >> 16)));
+          csv[2] = __half2float(__ushort_as_half((uint16_t)(sw.y & 0xffffu)));
+          csv[3] = __half2float(__ushort_as_half((uint16_t)(sw.y >> 16)));
+        } else {
+          const float csp = half ? __high2float(csp_cur) : __low2float(csp_cur);
+          csv[0] = csv[1] = csv[2] = csv[3] = csp;
+        }
+        float lg[4][4];                              // [head slot][token]
+#pragma unroll
+        for (int tk = 0; tk < 4; ++tk) {
+          float code[R];
+#pragma unroll
+          for (int k = 0; k < (CB == 8 ? R : R / 2); ++k) {
+            const int bi = tk * RCT + k;
+            const int b = (int)(int8_t)((cw[bi >> 2] >> (8 * (bi & 3))) & 0xffu);
+            if constexpr (CB == 8) {
+              code[k] = (float)b;
+            } else {
+              code[2 * k] = (float)((b << 28) >> 28);
+              code[2 * k + 1] = (float)(b >> 4);
+            }
+          }
+          const bool tv = p * PG + 4 * c + tk < sl_r;
+          const float cs = csv[tk] * a.scale * kL2e;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            float d = 0.f;
+#pragma unroll
+            for (int k = 0; k < R; ++k) d += code[k] * qa[g][k];
+            lg[g][tk] = tv ? d * cs : -INFINITY;
+          }
+        }
+        float agg[4];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          float mx = fmaxf(fmaxf(lg[g][0], lg[g][1]), fmaxf(lg[g][2], lg[g][3]));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+          if (a.tokmax) {
+            agg[g] = mx * kLn2;
+          } else {
+            // hardware 2^x / log2 (rel. error ~2^-22); 2^-inf = 0 covers
+            // masked tokens, and an all-masked row keeps agg = -inf
+            float sm = 0.f;
+#pragma unroll
+            for (int tk = 0; tk < 4; ++tk) sm += ex2_approx(lg[g][tk] - mx);
+            sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+            sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+            agg[g] = mx == -INFINITY ? -INFINITY : (mx + lg2_approx(sm)) * kLn2;
+          }
+        }
+        const float mus = half ? __high2float(cur.mus) : __low2float(cur.mus);
+        const float res = a.resid ? __half2float(a.resid[half ? cur.rowb : cur.rowa]) : 0.f;
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int g = 2 * c + jj;
+          float ag = -INFINITY;
+#pragma unroll
+          for (int gg = 0; gg < 4; ++gg) ag = gg == g ? agg[gg] : ag;
+          const int idx = 2 * half + jj;
+          const float qmu = (float)(128 * acc[0][0][idx] + acc[0][1][idx]) * qf.sq[jj] *
+                            mus * a.scale;
+          float S = qmu + ag;
+          if (a.resid) {
+            float qh = 0.f;
+#pragma unroll
+            for (int k = 0; k < R; ++k) qh += qtl[half][jj][k] * qtl[half][jj][k];
+            S += fmaxf(qsqv[jj] - qh, 0.f) * res * a.iso_coef;
+          }
+          Sv[half][jj] = S;
+          if (g < a.G) best[half] = fmaxf(best[half], S);
         }
       }
-      // CLSE: the out-of-subspace energy (|q|^2 - |q~|^2) * resid * coef
-      const float res = a.resid ? __half2float(a.resid[half ? cur.rowb : cur.rowa]) : 0.f;
+    } else {
 #pragma unroll
-      for (int jj = 0; jj < 2; ++jj) {
-        float mx = -INFINITY;
-#pragma unroll
-        for (int tk = 0; tk < PG; ++tk) mx = fmaxf(mx, tk2[jj][tk]);
-        float agg;
-        if (a.tokmax) {
-          agg = mx * kLn2;
-        } else {
-          float sm = 0.f;
-#pragma unroll
-          for (int tk = 0; tk < PG; ++tk) sm += exp2f(tk2[jj][tk] - mx);
-          agg = (mx + log2f(sm)) * kLn2;
+      for (int half = 0; half < 2; ++half) {
+        const int pl = m + 8 * half;                 // page within the tile
+        const int p = cur.p0 + pl;
+        const float mus = half ? __high2float(cur.mus) : __low2float(cur.mus);
+        float qt[2][R];
+  #pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int idx = 2 * half + jj;
+  #pragma unroll
+          for (int k = 0; k < R; ++k)
+            qt[jj][k] = (float)(128 * acc[1 + k][0][idx] + acc[1 + k][1][idx]) *
+                        (qf.sq[jj] * vdiv) * cur.vsf(half, k);
         }
-        const int idx = 2 * half + jj;
-        const float qmu = (float)(128 * acc[0][0][idx] + acc[0][1][idx]) * qf.sq[jj] *
-                          mus * a.scale;
-        float S = qmu + agg;
-        if (a.resid) {
-          float qh = 0.f;
-#pragma unroll
-          for (int k = 0; k < R; ++k) qh += qt[jj][k] * qt[jj][k];
-          S += fmaxf(qsqv[jj] - qh, 0.f) * res * a.iso_coef;
+        const float csp = half ? __high2float(csp_cur) : __low2float(csp_cur);
+        // token logits in the log2 domain: two passes (max, then sum)
+        float tk2[2][PG];
+  #pragma unroll
+        for (int tk = 0; tk < PG; ++tk) {
+          const bool tv = p * PG + tk < sl_r;
+          const uint8_t* row = cb + (pl * PG + tk) * RC;
+          float code[R];
+          if constexpr (CB == 8) {
+  #pragma unroll
+            for (int k = 0; k < R; ++k) code[k] = (float)(int8_t)row[k];
+          } else {
+  #pragma unroll
+            for (int k = 0; k < R; k += 2) {
+              const int b = (int8_t)row[k / 2];
+              code[k] = (float)((b << 28) >> 28);
+              code[k + 1] = (float)(b >> 4);
+            }
+          }
+          const float cs = (a.ctok ? __half2float(csb[pl * PG + tk]) : csp) * a.scale;
+  #pragma unroll
+          for (int jj = 0; jj < 2; ++jj) {
+            float d = 0.f;
+  #pragma unroll
+            for (int k = 0; k < R; ++k) d += code[k] * qt[jj][k];
+            tk2[jj][tk] = tv ? d * cs * kL2e : -INFINITY;
+          }
         }
-        Sv[half][jj] = S;
-        if (2 * c + jj < a.G) best[half] = fmaxf(best[half], S);
+        // CLSE: the out-of-subspace energy (|q|^2 - |q~|^2) * resid * coef
+        const float res = a.resid ? __half2float(a.resid[half ? cur.rowb : cur.rowa]) : 0.f;
+  #pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          float mx = -INFINITY;
+  #pragma unroll
+          for (int tk = 0; tk < PG; ++tk) mx = fmaxf(mx, tk2[jj][tk]);
+          float agg;
+          if (a.tokmax) {
+            agg = mx * kLn2;
+          } else {
+            float sm = 0.f;
+  #pragma unroll
+            for (int tk = 0; tk < PG; ++tk) sm += ex2_approx(tk2[jj][tk] - mx);
+            agg = mx == -INFINITY ? -INFINITY : (mx + lg2_approx(sm)) * kLn2;
+          }
+          const int idx = 2 * half + jj;
+          const float qmu = (float)(128 * acc[0][0][idx] + acc[0][1][idx]) * qf.sq[jj] *
+                            mus * a.scale;
+          float S = qmu + agg;
+          if (a.resid) {
+            float qh = 0.f;
+  #pragma unroll
+            for (int k = 0; k < R; ++k) qh += qt[jj][k] * qt[jj][k];
+            S += fmaxf(qsqv[jj] - qh, 0.f) * res * a.iso_coef;
+          }
+          Sv[half][jj] = S;
+          if (2 * c + jj < a.G) best[half] = fmaxf(best[half], S);
+        }
       }
     }
     if (a.write_h) {
@@ -757,9 +877,20 @@ r8_score_kernel(QuadArgs a) {
   cp_async_wait<0>();
 }
 
+template <int D, int CB, int VB, int R, bool TS>
+int launch_r8_k(const QuadArgs& a, cudaStream_t st);
+
 template <int D, int CB, int VB, int R = 8>
 int launch_r8(const QuadArgs& a, cudaStream_t st) {
-  auto k = r8_score_kernel<D, R, VB, CB>;
+  if constexpr (R <= 4) {
+    if (a.G <= 4 && !getenv("AMASS_CLSE_OLD")) return launch_r8_k<D, CB, VB, R, true>(a, st);
+  }
+  return launch_r8_k<D, CB, VB, R, false>(a, st);
+}
+
+template <int D, int CB, int VB, int R, bool TS>
+int launch_r8_k(const QuadArgs& a, cudaStream_t st) {
+  auto k = r8_score_kernel<D, R, VB, CB, TS>;
   constexpr int RC = R8Tok<R, CB>::RC;
   const size_t smem = (size_t)kQuadWarps * 2 * (16 * 16 * RC + 16 * 16 * 2);
   static int ps = 0;
