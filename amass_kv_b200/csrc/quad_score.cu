@@ -883,7 +883,7 @@ int launch_r8_k(const QuadArgs& a, cudaStream_t st);
 template <int D, int CB, int VB, int R = 8>
 int launch_r8(const QuadArgs& a, cudaStream_t st) {
   if constexpr (R <= 4) {
-    if (a.G <= 4 && !getenv("AMASS_CLSE_OLD")) return launch_r8_k<D, CB, VB, R, true>(a, st);
+    if (a.G <= 4) return launch_r8_k<D, CB, VB, R, true>(a, st);
   }
   return launch_r8_k<D, CB, VB, R, false>(a, st);
 }
