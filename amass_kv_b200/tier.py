@@ -19,6 +19,7 @@ ptr-select decode that reads each page from hot | staging | pinned.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 
@@ -53,6 +54,60 @@ class DevPtrTensor:
         return self._ptr
 
 
+def gpu_local_cpus(device) -> list | None:
+    """CPUs of the NUMA node nearest ``device`` (NVML's CPU affinity of the
+    GPU, looked up by PCI bus id so CUDA_VISIBLE_DEVICES renumbering does not
+    matter), or None when NVML is unavailable.  Read-only NVML queries."""
+    try:
+        import pynvml
+    except ImportError:
+        return None
+    props = torch.cuda.get_device_properties(device)
+    bus = (f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:"
+           f"{props.pci_device_id:02x}.0")
+    try:
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            n = (os.cpu_count() + 63) // 64
+            words = pynvml.nvmlDeviceGetCpuAffinity(h, n)
+        finally:
+            pynvml.nvmlShutdown()
+    except Exception:
+        return None
+    cpus = [64 * i + b for i, w in enumerate(words) for b in range(64)
+            if (int(w) >> b) & 1]
+    return cpus or None
+
+
+class _cpu_affinity:
+    """Run the body on ``cpus`` (first-touch placement of host pages on
+    their NUMA node), then restore the caller's affinity."""
+
+    def __init__(self, cpus):
+        self.cpus = cpus
+
+    def __enter__(self):
+        self.old = None
+        if self.cpus and hasattr(os, "sched_setaffinity"):
+            self.old = os.sched_getaffinity(0)
+            allowed = set(self.cpus) & self.old
+            if allowed:
+                os.sched_setaffinity(0, allowed)
+                # one writer thread: pool threads keep their own affinity
+                self.threads = torch.get_num_threads()
+                torch.set_num_threads(1)
+            else:
+                self.old = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.old is not None:
+            torch.set_num_threads(self.threads)
+            os.sched_setaffinity(0, self.old)
+        return False
+
+
 class MappedHostVPool:
     """Pinned host pool (L, NB, n_kv, page, d) + its device view.  The page of
     (layer, block, kv-head) starts at element ((l*NB + blk)*n_kv + kv)*page*d
@@ -60,7 +115,7 @@ class MappedHostVPool:
 
     def __init__(self, *, num_layers: int, num_blocks: int, n_kv: int,
                  page: int, d: int, dtype=torch.bfloat16, device=None,
-                 max_pool_gb: float = 256.0):
+                 max_pool_gb: float = 256.0, numa_local: bool = True):
         if dtype not in (torch.bfloat16, torch.float16):
             raise ValueError(f"pool dtype must be bf16/fp16, got {dtype}")
         self.L, self.NB, self.n_kv = num_layers, num_blocks, n_kv
@@ -73,8 +128,13 @@ class MappedHostVPool:
                 "max_pool_gb (host DRAM, not VRAM)")
         dev = torch.device(device) if device is not None else \
             torch.device("cuda", torch.cuda.current_device())
-        self.host = torch.zeros((num_layers, num_blocks, n_kv, page, d),
-                                dtype=dtype, pin_memory=True)
+        # pages are placed where they are first written: zero the pool from
+        # the CPUs next to this GPU, so its host-link reads stay on-node
+        self.numa_cpus = gpu_local_cpus(dev) if numa_local else None
+        with _cpu_affinity(self.numa_cpus):
+            self.host = torch.empty((num_layers, num_blocks, n_kv, page, d),
+                                    dtype=dtype, pin_memory=True)
+            self.host.zero_()
         self.dev_view = DevPtrTensor(host_device_pointer(self.host),
                                      torch.int16, dev, tuple(self.host.shape))
         self.pool_gib = pool_bytes / 2**30
