@@ -638,19 +638,20 @@ def run_c5(args):
         if k == 0:
             S.derive_page_params(st, sl, n5)
             S._score_launch(st, 0, qbuf, bt, n5, scale, COMBINE == "nrm")
-            S.select_pages(st, n5, from_score_h=COMBINE == "nrm")
         elif k == 1:
-            r5.gather_plan(0, st.page_table, st.page_cnt, bt, sl, n5)
+            S.select_pages(st, n5, from_score_h=COMBINE == "nrm")
         elif k == 2:
-            r5.gather_fetch(0, tier.staging, tier.pool.dev_view)
+            r5.gather_plan(0, st.page_table, st.page_cnt, bt, sl, n5)
         elif k == 3:
+            r5.gather_fetch(0, tier.staging, tier.pool.dev_view)
+        elif k == 4:
             T.mem_decode_ptrsel(qbuf, kv_k_only, bt, sl, st, out, tier, 0,
                                 scale=scale, entry_slots=r5.miss_pages)
         else:
             A.sparse_paged_decode_batched_cuda(qbuf, kv, bt, sl, st, out_res,
                                                scale=scale)
 
-    NS = 5
+    NS = 6
     set_q(0)
     for k in range(NS):                  # eager first use (attributes)
         stage(k)
@@ -661,12 +662,18 @@ def run_c5(args):
         with torch.cuda.graph(g):
             stage(k)
         graphs.append(g)
+    # the whole tier step (score .. tiered decode) as one graph: the
+    # reported value; the per-stage graphs above give its breakdown
+    g_step = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_step):
+        for k in range(5):
+            stage(k)
     torch.cuda.synchronize()
     page_bytes = PAGE * D * 2
     warm = max(args.warmup, 10)
     for i in range(1, warm + 1):
         set_q(i)
-        for g in graphs[:4]:
+        for g in graphs[:5]:
             g.replay()
     torch.cuda.synchronize()
     steps = max(args.steps, 20) if args.steps else 20
@@ -687,10 +694,21 @@ def run_c5(args):
             equal = equal and bool(torch.equal(out, out_res))
     t = np.array([[e[k].elapsed_time(e[k + 1]) for k in range(NS)]
                   for e in ev]) * 1e3                          # us
-    t_sel, t_plan, t_fetch, t_dec, t_res = t.mean(0)
-    tier_step = t_sel + t_plan + t_fetch + t_dec
+    t_score, t_select, t_plan, t_fetch, t_dec, t_res = t.mean(0)
+    # whole-step graph, same q drift, continuing the residency state
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(
+        enable_timing=True)
+    full = []
+    for i in range(steps):
+        set_q(warm + steps + 1 + i)
+        e0.record()
+        g_step.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        full.append(e0.elapsed_time(e1) * 1e3)
+    tier_step = float(np.mean(full))
     miss_b = np.array(misses) * page_bytes
-    link = float(miss_b.sum() / (t[:, 2].sum() * 1e-6) / 1e9) \
+    link = float(miss_b.sum() / (t[:, 3].sum() * 1e-6) / 1e9) \
         if miss_b.sum() else 0.0
     if world > 1:
         x = torch.tensor([tier_step], device=dev)
@@ -719,7 +737,10 @@ def run_c5(args):
                        f"pages ({hot_slots} slots/kv-head), budget 0.05, "
                        "quad r'=2 int4-V nrm, q rotating 0.02 rad/step",
                        "NB": NB},
-            "stage_us": {"derive+score+select": round(float(t_sel), 2),
+            "stage_us": {"note": "per-stage graphs (sum differs from the "
+                                 "whole-step value by graph boundaries)",
+                         "derive+score": round(float(t_score), 2),
+                         "select": round(float(t_select), 2),
                          "residency_plan": round(float(t_plan), 2),
                          "miss_fetch": round(float(t_fetch), 2),
                          "tiered_decode+merge": round(float(t_dec), 2),
