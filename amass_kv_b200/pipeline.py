@@ -25,13 +25,18 @@ class StepPipeline:
     host memory.  Host tensors should be pinned (the copies are
     asynchronous); ``out_host`` must not be read before ``synchronize()``.
 
-    st: a QuadState with its Stage-B buffers; kv_caches: per layer the
+    st: a QuadState with its Stage-B buffers (``scorer="clse"``: one built
+    with coordinates, ``coords="lse"``); kv_caches: per layer the
     (NB, 2, page, n_kv, d) bf16 cache; block_table (R, MP) int32 on the
     device (fixed for the pipeline's life -- replace its contents between
     steps only after ``synchronize()``)."""
 
     def __init__(self, st, kv_caches, block_table, *, n_req: int,
-                 scale: float, q_shape, device=None):
+                 scale: float, q_shape, device=None, scorer: str = "quad"):
+        if scorer not in ("quad", "clse"):
+            raise ValueError(f"scorer must be 'quad' or 'clse', got {scorer!r}")
+        self.select = S.select_pages_quad if scorer == "quad" else \
+            S.select_pages_clse
         dev = torch.device(device) if device is not None else \
             block_table.device
         self.dev, self.st, self.kv = dev, st, list(kv_caches)
@@ -74,8 +79,8 @@ class StepPipeline:
     def _step(self, layer: int, b: int) -> None:
         st, n = self.st, self.n_req
         S.derive_page_params(st, self.sl[b], n)
-        S.select_pages_quad(st, layer, self.q[b], self.bt, self.sl[b], n,
-                            self.scale, derive=False)
+        self.select(st, layer, self.q[b], self.bt, self.sl[b], n, self.scale,
+                    derive=False)
         A.sparse_paged_decode_batched_cuda(self.q[b], self.kv[layer], self.bt,
                                            self.sl[b], st, self.out[b],
                                            scale=self.scale)

@@ -342,13 +342,14 @@ def run_gpu(args):
     x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(
         enable_timing=True)
     pipe = None
-    if not kvmode and not batch.clse and not args.no_graph:
+    if not kvmode and not args.no_graph:
         # the serving form of the public API: captured layer-steps, copies
         # on their own streams overlapping the neighbouring steps
         from amass_kv_b200.pipeline import StepPipeline
         pipe = StepPipeline(batch.st, [batch.kv[l] for l in range(L)],
                             batch.bt, n_req=N_REQ, scale=batch.scale,
-                            q_shape=tuple(batch.q.shape[1:]), device=dev)
+                            q_shape=tuple(batch.q.shape[1:]), device=dev,
+                            scorer="clse" if batch.clse else "quad")
         for i in range(args.warmup):
             pipe.submit(i % L, qh[i % L], slh, outh)
         pipe.synchronize()
