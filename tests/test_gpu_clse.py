@@ -90,19 +90,22 @@ def test_clse_matches_reference(name, dev):
                                z["page_cnt"], ref)
 
 
-@pytest.mark.parametrize("seed,d,r,v_bits,c_bits,c_grain,combine", [
-    (11, 128, 2, 4, 4, "token", "nrm"),
-    (12, 128, 2, 4, 8, "page", "max"),
-    (13, 64, 8, 8, 8, "token", "nrm"),
+@pytest.mark.parametrize("seed,d,r,v_bits,c_bits,c_grain,combine,G", [
+    (11, 128, 2, 4, 4, "token", "nrm", 4),
+    (12, 128, 2, 4, 8, "page", "max", 4),
+    (13, 64, 8, 8, 8, "token", "nrm", 4),
+    (14, 128, 2, 4, 4, "token", "nrm", 2),   # token split, two head slots idle
+    (15, 128, 4, 4, 8, "token", "max", 3),   # rank 4, int8 codes (4-byte rows)
+    (16, 64, 4, 4, 4, "page", "nrm", 8),     # G = 8: per-lane-head form
 ])
 def test_clse_random_vs_oracle(seed, d, r, v_bits, c_bits, c_grain, combine,
-                               dev):
-    cs = make_clse_case(seed, n_req=5, n_kv=4, G=4, d=d,
+                               G, dev):
+    cs = make_clse_case(seed, n_req=5, n_kv=4, G=G, d=d,
                         ctxs=(3000, 1700, 16, 260, 900), r=r, v_bits=v_bits,
                         c_bits=c_bits, c_grain=c_grain)
     x = cs.extra
     NB = cs.K.shape[0]
-    st = _state(dev, NB=NB, n_kv=4, G=4, d=d, n_req=5, MP=cs.MP, r=r,
+    st = _state(dev, NB=NB, n_kv=4, G=G, d=d, n_req=5, MP=cs.MP, r=r,
                 v_bits=v_bits, c_bits=c_bits, c_grain=c_grain,
                 combine=combine, budget=0.1)
     _fill(st, cs.mu, cs.mu_s, cs.Vq, cs.V_s, cs.sig2, x["c"], x["c_s"],
@@ -115,7 +118,7 @@ def test_clse_random_vs_oracle(seed, d, r, v_bits, c_bits, c_grain, combine,
     nsh = st.n_sel_hi.cpu().numpy()
     sh = O.clse_score_h(cs.q, cs.mu, cs.mu_s, cs.Vq, cs.V_s, x["c"], x["c_s"],
                         x["resid"], cs.block_table, cs.seq_lens, nsh,
-                        scale=cs.scale, page=16, G=4, r=r, v_bits=v_bits,
+                        scale=cs.scale, page=16, G=G, r=r, v_bits=v_bits,
                         c_bits=c_bits, token_grain=c_grain == "token",
                         MP=cs.MP)
     ref = O.combine_nrm(sh, nsh) if combine == "nrm" else O.combine_max(sh, nsh)
