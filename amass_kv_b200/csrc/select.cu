@@ -14,6 +14,8 @@
 // MASS -- and the range shrinks to that bin.  A bin of at most 64 keys is
 // resolved exactly by ranking its members.  Typical units finish in one
 // level: one pass over global memory, one histogram pass, one compaction.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace amass {
@@ -91,12 +93,15 @@ struct SelArgs {
   float coverage;
 };
 
-// nrm fold of one unit (reference quad_score.py:293-315): sc[p] =
-// sum_g exp(S_g[p] - hmax_g) for p < nsh; writes score; resets hmax to -inf.
+// nrm fold of one unit (reference quad_score.py:293-315): sc[p - p_lo] =
+// sum_g exp(S_g[p] - hmax_g) for p in [p_lo, p_hi) (p_lo a multiple of 4);
+// writes score; resets hmax to -inf when `reset` (after the barrier).
 // GM: the largest G this instantiation serves (registers hold GM x KQ
 // 16-byte loads per thread, all issued before any use).
 template <int GM = 8, int KQ = 1>
-AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int nsh, float* sc) {
+AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int p_lo, int p_hi,
+                        float* sc, bool reset = true) {
+  const int nsh = p_hi;
   const float* sh = a.score_h + (int64_t)unit * a.G * a.SHS;
   float* hm_g = a.hmax + (int64_t)unit * a.G;
   float hm[GM];
@@ -109,7 +114,7 @@ AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int nsh, float* sc) {
     // 16-byte loads: thread owns page quads tid, tid + kSelThreads, ...
     constexpr int kQ = KQ;
     const int nq = (nsh + 3) >> 2;
-    for (int q0 = threadIdx.x; q0 < nq; q0 += kQ * kSelThreads) {
+    for (int q0 = (p_lo >> 2) + threadIdx.x; q0 < nq; q0 += kQ * kSelThreads) {
       float4 v[kQ][GM];
 #pragma unroll
       for (int i = 0; i < kQ; ++i) {
@@ -137,14 +142,14 @@ AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int nsh, float* sc) {
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int p = 4 * q + e;
-            if (p < nsh) { sc[p] = s4[e]; so[p] = s4[e]; }
+            if (p < nsh) { sc[p - p_lo] = s4[e]; so[p] = s4[e]; }
           }
         }
       }
     }
   } else {
     constexpr int kB = 8;
-    for (int p0 = threadIdx.x; p0 < nsh; p0 += kB * kSelThreads) {
+    for (int p0 = p_lo + threadIdx.x; p0 < nsh; p0 += kB * kSelThreads) {
       float v[kB][GM];
 #pragma unroll
       for (int i = 0; i < kB; ++i) {
@@ -161,14 +166,14 @@ AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int nsh, float* sc) {
 #pragma unroll
           for (int g = 0; g < GM; ++g)
             if (g < a.G) s1 += expf(v[i][g] - hm[g]);
-          sc[p] = s1;
+          sc[p - p_lo] = s1;
           so[p] = s1;
         }
       }
     }
   }
   __syncthreads();
-  if (threadIdx.x < a.G) hm_g[threadIdx.x] = -INFINITY;
+  if (reset && threadIdx.x < a.G) hm_g[threadIdx.x] = -INFINITY;
 }
 
 __global__ void __launch_bounds__(kSelThreads)
@@ -182,7 +187,7 @@ nrm_combine_kernel(SelArgs a) {
     if (threadIdx.x < a.G) a.hmax[(int64_t)unit * a.G + threadIdx.x] = -INFINITY;
     return;
   }
-  nrm_fold(a, unit, nsh, sc);
+  nrm_fold(a, unit, 0, nsh, sc);
 }
 
 struct SelShared {
@@ -203,14 +208,45 @@ struct SelShared {
   uint32_t tau;
   uint32_t lowest;
   uint32_t kmin, kmax;
+  // cluster form: the merged histogram / candidates and exchange slots
+  // that the other CTAs of the unit read through distributed shared memory
+  uint32_t mhist[kBins];
+  float mmass[kBins];
+  uint32_t acand[kCand];
+  float amass[kCand];
+  int nall;
+  uint32_t x_kmin, x_kmax;
+  float x_vmax, x_tot, x_alw;
+  int x_above, x_cnt;
 };
+
+namespace cg = cooperative_groups;
+
+// all-reduce of a per-CTA value over the cluster: every CTA publishes its
+// value in `slot` (its own shared memory), then reads all ranks' slots in
+// rank order (identical result in every CTA).  One cluster barrier.
+template <typename T, typename Op>
+AMASS_DEV T cl_allreduce(T* slot, T v, Op op) {
+  cg::cluster_group cl = cg::this_cluster();
+  if (threadIdx.x == 0) *slot = v;
+  cl.sync();
+  T r = *cl.map_shared_rank(slot, 0);
+  for (unsigned k = 1; k < cl.num_blocks(); ++k)
+    r = op(r, *cl.map_shared_rank(slot, k));
+  return r;
+}
 
 // tau over the keys of sc[lo_p, hi_p).  COV: mass walk to `need`; else the
 // k-th largest key.  mass(v) = LIN ? v : exp(v - shift).
-template <bool COV, bool LIN>
+// CLU: the unit's pages are spread over the CTAs of a cluster (sc / lo_p /
+// hi_p are this CTA's slice); histograms and candidates are merged across
+// the cluster, so every CTA walks the same merged bins to the same tau.
+template <bool COV, bool LIN, bool CLU = false>
 AMASS_DEV uint32_t find_tau(const float* sc, int lo_p, int hi_p, int k,
                             float need, float shift_v, uint32_t kmin,
                             uint32_t kmax, SelShared& sh) {
+  uint32_t* H = CLU ? sh.mhist : sh.hist;
+  float* HM = CLU ? sh.mmass : sh.hmass;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint32_t lo = kmin, hi = kmax;
   if (COV && !(need > 0.f)) return kmax;      // b = 1: the top page only
@@ -233,7 +269,23 @@ AMASS_DEV uint32_t find_tau(const float* sc, int lo_p, int hi_p, int k,
         if (COV) atomicAdd(&sh.hmass[b], LIN ? v : expf(v - shift_v));
       }
     }
-    __syncthreads();
+    if constexpr (CLU) {
+      cg::cluster_group cl = cg::this_cluster();
+      cl.sync();                       // every slice's histogram is built
+      for (int i = threadIdx.x; i < kBins; i += kSelThreads) {
+        uint32_t c = 0;
+        float mm = 0.f;
+        for (unsigned q = 0; q < cl.num_blocks(); ++q) {
+          c += cl.map_shared_rank(sh.hist, q)[i];
+          if (COV) mm += cl.map_shared_rank(sh.hmass, q)[i];
+        }
+        sh.mhist[i] = c;
+        if (COV) sh.mmass[i] = mm;
+      }
+      cl.sync();                       // remote reads done before reuse
+    } else {
+      __syncthreads();
+    }
     // bin scan by the whole block: warp w owns the w-th 1/kSelWarps of the
     // bins counted from the top, each lane kPL consecutive bins
     {
@@ -243,8 +295,8 @@ AMASS_DEV uint32_t find_tau(const float* sc, int lo_p, int hi_p, int k,
       float ml = 0.f;
 #pragma unroll
       for (int i = 0; i < kPL; ++i) {
-        cl += sh.hist[kBins - 1 - (d0 + i)];
-        if (COV) ml += sh.hmass[kBins - 1 - (d0 + i)];
+        cl += H[kBins - 1 - (d0 + i)];
+        if (COV) ml += HM[kBins - 1 - (d0 + i)];
       }
       uint32_t ci = cl;
       float mi = ml;
@@ -268,9 +320,9 @@ AMASS_DEV uint32_t find_tau(const float* sc, int lo_p, int hi_p, int k,
         float am = mex;
         for (int i = 0; i < kPL; ++i) {
           const int b = kBins - 1 - (d0 + i);
-          const uint32_t cb = sh.hist[b];
+          const uint32_t cb = H[b];
           if (cb == 0) continue;
-          const float mm = COV ? sh.hmass[b] : 0.f;
+          const float mm = COV ? HM[b] : 0.f;
           if (COV ? (am + mm >= need) : (ac + cb >= (uint32_t)k)) {
             sh.bin = b; sh.above_c = ac; sh.above_m = am; sh.hit = 1;
             break;
@@ -292,11 +344,11 @@ AMASS_DEV uint32_t find_tau(const float* sc, int lo_p, int hi_p, int k,
           float lm = 0.f;
           for (int i = 0; i < kPL; ++i) {
             const int b = kBins - 1 - (d0 + i);
-            const uint32_t cb = sh.hist[b];
+            const uint32_t cb = H[b];
             if (cb == 0) continue;
             last = b; lc = ac; lm = am;
             ac += cb;
-            am += COV ? sh.hmass[b] : 0.f;
+            am += COV ? HM[b] : 0.f;
           }
           sh.bin = last < 0 ? 0 : last;
           sh.above_c = lc;
@@ -306,7 +358,7 @@ AMASS_DEV uint32_t find_tau(const float* sc, int lo_p, int hi_p, int k,
     }
     __syncthreads();
     const int bin = sh.bin;
-    const uint32_t cnt_bin = sh.hist[bin];
+    const uint32_t cnt_bin = H[bin];
     k -= (int)sh.above_c;
     need -= sh.above_m;
     const uint32_t blo = lo + ((uint32_t)bin << shift);
@@ -327,20 +379,41 @@ AMASS_DEV uint32_t find_tau(const float* sc, int lo_p, int hi_p, int k,
         }
       }
       if (threadIdx.x == 0) { sh.tau = 0xffffffffu; sh.lowest = 0xffffffffu; }
+      uint32_t* CK = sh.cand;
+      float* CM = sh.cmass;
+      if constexpr (CLU) {
+        cg::cluster_group cl = cg::this_cluster();
+        cl.sync();                     // every slice's candidates listed
+        if (threadIdx.x == 0) {
+          int off = 0;
+          for (unsigned q = 0; q < cl.num_blocks(); ++q) {
+            const int nq = *cl.map_shared_rank(&sh.ncand, q);
+            const uint32_t* ck = cl.map_shared_rank(sh.cand, q);
+            const float* cm = cl.map_shared_rank(sh.cmass, q);
+            for (int j = 0; j < nq && off < kCand; ++j, ++off) {
+              sh.acand[off] = ck[j];
+              if (COV) sh.amass[off] = cm[j];
+            }
+          }
+          sh.nall = off;
+        }
+        CK = sh.acand;
+        CM = sh.amass;
+      }
       __syncthreads();
       {
         // rank the members in parallel: 4 threads per candidate, each
         // comparing against a quarter of the members
-        const int n = sh.ncand;
+        const int n = CLU ? sh.nall : sh.ncand;
         const int j = threadIdx.x >> 2, part = threadIdx.x & 3;
-        const uint32_t key = j < n ? sh.cand[j] : 0u;
+        const uint32_t key = j < n ? CK[j] : 0u;
         uint32_t ab = 0, eq = 0;
         float mab = 0.f, meq = 0.f;
         if (j < n) {
           for (int t = part; t < n; t += 4) {
-            const uint32_t o = sh.cand[t];
-            if (o > key) { ab++; if (COV) mab += sh.cmass[t]; }
-            else if (o == key) { eq++; if (COV) meq += sh.cmass[t]; }
+            const uint32_t o = CK[t];
+            if (o > key) { ab++; if (COV) mab += CM[t]; }
+            else if (o == key) { eq++; if (COV) meq += CM[t]; }
           }
         }
 #pragma unroll
@@ -373,55 +446,76 @@ AMASS_DEV uint32_t find_tau(const float* sc, int lo_p, int hi_p, int k,
 }
 
 // FOLD: fold score_h (nrm) into score first.  LIN: page mass = score (nrm
-// semantics) instead of exp(score - max) (max semantics).
-template <bool FOLD, bool LIN, bool COVERAGE, int GM = 8>
+// semantics) instead of exp(score - max) (max semantics).  CLU: one unit per
+// thread-block cluster -- CTA `rank` owns the slice [s0, s1) of the scored
+// pages (fold, statistics and histograms of its slice, merged over the
+// cluster through distributed shared memory) and compacts that slice (the
+// last rank also the unscored tail) at an offset taken from the lower
+// ranks' counts; used when there are few units, so a long unit's latency is
+// spread over several SMs.
+template <bool FOLD, bool LIN, bool COVERAGE, int GM = 8, bool CLU = false>
 __global__ void __launch_bounds__(kSelThreads, 4)
 select_kernel(SelArgs a) {
   grid_dep_wait();     // inputs written by the previous kernel
   grid_dep_launch();
-  extern __shared__ float sc[];
+  extern __shared__ float sc[];                 // this CTA's slice
   __shared__ SelShared sh;
-  const int unit = blockIdx.x;
+  int nb = 1, rank = 0;
+  if constexpr (CLU) {
+    cg::cluster_group cl = cg::this_cluster();
+    nb = (int)cl.num_blocks();
+    rank = (int)cl.block_rank();
+  }
+  const int unit = blockIdx.x / nb;
   const int r = unit / a.n_kv;
   const int npg = max(a.npg[r], 0);
   const int nsh = a.nsh[r];
   const int sink = a.sink;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nsc = max(nsh, 0);
+  const int chunk = ((nsc + nb - 1) / nb + 3) & ~3;
+  const int s0 = min(rank * chunk, nsc), s1 = min(s0 + chunk, nsc);
   if (threadIdx.x == 0) { sh.kmin = 0xffffffffu; sh.kmax = 0u; }
   SEL_PROBE(0);
   if (nsh > 0) {
     if (FOLD) {
-      nrm_fold<GM, (GM <= 4 ? 2 : 1)>(a, unit, nsh, sc);
+      nrm_fold<GM, (GM <= 4 ? 2 : 1)>(a, unit, s0, s1, sc, !CLU);
     } else {
       const float* si = a.score + (int64_t)unit * a.MP;
       constexpr int kB = 8;
-      for (int p0 = threadIdx.x; p0 < nsh; p0 += kB * kSelThreads) {
+      for (int p0 = s0 + threadIdx.x; p0 < s1; p0 += kB * kSelThreads) {
         float v[kB];
 #pragma unroll
         for (int i = 0; i < kB; ++i) {
           const int p = p0 + i * kSelThreads;
-          v[i] = p < nsh ? __ldcg(si + p) : 0.f;
+          v[i] = p < s1 ? __ldcg(si + p) : 0.f;
         }
 #pragma unroll
         for (int i = 0; i < kB; ++i) {
           const int p = p0 + i * kSelThreads;
-          if (p < nsh) sc[p] = v[i];
+          if (p < s1) sc[p - s0] = v[i];
         }
       }
     }
-  } else if (FOLD && threadIdx.x < a.G) {
+  } else if (FOLD && !CLU && threadIdx.x < a.G) {
     a.hmax[(int64_t)unit * a.G + threadIdx.x] = -INFINITY;
+  }
+  if constexpr (CLU) {
+    cg::this_cluster().sync();               // every slice has read hmax
+    if (FOLD && rank == 0 && threadIdx.x < a.G)
+      a.hmax[(int64_t)unit * a.G + threadIdx.x] = -INFINITY;
   }
   __syncthreads();
   SEL_PROBE(1);
   const int nsel = nsh - sink;
   const bool keep_all = nsel <= 1;
+  const int lo_sel = max(sink, s0);            // selectable part of the slice
   uint32_t tau = 0;
   int b_used = 1;
   if (!keep_all) {
     uint32_t kmin = 0xffffffffu, kmax = 0;
-    for (int p = sink + threadIdx.x; p < nsh; p += kSelThreads) {
-      const uint32_t key = float_key(sc[p]);
+    for (int p = lo_sel + threadIdx.x; p < s1; p += kSelThreads) {
+      const uint32_t key = float_key(sc[p - s0]);
       kmin = min(kmin, key);
       kmax = max(kmax, key);
     }
@@ -437,49 +531,67 @@ select_kernel(SelArgs a) {
     __syncthreads();
     kmin = sh.kmin;
     kmax = sh.kmax;
+    if constexpr (CLU) {
+      kmin = cl_allreduce(&sh.x_kmin, kmin,
+                          [](uint32_t x, uint32_t y) { return min(x, y); });
+      kmax = cl_allreduce(&sh.x_kmax, kmax,
+                          [](uint32_t x, uint32_t y) { return max(x, y); });
+    }
     if (COVERAGE) {
       float shiftv = 0.f;
       if (!LIN) {
         float vmax = -INFINITY;
-        for (int p = threadIdx.x; p < nsh; p += kSelThreads)
-          vmax = fmaxf(vmax, sc[p]);
+        for (int p = s0 + threadIdx.x; p < s1; p += kSelThreads)
+          vmax = fmaxf(vmax, sc[p - s0]);
         shiftv = block_reduce(vmax, sh.red,
                               [](float x, float y) { return fmaxf(x, y); });
+        if constexpr (CLU)
+          shiftv = cl_allreduce(&sh.x_vmax, shiftv,
+                                [](float x, float y) { return fmaxf(x, y); });
       }
       float tot = 0.f, alw = 0.f;
-      for (int p = threadIdx.x; p < nsh; p += kSelThreads) {
-        const float m = LIN ? sc[p] : expf(sc[p] - shiftv);
+      for (int p = s0 + threadIdx.x; p < s1; p += kSelThreads) {
+        const float m = LIN ? sc[p - s0] : expf(sc[p - s0] - shiftv);
         tot += m;
         if (p < sink) alw += m;
       }
       auto add = [](float x, float y) { return x + y; };
       tot = block_reduce(tot, sh.red, add);
       alw = block_reduce(alw, sh.red, add);
+      if constexpr (CLU) {
+        tot = cl_allreduce(&sh.x_tot, tot, add);
+        alw = cl_allreduce(&sh.x_alw, alw, add);
+      }
       const float need = fmaxf(a.coverage * tot - alw, 0.f);
-      tau = find_tau<true, LIN>(sc, sink, nsh, 0, need, shiftv, kmin, kmax, sh);
+      tau = find_tau<true, LIN, CLU>(sc, lo_sel - s0, s1 - s0, 0, need, shiftv,
+                                     kmin, kmax, sh);
       int above = 0;
-      for (int p = sink + threadIdx.x; p < nsh; p += kSelThreads)
-        above += float_key(sc[p]) > tau;
-      above = block_reduce(above, reinterpret_cast<int*>(sh.red),
-                           [](int x, int y) { return x + y; });
+      for (int p = lo_sel + threadIdx.x; p < s1; p += kSelThreads)
+        above += float_key(sc[p - s0]) > tau;
+      auto iadd = [](int x, int y) { return x + y; };
+      above = block_reduce(above, reinterpret_cast<int*>(sh.red), iadd);
+      if constexpr (CLU) above = cl_allreduce(&sh.x_above, above, iadd);
       b_used = above + 1;
     } else {
       const int b = a.b_fix[r];
       b_used = b;
       SEL_PROBE(2);
-      tau = find_tau<false, true>(sc, sink, nsh, b, 0.f, 0.f, kmin, kmax, sh);
+      tau = find_tau<false, true, CLU>(sc, lo_sel - s0, s1 - s0, b, 0.f, 0.f,
+                                       kmin, kmax, sh);
     }
   }
   SEL_PROBE(3);
-  if (a.b_unit && threadIdx.x == 0) a.b_unit[unit] = b_used;
+  if (a.b_unit && threadIdx.x == 0 && rank == 0) a.b_unit[unit] = b_used;
 
-  // ascending compaction over [0, npg): each thread owns a contiguous run of
-  // pages; one block-wide exclusive scan of the per-thread counts
+  // ascending compaction of this CTA's range [c0, c1) (the whole [0, npg)
+  // without a cluster): each thread owns a contiguous run of pages; one
+  // block-wide exclusive scan of the per-thread counts
   int32_t* tab = a.tab + (int64_t)unit * a.MP;
-  const int per = (npg + kSelThreads - 1) / kSelThreads;
-  const int p_lo = threadIdx.x * per, p_hi = min(p_lo + per, npg);
+  const int c0 = s0, c1 = (rank == nb - 1) ? max(npg, s1) : s1;
+  const int per = (c1 - c0 + kSelThreads - 1) / kSelThreads;
+  const int p_lo = c0 + threadIdx.x * per, p_hi = min(p_lo + per, c1);
   auto keep_page = [&](int p) {
-    return keep_all || p < sink || p >= nsh || float_key(sc[p]) >= tau;
+    return keep_all || p < sink || p >= nsh || float_key(sc[p - s0]) >= tau;
   };
   // keep bits of this thread's run (at most 64 pages per thread: MP <= 16K)
   uint64_t bits = 0;
@@ -502,25 +614,90 @@ select_kernel(SelArgs a) {
     if (w < warp) off += v;
     total += v;
   }
-  off += incl - mine;
+  int base = 0, all = total;
+  if constexpr (CLU) {
+    cg::cluster_group cl = cg::this_cluster();
+    if (threadIdx.x == 0) sh.x_cnt = total;
+    cl.sync();
+    all = 0;
+    for (int q = 0; q < nb; ++q) {
+      const int cq = *cl.map_shared_rank(&sh.x_cnt, q);
+      if (q < rank) base += cq;
+      all += cq;
+    }
+  }
+  off += base + incl - mine;
   while (bits) {
     const int i = __ffsll(bits) - 1;
     bits &= bits - 1;
     tab[off++] = p_lo + i;
   }
-  for (int p = total + threadIdx.x; p < a.MP; p += kSelThreads) tab[p] = -1;
-  if (threadIdx.x == 0) a.cnt[unit] = total;
+  for (int p = all + rank * kSelThreads + threadIdx.x; p < a.MP;
+       p += nb * kSelThreads)
+    tab[p] = -1;
+  if (threadIdx.x == 0 && rank == 0) a.cnt[unit] = all;
+  if constexpr (CLU) cg::this_cluster().sync();   // peers' reads of sh done
   SEL_PROBE(5);
 }
 
 constexpr int kMaxSmem = 160 * 1024;
 
+// cluster launch (one unit per cluster of `cl` CTAs) with programmatic
+// dependent launch
+template <typename... KArgs, typename... Args>
+int launch_cluster_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                       size_t smem, cudaStream_t st, int cl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  at[1].id = cudaLaunchAttributeClusterDimension;
+  at[1].val.clusterDim.x = cl;
+  at[1].val.clusterDim.y = 1;
+  at[1].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kernel, args...) == cudaSuccess
+             ? AMASS_OK
+             : AMASS_ERR_CUDA;
+}
+
+// CTAs per unit for top-b selection: a cluster of up to 8 when the units
+// alone would leave most of the GPU idle (units x CTAs kept within about 4
+// CTAs per SM).  Measured on B200: C5 (128 units of ~4.6K pages) whole tier
+// step 234.9 us -> 216.9 (2 CTAs) -> 211.1 (4).  Coverage selection stays at
+// one CTA per unit: its mass-weighted walk merges more levels across the
+// cluster and was slower (C2, 8 units: 45.4 -> 55.2 us at 2 CTAs).
+inline int select_cluster_size(int units) {
+  int cl = 1;
+  while (cl < 8 && (long long)units * cl * 2 <= (long long)num_sms() * 4) cl *= 2;
+  return cl;
+}
+
 template <bool FOLD, bool LIN, bool COV>
 int launch_select(const SelArgs& a, int units, cudaStream_t st) {
-  const size_t smem = (size_t)a.MP * sizeof(float);
   const bool g4 = FOLD && a.G <= 4;
+  const int cl = COV ? 1 : select_cluster_size(units);
+  static unsigned long long configured[4] = {0, 0, 0, 0};
+  if (cl > 1) {
+    auto k = g4 ? select_kernel<FOLD, LIN, COV, 4, true>
+                : select_kernel<FOLD, LIN, COV, 8, true>;
+    const int chunk = ((a.MP + cl - 1) / cl + 3) & ~3;
+    const size_t smem = (size_t)chunk * sizeof(float);
+    if (first_on_device(configured[2 + (g4 ? 1 : 0)]))
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kMaxSmem);
+    if (int rc = launch_cluster_pdl(k, dim3(units * cl), dim3(kSelThreads),
+                                    smem, st, cl, a))
+      return rc;
+    return launch_status();
+  }
+  const size_t smem = (size_t)a.MP * sizeof(float);
   auto k = g4 ? select_kernel<FOLD, LIN, COV, 4> : select_kernel<FOLD, LIN, COV, 8>;
-  static unsigned long long configured[2] = {0, 0};
   if (first_on_device(configured[g4 ? 1 : 0])) {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          kMaxSmem);
