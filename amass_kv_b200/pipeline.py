@@ -97,7 +97,8 @@ class StepPipeline:
         # compute: inputs landed and the previous output of b copied out
         self.compute.wait_event(self.up[b])
         self.compute.wait_event(self.down[b])
-        self.graphs[layer][b].replay()
+        with torch.cuda.stream(self.compute):     # whatever the caller's stream
+            self.graphs[layer][b].replay()
         self.done[b].record(self.compute)
         self.d2h.wait_event(self.done[b])
         with torch.cuda.stream(self.d2h):
