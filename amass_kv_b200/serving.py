@@ -35,8 +35,9 @@ from .attention import ensure_stage_b_buffers
 
 
 class MemSession:
-    """One model's mem-v (``offload_k=False``) or mem-kv tier plus its quad
-    selection state, sized once from engine maxima.
+    """One model's mem-v (``offload_k=False``) or mem-kv tier plus its
+    selection state (``scorer`` "quad", or "clse" -- the reference config's
+    default -- with per-token coordinates), sized once from engine maxima.
 
     Device memory: the K-only cache (L, NB, 1, page, n_kv, d) (a one-block
     stand-in under mem-kv, whose K lives in the tier), quad summaries, the
@@ -49,7 +50,8 @@ class MemSession:
                  hot_slots: int | None = None, budget: float = 0.05,
                  rank: int = 2, v_bits: int = 4, combine: str = "nrm",
                  coverage=None, offload_k: bool = False, device="cuda",
-                 max_pool_gb: float = 256.0):
+                 max_pool_gb: float = 256.0, scorer: str = "quad",
+                 c_bits: int = 4, c_grain: str = "token"):
         dev = torch.device(device)
         self.device = dev
         self.L, self.NB, self.n_kv, self.G = num_layers, num_blocks, n_kv, G
@@ -65,12 +67,17 @@ class MemSession:
         nb_k = 1 if offload_k else num_blocks
         self.k_cache = torch.zeros((num_layers, nb_k, 1, page, n_kv, head_dim),
                                    dtype=torch.bfloat16, device=dev)
+        if scorer not in ("quad", "clse"):
+            raise ValueError(f"scorer must be 'quad' or 'clse', got {scorer!r}")
+        self.scorer = scorer
+        extra = dict(coords="lse", c_bits=c_bits, c_grain=c_grain) \
+            if scorer == "clse" else {}
         self.st = S.QuadState(dev, num_layers=num_layers,
                               num_blocks=num_blocks, n_kv=n_kv, G=G,
                               head_dim=head_dim, page=page, max_reqs=max_reqs,
                               max_pages=max_pages, rank=rank, budget=budget,
                               v_bits=v_bits, combine=combine,
-                              coverage=coverage)
+                              coverage=coverage, **extra)
         ensure_stage_b_buffers(self.st, dev)
         self._n_req = 0
         self._bt = self._sl = None
@@ -110,8 +117,9 @@ class MemSession:
         l, n_req = int(layer), self._n_req
         if n_req == 0:
             return
-        S.select_pages_quad(self.st, l, q, self._bt, self._sl, n_req, scale,
-                            derive=False)
+        select = S.select_pages_clse if self.scorer == "clse" else \
+            S.select_pages_quad
+        select(self.st, l, q, self._bt, self._sl, n_req, scale, derive=False)
         T.mem_dynamic_decode(q, self.k_cache[l], self._bt, self._sl, self.st,
                              out, self.tier, l, scale=scale)
 

@@ -41,8 +41,9 @@ def _steps(rng, R, cap, n_prefill, n_decode, chunk):
     return out
 
 
-@pytest.mark.parametrize("offload_k", [False, True])
-def test_mem_session_bitwise_equals_resident(dev, offload_k):
+@pytest.mark.parametrize("offload_k,scorer", [(False, "quad"), (True, "quad"),
+                                              (False, "clse")])
+def test_mem_session_bitwise_equals_resident(dev, offload_k, scorer):
     rng = np.random.default_rng(3 + offload_k)
     L, R, MP, page, n_kv, G, d = 2, 3, 24, 16, 2, 4, 128
     NB = R * MP + 7
@@ -50,7 +51,8 @@ def test_mem_session_bitwise_equals_resident(dev, offload_k):
     sess = MemSession(num_layers=L, num_blocks=NB, n_kv=n_kv, G=G,
                       head_dim=d, max_reqs=R, max_pages=MP,
                       max_tokens=R * chunk, page=page, hot_slots=20,
-                      budget=0.3, offload_k=offload_k, device=dev)
+                      budget=0.3, offload_k=offload_k, device=dev,
+                      scorer=scorer)
     bt_np = rng.permutation(NB)[:R * MP].astype(np.int32).reshape(R, MP)
     bt = torch.from_numpy(bt_np).to(dev)
     kv_full = torch.zeros((L, NB, 2, page, n_kv, d), dtype=torch.bfloat16,
