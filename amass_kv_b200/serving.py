@@ -112,8 +112,9 @@ class MemSession:
                            key=key if self.offload_k else None)
 
     def decode(self, layer: int, q, out, *, scale: float) -> None:
-        """Pure-decode attention of one layer into ``out[:n_req]``: quad
-        select, residency step and the ptr-select tiered decode."""
+        """Pure-decode attention of one layer into ``out[:n_req]``: Stage-A
+        selection (quad or CLSE), residency step and the ptr-select tiered
+        decode."""
         l, n_req = int(layer), self._n_req
         if n_req == 0:
             return
