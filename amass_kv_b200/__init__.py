@@ -8,8 +8,7 @@ C ABI in ``include/amass_b200.h``):
              select_pages, select_pages_quad                      (Stage A)
   attention  ResidentVSource, ensure_stage_b_buffers,
              sparse_paged_decode_batched_cuda                     (Stage B)
-  config     AmassConfig
-"""
-from .config import AmassConfig  # noqa: F401
 
-__all__ = ["AmassConfig"]
+The configuration object stays the reference's own ``AmassConfig``; callers
+pass its fields (budget, coverage, combine, ...) to the state constructors.
+"""

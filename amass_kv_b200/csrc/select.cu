@@ -26,17 +26,6 @@ constexpr int kSelWarps = kSelThreads / 32;
 constexpr int kBins = 1024;
 constexpr int kCand = 64;
 
-#ifdef AMASS_SEL_PROBE
-__device__ unsigned long long g_sel_probe[8192 * 8];
-#define SEL_PROBE(k)                                                        \
-  if (threadIdx.x == 0) {                                                   \
-    unsigned long long t_;                                                  \
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                  \
-    g_sel_probe[blockIdx.x * 8 + (k)] = t_;                                 \
-  }
-#else
-#define SEL_PROBE(k)
-#endif
 
 // ---------------------------------------------------------------------------
 // derive_page_params (reference selection/select.py:30-45)
@@ -364,9 +353,6 @@ AMASS_DEV uint32_t find_tau(const float* sc, int lo_p, int hi_p, int k,
     const uint32_t blo = lo + ((uint32_t)bin << shift);
     const uint64_t bend = (uint64_t)blo + ((1ull << shift) - 1);
     const uint32_t bhi = bend < (uint64_t)hi ? (uint32_t)bend : hi;
-#ifdef AMASS_SEL_PROBE
-    if (threadIdx.x == 0) g_sel_probe[blockIdx.x * 8 + 6] = level + 1 + 100 * (cnt_bin <= (uint32_t)kCand);
-#endif
     if (blo == bhi) return blo;
     if (cnt_bin <= (uint32_t)kCand) {
       for (int p = lo_p + threadIdx.x; p < hi_p; p += kSelThreads) {
@@ -476,7 +462,6 @@ select_kernel(SelArgs a) {
   const int chunk = ((nsc + nb - 1) / nb + 3) & ~3;
   const int s0 = min(rank * chunk, nsc), s1 = min(s0 + chunk, nsc);
   if (threadIdx.x == 0) { sh.kmin = 0xffffffffu; sh.kmax = 0u; }
-  SEL_PROBE(0);
   if (nsh > 0) {
     if (FOLD) {
       nrm_fold<GM, (GM <= 4 ? 2 : 1)>(a, unit, s0, s1, sc, !CLU);
@@ -506,7 +491,6 @@ select_kernel(SelArgs a) {
       a.hmax[(int64_t)unit * a.G + threadIdx.x] = -INFINITY;
   }
   __syncthreads();
-  SEL_PROBE(1);
   const int nsel = nsh - sink;
   const bool keep_all = nsel <= 1;
   const int lo_sel = max(sink, s0);            // selectable part of the slice
@@ -575,12 +559,10 @@ select_kernel(SelArgs a) {
     } else {
       const int b = a.b_fix[r];
       b_used = b;
-      SEL_PROBE(2);
       tau = find_tau<false, true, CLU>(sc, lo_sel - s0, s1 - s0, b, 0.f, 0.f,
                                        kmin, kmax, sh);
     }
   }
-  SEL_PROBE(3);
   if (a.b_unit && threadIdx.x == 0 && rank == 0) a.b_unit[unit] = b_used;
 
   // ascending compaction of this CTA's range [c0, c1) (the whole [0, npg)
@@ -606,7 +588,6 @@ select_kernel(SelArgs a) {
   }
   if (lane == 31) sh.wsum[warp] = incl;
   __syncthreads();
-  SEL_PROBE(4);
   int off = 0, total = 0;
 #pragma unroll
   for (int w = 0; w < kSelWarps; ++w) {
@@ -637,7 +618,6 @@ select_kernel(SelArgs a) {
     tab[p] = -1;
   if (threadIdx.x == 0 && rank == 0) a.cnt[unit] = all;
   if constexpr (CLU) cg::this_cluster().sync();   // peers' reads of sh done
-  SEL_PROBE(5);
 }
 
 constexpr int kMaxSmem = 160 * 1024;

@@ -44,17 +44,6 @@ constexpr int kPlanMaxReq = 4096;
 constexpr int kPer = 4;                 // entries per thread per round
 constexpr size_t kPlanSmem = 200 * 1024;
 
-#ifdef AMASS_PLAN_PROBE
-__device__ unsigned long long g_plan_probe[64 * 16];
-#define PLAN_PROBE(k)                                                       \
-  if (threadIdx.x == 0) {                                                   \
-    unsigned long long t_;                                                  \
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                  \
-    g_plan_probe[blockIdx.x * 16 + (k)] = t_;                               \
-  }
-#else
-#define PLAN_PROBE(k)
-#endif
 
 struct PlanArgs {
   const int32_t* tab;     // (R, n_kv, MP)
@@ -194,7 +183,6 @@ tier_plan_kernel(PlanArgs a) {
   int32_t* s2p = a.s2p + (int64_t)kv * a.S;
   int32_t* lru = a.lru + (int64_t)kv * a.S;
   if (tid == 0) { dropped = 0; nT = 0; }
-  PLAN_PROBE(0);
 
   // ---- request offsets of this kv-head's selected pages ------------------
   int total;
@@ -211,8 +199,6 @@ tier_plan_kernel(PlanArgs a) {
     if (tid == 0) sm.reqoff[a.n_req] = total;
     __syncthreads();
   }
-
-  PLAN_PROBE(1);
   // ---- (1) misses in (request, entry) order: each thread reads kPer
   //      consecutive entries of the classified list; one block scan per
   //      round orders the appends.  (Hits were touched by the classifier.)
@@ -253,8 +239,6 @@ tier_plan_kernel(PlanArgs a) {
   }
   __syncthreads();
   const int M = min(mtot, a.max_miss);
-
-  PLAN_PROBE(2);
   // ---- (2) dedup: the first occurrence of a block claims page2slot -------
   for (int i = tid; i < M; i += kPlanThreads)
     atomicMin(&p2s[sm.mblk[i]], INT_MIN + i);
@@ -269,7 +253,6 @@ tier_plan_kernel(PlanArgs a) {
   }
   int U;
   const int ubase = block_scan_excl(nu, wtot, &U);
-  PLAN_PROBE(3);
 
   // ---- (3) victims: the `take` smallest (lru, slot) among slots with
   //      lru < clk, in order.  Radix-select the take-th smallest lru T
@@ -311,7 +294,6 @@ tier_plan_kernel(PlanArgs a) {
   }
   const int E = (int)ne;
   const int take = min(U, E);
-  PLAN_PROBE(4);
   if (take > 0) {
     const unsigned range = vmax - vmin;
     const int nbits = range ? 32 - __clz(range) : 0;
@@ -342,7 +324,6 @@ tier_plan_kernel(PlanArgs a) {
       below += sel_below;
       __syncthreads();
     }
-  PLAN_PROBE(5);
     const unsigned T = vmin + prefix;           // biased lru of the threshold
     const int c = below;                        // slots with lru < T
     // keys of the slots older than T (unordered), then sorted
@@ -377,7 +358,6 @@ tier_plan_kernel(PlanArgs a) {
       for (int k = tid; k < c; k += kPlanThreads)
         sm.victim[k] = (int)(sm.keys[k] & 0xffffffffu);
     }
-  PLAN_PROBE(6);
     // slots with lru == T in index order fill victims [c, take): each
     // thread scans a contiguous run of slots, one block scan orders them
     {
@@ -397,8 +377,6 @@ tier_plan_kernel(PlanArgs a) {
     }
     __syncthreads();
   }
-
-  PLAN_PROBE(7);
   // ---- (4) install: the k-th unique miss takes victim k -----------------
   int32_t* fl = a.flist + (int64_t)kv * a.S * 2;
   int k = ubase;
@@ -421,7 +399,6 @@ tier_plan_kernel(PlanArgs a) {
     ++k;
   }
   __syncthreads();
-  PLAN_PROBE(8);
   if (tid == 0) {
     a.fcnt[kv] = take;
     if (dropped) atomicExch(a.overflow, 1);
@@ -603,7 +580,10 @@ extern "C" int amass_tier_plan(const int32_t* page_table,
   {
     const int chunks = (max_pages + kClsChunk - 1) / kClsChunk;
     const long long warps = (long long)n_req * n_kv * chunks;
-    const int grid = (int)std::min<long long>((warps + 7) / 8, num_sms() * 8LL);
+    // an empty batch still runs the plan (the clock advances, as in the
+    // reference's gather_plan): one idle classify CTA
+    const int grid = (int)std::max<long long>(
+        1, std::min<long long>((warps + 7) / 8, num_sms() * 8LL));
     if (int rc = launch_pdl(tier_classify_kernel, dim3(grid), dim3(256), 0, st,
                             a))
       return rc;

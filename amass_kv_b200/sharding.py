@@ -100,7 +100,7 @@ class HeadGather:
         if mode == "p2p":
             # plain peer mappings only: no NVLink multicast objects
             import os
-            os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+            os.environ["TORCH_SYMM_MEM_DISABLE_MULTICAST"] = "1"
             import torch.distributed._symmetric_memory as symm
             if self.world > 8:
                 raise ValueError("p2p gather supports up to 8 ranks")

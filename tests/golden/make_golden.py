@@ -1,7 +1,7 @@
 """Generate golden vectors by running the REFERENCE's own kernels on CPU.
 
 Run in a container that has the reference source tree (read-only) at
-``$AMASS_REF_SRC`` (default ``/root/reference/src``):
+``$AMASS_REF_SRC`` (required; no default path):
 
     python tests/golden/make_golden.py
 
@@ -26,7 +26,9 @@ import types
 
 os.environ["TRITON_INTERPRET"] = "1"
 os.environ.setdefault("AMASS_EIGH", "torch")
-REF = os.environ.get("AMASS_REF_SRC", "/root/reference/src")
+REF = os.environ.get("AMASS_REF_SRC")
+if not REF:
+    sys.exit("set AMASS_REF_SRC to the reference checkout's src/ directory")
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 sys.path.insert(0, REF)

@@ -391,3 +391,25 @@ def test_tier_dma_coalesced_runs(mem_kv, dev):
     for a, b in zip(res["kernel"], res["dma"]):
         if a is not None:
             assert np.array_equal(a, b)
+
+
+def test_tier_plan_empty_batch(dev):
+    """An empty batch is a valid plan call: status 0, no installs, the maps
+    unchanged and the step clock advanced once (reference residency.py
+    gather_plan increments the clock before its kernels)."""
+    NB, MP = 64, 8
+    t = T.Tier(num_layers=1, num_blocks=NB, n_kv=2, page=16, d=128,
+               hot_slots=16, max_reqs=2, max_pages=MP, n_vslots=4, device=dev)
+    r5 = t.residency
+    tab = torch.full((2, 2, MP), -1, dtype=torch.int32, device=dev)
+    cnt = torch.zeros((2, 2), dtype=torch.int32, device=dev)
+    bt = torch.zeros((2, MP), dtype=torch.int32, device=dev)
+    sl = torch.zeros((2,), dtype=torch.int32, device=dev)
+    p2s, lru = r5.page2slot.clone(), r5.lru_clock.clone()
+    c0 = int(r5.clock[0])
+    r5.gather_plan(0, tab, cnt, bt, sl, 0)
+    torch.cuda.synchronize()
+    assert int(r5.clock[0]) == c0 + 1
+    assert int(r5.fetch_cnt.sum()) == 0
+    assert torch.equal(r5.page2slot, p2s)
+    assert torch.equal(r5.lru_clock, lru)
