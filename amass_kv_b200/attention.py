@@ -6,9 +6,12 @@ Mirrors the reference's ``amass.attention`` surface for the hot path:
   ensure_stage_b_buffers(st, ...)   attention/decode.py:98-114
   sparse_paged_decode_batched_cuda  attention/decode_cuda.py:1376-1465
 
-The split-K partials keep the reference layout (R, n_kv, split, G[, d]);
-the pages-per-chunk rule pps = max(ceil(cnt/split), pps_min) is the
-reference's (decode.py:154-160), so chunk c of a unit covers the same pages.
+The split-K partials keep the reference layout (R, n_kv, split, G[, d]).
+How a unit's pages are cut into partials is the kernel's own choice (equal
+runs of the flat page list, one per warp of the grid, so ragged batches
+balance); the reference's chunk rule pps = max(ceil(cnt/split), PPS_MIN)
+(decode.py:154-160) is another cut of the same exact softmax re-association.
+``pps_min`` here is the floor on pages per run.
 """
 from __future__ import annotations
 
@@ -63,12 +66,9 @@ def ensure_stage_b_buffers(st, device, split: int = DEFAULT_SPLIT) -> None:
 
 
 def pps_min_for(n_req: int) -> int:
-    """Minimum pages per chunk.  32 at every batch size measured on B200:
-    at the C3 batch (64 requests) 8 -> 88 us, 16 -> 73 us, 32 -> 65 us for
-    decode + merge; at batch 1 with coverage 0.95 (~830 pages per unit)
-    4 -> 44.3 us, 16 -> 34.9 us, 32 -> 28.6 us, 64 -> 28.7 us (fewer chunk
-    epilogues and partials to merge)."""
-    return 32
+    """Floor on the pages of one warp run (the run length is otherwise the
+    balanced share of the batch's selected pages)."""
+    return 8
 
 
 def sparse_paged_decode_batched_cuda(q, kv_cache, block_table, seq_lens, st,

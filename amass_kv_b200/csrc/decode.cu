@@ -2,25 +2,26 @@
 // with a log-sum-exp merge (reference attention/decode.py:128-241,
 // attention/merge.py:21-50).
 //
-// Work decomposition.  A (request, kv-head) unit with cnt selected pages is
-// cut into chunks of pps = max(ceil(cnt/split), pps_min) pages (the
-// reference's rule, decode.py:154-160); a chunk is one work item.  A
-// persistent grid of 4-warp CTAs walks the flat item list (each CTA first
-// scans the per-unit chunk counts into shared memory, then strides over the
-// items), so ragged batches balance across the SMs without empty programs.
-// Inside an item the four warps take pages round-robin; each warp streams its
-// pages through its own NST-deep cp.async ring in shared memory (16-byte
-// copies into an XOR-swizzled [token][d] tile, zero-filled beyond seq_len) and
-// the ring runs across item boundaries.
+// Work decomposition.  The selected pages of all (request, kv-head) units,
+// units in order, form one flat list of P pages.  A persistent grid of 4-warp
+// CTAs cuts it into equal contiguous runs, one per warp (each CTA first scans
+// the per-unit page counts into shared memory), so a ragged batch balances
+// across the SMs to within one page.  A run that crosses a unit boundary
+// writes one (m, l, acc) partial per unit it touches; the partials of a unit
+// are the consecutive runs that cover it.  Each warp streams its pages
+// through its own NST-deep cp.async ring in shared memory (16-byte copies
+// into an XOR-swizzled [token][d] tile, zero-filled beyond seq_len); the ring
+// runs across unit boundaries.  (The reference cuts each unit into
+// pps = max(ceil(cnt/split), PPS_MIN)-page chunks, decode.py:154-160; any
+// cut is an exact re-association of the same softmax.)
 //
 // Per page a warp computes the transposed products: S^T = K Q^T
 // (m16n8k16 bf16 MMAs, rows = the 16 tokens from ldmatrix, cols = the G query
 // heads of the group), an online softmax per head in the log2 domain, and
 // O^T += V^T P^T (V^T via ldmatrix.trans, P^T moved into the B operand with
-// movmatrix) -- D/16 MMAs for each product, half of the head-major form.  At the end of an
-// item the four warp states are merged through shared memory and written as
-// one (m, l, acc) partial; a second kernel merges the partials of each
-// (request, query head) and writes bf16 output.
+// movmatrix) -- D/16 MMAs for each product, half of the head-major form.  A
+// second kernel merges the partials of each (request, query head) and writes
+// bf16 output.
 #include <cstdlib>
 
 #include "common.cuh"
@@ -67,6 +68,7 @@ struct DecArgs {
   const int32_t* vbo;           // (NB,)
   const int32_t* eslot;         // (R, n_kv, MP) classified entries or null
   int t_layer, t_NB, t_S;
+  int dec_warps;                // warps of the decode grid (run split)
   // merged rows go to n_out buffers (this GPU's `out` alone, or every
   // rank's output under kv-head sharding: peer addresses over NVLink), at
   // global head head_off + local head
@@ -74,16 +76,17 @@ struct DecArgs {
   int n_out, head_off;
 };
 
-AMASS_DEV int unit_pps(int cnt, int split, int pps_min) {
-  return max((cnt + split - 1) / split, pps_min);
+// Pages per warp run: the flat list of P selected pages (units in order) is
+// cut into runs of `share` pages, one per warp of the grid (nw warps), so the
+// runs are balanced to within one page whatever the unit sizes; a run that
+// crosses units writes one partial per unit it touches.  The floor
+// ceil(cmax / (split - 1)) bounds the partials of any unit by `split`.
+AMASS_DEV int range_share(int P, int cmax, int nw, int split, int pps_min) {
+  int s = (P + nw - 1) / max(nw, 1);
+  s = max(s, max(pps_min, 1));
+  s = max(s, (cmax + split - 2) / (split - 1));
+  return s;
 }
-
-// Cursor over the (item, page) sequence one warp consumes.
-struct Cursor {
-  int item;   // flat item index (>= W: exhausted)
-  int unit;
-  int j, j1;  // next page index inside the unit's page table, chunk end
-};
 
 template <int D>
 struct Tile {
@@ -103,86 +106,77 @@ decode_kernel(DecArgs a) {
   using T = Tile<D>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;                                    // warps x NST
-  float* mbuf = reinterpret_cast<float*>(smem + kDecWarps * NST * T::kStageBytes);
-  float* lbuf = mbuf + kDecWarps * 8;
-  float* abuf = lbuf + kDecWarps * 8;                        // warps x G x D
-  int* meta = reinterpret_cast<int*>(abuf + kDecWarps * a.G * D);  // warps x NST
-  int* prefix = meta + kDecWarps * NST;                      // units + 1
+  int* meta = reinterpret_cast<int*>(smem + kDecWarps * NST * T::kStageBytes);
+  int* pfx = meta + kDecWarps * NST;                         // units + 1
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int U = a.units;
 
-  // ---- chunk-count prefix over units (each CTA redundantly; tiny) ---------
+  // ---- page prefix over units and the largest unit (every CTA; tiny) -----
+  __shared__ int wtot[kDecWarps], wmx[kDecWarps];
   {
     const int per = (U + kDecThreads - 1) / kDecThreads;
     const int u0 = threadIdx.x * per;
-    int local = 0;
+    int local = 0, mx = 0;
     for (int u = u0; u < min(u0 + per, U); ++u) {
-      const int c = a.cnt[u];
-      local += c > 0 ? (c + unit_pps(c, a.split, a.pps_min) - 1) /
-                           unit_pps(c, a.split, a.pps_min)
-                     : 0;
+      const int c = max(a.cnt[u], 0);
+      local += c;
+      mx = max(mx, c);
     }
-    // block exclusive scan of `local`
     int incl = local;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int t = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += t;
+      mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     }
-    __shared__ int wtot[kDecWarps];
     if (lane == 31) wtot[warp] = incl;
+    if (lane == 0) wmx[warp] = mx;
     __syncthreads();
     int woff = 0;
     for (int w = 0; w < warp; ++w) woff += wtot[w];
     int run = woff + incl - local;
     for (int u = u0; u < min(u0 + per, U); ++u) {
-      prefix[u] = run;
-      const int c = a.cnt[u];
-      run += c > 0 ? (c + unit_pps(c, a.split, a.pps_min) - 1) /
-                         unit_pps(c, a.split, a.pps_min)
-                   : 0;
+      pfx[u] = run;
+      run += max(a.cnt[u], 0);
     }
-    if (threadIdx.x == kDecThreads - 1) prefix[U] = run;
+    if (threadIdx.x == kDecThreads - 1) pfx[U] = run;
     __syncthreads();
   }
-  const int W = prefix[U];
-  if ((int)blockIdx.x >= W) return;
-
-  // locate the unit of item i: largest u with prefix[u] <= i
-  auto find_unit = [&](int i) {
+  int cmax = 0;
+#pragma unroll
+  for (int w = 0; w < kDecWarps; ++w) cmax = max(cmax, wmx[w]);
+  const int P = pfx[U];
+  const int share = range_share(P, cmax, (int)gridDim.x * kDecWarps, a.split,
+                                a.pps_min);
+  // ---- this warp's contiguous run [g0, g1) of the flat page list ---------
+  const int w = blockIdx.x * kDecWarps + warp;
+  const int g0 = (int)min((int64_t)w * share, (int64_t)P);
+  const int g1 = min(g0 + share, P);
+  if (g0 >= g1) return;
+  // unit holding flat page f: largest u with pfx[u] <= f (and pfx[u+1] > f)
+  auto unit_of = [&](int f) {
     int lo = 0, hi = U - 1;
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
-      if (prefix[mid] <= i) lo = mid; else hi = mid - 1;
+      if (pfx[mid] <= f) lo = mid; else hi = mid - 1;
     }
     return lo;
-  };
-  auto set_item = [&](Cursor& cu, int item) {
-    cu.item = item;
-    if (item >= W) return;
-    const int u = find_unit(item);
-    const int c = a.cnt[u];
-    const int pps = unit_pps(c, a.split, a.pps_min);
-    const int j0 = (item - prefix[u]) * pps;
-    cu.unit = u;
-    cu.j = j0 + warp;
-    cu.j1 = min(j0 + pps, c);
   };
 
   uint8_t* my_stages = stages + warp * NST * T::kStageBytes;
   int* my_meta = meta + warp * NST;
 
-  // issue the cp.async loads of the cursor's current page (if any) into slot
-  auto issue = [&](Cursor& cu, int slot) {
-    // advance past items where this warp has no page
-    while (cu.item < W && cu.j >= cu.j1) set_item(cu, cu.item + gridDim.x);
-    if (cu.item < W) {
-      const int u = cu.unit;
+  // issue cursor: flat page fi of unit ui
+  int fi = g0, ui = unit_of(g0);
+  auto issue = [&](int slot) {
+    if (fi < g1) {
+      const int u = ui;
+      const int j = fi - pfx[u];
       const int r = u / a.n_kv, kv = u - r * a.n_kv;
-      const int pt = a.tab[(int64_t)u * a.MP + cu.j];
+      const int pt = a.tab[(int64_t)u * a.MP + j];
       // hot slot of a classified hit (-(slot + 2)), loaded beside pt
-      const int ev = (TIER && a.eslot) ? a.eslot[(int64_t)u * a.MP + cu.j] : -1;
+      const int ev = (TIER && a.eslot) ? a.eslot[(int64_t)u * a.MP + j] : -1;
       const int64_t blk = a.bt[(int64_t)r * a.bt_stride + pt];
       const int seq = a.sl[r];
       const int valid = min(16, seq - pt * 16);
@@ -222,27 +216,25 @@ decode_kernel(DecArgs a) {
         cp_async16(sbase + doff, kp + rr * kst + ch * 8, ok);
         cp_async16(sbase + T::kTileBytes + doff, vp + rr * vst + ch * 8, ok);
       }
-      cu.j += kDecWarps;
+      ++fi;
+      while (ui < U - 1 && pfx[ui + 1] <= fi) ++ui;
     }
     cp_async_commit();
   };
 
-  Cursor ic, cc;  // issue cursor, compute cursor
-  set_item(ic, blockIdx.x);
-  set_item(cc, blockIdx.x);
 #pragma unroll
-  for (int s = 0; s < NST - 1; ++s) issue(ic, s);
+  for (int s = 0; s < NST - 1; ++s) issue(s);
   int slot_c = 0, slot_i = NST - 1;
 
   const int g = lane >> 2, c4 = lane & 3;
   constexpr int KS = D / 16;
+  int fc = g0, uc = unit_of(g0);
 
-  for (int item = blockIdx.x; item < W; item += gridDim.x) {
-    // cc tracks `item` here (set_item already done for the first one)
-    if (cc.item != item) set_item(cc, item);
-    const int u = cc.unit;
+  while (fc < g1) {
+    const int u = uc;
+    const int seg_end = min(pfx[u + 1], g1);
     const int r = u / a.n_kv, kv = u - r * a.n_kv;
-    // Q fragment (A operand): rows = query heads of the group
+    // Q fragment (B operand): cols = query heads of the group
     uint32_t qa[KS][2];
     {
       const bool gv = g < a.G;
@@ -263,8 +255,8 @@ decode_kernel(DecArgs a) {
 #pragma unroll
     for (int i = 0; i < D / 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 
-    for (; cc.j < cc.j1; cc.j += kDecWarps) {
-      issue(ic, slot_i);
+    for (; fc < seg_end; ++fc) {
+      issue(slot_i);
       slot_i = (slot_i + 1 == NST) ? 0 : slot_i + 1;
       cp_async_wait<NST - 1>();
       __syncwarp();
@@ -329,21 +321,22 @@ decode_kernel(DecArgs a) {
       slot_c = (slot_c + 1 == NST) ? 0 : slot_c + 1;
     }
 
-    // ---- merge the 4 warp states of this item and write one partial ------
+    // ---- this warp's partial of unit u: slot = segment index ------------
 #pragma unroll
     for (int o_ = 4; o_ < 32; o_ <<= 1) {
       l_i[0] += __shfl_xor_sync(0xffffffffu, l_i[0], o_);
       l_i[1] += __shfl_xor_sync(0xffffffffu, l_i[1], o_);
     }
+    const int64_t slotp = (int64_t)u * a.split + (w - pfx[u] / share);
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const int hh = 2 * c4 + j;
       if (hh < a.G) {
         if (g == 0) {
-          mbuf[warp * 8 + hh] = m_i[j];
-          lbuf[warp * 8 + hh] = l_i[j];
+          a.m_part[slotp * a.G + hh] = m_i[j];
+          a.l_part[slotp * a.G + hh] = l_i[j];
         }
-        float* ab = abuf + (warp * a.G + hh) * D;
+        float* ab = a.acc_part + (slotp * a.G + hh) * D;
 #pragma unroll
         for (int dt = 0; dt < D / 16; ++dt) {
           ab[16 * dt + g] = o[dt][j];
@@ -351,36 +344,14 @@ decode_kernel(DecArgs a) {
         }
       }
     }
-    __syncthreads();
-    {
-      const int chunk = item - prefix[u];
-      const int64_t slotp = (int64_t)u * a.split + chunk;
-      for (int e = threadIdx.x; e < a.G * D; e += kDecThreads) {
-        const int gg = e / D, dd = e - gg * D;
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, mbuf[w * 8 + gg]);
-        float acc = 0.f, L = 0.f;
-#pragma unroll
-        for (int w = 0; w < kDecWarps; ++w) {
-          const float mw = mbuf[w * 8 + gg];
-          const float sc = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
-          acc += sc * abuf[(w * a.G + gg) * D + dd];
-          L += sc * lbuf[w * 8 + gg];
-        }
-        a.acc_part[(slotp * a.G + gg) * D + dd] = acc;
-        if (dd == 0) {
-          a.m_part[slotp * a.G + gg] = M;
-          a.l_part[slotp * a.G + gg] = L;
-        }
-      }
-    }
-    __syncthreads();
+    // next non-empty unit
+    uc = u + 1;
+    while (uc < U - 1 && pfx[uc + 1] <= fc) ++uc;
   }
   cp_async_wait<0>();
 }
 
-// ---- merge of the chunk partials (reference attention/merge.py:30-50) -----
+// ---- merge of the run partials (reference attention/merge.py:30-50) -------
 template <int D>
 __global__ void __launch_bounds__(128)
 merge_kernel(DecArgs a) {
@@ -393,7 +364,21 @@ merge_kernel(DecArgs a) {
   const int r = idx / H, h = idx - r * H;
   const int kv = h / a.G, g = h - kv * a.G;
   const int u = r * a.n_kv + kv;
-  const int c = a.cnt[u];
+  // the decode's run split: pages before unit u, all pages, largest unit
+  int pre = 0, tot = 0, cmx = 0;
+  for (int v = lane; v < a.units; v += 32) {
+    const int cv = max(a.cnt[v], 0);
+    tot += cv;
+    cmx = max(cmx, cv);
+    if (v < u) pre += cv;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    pre += __shfl_xor_sync(0xffffffffu, pre, o);
+    tot += __shfl_xor_sync(0xffffffffu, tot, o);
+    cmx = max(cmx, __shfl_xor_sync(0xffffffffu, cmx, o));
+  }
+  const int c = max(a.cnt[u], 0);
   constexpr int PER = D / 32;
   float acc[PER];
 #pragma unroll
@@ -401,10 +386,10 @@ merge_kernel(DecArgs a) {
   float Mrun = -INFINITY;
   float L = 0.f;
   if (c > 0) {
-    // all chunk weights in one parallel round of loads (lane = chunk), then
-    // independent acc loads per chunk: no dependent chain across chunks
-    const int pps = unit_pps(c, a.split, a.pps_min);
-    const int nact = (c + pps - 1) / pps;
+    // all run weights in one parallel round of loads (lane = run), then
+    // independent acc loads per run: no dependent chain across runs
+    const int share = range_share(tot, cmx, a.dec_warps, a.split, a.pps_min);
+    const int nact = (pre + c - 1) / share - pre / share + 1;
     const int64_t s0 = (int64_t)u * a.split;
     for (int base = 0; base < nact; base += 32) {
       const int ch = base + lane;
@@ -417,7 +402,7 @@ merge_kernel(DecArgs a) {
       float M = m;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-      // chunks of this round are merged relative to their own max; rounds
+      // runs of this round are merged relative to their own max; rounds
       // (only when nact > 32) are rare and combined by rescaling below
       const float w = (m == -INFINITY) ? 0.f : exp2f(m - M);
       float lw = w * l;
@@ -470,16 +455,14 @@ merge_kernel(DecArgs a) {
 }
 
 template <int D, int NST>
-size_t decode_smem(int G, int units) {
+size_t decode_smem(int units) {
   return (size_t)kDecWarps * NST * Tile<D>::kStageBytes +
-         (size_t)kDecWarps * 8 * 2 * sizeof(float) +
-         (size_t)kDecWarps * G * D * sizeof(float) +
          (size_t)kDecWarps * NST * sizeof(int) + (size_t)(units + 1) * sizeof(int);
 }
 
 template <int D, int NST, bool TIER>
 int launch_decode(const DecArgs& a, cudaStream_t st) {
-  const size_t smem = decode_smem<D, NST>(a.G, a.units);
+  const size_t smem = decode_smem<D, NST>(a.units);
   if (smem > 220 * 1024) return AMASS_ERR_UNSUPPORTED;
   auto kern = decode_kernel<D, NST, TIER>;
   static unsigned long long configured = 0;
@@ -491,11 +474,13 @@ int launch_decode(const DecArgs& a, cudaStream_t st) {
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecThreads, smem);
   if (per_sm < 1) per_sm = 1;
   const int grid = num_sms() * per_sm;
-  if (int rc = launch_pdl(kern, dim3(grid), dim3(kDecThreads), smem, st, a)) return rc;
+  DecArgs b = a;
+  b.dec_warps = grid * kDecWarps;
+  if (int rc = launch_pdl(kern, dim3(grid), dim3(kDecThreads), smem, st, b)) return rc;
   int rc = launch_status();
   if (rc) return rc;
   const int heads = a.n_req * a.n_kv * a.G;
-  if (int rc = launch_pdl(merge_kernel<D>, dim3((heads + 3) / 4), dim3(128), 0, st, a)) return rc;
+  if (int rc = launch_pdl(merge_kernel<D>, dim3((heads + 3) / 4), dim3(128), 0, st, b)) return rc;
   return launch_status();
 }
 
@@ -523,7 +508,7 @@ int resident_decode(
       return AMASS_ERR_ARG;
   if (head_dim == 128 && ((o_stride_t % 4) || (o_stride_h % 4)))
     return AMASS_ERR_ARG;
-  if (n_req < 0 || n_kv <= 0 || G <= 0 || split <= 0 || pps_min <= 0 ||
+  if (n_req < 0 || n_kv <= 0 || G <= 0 || split < 2 || pps_min <= 0 ||
       max_pages <= 0)
     return AMASS_ERR_ARG;
   if (n_req == 0) return AMASS_OK;
@@ -616,7 +601,7 @@ extern "C" int amass_tier_decode(
     float scale, int n_req, int n_kv, int G, int head_dim, int page,
     int max_pages, void* stream) {
   using namespace amass;
-  if (n_req < 0 || n_kv <= 0 || G <= 0 || split <= 0 || pps_min <= 0 ||
+  if (n_req < 0 || n_kv <= 0 || G <= 0 || split < 2 || pps_min <= 0 ||
       max_pages <= 0 || layer < 0 || num_blocks <= 0 || hot_slots <= 0)
     return AMASS_ERR_ARG;
   if (n_req == 0) return AMASS_OK;
@@ -726,7 +711,7 @@ extern "C" int amass_sparse_decode_noalloc(
     int64_t o_stride_t, int64_t o_stride_h, float scale, int n_req, int n_kv,
     int G, int head_dim, int page, int max_pages, void* stream) {
   using namespace amass;
-  if (n_req < 0 || n_kv <= 0 || G <= 0 || split <= 0 || head_dim <= 0)
+  if (n_req < 0 || n_kv <= 0 || G <= 0 || split < 2 || head_dim <= 0)
     return AMASS_ERR_ARG;
   // partial layout: m (units*split*G), l (same), acc (units*split*G*D)
   const size_t slots = (size_t)n_req * n_kv * split * G;

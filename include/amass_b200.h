@@ -210,11 +210,13 @@ int amass_tag_stale(const void* const* k_layers, int n_layers, int64_t k_sb,
  * (Triton golden attention/decode.py:247-304 + merge.py:21-50).
  * K/V tiles are addressed as base + blk*s_b + tok*s_t + kv*s_h (elements,
  * bf16), which covers vLLM's (nb, 2, page, n_kv, d) and (2, nb, ...) caches.
- * Per (request, kv-head) unit: pps = max(ceil(cnt/split), pps_min) pages per
- * chunk; chunk partials go to m_part/l_part (R, n_kv, split, G) and acc_part
- * (R, n_kv, split, G, d) fp32; a merge writes out (T, H, d) bf16 rows
- * [0, n_req) in place (0 for empty units).  head_dim in {64, 128}, G <= 8,
- * page = 16. */
+ * The selected pages of all units form one flat list cut into equal runs
+ * (at least pps_min pages, one per warp of the persistent grid, and long
+ * enough that no unit needs more than `split` of them); each run writes one
+ * partial per unit it touches to m_part/l_part (R, n_kv, split, G) and
+ * acc_part (R, n_kv, split, G, d) fp32; a merge writes out (T, H, d) bf16
+ * rows [0, n_req) in place (0 for empty units).  split >= 2, head_dim in
+ * {64, 128}, G <= 8, page = 16. */
 int amass_sparse_decode(const void* q, int64_t q_stride_t, int64_t q_stride_h,
                         const void* k, int64_t k_sb, int64_t k_st,
                         int64_t k_sh, const void* v, int64_t v_sb,
