@@ -167,6 +167,15 @@ AMASS_DEV void ldsm_x4_t(uint32_t* r, uint32_t saddr) {
       : "r"(saddr));
 }
 
+// L2 eviction-priority policies: evict_first for data read once (streamed
+// summaries and K/V pages), evict_last for data re-read soon (per-head
+// scores between the scorer and the select)
+AMASS_DEV uint64_t l2_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
 // --------------------------------------------------------------------------
 // cp.async (16 B, L2-only caching; src_bytes = 0 zero-fills the destination)
 // --------------------------------------------------------------------------
@@ -177,6 +186,12 @@ AMASS_DEV void cp_async16(uint32_t dst, const void* src, bool valid) {
   int n = valid ? 16 : 0;
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
                :: "r"(dst), "l"(src), "r"(n));
+}
+AMASS_DEV void cp_async16_pol(uint32_t dst, const void* src, bool valid,
+                              uint64_t pol) {
+  int n = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;"
+               :: "r"(dst), "l"(src), "r"(n), "l"(pol));
 }
 AMASS_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
 template <int N>
@@ -189,6 +204,28 @@ AMASS_DEV uint4 ldg_nc_v4(const void* p) {
   uint4 r;
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+// the same with an L2 eviction-priority policy (createpolicy)
+AMASS_DEV uint4 ldg_nc_v4_pol(const void* p, uint64_t pol) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p), "l"(pol));
+  return r;
+}
+AMASS_DEV uint64_t l2_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+AMASS_DEV void stg_f32_pol(float* p, float v, uint64_t pol) {
+  asm volatile("st.global.L1::no_allocate.L2::cache_hint.f32 [%0], %1, %2;"
+               :: "l"(p), "f"(v), "l"(pol) : "memory");
+}
+AMASS_DEV float4 ldcg_f4_pol(const float4* p, uint64_t pol) {
+  float4 r;
+  asm volatile("ld.global.cg.L2::cache_hint.v4.f32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "l"(p), "l"(pol));
   return r;
 }
 AMASS_DEV uint2 ldg_nc_v2(const void* p) {

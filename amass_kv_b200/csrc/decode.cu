@@ -29,7 +29,15 @@
 namespace amass {
 namespace {
 
-constexpr int kDecWarps = 4;
+// warps per CTA and cp.async ring depth per warp (head_dim 128); override
+// at build time only for tuning sweeps
+#ifndef AMASS_DEC_WARPS
+#define AMASS_DEC_WARPS 8
+#endif
+#ifndef AMASS_DEC_NST
+#define AMASS_DEC_NST 2
+#endif
+constexpr int kDecWarps = AMASS_DEC_WARPS;
 constexpr int kMaxPeers = 8;
 constexpr int kDecThreads = kDecWarps * 32;
 
@@ -167,21 +175,26 @@ decode_kernel(DecArgs a) {
   uint8_t* my_stages = stages + warp * NST * T::kStageBytes;
   int* my_meta = meta + warp * NST;
 
-  // issue cursor: flat page fi of unit ui
-  int fi = g0, ui = unit_of(g0);
-  auto issue = [&](int slot) {
-    if (fi < g1) {
-      const int u = ui;
-      const int j = fi - pfx[u];
+  // Index batches: lane i resolves page ib + i of this run -- page table,
+  // block table and (tier) source lookups -- into the K and V tile
+  // addresses and the valid row count, 32 pages per round of independent
+  // loads, so the copy stream never waits on a dependent index load.
+  int ib = g0;
+  uint64_t bk = 0, bv = 0;
+  int bvalid = 0, bkst = 0, bvst = 0;
+  auto resolve = [&](int base) {
+    ib = base;
+    const int f = base + lane;
+    if (f < g1) {
+      const int u = unit_of(f);
+      const int j = f - pfx[u];
       const int r = u / a.n_kv, kv = u - r * a.n_kv;
       const int pt = a.tab[(int64_t)u * a.MP + j];
       // hot slot of a classified hit (-(slot + 2)), loaded beside pt
       const int ev = (TIER && a.eslot) ? a.eslot[(int64_t)u * a.MP + j] : -1;
       const int64_t blk = a.bt[(int64_t)r * a.bt_stride + pt];
       const int seq = a.sl[r];
-      const int valid = min(16, seq - pt * 16);
-      if (lane == 0) my_meta[slot] = valid;
-      const uint32_t sbase = smem_u32(my_stages + slot * T::kStageBytes);
+      bvalid = min(16, seq - pt * 16);
       const __nv_bfloat16* kp = a.k + blk * a.k_sb + kv * a.k_sh;
       const __nv_bfloat16* vp = a.v + blk * a.v_sb + kv * a.v_sh;
       int64_t kst = a.k_st, vst = a.v_st;
@@ -206,6 +219,31 @@ decode_kernel(DecArgs a) {
         vp = hv + off;
         if (a.hot_k) { kp = hk + off; kst = vst; }
       }
+      bk = reinterpret_cast<uint64_t>(kp);
+      bv = reinterpret_cast<uint64_t>(vp);
+      bkst = (int)kst;
+      bvst = (int)vst;
+    }
+  };
+  resolve(g0);
+  // K/V pages are read once: first out of L2, so the page and block
+  // tables, partials and the next stage's inputs stay resident
+  const uint64_t pol = l2_evict_first();
+  // issue cursor: flat page fi of this run
+  int fi = g0;
+  auto issue = [&](int slot) {
+    if (fi < g1) {
+      if (fi - ib >= 32) resolve(fi);
+      const int k = fi - ib;
+      const int valid = __shfl_sync(0xffffffffu, bvalid, k);
+      const __nv_bfloat16* kp = reinterpret_cast<const __nv_bfloat16*>(
+          __shfl_sync(0xffffffffu, bk, k));
+      const __nv_bfloat16* vp = reinterpret_cast<const __nv_bfloat16*>(
+          __shfl_sync(0xffffffffu, bv, k));
+      const int kst = __shfl_sync(0xffffffffu, bkst, k);
+      const int vst = __shfl_sync(0xffffffffu, bvst, k);
+      if (lane == 0) my_meta[slot] = valid;
+      const uint32_t sbase = smem_u32(my_stages + slot * T::kStageBytes);
 #pragma unroll
       for (int i = 0; i < (16 * T::kChunks) / 32; ++i) {
         const int id = lane + 32 * i;
@@ -213,11 +251,10 @@ decode_kernel(DecArgs a) {
         const bool ok = row < valid;
         const uint32_t doff = row * T::kRowBytes + swz(row, ch) * 16;
         const int rr = ok ? row : 0;
-        cp_async16(sbase + doff, kp + rr * kst + ch * 8, ok);
-        cp_async16(sbase + T::kTileBytes + doff, vp + rr * vst + ch * 8, ok);
+        cp_async16_pol(sbase + doff, kp + rr * kst + ch * 8, ok, pol);
+        cp_async16_pol(sbase + T::kTileBytes + doff, vp + rr * vst + ch * 8, ok, pol);
       }
       ++fi;
-      while (ui < U - 1 && pfx[ui + 1] <= fi) ++ui;
     }
     cp_async_commit();
   };
@@ -545,7 +582,7 @@ int resident_decode(
   a.p2s = a.vbo = a.eslot = nullptr;
   a.t_layer = a.t_NB = a.t_S = 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (head_dim == 128) return launch_decode<128, 2, false>(a, st);
+  if (head_dim == 128) return launch_decode<128, AMASS_DEC_NST, false>(a, st);
   if (head_dim == 64) return launch_decode<64, 3, false>(a, st);
   return AMASS_ERR_UNSUPPORTED;
 }
@@ -655,7 +692,7 @@ extern "C" int amass_tier_decode(
   a.p2s = page2slot; a.vbo = vbo; a.eslot = entry_slots;
   a.t_layer = layer; a.t_NB = num_blocks; a.t_S = hot_slots;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (head_dim == 128) return launch_decode<128, 2, true>(a, st);
+  if (head_dim == 128) return launch_decode<128, AMASS_DEC_NST, true>(a, st);
   if (head_dim == 64) return launch_decode<64, 3, true>(a, st);
   return AMASS_ERR_UNSUPPORTED;
 }
