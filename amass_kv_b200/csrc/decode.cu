@@ -77,6 +77,7 @@ struct DecArgs {
   const int32_t* eslot;         // (R, n_kv, MP) classified entries or null
   int t_layer, t_NB, t_S;
   int dec_warps;                // warps of the decode grid (run split)
+  int merge_wph;                // merge warps per (request, head) row
   // merged rows go to n_out buffers (this GPU's `out` alone, or every
   // rank's output under kv-head sharding: peer addresses over NVLink), at
   // global head head_off + local head
@@ -389,49 +390,61 @@ decode_kernel(DecArgs a) {
 }
 
 // ---- merge of the run partials (reference attention/merge.py:30-50) -------
+// A 256-thread CTA merges 8 / WPH (request, query head) rows; WPH warps
+// share one row's partials (partial j goes to warp j % WPH) and combine
+// their (m, l, acc) through shared memory.  WPH > 1 when there are few rows
+// and many partials per row (small batches): it keeps the merge from
+// running on a handful of warps.
+constexpr int kMergeThreads = 256;
+
 template <int D>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(kMergeThreads)
 merge_kernel(DecArgs a) {
   grid_dep_wait();     // inputs written by the previous kernel
   grid_dep_launch();
+  constexpr int PER = D / 32;
+  __shared__ float sM[8], sL[8];
+  __shared__ float sacc[8][D];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int WPH = a.merge_wph;
+  const int part = warp % WPH;
   const int H = a.n_kv * a.G;
-  const int idx = blockIdx.x * 4 + warp;  // (r, h)
-  if (idx >= a.n_req * H) return;
-  const int r = idx / H, h = idx - r * H;
+  const int idx = blockIdx.x * (8 / WPH) + warp / WPH;  // (r, h)
+  const bool live = idx < a.n_req * H;
+  const int r = live ? idx / H : 0, h = live ? idx - r * H : 0;
   const int kv = h / a.G, g = h - kv * a.G;
   const int u = r * a.n_kv + kv;
-  // the decode's run split: pages before unit u, all pages, largest unit
-  int pre = 0, tot = 0, cmx = 0;
-  for (int v = lane; v < a.units; v += 32) {
-    const int cv = max(a.cnt[v], 0);
-    tot += cv;
-    cmx = max(cmx, cv);
-    if (v < u) pre += cv;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    pre += __shfl_xor_sync(0xffffffffu, pre, o);
-    tot += __shfl_xor_sync(0xffffffffu, tot, o);
-    cmx = max(cmx, __shfl_xor_sync(0xffffffffu, cmx, o));
-  }
-  const int c = max(a.cnt[u], 0);
-  constexpr int PER = D / 32;
   float acc[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) acc[i] = 0.f;
   float Mrun = -INFINITY;
   float L = 0.f;
+  const int c = live ? max(a.cnt[u], 0) : 0;
   if (c > 0) {
-    // all run weights in one parallel round of loads (lane = run), then
-    // independent acc loads per run: no dependent chain across runs
+    // the decode's run split: pages before unit u, all pages, largest unit
+    int pre = 0, tot = 0, cmx = 0;
+    for (int v = lane; v < a.units; v += 32) {
+      const int cv = max(a.cnt[v], 0);
+      tot += cv;
+      cmx = max(cmx, cv);
+      if (v < u) pre += cv;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      pre += __shfl_xor_sync(0xffffffffu, pre, o);
+      tot += __shfl_xor_sync(0xffffffffu, tot, o);
+      cmx = max(cmx, __shfl_xor_sync(0xffffffffu, cmx, o));
+    }
     const int share = range_share(tot, cmx, a.dec_warps, a.split, a.pps_min);
     const int nact = (pre + c - 1) / share - pre / share + 1;
+    const int mine = nact > part ? (nact - part + WPH - 1) / WPH : 0;
     const int64_t s0 = (int64_t)u * a.split;
-    for (int base = 0; base < nact; base += 32) {
-      const int ch = base + lane;
+    // all run weights of a round in one parallel round of loads (lane =
+    // run), then independent acc loads per run
+    for (int base = 0; base < mine; base += 32) {
+      const int ch = part + (base + lane) * WPH;
       float m = -INFINITY, l = 0.f;
-      if (ch < nact) {
+      if (base + lane < mine) {
         m = a.m_part[(s0 + ch) * a.G + g];
         l = a.l_part[(s0 + ch) * a.G + g];
         if (!(l > 0.f)) m = -INFINITY;
@@ -440,7 +453,7 @@ merge_kernel(DecArgs a) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
       // runs of this round are merged relative to their own max; rounds
-      // (only when nact > 32) are rare and combined by rescaling below
+      // (more than 32 runs per warp) are combined by rescaling below
       const float w = (m == -INFINITY) ? 0.f : exp2f(m - M);
       float lw = w * l;
 #pragma unroll
@@ -448,11 +461,12 @@ merge_kernel(DecArgs a) {
       float racc[PER];
 #pragma unroll
       for (int i = 0; i < PER; ++i) racc[i] = 0.f;
-      const int n = min(32, nact - base);
+      const int n = min(32, mine - base);
 #pragma unroll 8
       for (int j = 0; j < n; ++j) {
         const float wj = __shfl_sync(0xffffffffu, w, j);
-        const float* ap = a.acc_part + ((s0 + base + j) * a.G + g) * D + lane * PER;
+        const int chj = part + (base + j) * WPH;
+        const float* ap = a.acc_part + ((s0 + chj) * a.G + g) * D + lane * PER;
 #pragma unroll
         for (int i = 0; i < PER; i += 2) {
           const float2 x = __ldcg(reinterpret_cast<const float2*>(ap + i));
@@ -475,6 +489,29 @@ merge_kernel(DecArgs a) {
       }
     }
   }
+  if (WPH > 1) {
+    // the WPH warps of a row combine through shared memory
+    if (lane == 0) { sM[warp] = Mrun; sL[warp] = L; }
+#pragma unroll
+    for (int i = 0; i < PER; ++i) sacc[warp][lane * PER + i] = acc[i];
+    __syncthreads();
+    if (part == 0) {
+      float M = -INFINITY;
+      for (int p = 0; p < WPH; ++p) M = fmaxf(M, sM[warp + p]);
+      float Lt = 0.f;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) acc[i] = 0.f;
+      for (int p = 0; p < WPH; ++p) {
+        const float mp = sM[warp + p];
+        const float sp = (mp == -INFINITY) ? 0.f : exp2f(mp - M);
+        Lt += sp * sL[warp + p];
+#pragma unroll
+        for (int i = 0; i < PER; ++i) acc[i] += sp * sacc[warp + p][lane * PER + i];
+      }
+      L = Lt;
+    }
+  }
+  if (!live || part != 0) return;
   const float inv = L > 0.f ? 1.f / L : 0.f;
   uint32_t w[PER / 2];
 #pragma unroll
@@ -517,7 +554,15 @@ int launch_decode(const DecArgs& a, cudaStream_t st) {
   int rc = launch_status();
   if (rc) return rc;
   const int heads = a.n_req * a.n_kv * a.G;
-  if (int rc = launch_pdl(merge_kernel<D>, dim3((heads + 3) / 4), dim3(128), 0, st, b)) return rc;
+  // warps per merged row: enough rows x warps for one 8-warp CTA per SM
+  // (1 at the C3 batch of 64 requests, 8 at batch 1)
+  int wph = 1;
+  while (wph < 8 && (long long)heads * wph < (long long)num_sms() * 8) wph <<= 1;
+  b.merge_wph = wph;
+  const int hpb = 8 / wph;
+  if (int rc = launch_pdl(merge_kernel<D>, dim3((heads + hpb - 1) / hpb),
+                          dim3(kMergeThreads), 0, st, b))
+    return rc;
   return launch_status();
 }
 

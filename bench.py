@@ -47,6 +47,7 @@ UNIT = "us/layer/step"
 N_REQ, N_KV, G, D, PAGE = 64, 8, 4, 128, 16
 RANK_Q, V_BITS, BUDGET, COMBINE = 2, 4, 0.05, "nrm"
 SCORER = "quad"                     # --scorer: quad (headline) or clse
+
 B_SUM = D + 2 + D * RANK_Q // 2 + 2 * RANK_Q + 2 * RANK_Q     # 266 B
 
 
@@ -186,6 +187,11 @@ class Batch:
         self.scale = 1.0 / math.sqrt(D)
         self.out = torch.empty(n_req, n_kv * G, D, dtype=torch.bfloat16,
                                device=dev)
+        # stage 0 = derive + score, 1 = nrm fold + select, 2 = split-K
+        # decode + merge
+        self.stages = (0, 1, 2)
+        self.stage_names = {0: "derive+quad_score", 1: "select",
+                            2: "sparse_decode+merge"}
         # derive, q-limbs, score, select, decode, merge
         self.launches_per_step = 6
         self.pps_min = None
@@ -217,7 +223,7 @@ class Batch:
                                                pps_min=self.pps_min)
 
     def step(self, layer, q=None):
-        for k in range(3):
+        for k in self.stages:
             self.stage(layer, k, q)
 
     def algorithmic_bytes(self, layer):
@@ -237,11 +243,12 @@ class Batch:
                     total=score_b + kv_b + qo, pages=int(cnt.sum()),
                     mean_ctx=float(np.mean(self.ctxs)))
 
-    def capture(self, cap_mode, stages=(0, 1, 2)):
+    def capture(self, cap_mode, stages=None):
         """One CUDA graph per layer of the given stages (eager warm-up of every
         layer on a side stream first: kernel attributes are set outside
         capture)."""
         import torch
+        stages = self.stages if stages is None else stages
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
@@ -299,21 +306,21 @@ def _stage_times(batch, cap_mode, steps, warmup):
     """Per-stage device time: each stage of a layer-step captured as its own
     CUDA graph, graphs replayed back to back with events between them on the
     launching stream (no host gaps inside the measured intervals); and the
-    marginal cost of each stage inside the whole step (prefix graphs
-    score / score+select / score+select+decode)."""
+    marginal cost of each stage inside the whole step (prefix graphs of the
+    first 1, 2, ... stages).  Returns {stage: ms} twice."""
     import torch
-    L = batch.layers
-    stage_graphs = [[None] * 3 for _ in range(L)]
+    L, ks = batch.layers, batch.stages
+    nk = len(ks)
+    stage_graphs = [[None] * nk for _ in range(L)]
     for l in range(L):
-        for k in range(3):
+        for j, k in enumerate(ks):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, capture_error_mode=cap_mode):
                 batch.stage(l, k)
-            stage_graphs[l][k] = g
-    prefix = [batch.capture(cap_mode, stages=tuple(range(k + 1)))
-              for k in range(3)]
+            stage_graphs[l][j] = g
+    prefix = [batch.capture(cap_mode, stages=ks[:j + 1]) for j in range(nk)]
     torch.cuda.synchronize()
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(nk + 1)]
           for _ in range(steps)]
     for i in range(warmup):
         for g in stage_graphs[i % L]:
@@ -321,12 +328,12 @@ def _stage_times(batch, cap_mode, steps, warmup):
     for i in range(steps):
         gs = stage_graphs[i % L]
         ev[i][0].record()
-        for k in range(3):
-            gs[k].replay()
-            ev[i][k + 1].record()
+        for j in range(nk):
+            gs[j].replay()
+            ev[i][j + 1].record()
     torch.cuda.synchronize()
-    iso = [float(np.mean([e[k].elapsed_time(e[k + 1]) for e in ev]))
-           for k in range(3)]
+    iso = {k: float(np.mean([e[j].elapsed_time(e[j + 1]) for e in ev]))
+           for j, k in enumerate(ks)}
     pref = []
     for gs in prefix:
         for i in range(warmup):
@@ -339,7 +346,7 @@ def _stage_times(batch, cap_mode, steps, warmup):
         e1.record()
         torch.cuda.synchronize()
         pref.append(e0.elapsed_time(e1) / steps)
-    marg = [pref[0], pref[1] - pref[0], pref[2] - pref[1]]
+    marg = {k: pref[j] - (pref[j - 1] if j else 0.0) for j, k in enumerate(ks)}
     return iso, marg
 
 
@@ -362,12 +369,13 @@ def _measure_c3(batch, args, world, dev, cap_mode, clocks=False):
     return float(statistics.median(reps)), reps, clk
 
 
-def _roofline(alg, t_stage_ms, peak, peak_kind):
+def _roofline(batch, alg, t_stage_ms, peak, peak_kind):
+    """The dominant stage's algorithmic bytes over its live time."""
     a_score = np.mean([a["score"] for a in alg])
     a_decode = np.mean([a["decode"] for a in alg])
-    kernels = {"derive+quad_score": (t_stage_ms[0], a_score),
-               "select": (t_stage_ms[1], 0.0),
-               "sparse_decode+merge": (t_stage_ms[2], a_decode)}
+    bytes_of = {0: a_score, 1: 0.0, 2: a_decode}
+    kernels = {batch.stage_names[k]: (t_stage_ms[k], bytes_of[k])
+               for k in batch.stages}
     dom = max(kernels, key=lambda k: kernels[k][0])
     if kernels[dom][1] == 0:
         dom = "sparse_decode+merge"
@@ -446,7 +454,9 @@ def _kv_layout(args, world, rank, dev):
     mine = {"rank": rank, "kv_heads": N_KV // world,
             "alg_bytes": int(np.mean([a["total"] for a in alg])),
             "decode_merge_gather_us": round(iso_g[2] * 1e3, 2),
-            "decode_merge_local_us": round(iso_l[2] * 1e3, 2)}
+            "decode_merge_local_us": round(iso_l[2] * 1e3, 2),
+            "stage_us": {batch.stage_names[k]: round(v * 1e3, 2)
+                         for k, v in iso_g.items()}}
     per = [None] * world
     dist.all_gather_object(per, mine)
     res = {"value": round(med * 1e3, 2), "unit": UNIT,
@@ -497,12 +507,13 @@ def run_gpu(args):
     own = med if world == 1 else _measure_c3(batch, args, 1, dev,
                                              "global")[0]
     e2e = _e2e(batch, args, world, dev)
-    kernels, roof = _roofline(alg, iso, peak, peak_kind)
+    kernels, roof = _roofline(batch, alg, iso, peak, peak_kind)
     a_total = float(np.mean([a["total"] for a in alg]))
     rank_info = {"rank": rank, "requests": len(mine),
                  "ctx_tokens": int(ctxs[mine].sum()),
                  "alg_bytes": int(a_total), "own_us": round(own * 1e3, 2),
-                 "stage_us": [round(x * 1e3, 2) for x in iso]}
+                 "stage_us": {batch.stage_names[k]: round(v * 1e3, 2)
+                              for k, v in iso.items()}}
     per_rank = [rank_info]
     if world > 1:
         per_rank = [None] * world
@@ -576,21 +587,18 @@ def run_gpu(args):
                                       "max-over-ranks step time / (N x peak)"},
             "roofline": roof,
             "kernel_us": {k: round(v[0] * 1e3, 2) for k, v in kernels.items()},
-            "marginal_us": {"derive+quad_score": round(marg[0] * 1e3, 2),
-                            "select": round(marg[1] * 1e3, 2),
-                            "sparse_decode+merge": round(marg[2] * 1e3, 2)},
+            "marginal_us": {batch.stage_names[k]: round(v * 1e3, 2)
+                            for k, v in marg.items()},
             "per_rank": per_rank,
             "e2e": e2e,
-            "gpu_launches": batch_launches(args),
+            "gpu_launches": batch_launches(batch, args),
             "clocks": clk,
         }
         if world > 1:
             lim = max(per_rank, key=lambda p: p["own_us"])
             line["limiter"] = {
                 "rank": lim["rank"], "own_us": lim["own_us"],
-                "stage": ["derive+quad_score", "select",
-                          "sparse_decode+merge"][int(np.argmax(
-                              lim["stage_us"]))],
+                "stage": max(lim["stage_us"], key=lim["stage_us"].get),
                 "bytes_imbalance": round(max(p["alg_bytes"] for p in per_rank)
                                          / (tot_bytes / world), 4)}
         if layouts:
@@ -613,9 +621,8 @@ def run_gpu(args):
         os._exit(0)
 
 
-def batch_launches(args):
-    # derive, q-limbs, score, select, decode, merge per layer-step
-    return 6 * args.steps * args.repeats
+def batch_launches(batch, args):
+    return batch.launches_per_step * args.steps * args.repeats
 
 
 def _ctx32k(args, dev, peak, peak_kind):
