@@ -414,20 +414,26 @@ merge_kernel(DecArgs a) {
   const int r = live ? idx / H : 0, h = live ? idx - r * H : 0;
   const int kv = h / a.G, g = h - kv * a.G;
   const int u = r * a.n_kv + kv;
-  float acc[PER];
+  // the decode's run split, once per CTA: pages of all units and of the
+  // units before this CTA's first unit (every thread's loads in flight
+  // together), the largest unit; then each row adds the few units between
+  __shared__ int red[3][8];
+  const int H_ = a.n_kv * a.G;
+  const int idx0 = blockIdx.x * (8 / WPH);
+  const int u_lo = min(idx0, a.n_req * H_ - 1) / a.G;
+  int tot = 0, pre = 0, cmx = 0;
+  {
+    constexpr int kU = 4;
+    for (int v0 = threadIdx.x * kU; v0 < a.units; v0 += kMergeThreads * kU) {
+      int cv[kU];
 #pragma unroll
-  for (int i = 0; i < PER; ++i) acc[i] = 0.f;
-  float Mrun = -INFINITY;
-  float L = 0.f;
-  const int c = live ? max(a.cnt[u], 0) : 0;
-  if (c > 0) {
-    // the decode's run split: pages before unit u, all pages, largest unit
-    int pre = 0, tot = 0, cmx = 0;
-    for (int v = lane; v < a.units; v += 32) {
-      const int cv = max(a.cnt[v], 0);
-      tot += cv;
-      cmx = max(cmx, cv);
-      if (v < u) pre += cv;
+      for (int j = 0; j < kU; ++j) cv[j] = v0 + j < a.units ? max(a.cnt[v0 + j], 0) : 0;
+#pragma unroll
+      for (int j = 0; j < kU; ++j) {
+        tot += cv[j];
+        cmx = max(cmx, cv[j]);
+        if (v0 + j < u_lo) pre += cv[j];
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -435,6 +441,24 @@ merge_kernel(DecArgs a) {
       tot += __shfl_xor_sync(0xffffffffu, tot, o);
       cmx = max(cmx, __shfl_xor_sync(0xffffffffu, cmx, o));
     }
+    if (lane == 0) { red[0][warp] = pre; red[1][warp] = tot; red[2][warp] = cmx; }
+    __syncthreads();
+    pre = tot = cmx = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      pre += red[0][w];
+      tot += red[1][w];
+      cmx = max(cmx, red[2][w]);
+    }
+  }
+  float acc[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) acc[i] = 0.f;
+  float Mrun = -INFINITY;
+  float L = 0.f;
+  const int c = live ? max(a.cnt[u], 0) : 0;
+  if (c > 0) {
+    for (int v = u_lo; v < u; ++v) pre += max(a.cnt[v], 0);
     const int share = range_share(tot, cmx, a.dec_warps, a.split, a.pps_min);
     const int nact = (pre + c - 1) / share - pre / share + 1;
     const int mine = nact > part ? (nact - part + WPH - 1) / WPH : 0;
