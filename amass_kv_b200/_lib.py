@@ -36,6 +36,10 @@ _SIGS = {
     "amass_quad_score": [_P, _L, _L, _P, _P, _P, _P, _P, _P, _L, _P, _P, _P,
                          _L, _P, _P, _P, _F, _I, _I, _I, _I, _I, _I, _I, _I,
                          _I, _P],
+    "amass_quad_score_derive": [_P, _P, _P, _P, _P, _I, _I, _P, _L, _L, _P,
+                                _P, _P, _P, _P, _P, _L, _P, _P, _L, _P, _P,
+                                _P, _F, _I, _I, _I, _I, _I, _I, _I, _I, _I,
+                                _P],
     "amass_r8_score": [_P, _L, _L, _P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _P,
                        _P, _P, _F, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P],
     "amass_clse_score": [_P, _L, _L, _P, _P, _P, _P, _P, _P, _I, _P, _P, _L,

@@ -73,6 +73,25 @@ inline int num_sms() {
 }
 
 // --------------------------------------------------------------------------
+// derive_page_params of one request (reference selection/select.py:30-45):
+// npg = ceil(s / page), n_sel_hi = npg - window, b = clamp(ceil(fp64
+// (n_sel_hi - sink) * budget), 1, max(n_sel_hi - sink, 1))
+// --------------------------------------------------------------------------
+AMASS_DEV void derive_one(int s, double bud, int page, int win, int sink,
+                          int32_t* npg_o, int32_t* nsh_o, int32_t* b_o) {
+  const int npg = (s + page - 1) / page;
+  const int nsh = npg - win;
+  const int nsel = nsh - sink;
+  const double bf = ceil((double)nsel * bud);
+  int b = (int)bf;
+  b = max(b, 1);
+  b = min(b, max(nsel, 1));
+  *npg_o = npg;
+  *nsh_o = nsh;
+  *b_o = b;
+}
+
+// --------------------------------------------------------------------------
 // order-preserving float <-> uint32 keys (larger float -> larger key)
 // --------------------------------------------------------------------------
 AMASS_DEV uint32_t float_key(float f) {

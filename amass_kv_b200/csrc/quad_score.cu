@@ -70,6 +70,13 @@ struct QuadArgs {
   float iso_coef;       // s^2 / (2 P (d - r))
   int ctok;             // coordinate scales per token (1) or per page (0)
   int write_h;          // per-head scores + hmax (nrm) instead of the max
+  // derive_page_params folded into the q prologue (null dv_sl: not asked)
+  const int32_t* dv_sl;
+  const double* dv_budget;
+  int32_t* dv_npg;
+  int32_t* dv_nsh;
+  int32_t* dv_b;
+  int dv_win, dv_sink;
 };
 
 AMASS_DEV void atomic_max_float(float* addr, float v) {
@@ -92,6 +99,13 @@ template <int D>
 __global__ void __launch_bounds__(256) q_limbs_kernel(QuadArgs a) {
   grid_dep_wait();     // inputs written by the previous kernel
   grid_dep_launch();
+  if (a.dv_sl && blockIdx.x == 0) {
+    // this step's page parameters for the scorer (the next launch)
+    const double bud = a.dv_budget[0];
+    for (int i = threadIdx.x; i < a.n_req; i += blockDim.x)
+      derive_one(a.dv_sl[i], bud, a.page, a.dv_win, a.dv_sink, a.dv_npg + i,
+                 a.dv_nsh + i, a.dv_b + i);
+  }
   const int H = a.n_kv * a.G;
   const int idx = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -952,19 +966,18 @@ int dispatch_rank(const QuadArgs& a, int rank, int v_bits, bool write_h,
 }  // namespace
 }  // namespace amass
 
-extern "C" int amass_quad_score(const void* q, int64_t q_stride_t,
-                                int64_t q_stride_h, const int8_t* mu,
-                                const void* mu_scale, const int8_t* V,
-                                const void* V_scale, const void* sig2,
-                                const int32_t* block_table, int64_t bt_stride,
-                                const int32_t* n_sel_hi, float* score,
-                                float* score_h, int64_t sh_stride,
-                                float* hmax, int8_t* q8_ws,
-                                float* qs_ws, float scale, int n_req,
-                                int n_kv, int G, int head_dim, int page,
-                                int rank, int v_bits, int max_pages,
-                                int write_h, void* stream) {
-  using namespace amass;
+namespace amass {
+namespace {
+int quad_score_impl(const void* q, int64_t q_stride_t, int64_t q_stride_h,
+                    const int8_t* mu, const void* mu_scale, const int8_t* V,
+                    const void* V_scale, const void* sig2,
+                    const int32_t* block_table, int64_t bt_stride,
+                    const int32_t* n_sel_hi, float* score, float* score_h,
+                    int64_t sh_stride, float* hmax, int8_t* q8_ws,
+                    float* qs_ws, float scale, int n_req, int n_kv, int G,
+                    int head_dim, int page, int rank, int v_bits,
+                    int max_pages, int write_h, void* stream,
+                    const QuadArgs* derive) {
   if (n_req < 0 || n_kv <= 0 || G <= 0 || max_pages <= 0) return AMASS_ERR_ARG;
   if (n_req == 0) return AMASS_OK;
   if (!q || !mu || !mu_scale || !V || !V_scale || !sig2 || !block_table ||
@@ -980,6 +993,15 @@ extern "C" int amass_quad_score(const void* q, int64_t q_stride_t,
       (reinterpret_cast<uintptr_t>(q8_ws) & 15))
     return AMASS_ERR_ARG;
   QuadArgs a{};
+  if (derive) {
+    a.dv_sl = derive->dv_sl;
+    a.dv_budget = derive->dv_budget;
+    a.dv_npg = derive->dv_npg;
+    a.dv_nsh = derive->dv_nsh;
+    a.dv_b = derive->dv_b;
+    a.dv_win = derive->dv_win;
+    a.dv_sink = derive->dv_sink;
+  }
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.q_st = q_stride_t;
   a.q_sh = q_stride_h;
@@ -1003,10 +1025,62 @@ extern "C" int amass_quad_score(const void* q, int64_t q_stride_t,
   a.n_kv = n_kv;
   a.G = G;
   a.MP = max_pages;
+  a.page = page;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (head_dim == 128) return dispatch_rank<128>(a, rank, v_bits, write_h, st);
   if (head_dim == 64) return dispatch_rank<64>(a, rank, v_bits, write_h, st);
   return AMASS_ERR_UNSUPPORTED;
+}
+}  // namespace
+}  // namespace amass
+
+extern "C" int amass_quad_score(const void* q, int64_t q_stride_t,
+                                int64_t q_stride_h, const int8_t* mu,
+                                const void* mu_scale, const int8_t* V,
+                                const void* V_scale, const void* sig2,
+                                const int32_t* block_table, int64_t bt_stride,
+                                const int32_t* n_sel_hi, float* score,
+                                float* score_h, int64_t sh_stride,
+                                float* hmax, int8_t* q8_ws,
+                                float* qs_ws, float scale, int n_req,
+                                int n_kv, int G, int head_dim, int page,
+                                int rank, int v_bits, int max_pages,
+                                int write_h, void* stream) {
+  return amass::quad_score_impl(q, q_stride_t, q_stride_h, mu, mu_scale, V,
+                                V_scale, sig2, block_table, bt_stride,
+                                n_sel_hi, score, score_h, sh_stride, hmax,
+                                q8_ws, qs_ws, scale, n_req, n_kv, G, head_dim,
+                                page, rank, v_bits, max_pages, write_h, stream,
+                                nullptr);
+}
+
+extern "C" int amass_quad_score_derive(
+    const int32_t* seq_lens, const double* budget64, int32_t* n_pages,
+    int32_t* n_sel_hi, int32_t* b_fix, int window_pages, int sink_pages,
+    const void* q, int64_t q_stride_t, int64_t q_stride_h, const int8_t* mu,
+    const void* mu_scale, const int8_t* V, const void* V_scale,
+    const void* sig2, const int32_t* block_table, int64_t bt_stride,
+    float* score, float* score_h, int64_t sh_stride, float* hmax,
+    int8_t* q8_ws, float* qs_ws, float scale, int n_req, int n_kv, int G,
+    int head_dim, int page, int rank, int v_bits, int max_pages, int write_h,
+    void* stream) {
+  using namespace amass;
+  if (!seq_lens || !budget64 || !n_pages || !n_sel_hi || !b_fix ||
+      window_pages < 0 || sink_pages < 0)
+    return AMASS_ERR_ARG;
+  QuadArgs d{};
+  d.dv_sl = seq_lens;
+  d.dv_budget = budget64;
+  d.dv_npg = n_pages;
+  d.dv_nsh = n_sel_hi;
+  d.dv_b = b_fix;
+  d.dv_win = window_pages;
+  d.dv_sink = sink_pages;
+  return quad_score_impl(q, q_stride_t, q_stride_h, mu, mu_scale, V, V_scale,
+                         sig2, block_table, bt_stride, n_sel_hi, score,
+                         score_h, sh_stride, hmax, q8_ws, qs_ws, scale, n_req,
+                         n_kv, G, head_dim, page, rank, v_bits, max_pages,
+                         write_h, stream, &d);
 }
 
 

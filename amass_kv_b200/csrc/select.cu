@@ -17,19 +17,8 @@ __global__ void derive_kernel(const int32_t* __restrict__ sl,
   grid_dep_launch();
   const double bud = budget[0];
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_req;
-       i += gridDim.x * blockDim.x) {
-    const int s = sl[i];
-    const int npg = (s + page - 1) / page;
-    const int nsh = npg - win;
-    const int nsel = nsh - sink;
-    const double bf = ceil((double)nsel * bud);
-    int b = (int)bf;
-    b = max(b, 1);
-    b = min(b, max(nsel, 1));
-    npg_o[i] = npg;
-    nsh_o[i] = nsh;
-    b_o[i] = b;
-  }
+       i += gridDim.x * blockDim.x)
+    derive_one(sl[i], bud, page, win, sink, npg_o + i, nsh_o + i, b_o + i);
 }
 
 __global__ void __launch_bounds__(kSelThreads)

@@ -78,9 +78,8 @@ class StepPipeline:
 
     def _step(self, layer: int, b: int) -> None:
         st, n = self.st, self.n_req
-        S.derive_page_params(st, self.sl[b], n)
         self.select(st, layer, self.q[b], self.bt, self.sl[b], n, self.scale,
-                    derive=False)
+                    derive=True)
         A.sparse_paged_decode_batched_cuda(self.q[b], self.kv[layer], self.bt,
                                            self.sl[b], st, self.out[b],
                                            scale=self.scale)

@@ -171,13 +171,32 @@ def _prepare(st, device, write_h):
     st._amass_ready = True
 
 
-def _score_launch(st, layer, q, block_table, n_req, scale, write_h):
+def _score_launch(st, layer, q, block_table, n_req, scale, write_h,
+                  seq_lens=None):
+    """quad scorer launch; with ``seq_lens`` the step's page parameters
+    (derive_page_params) are computed in the same launches."""
     _prepare(st, q.device, write_h)
     mu, mu_s, V, V_s, sig2 = (st.quad_mu[layer], st.mu_scale[layer],
                               st.quad_V[layer], st.V_scale[layer],
                               st.quad_sig2[layer])
     r, v_bits = _rank_bits(st, V)
     _check_q(q, st)
+    if seq_lens is not None:
+        if n_req > st.max_reqs:
+            raise ValueError(f"n_req {n_req} > max_reqs {st.max_reqs}")
+        _lib.call("amass_quad_score_derive", ptr(seq_lens), ptr(st.budget64),
+                  ptr(st.n_pages), ptr(st.n_sel_hi), ptr(st.b_fix),
+                  int(st.window_pages), int(st.sink_pages), ptr(q),
+                  q.stride(0), q.stride(1), ptr(mu), ptr(mu_s), ptr(V),
+                  ptr(V_s), ptr(sig2), ptr(block_table),
+                  block_table.stride(0), ptr(st.score),
+                  ptr(st.score_h) if write_h else 0,
+                  st.score_h.stride(2) if write_h else 0,
+                  ptr(st.hmax) if write_h else 0, ptr(st.q8), ptr(st.qs),
+                  float(scale), int(n_req), int(st.n_kv), int(st.G),
+                  int(st.d), int(st.page), r, v_bits, int(st.max_pages),
+                  1 if write_h else 0, _lib.stream_of(q.device))
+        return
     _lib.call("amass_quad_score", ptr(q), q.stride(0), q.stride(1), ptr(mu),
               ptr(mu_s), ptr(V), ptr(V_s), ptr(sig2), ptr(block_table),
               block_table.stride(0), ptr(st.n_sel_hi), ptr(st.score),
@@ -247,10 +266,9 @@ def select_pages_quad(st, layer: int, q, block_table, seq_lens, n_req: int,
                       coverage=None) -> None:
     """One-call Stage A (quad): (derive) + score + fused fold/select.
     Writes st.page_table / st.page_cnt (and st.score)."""
-    if derive:
-        derive_page_params(st, seq_lens, n_req)
     nrm = getattr(st, "combine", "max") == "nrm"
-    _score_launch(st, layer, q, block_table, n_req, scale, nrm)
+    _score_launch(st, layer, q, block_table, n_req, scale, nrm,
+                  seq_lens=seq_lens if derive else None)
     select_pages(st, n_req, coverage=coverage, from_score_h=nrm)
 
 

@@ -192,8 +192,8 @@ class Batch:
         self.stages = (0, 1, 2)
         self.stage_names = {0: "derive+quad_score", 1: "select",
                             2: "sparse_decode+merge"}
-        # derive, q-limbs, score, select, decode, merge
-        self.launches_per_step = 6
+        # q-limbs (+ derive), score, select, decode, merge; CLSE: + derive
+        self.launches_per_step = 6 if self.clse else 5
         self.pps_min = None
 
     def stage(self, layer, k, q=None):
@@ -205,11 +205,12 @@ class Batch:
         q = self.q[l] if q is None else q
         nrm = COMBINE == "nrm"
         if k == 0:
-            S.derive_page_params(st, self.sl, n)
             if self.clse:
+                S.derive_page_params(st, self.sl, n)
                 S.clse_score_cuda(st, l, q, self.bt, self.sl, n, self.scale)
             else:
-                S._score_launch(st, l, q, self.bt, n, self.scale, nrm)
+                S._score_launch(st, l, q, self.bt, n, self.scale, nrm,
+                                seq_lens=self.sl)
         elif k == 1:
             S.select_pages(st, n, from_score_h=nrm)
         elif self.gather is not None:

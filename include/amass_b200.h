@@ -84,6 +84,24 @@ int amass_quad_score(const void* q, int64_t q_stride_t, int64_t q_stride_h,
                      int rank, int v_bits, int max_pages, int write_h,
                      void* stream);
 
+/* quad_score_derive -- derive_page_params (selection/select.py:30-54) and
+ * quad_score_cuda (selection/quad_score_cuda.py:1724-1794), the first two
+ * calls of the reference's _quad_select_adapter (backend/_runtime.py:
+ * 183-263), in the launches of amass_quad_score alone: the q-limb prologue
+ * also writes n_pages / n_sel_hi / b_fix from seq_lens and budget64 (as
+ * amass_derive_page_params), and the scorer reads that n_sel_hi.  Other
+ * arguments as amass_quad_score. */
+int amass_quad_score_derive(
+    const int32_t* seq_lens, const double* budget64, int32_t* n_pages,
+    int32_t* n_sel_hi, int32_t* b_fix, int window_pages, int sink_pages,
+    const void* q, int64_t q_stride_t, int64_t q_stride_h, const int8_t* mu,
+    const void* mu_scale, const int8_t* V, const void* V_scale,
+    const void* sig2, const int32_t* block_table, int64_t bt_stride,
+    float* score, float* score_h, int64_t sh_stride, float* hmax,
+    int8_t* q8_ws, float* qs_ws, float scale, int n_req, int n_kv, int G,
+    int head_dim, int page, int rank, int v_bits, int max_pages, int write_h,
+    void* stream);
+
 /* nrm combine -- replaces the two passes of selection/quad_score.py:276-315
  * (CUDA twin quad_score_cuda.py:1446-1547): with hmax[r,kv,g] = the per-head
  * page max that amass_quad_score accumulated, score[r,kv,p] =

@@ -74,6 +74,10 @@ def test_select_and_decode(name, dev):
     A.sparse_paged_decode_batched_cuda(c.q, c.kv, c.bt, c.sl, st, c.out,
                                        A.ResidentVSource(c.kv), scale=c.scale)
     torch.cuda.synchronize()
+    # the page parameters derived inside the scorer's launches
+    assert np.array_equal(st.n_pages.cpu().numpy(), z["n_pages"])
+    assert np.array_equal(st.n_sel_hi.cpu().numpy(), z["n_sel_hi"])
+    assert np.array_equal(st.b_fix.cpu().numpy(), z["b_fix"])
     tab = st.page_table.cpu().numpy()
     cnt = st.page_cnt.cpu().numpy()
     ref_sc = np.where(np.isnan(z["score"]), -np.inf, z["score"])
