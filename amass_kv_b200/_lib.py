@@ -88,6 +88,10 @@ _SIGS = {
                           _L, _P, _P, _P, _P, _P, _I, _I, _I, _P, _L, _P, _P, _P,
                           _P, _P, _P, _I, _I, _P, _L, _L, _F, _I, _I, _I, _I,
                           _I, _I, _P],
+    "amass_tier_decode_install": [_P, _L, _L, _P, _L, _L, _L, _P, _P, _P, _P,
+                                  _L, _L, _L, _P, _P, _P, _P, _P, _P, _I, _I,
+                                  _I, _P, _L, _P, _P, _P, _P, _P, _P, _I, _I,
+                                  _P, _L, _L, _F, _I, _I, _I, _I, _I, _I, _P],
 }
 
 _lib = None

@@ -76,6 +76,12 @@ struct DecArgs {
   const int32_t* vbo;           // (NB,)
   const int32_t* eslot;         // (R, n_kv, MP) classified entries or null
   int t_layer, t_NB, t_S;
+  // install mode (TIER): a page the residency plan installed this step is
+  // read from its source (staging or pinned) and its tile is then written
+  // into the assigned hot slot (and written through to the pinned pool when
+  // it came from staging unflushed) -- the miss fetch, done by the decode
+  int8_t* pvalid;               // (n_kv, NB) this layer, or null
+  int install;
   int dec_warps;                // warps of the decode grid (run split)
   int merge_wph;                // merge warps per (request, head) row
   // merged rows go to n_out buffers (this GPU's `out` alone, or every
@@ -107,6 +113,21 @@ struct Tile {
 
 AMASS_DEV uint32_t swz(int row, int chunk) { return chunk ^ (row & 7); }
 
+// one landed 16 x D tile (XOR-swizzled rows in shared memory) to a dense
+// row-major tile in global memory, 16-byte stores
+template <int D>
+AMASS_DEV void install_tile(const uint8_t* src, uint8_t* dst, int lane) {
+  using T = Tile<D>;
+#pragma unroll
+  for (int i = 0; i < (16 * T::kChunks) / 32; ++i) {
+    const int id = lane + 32 * i;
+    const int row = id / T::kChunks, ch = id % T::kChunks;
+    const uint4 x = *reinterpret_cast<const uint4*>(
+        src + row * T::kRowBytes + swz(row, ch) * 16);
+    *reinterpret_cast<uint4*>(dst + row * T::kRowBytes + ch * 16) = x;
+  }
+}
+
 template <int D, int NST, bool TIER>
 __global__ void __launch_bounds__(kDecThreads)
 decode_kernel(DecArgs a) {
@@ -115,7 +136,10 @@ decode_kernel(DecArgs a) {
   using T = Tile<D>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;                                    // warps x NST
-  int* meta = reinterpret_cast<int*>(smem + kDecWarps * NST * T::kStageBytes);
+  // per stage: install targets (hot V, hot K, pinned V, pinned K, valid
+  // flag; 0 = none), then the valid row count
+  uint64_t* inst = reinterpret_cast<uint64_t*>(smem + kDecWarps * NST * T::kStageBytes);
+  int* meta = reinterpret_cast<int*>(inst + kDecWarps * NST * 5);
   int* pfx = meta + kDecWarps * NST;                         // units + 1
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -175,6 +199,7 @@ decode_kernel(DecArgs a) {
 
   uint8_t* my_stages = stages + warp * NST * T::kStageBytes;
   int* my_meta = meta + warp * NST;
+  uint64_t* my_inst = inst + warp * NST * 5;
 
   // Index batches: lane i resolves page ib + i of this run -- page table,
   // block table and (tier) source lookups -- into the K and V tile
@@ -183,6 +208,7 @@ decode_kernel(DecArgs a) {
   int ib = g0;
   uint64_t bk = 0, bv = 0;
   int bvalid = 0, bkst = 0, bvst = 0;
+  uint64_t bi_v = 0, bi_k = 0, bw_v = 0, bw_k = 0, bw_f = 0;   // install mode
   auto resolve = [&](int base) {
     ib = base;
     const int f = base + lane;
@@ -199,11 +225,15 @@ decode_kernel(DecArgs a) {
       const __nv_bfloat16* kp = a.k + blk * a.k_sb + kv * a.k_sh;
       const __nv_bfloat16* vp = a.v + blk * a.v_sb + kv * a.v_sh;
       int64_t kst = a.k_st, vst = a.v_st;
+      bi_v = bi_k = bw_v = bw_k = bw_f = 0;
       if constexpr (TIER) {
         // one source decision per page, on the address (same bytes, so the
         // math matches the resident decode bit for bit)
         const int hslot = ev <= -2 ? -ev - 2 : a.p2s[(int64_t)kv * a.t_NB + blk];
-        const bool use_hot = ev <= -2 || ((pt + 1) * 16 <= seq && hslot >= 0);
+        const bool complete = (pt + 1) * 16 <= seq;
+        // install mode: a miss the plan gave a slot is not in it yet
+        const bool installed = a.install && ev >= 0 && complete && hslot >= 0;
+        const bool use_hot = ev <= -2 || (complete && hslot >= 0 && !installed);
         const int vb = use_hot ? -1 : a.vbo[blk];
         int64_t off;
         const __nv_bfloat16 *hv, *hk;
@@ -219,6 +249,20 @@ decode_kernel(DecArgs a) {
         }
         vp = hv + off;
         if (a.hot_k) { kp = hk + off; kst = vst; }
+        if (installed) {
+          const int64_t hoff = ((int64_t)kv * a.t_S + hslot) * (16 * D);
+          bi_v = reinterpret_cast<uint64_t>(a.hot_v + hoff);
+          if (a.hot_k) bi_k = reinterpret_cast<uint64_t>(a.hot_k + hoff);
+          const int64_t vrow = (int64_t)kv * a.t_NB + blk;
+          if (vb >= 0 && a.pvalid[vrow] == 0) {
+            // staged and not flushed: write through to the pinned pool
+            const int64_t poff =
+                (((int64_t)a.t_layer * a.t_NB + blk) * a.n_kv + kv) * (16 * D);
+            bw_v = reinterpret_cast<uint64_t>(a.pool_v + poff);
+            if (a.hot_k) bw_k = reinterpret_cast<uint64_t>(a.pool_k + poff);
+            bw_f = reinterpret_cast<uint64_t>(a.pvalid + vrow);
+          }
+        }
       }
       bk = reinterpret_cast<uint64_t>(kp);
       bv = reinterpret_cast<uint64_t>(vp);
@@ -244,6 +288,17 @@ decode_kernel(DecArgs a) {
       const int kst = __shfl_sync(0xffffffffu, bkst, k);
       const int vst = __shfl_sync(0xffffffffu, bvst, k);
       if (lane == 0) my_meta[slot] = valid;
+      if (TIER && a.install) {
+        const uint64_t iv = __shfl_sync(0xffffffffu, bi_v, k);
+        const uint64_t ik = __shfl_sync(0xffffffffu, bi_k, k);
+        const uint64_t wv = __shfl_sync(0xffffffffu, bw_v, k);
+        const uint64_t wk = __shfl_sync(0xffffffffu, bw_k, k);
+        const uint64_t wf = __shfl_sync(0xffffffffu, bw_f, k);
+        if (lane == 0) {
+          uint64_t* m = my_inst + slot * 5;
+          m[0] = iv; m[1] = ik; m[2] = wv; m[3] = wk; m[4] = wf;
+        }
+      }
       const uint32_t sbase = smem_u32(my_stages + slot * T::kStageBytes);
 #pragma unroll
       for (int i = 0; i < (16 * T::kChunks) / 32; ++i) {
@@ -301,6 +356,19 @@ decode_kernel(DecArgs a) {
       const uint32_t kbase = smem_u32(my_stages + slot_c * T::kStageBytes);
       const uint32_t vbase = kbase + T::kTileBytes;
       const int valid = my_meta[slot_c];
+      if (TIER && a.install) {
+        const uint64_t* m = my_inst + slot_c * 5;
+        if (m[0]) {
+          // the page's tiles (complete pages: all 16 rows) into the hot slot
+          const uint8_t* st_k = my_stages + slot_c * T::kStageBytes;
+          const uint8_t* st_v = st_k + T::kTileBytes;
+          install_tile<D>(st_v, reinterpret_cast<uint8_t*>(m[0]), lane);
+          if (m[1]) install_tile<D>(st_k, reinterpret_cast<uint8_t*>(m[1]), lane);
+          if (m[2]) install_tile<D>(st_v, reinterpret_cast<uint8_t*>(m[2]), lane);
+          if (m[3]) install_tile<D>(st_k, reinterpret_cast<uint8_t*>(m[3]), lane);
+          if (m[4] && lane == 0) *reinterpret_cast<int8_t*>(m[4]) = 1;
+        }
+      }
 
       // S^T = K Q^T: rows = the 16 tokens, cols = the query heads; A = K
       // from shared memory (ldmatrix), B = the q fragment; two accumulators
@@ -555,6 +623,7 @@ merge_kernel(DecArgs a) {
 template <int D, int NST>
 size_t decode_smem(int units) {
   return (size_t)kDecWarps * NST * Tile<D>::kStageBytes +
+         (size_t)kDecWarps * NST * 5 * sizeof(uint64_t) +
          (size_t)kDecWarps * NST * sizeof(int) + (size_t)(units + 1) * sizeof(int);
 }
 
@@ -694,7 +763,9 @@ extern "C" int amass_sparse_decode_gather(
       o_stride_h, scale, n_req, n_kv, G, head_dim, page, max_pages, stream);
 }
 
-extern "C" int amass_tier_decode(
+namespace amass {
+namespace {
+int tier_decode_impl(
     const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k,
     int64_t k_sb, int64_t k_st, int64_t k_sh, const void* hot_v,
     const void* hot_k, const void* stg_v, const void* stg_k, int64_t svb,
@@ -705,8 +776,7 @@ extern "C" int amass_tier_decode(
     const int32_t* seq_lens, float* m_part, float* l_part, float* acc_part,
     int split, int pps_min, void* out, int64_t o_stride_t, int64_t o_stride_h,
     float scale, int n_req, int n_kv, int G, int head_dim, int page,
-    int max_pages, void* stream) {
-  using namespace amass;
+    int max_pages, void* stream, int8_t* pool_valid, int install) {
   if (n_req < 0 || n_kv <= 0 || G <= 0 || split < 2 || pps_min <= 0 ||
       max_pages <= 0 || layer < 0 || num_blocks <= 0 || hot_slots <= 0)
     return AMASS_ERR_ARG;
@@ -760,10 +830,56 @@ extern "C" int amass_tier_decode(
   a.svb = svb; a.svt = svt; a.svh = svh;
   a.p2s = page2slot; a.vbo = vbo; a.eslot = entry_slots;
   a.t_layer = layer; a.t_NB = num_blocks; a.t_S = hot_slots;
+  a.pvalid = pool_valid; a.install = install;
+  if (install && (!pool_valid || !entry_slots)) return AMASS_ERR_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (head_dim == 128) return launch_decode<128, AMASS_DEC_NST, true>(a, st);
   if (head_dim == 64) return launch_decode<64, 3, true>(a, st);
   return AMASS_ERR_UNSUPPORTED;
+}
+}  // namespace
+}  // namespace amass
+
+extern "C" int amass_tier_decode(
+    const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k,
+    int64_t k_sb, int64_t k_st, int64_t k_sh, const void* hot_v,
+    const void* hot_k, const void* stg_v, const void* stg_k, int64_t svb,
+    int64_t svt, int64_t svh, const void* pool_v, const void* pool_k,
+    const int32_t* page2slot, const int32_t* vbo, const int32_t* entry_slots,
+    int layer, int num_blocks, int hot_slots, const int32_t* block_table,
+    int64_t bt_stride, const int32_t* page_table, const int32_t* page_cnt,
+    const int32_t* seq_lens, float* m_part, float* l_part, float* acc_part,
+    int split, int pps_min, void* out, int64_t o_stride_t, int64_t o_stride_h,
+    float scale, int n_req, int n_kv, int G, int head_dim, int page,
+    int max_pages, void* stream) {
+  return amass::tier_decode_impl(
+      q, q_stride_t, q_stride_h, k, k_sb, k_st, k_sh, hot_v, hot_k, stg_v,
+      stg_k, svb, svt, svh, pool_v, pool_k, page2slot, vbo, entry_slots, layer,
+      num_blocks, hot_slots, block_table, bt_stride, page_table, page_cnt,
+      seq_lens, m_part, l_part, acc_part, split, pps_min, out, o_stride_t,
+      o_stride_h, scale, n_req, n_kv, G, head_dim, page, max_pages, stream,
+      nullptr, 0);
+}
+
+extern "C" int amass_tier_decode_install(
+    const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k,
+    int64_t k_sb, int64_t k_st, int64_t k_sh, void* hot_v, void* hot_k,
+    const void* stg_v, const void* stg_k, int64_t svb, int64_t svt,
+    int64_t svh, void* pool_v, void* pool_k, int8_t* pool_valid,
+    const int32_t* page2slot, const int32_t* vbo, const int32_t* entry_slots,
+    int layer, int num_blocks, int hot_slots, const int32_t* block_table,
+    int64_t bt_stride, const int32_t* page_table, const int32_t* page_cnt,
+    const int32_t* seq_lens, float* m_part, float* l_part, float* acc_part,
+    int split, int pps_min, void* out, int64_t o_stride_t, int64_t o_stride_h,
+    float scale, int n_req, int n_kv, int G, int head_dim, int page,
+    int max_pages, void* stream) {
+  return amass::tier_decode_impl(
+      q, q_stride_t, q_stride_h, k, k_sb, k_st, k_sh, hot_v, hot_k, stg_v,
+      stg_k, svb, svt, svh, pool_v, pool_k, page2slot, vbo, entry_slots, layer,
+      num_blocks, hot_slots, block_table, bt_stride, page_table, page_cnt,
+      seq_lens, m_part, l_part, acc_part, split, pps_min, out, o_stride_t,
+      o_stride_h, scale, n_req, n_kv, G, head_dim, page, max_pages, stream,
+      pool_valid, 1);
 }
 
 // ---------------------------------------------------------------------------

@@ -124,6 +124,46 @@ class MemSession:
         T.mem_dynamic_decode(q, self.k_cache[l], self._bt, self._sl, self.st,
                              out, self.tier, l, scale=scale)
 
+    # -- the reference's attention-backend seam ------------------------------
+    def bind_kv_caches(self, kv_caches) -> None:
+        """Layer index by cache address, as the reference's
+        ``_runtime.tier_layer_index`` (backend/_runtime.py:124-135): the
+        engine's per-layer K-only cache tensors in layer order."""
+        self._lidx = {int(t.data_ptr()): i for i, t in enumerate(kv_caches)}
+
+    def begin_step_from_metadata(self, m) -> None:
+        """The builder half of the seam: once per step with the step's
+        attention metadata (reference backend/builder.py, which runs the
+        tier's begin_step and derive there).  ``m`` carries block_table,
+        seq_lens, query_start_loc, max_query_len and num_actual_tokens."""
+        self.begin_step(m.block_table, m.seq_lens, m.query_start_loc,
+                        int(m.max_query_len), int(m.num_actual_tokens))
+
+    def forward_mem(self, layer, query, key, value, kv_cache, m, output,
+                    output_scale=None, output_block_scale=None, *,
+                    scale: float):
+        """The attention half: the reference's ``_forward_mem(self, layer,
+        query, key, value, kv_cache, m, output, output_scale,
+        output_block_scale)`` (backend/attn.py:85-120) with its follow-up
+        filled in.  Writes this step's K and V (staging / K-only cache) and,
+        on a pure-decode step, runs the tiered decode into ``output``
+        (T, H*d) or (T, H, d) and returns it.  Returns None on other steps:
+        the engine's own prefill attention runs there, as in the reference
+        while its flag is off."""
+        lidx = self._lidx.get(int(kv_cache.data_ptr())) if \
+            getattr(self, "_lidx", None) else None
+        if lidx is None:
+            lidx = int(getattr(layer, "layer_idx"))
+        n_tok = int(m.num_actual_tokens)
+        self.write_kv(lidx, key[:n_tok], value[:n_tok],
+                      m.slot_mapping[:n_tok], n_tok)
+        if int(m.max_query_len) != 1:
+            return None
+        out3 = output if output.dim() == 3 else output.view(
+            output.shape[0], self.n_kv * self.G, self.d)
+        self.decode(lidx, query, out3, scale=scale)
+        return output
+
     def refresh_summaries(self, rows=None) -> int:
         """Rebuild the last complete page of every (selected) request in all
         layers (after the step's K writes; reference builder.py:366-479's

@@ -643,13 +643,18 @@ class Tier:
 
 def mem_decode_ptrsel(q, kv_cache, block_table, seq_lens, st, out, tier,
                       lidx: int, *, scale=None, pps_min=None,
-                      entry_slots=None) -> None:
+                      entry_slots=None, install: bool = False) -> None:
     """ptr-select tiered split-K decode + merge into ``out[:n_req]`` (bf16):
     per page V (and K under mem-kv) from hot | staging | pinned
     (reference tier/decode_mem.py:169-222).  Bitwise equal to the resident
     decode on the same bytes.  ``entry_slots``: the residency's
     ``miss_pages`` right after its plan for this same selection (hits then
-    skip the page2slot lookup), else None."""
+    skip the page2slot lookup), else None.  ``install`` (needs
+    ``entry_slots``): the plan's fetch is done here instead of by
+    ``gather_fetch`` -- each page the plan installed is read from staging or
+    the pinned pool and written into its hot slot (written through to the
+    pinned pool when it was staged and unflushed), so each miss crosses the
+    host link once and the separate fetch launch goes away."""
     if scale is None:
         # the state's softmax scale, else 1/sqrt(head_dim)
         scale = getattr(st, "scale", None) or q.shape[-1] ** -0.5
@@ -672,11 +677,15 @@ def mem_decode_ptrsel(q, kv_cache, block_table, seq_lens, st, out, tier,
         pool_k = 0
     if q.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
         raise ValueError("q and out must be bf16")
-    _lib.call("amass_tier_decode", ptr(q), q.stride(0), q.stride(1),
+    if install and entry_slots is None:
+        raise ValueError("install needs the plan's entry_slots")
+    fn = "amass_tier_decode_install" if install else "amass_tier_decode"
+    pv = (ptr(r5.pool_valid[l]),) if install else ()
+    _lib.call(fn, ptr(q), q.stride(0), q.stride(1),
               ptr(kres), skb, skt, skh,
               ptr(r5.hot[l]), ptr(r5.hot_k[l]) if tier.offload_k else 0,
               ptr(vp), ptr(stg_k), vp.stride(0), vp.stride(1), vp.stride(2),
-              tier.pool.dev_view.data_ptr(), pool_k,
+              tier.pool.dev_view.data_ptr(), pool_k, *pv,
               ptr(r5.page2slot[l]), ptr(stg.vbo), ptr(entry_slots), l, r5.NB,
               r5.S,
               ptr(block_table), block_table.stride(0), ptr(st.page_table),
@@ -703,10 +712,17 @@ def mem_dynamic_decode(q, kv_cache, block_table, seq_lens, st, out, tier,
     n_req = seq_lens.shape[0]
     es = None
     if fetch == "kernel":
+        r5 = tier.residency
+        if st.page_table.shape[-1] == r5.MP:
+            # plan, then the decode fetches the installed misses itself
+            r5.gather_plan(lidx, st.page_table, st.page_cnt, block_table,
+                           seq_lens, n_req)
+            mem_decode_ptrsel(q, kv_cache, block_table, seq_lens, st, out,
+                              tier, lidx, scale=scale,
+                              entry_slots=r5.miss_pages, install=True)
+            return
         tier.step(lidx, st.page_table, st.page_cnt, block_table, seq_lens,
                   n_req)
-        if st.page_table.shape[-1] == tier.residency.MP:
-            es = tier.residency.miss_pages
     elif fetch == "dma":
         tier.step_dma(lidx, st.page_table, st.page_cnt, block_table, seq_lens,
                       n_req, wait=True)

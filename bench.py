@@ -962,8 +962,8 @@ def run_c5(args):
 
     def stage(k):
         if k == 0:
-            S.derive_page_params(st, sl, n5)
-            S._score_launch(st, 0, qbuf, bt, n5, scale, COMBINE == "nrm")
+            S._score_launch(st, 0, qbuf, bt, n5, scale, COMBINE == "nrm",
+                            seq_lens=sl)
         elif k == 1:
             S.select_pages(st, n5, from_score_h=COMBINE == "nrm")
         elif k == 2:
@@ -973,73 +973,108 @@ def run_c5(args):
         elif k == 4:
             T.mem_decode_ptrsel(qbuf, kv_k_only, bt, sl, st, out, tier, 0,
                                 scale=scale, entry_slots=r5.miss_pages)
-        else:
+        elif k == 5:
             A.sparse_paged_decode_batched_cuda(qbuf, kv, bt, sl, st, out_res,
                                                scale=scale)
+        else:
+            # the product path (mem_dynamic_decode, fetch="kernel"): the
+            # decode fetches the plan's installs itself
+            T.mem_decode_ptrsel(qbuf, kv_k_only, bt, sl, st, out, tier, 0,
+                                scale=scale, entry_slots=r5.miss_pages,
+                                install=True)
 
-    NS = 6
+    # path A (product): score, select, plan, decode-with-install, and the
+    # resident decode of the same pages for the equality check; path B:
+    # score, select, plan, separate fetch, decode
+    paths = {"install": (0, 1, 2, 6), "separate_fetch": (0, 1, 2, 3, 4)}
     set_q(0)
-    for k in range(NS):                  # eager first use (attributes)
+    for k in range(7):                   # eager first use (attributes)
         stage(k)
     torch.cuda.synchronize()
-    graphs = []
-    for k in range(NS):
+    graphs = {}
+    for k in range(7):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             stage(k)
-        graphs.append(g)
-    # the whole tier step (score .. tiered decode) as one graph: the
-    # reported value; the per-stage graphs above give its breakdown
-    g_step = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_step):
-        for k in range(5):
-            stage(k)
+        graphs[k] = g
+    g_path = {}
+    for name, ks in paths.items():
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for k in ks:
+                stage(k)
+        g_path[name] = g
     torch.cuda.synchronize()
     page_bytes = PAGE * D * 2
     warm = max(args.warmup, 10)
-    for i in range(1, warm + 1):
-        set_q(i)
-        for g in graphs[:5]:
-            g.replay()
-    torch.cuda.synchronize()
     steps = max(args.steps, 20) if args.steps else 20
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(NS + 1)]
-          for _ in range(steps)]
+    qi = [0]
+
+    def next_q():
+        qi[0] += 1
+        set_q(qi[0])
+
+    res = {}
     misses, selected, equal = [], [], True
     with ClockSampler(dev) as clk:
-        for i in range(steps):
-            set_q(warm + 1 + i)
-            ev[i][0].record()
-            for k in range(NS):
-                graphs[k].replay()
-                ev[i][k + 1].record()
+        for name, ks in paths.items():
+            stage_ks = ks + (5,)
+            for _ in range(warm):
+                next_q()
+                for k in ks:
+                    graphs[k].replay()
             torch.cuda.synchronize()
-            misses.append(int(r5.fetch_cnt.sum()))
-            cnt = st.page_cnt.cpu().numpy()
-            selected.append(int(cnt.sum()))
-            equal = equal and bool(torch.equal(out, out_res))
-    t = np.array([[e[k].elapsed_time(e[k + 1]) for k in range(NS)]
-                  for e in ev]) * 1e3                          # us
-    t_score, t_select, t_plan, t_fetch, t_dec, t_res = t.mean(0)
-    # whole-step graph, same q drift, continuing the residency state
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(
-        enable_timing=True)
-    full = []
-    for i in range(steps):
-        set_q(warm + steps + 1 + i)
-        e0.record()
-        g_step.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        full.append(e0.elapsed_time(e1) * 1e3)
-    tier_step = float(np.mean(full))
-    miss_b = np.array(misses) * page_bytes
-    link = float(miss_b.sum() / (t[:, 3].sum() * 1e-6) / 1e9) \
-        if miss_b.sum() else 0.0
+            ev = [[torch.cuda.Event(enable_timing=True)
+                   for _ in range(len(stage_ks) + 1)] for _ in range(steps)]
+            for i in range(steps):
+                next_q()
+                ev[i][0].record()
+                for j, k in enumerate(stage_ks):
+                    graphs[k].replay()
+                    ev[i][j + 1].record()
+                torch.cuda.synchronize()
+                if name == "install":
+                    misses.append(int(r5.fetch_cnt.sum()))
+                    selected.append(int(st.page_cnt.sum()))
+                equal = equal and bool(torch.equal(out, out_res))
+            t = np.array([[e[j].elapsed_time(e[j + 1])
+                           for j in range(len(stage_ks))] for e in ev]) * 1e3
+            # whole-step graph, continuing the residency state
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(
+                enable_timing=True)
+            full = []
+            for i in range(steps):
+                next_q()
+                e0.record()
+                g_path[name].replay()
+                e1.record()
+                torch.cuda.synchronize()
+                full.append(e0.elapsed_time(e1) * 1e3)
+            res[name] = (float(np.median(full)), dict(zip(stage_ks,
+                                                          t.mean(0))))
+    tier_step = res["install"][0]
     if world > 1:
         x = torch.tensor([tier_step], device=dev)
         dist.all_reduce(x, op=dist.ReduceOp.MAX)
         tier_step = float(x.item())
+    names = {0: "derive+score", 1: "select", 2: "residency_plan",
+             3: "miss_fetch", 4: "tiered_decode+merge",
+             5: "resident_decode+merge",
+             6: "tiered_decode+merge_with_fetch"}
+    miss_b = float(np.mean(misses)) * page_bytes
+    t_sep_fetch = res["separate_fetch"][1][3]
+    link_fetch = miss_b / (t_sep_fetch * 1e-6) / 1e9 if miss_b else 0.0
+    peaks = _host_link_peaks(tier, r5, dev)
+    # DRAM-tier roofline of the install decode: its HBM bytes (K tiles and
+    # hot V tiles of the selected pages, q/out) at the HBM peak plus the miss
+    # bytes at the measured host-link peak
+    hbm, kind = _peaks()
+    sel_pages = float(np.mean(selected))
+    miss_pages = float(np.mean(misses))
+    hbm_bytes = sel_pages * page_bytes * 2 - miss_pages * page_bytes + \
+        n5 * C5_KV * C5_G * D * 4
+    t_roof = hbm_bytes / (hbm * 1e9) + miss_b / (peaks["uva_read_gbs"] * 1e9)
+    t_inst = res["install"][1][6] * 1e-6
     wp = _c5_write_path(T, tier, kv, bt, sl, n5, NB, MP)
     wp["begin_step_us_one_cta_walk"] = _c5_write_path(
         T, tier, kv, bt, sl, n5, NB, MP, cand_cap=0)["begin_step_us_per_step"]
@@ -1065,18 +1100,26 @@ def run_c5(args):
                        "NB": NB},
             "stage_us": {"note": "per-stage graphs (sum differs from the "
                                  "whole-step value by graph boundaries)",
-                         "derive+score": round(float(t_score), 2),
-                         "select": round(float(t_select), 2),
-                         "residency_plan": round(float(t_plan), 2),
-                         "miss_fetch": round(float(t_fetch), 2),
-                         "tiered_decode+merge": round(float(t_dec), 2),
-                         "resident_decode+merge": round(float(t_res), 2)},
+                         **{names[k]: round(float(v), 2)
+                            for k, v in res["install"][1].items()}},
+            "separate_fetch_path": {
+                "value": round(res["separate_fetch"][0], 2),
+                "stage_us": {names[k]: round(float(v), 2)
+                             for k, v in res["separate_fetch"][1].items()}},
+            "dram_tier_roofline": {
+                "kernel": "tiered_decode+merge_with_fetch",
+                "hbm_bytes": int(hbm_bytes), "miss_bytes": int(miss_b),
+                "roofline_us": round(t_roof * 1e6, 2),
+                "achieved_us": round(t_inst * 1e6, 2),
+                "frac": round(t_roof / t_inst, 4),
+                "formula": "hbm_bytes / hbm_peak + miss_bytes / uva_read_gbs"},
+            "host_link": {**peaks,
+                          "separate_fetch_gbs": round(link_fetch, 2)},
             "write_path": wp,
             "hit_rate": round(1.0 - float(np.sum(misses)) /
                               max(1, float(np.sum(selected))), 4),
             "miss_pages_per_step": round(float(np.mean(misses)), 1),
             "selected_pages_per_step": round(float(np.mean(selected)), 1),
-            "host_link_gbs": round(link, 2),
             "vram_saved_frac": round(saved, 4),
             "tiered_equals_resident": equal,
             "hbm_peak_gbs": hbm, "peak_kind": kind,
@@ -1085,6 +1128,53 @@ def run_c5(args):
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def _host_link_peaks(tier, r5, dev):
+    """Host-link peaks on this box: a 256 MiB pinned -> device copy (copy
+    engine) and the tier's UVA fetch kernel reading every hot slot's page
+    from the pinned pool at once (the kernel that serves misses).  Leaves the
+    residency maps untouched; the hot buffer is overwritten, so this runs
+    after the timed steps."""
+    import torch
+    src = torch.empty(256 << 20, dtype=torch.uint8, pin_memory=True)
+    dst = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(2):
+        dst.copy_(src, non_blocking=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(
+        enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        dst.copy_(src, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    h2d = 5 * src.numel() / (e0.elapsed_time(e1) * 1e-3) / 1e9
+    del src, dst
+    # synthetic full fetch: slot s of head k <- block s (every entry flushed)
+    fl, fc = r5.fetch_list.clone(), r5.fetch_cnt.clone()
+    S = r5.S
+    ar = torch.arange(S, dtype=torch.int32, device=dev)
+    r5.fetch_list[:, :S, 0] = ar % r5.NB
+    r5.fetch_list[:, :S, 1] = ar
+    r5.fetch_cnt.fill_(S)
+    valid = r5.pool_valid.clone()
+    r5.pool_valid.fill_(1)
+    r5.gather_fetch(0, tier.staging, tier.pool.dev_view)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(3):
+        r5.gather_fetch(0, tier.staging, tier.pool.dev_view)
+    e1.record()
+    torch.cuda.synchronize()
+    nbytes = 3 * r5.n_kv * S * r5.page * r5.d * 2
+    uva = nbytes / (e0.elapsed_time(e1) * 1e-3) / 1e9
+    r5.fetch_list.copy_(fl)
+    r5.fetch_cnt.copy_(fc)
+    r5.pool_valid.copy_(valid)
+    return {"h2d_copy_gbs": round(h2d, 2), "uva_read_gbs": round(uva, 2),
+            "how": "256 MiB pinned->device copy; tier fetch kernel reading "
+                   "every hot slot's page (n_kv x S pages) over UVA"}
 
 
 def _c5_write_path(T, tier, kv, bt, sl, n5, NB, MP, n_steps=64,

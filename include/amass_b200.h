@@ -477,6 +477,32 @@ int amass_tier_decode(
     float scale, int n_req, int n_kv, int G, int head_dim, int page,
     int max_pages, void* stream);
 
+/* tier_decode_install -- amass_tier_decode that also does the plan's miss
+ * fetch (replaces Residency.gather_fetch, tier/residency.py:196-248,
+ * 409-436, which the reference runs between the plan and the decode,
+ * tier/decode_mem.py:225-274).  entry_slots (the plan's classified entries)
+ * is required: a page whose entry is a miss that the plan gave a hot slot
+ * (page2slot >= 0, complete page) is read from staging (vbo >= 0) or the
+ * pinned pool -- not from the slot, which is not filled yet -- and its V
+ * tile (and K tile under mem-kv) is then written into that slot; when it
+ * came from staging and pool_valid (n_kv, NB) is 0 it is also written
+ * through to the pinned pool and pool_valid set to 1, as the fetch does.
+ * Each miss thus crosses the host link once.  Output, hot slots, pinned
+ * pool and pool_valid end equal to plan + amass_tier_fetch +
+ * amass_tier_decode. */
+int amass_tier_decode_install(
+    const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k,
+    int64_t k_sb, int64_t k_st, int64_t k_sh, void* hot_v, void* hot_k,
+    const void* stg_v, const void* stg_k, int64_t svb, int64_t svt,
+    int64_t svh, void* pool_v, void* pool_k, int8_t* pool_valid,
+    const int32_t* page2slot, const int32_t* vbo, const int32_t* entry_slots,
+    int layer, int num_blocks, int hot_slots, const int32_t* block_table,
+    int64_t bt_stride, const int32_t* page_table, const int32_t* page_cnt,
+    const int32_t* seq_lens, float* m_part, float* l_part, float* acc_part,
+    int split, int pps_min, void* out, int64_t o_stride_t, int64_t o_stride_h,
+    float scale, int n_req, int n_kv, int G, int head_dim, int page,
+    int max_pages, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -102,3 +102,66 @@ def test_mem_session_bitwise_equals_resident(dev, offload_k, scorer):
     assert int(sess.tier.residency.clock[0]) > decoded
     vb = sess.vram_bytes()
     assert vb["k_cache"] < vb["resident_kv_equivalent"]
+
+
+def test_forward_mem_seam(dev):
+    """The reference's attention seam driven as vLLM drives it, without
+    model weights: per step the builder half (begin_step_from_metadata)
+    runs once, then every layer calls forward_mem(layer, query, key, value,
+    kv_cache, attn_metadata, output) with the reference's argument list
+    (backend/attn.py:85-120); the layer is found from its cache address.
+    Pure-decode outputs are bitwise equal to the resident decode of a full
+    K+V cache; prefill steps return None (the engine's attention runs)."""
+    from types import SimpleNamespace
+    rng = np.random.default_rng(17)
+    L, R, MP, page, n_kv, G, d = 2, 3, 16, 16, 2, 4, 128
+    NB = R * MP + 5
+    sess = MemSession(num_layers=L, num_blocks=NB, n_kv=n_kv, G=G,
+                      head_dim=d, max_reqs=R, max_pages=MP,
+                      max_tokens=R * 64, page=page, hot_slots=16, budget=0.3,
+                      device=dev)
+    k_caches = [sess.k_cache[l] for l in range(L)]
+    sess.bind_kv_caches(k_caches)
+    bt_np = rng.permutation(NB)[:R * MP].astype(np.int32).reshape(R, MP)
+    bt = torch.from_numpy(bt_np).to(dev)
+    kv_full = torch.zeros((L, NB, 2, page, n_kv, d), dtype=torch.bfloat16,
+                          device=dev)
+    scale = d ** -0.5
+    decoded = 0
+    for s, (sl, ql) in enumerate(_steps(rng, R, MP * page, 2, 12, 64)):
+        qsl = np.concatenate([[0], np.cumsum(ql)]).astype(np.int32)
+        n_tok = int(qsl[-1])
+        pos = np.concatenate([np.arange(sl[r] - ql[r], sl[r])
+                              for r in range(R)])
+        req = np.repeat(np.arange(R), ql)
+        slots = torch.from_numpy(bt_np[req, pos // page].astype(np.int64) *
+                                 page + pos % page).to(dev)
+        m = SimpleNamespace(block_table=bt, seq_lens=torch.from_numpy(sl).to(dev),
+                            query_start_loc=torch.from_numpy(qsl).to(dev),
+                            max_query_len=int(ql.max()),
+                            num_actual_tokens=n_tok, slot_mapping=slots)
+        sess.begin_step_from_metadata(m)
+        for l in range(L):
+            k = torch.randn((n_tok, n_kv, d), device=dev).to(torch.bfloat16)
+            v = torch.randn((n_tok, n_kv, d), device=dev).to(torch.bfloat16)
+            q = torch.randn((n_tok, n_kv * G, d), device=dev).to(torch.bfloat16)
+            out = torch.zeros((n_tok, n_kv * G * d), dtype=torch.bfloat16,
+                              device=dev)
+            got = sess.forward_mem(SimpleNamespace(), q, k, v, k_caches[l], m,
+                                   out, None, None, scale=scale)
+            blk, off = slots // page, slots % page
+            kv_full[l, blk, 0, off] = k
+            kv_full[l, blk, 1, off] = v
+            if m.max_query_len != 1:
+                assert got is None
+                continue
+            ref = torch.zeros((R, n_kv * G, d), dtype=torch.bfloat16,
+                              device=dev)
+            A.sparse_paged_decode_batched_cuda(q, kv_full[l], bt, m.seq_lens,
+                                               sess.st, ref, scale=scale)
+            torch.cuda.synchronize(dev)
+            assert got is out
+            assert torch.equal(out.view(R, n_kv * G, d), ref), (s, l)
+            decoded += 1
+        sess.refresh_summaries()
+    assert decoded >= 20

@@ -413,3 +413,68 @@ def test_tier_plan_empty_batch(dev):
     assert int(r5.fetch_cnt.sum()) == 0
     assert torch.equal(r5.page2slot, p2s)
     assert torch.equal(r5.lru_clock, lru)
+
+
+@pytest.mark.parametrize("mem_kv", [False, True])
+def test_install_decode_equals_plan_fetch_decode(mem_kv, dev):
+    """The decode that fetches the plan's installs itself ends every step
+    with the same output, hot buffer, pinned pool and validity as plan +
+    separate fetch kernel + decode (staged unflushed pages included)."""
+    c = _random_tier_case(9, n_req=5, n_kv=4, G=4, d=128, S=48, steps=5,
+                          mem_kv=mem_kv)
+    NB, MP, L, layer = c["NB"], c["MP"], c["L"], c["layer"]
+    Vb = torch.from_numpy(c["V"]).to(torch.bfloat16)
+    Kb = torch.from_numpy(c["K"]).to(torch.bfloat16)
+    rng = np.random.default_rng(9)
+    staged = rng.choice(NB, 10, replace=False)
+    tiers = []
+    for _ in range(2):
+        t = T.Tier(num_layers=L, num_blocks=NB, n_kv=4, page=16, d=128,
+                   hot_slots=48, max_reqs=5, max_pages=MP, n_vslots=16,
+                   offload_k=mem_kv, device=dev)
+        t.pool.host[layer].copy_(Vb.permute(0, 2, 1, 3))
+        if mem_kv:
+            t.pool_k.host[layer].copy_(Kb.permute(0, 2, 1, 3))
+        t.residency.pool_valid.fill_(1)
+        vbo = np.full(NB, -1, np.int32)
+        for i, blk in enumerate(staged):
+            vbo[blk] = i
+            t.staging.v_pool[layer, i].copy_(Vb[blk])
+            t.pool.host[layer, blk].fill_(5.0)
+            if mem_kv:
+                t.staging.k_pool[layer, i].copy_(Kb[blk])
+                t.pool_k.host[layer, blk].fill_(-2.0)
+            t.residency.pool_valid[layer, :, blk] = 0
+        t.staging.vbo.copy_(torch.from_numpy(vbo))
+        tiers.append(t)
+    kv_true = torch.stack([Kb, Vb], 1).contiguous().to(dev)
+    kv_dev = kv_true if not mem_kv else torch.zeros_like(kv_true)
+    bt = torch.from_numpy(c["bt"]).to(dev)
+    sl = torch.from_numpy(c["ctx"]).to(dev)
+    st = _state(dev, n_req=5, n_kv=4, G=4, d=128, NB=NB, MP=MP)
+    for s, (tab, cnt) in enumerate(c["sels"]):
+        st.page_table.copy_(torch.from_numpy(tab))
+        st.page_cnt.copy_(torch.from_numpy(cnt))
+        q = torch.randn(5, 16, 128, device=dev).to(torch.bfloat16)
+        outs = [torch.zeros_like(q) for _ in range(2)]
+        # tier 0: the product path (plan, decode fetching the installs)
+        T.mem_dynamic_decode(q, kv_dev, bt, sl, st, outs[0], tiers[0], layer,
+                             scale=128 ** -0.5)
+        # tier 1: plan + separate fetch kernel + decode
+        r1 = tiers[1].residency
+        tiers[1].step(layer, st.page_table, st.page_cnt, bt, sl, 5)
+        T.mem_decode_ptrsel(q, kv_dev, bt, sl, st, outs[1], tiers[1], layer,
+                            scale=128 ** -0.5, entry_slots=r1.miss_pages)
+        torch.cuda.synchronize()
+        a, b = tiers[0].residency, tiers[1].residency
+        assert torch.equal(outs[0], outs[1]), s
+        assert torch.equal(a.page2slot, b.page2slot), s
+        assert torch.equal(a.pool_valid, b.pool_valid), s
+        res_mask = a.slot2page[layer] >= 0
+        assert torch.equal(a.hot[layer][res_mask], b.hot[layer][res_mask]), s
+        if mem_kv:
+            assert torch.equal(a.hot_k[layer][res_mask],
+                               b.hot_k[layer][res_mask]), s
+        assert torch.equal(tiers[0].pool.host, tiers[1].pool.host), s
+        if mem_kv:
+            assert torch.equal(tiers[0].pool_k.host, tiers[1].pool_k.host), s
