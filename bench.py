@@ -522,6 +522,8 @@ def run_gpu(args):
     tot_bytes = sum(p["alg_bytes"] for p in per_rank)
     job_gbs = tot_bytes / (med * 1e-3) / 1e9
 
+    launches = batch_launches(batch, args)
+    names = dict(batch.stage_names)
     parity = cpu = None
     ctx32 = None
     if world == 1:
@@ -588,11 +590,11 @@ def run_gpu(args):
                                       "max-over-ranks step time / (N x peak)"},
             "roofline": roof,
             "kernel_us": {k: round(v[0] * 1e3, 2) for k, v in kernels.items()},
-            "marginal_us": {batch.stage_names[k]: round(v * 1e3, 2)
+            "marginal_us": {names[k]: round(v * 1e3, 2)
                             for k, v in marg.items()},
             "per_rank": per_rank,
             "e2e": e2e,
-            "gpu_launches": batch_launches(batch, args),
+            "gpu_launches": launches,
             "clocks": clk,
         }
         if world > 1:

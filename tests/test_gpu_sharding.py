@@ -1,6 +1,8 @@
 """Multi-GPU layouts on B200s: the kv-head-sharded decode (merge kernel that
 stores into every rank's output over NVLink + peer barrier, and the NCCL
-all-gather variant) is bitwise equal to the single-GPU decode of all heads.
+all-gather variant) places every rank's rows bit for bit as that rank's own
+decode of its heads, and matches the single-GPU decode of all heads within
+bf16 tolerance.
 World 1 runs on one GPU; worlds 2 and 4 run when that many GPUs are
 visible."""
 import os
@@ -85,8 +87,29 @@ def _worker(rank, world, port, mode, q):
             outs.append(o.clone())
         if mode == "p2p":
             g.check()
-        ok = all(bool(torch.equal(o, ref)) for o in outs)
-        q.put((rank, ok, float((outs[-1].float() - ref.float()).abs().max())))
+        # every rank's rows equal that rank's own decode of its heads, bit
+        # for bit (the same kernels on the same per-rank batch), computed
+        # here for all ranks' head ranges
+        exp = torch.zeros_like(qf)
+        for rr in range(world):
+            lo2, hi2 = SH.kv_head_range(n_kv, world, rr)
+            st2 = _state(dev, b, n_kv, G, lo2, hi2, n_req, MP)
+            q2 = qf[:, lo2 * G:hi2 * G].contiguous()
+            _select(st2, q2, bt, sl, n_req, scale)
+            o2 = torch.zeros_like(q2)
+            A.sparse_paged_decode_batched_cuda(
+                q2, kv[:, :, :, lo2:hi2].contiguous(), bt, sl, st2, o2,
+                scale=scale)
+            exp[:, lo2 * G:hi2 * G] = o2
+        torch.cuda.synchronize()
+        ok = all(bool(torch.equal(o, exp)) for o in outs)
+        # and the all-heads decode within bf16 tolerance (the split-K cut
+        # of a unit depends on the batch's total pages, so fp32 sums
+        # associate differently)
+        err = float((outs[-1].float() - ref.float()).abs().max())
+        ok = ok and torch.allclose(outs[-1].float(), ref.float(), atol=2e-2,
+                                   rtol=1e-2)
+        q.put((rank, ok, err))
     except Exception as e:  # report instead of hanging the parent
         q.put((rank, False, repr(e)))
     finally:
