@@ -65,13 +65,15 @@ struct SelArgs {
 // 16-byte loads per thread, all issued before any use).
 template <int GM = 8, int KQ = 1>
 AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int p_lo, int p_hi,
-                        float* sc, bool reset = true) {
+                        float* sc, bool reset = true,
+                        const float* hm_in = nullptr) {
   const int nsh = p_hi;
   const float* sh = a.score_h + (int64_t)unit * a.G * a.SHS;
   float* hm_g = a.hmax + (int64_t)unit * a.G;
   float hm[GM];
 #pragma unroll
-  for (int g = 0; g < GM; ++g) hm[g] = g < a.G ? __ldcg(hm_g + g) : 0.f;
+  for (int g = 0; g < GM; ++g)
+    hm[g] = hm_in ? hm_in[g] : (g < a.G ? __ldcg(hm_g + g) : 0.f);
   float* so = a.score + (int64_t)unit * a.MP;
   // batches of pages per thread: every load of a batch issues before any
   // use, so a long unit costs a few memory round trips, not one per page
@@ -411,8 +413,15 @@ template <bool FOLD, bool LIN, bool COVERAGE, int GM = 8, bool CLU = false>
 AMASS_DEV void select_unit(const SelArgs& a, const int unit, const int nb,
                            const int rank, float* sc, SelShared& sh) {
   const int r = unit / a.n_kv;
-  const int npg = max(a.npg[r], 0);
+  // every per-unit scalar the selection needs, loaded together
+  const int npg_raw = a.npg[r];
   const int nsh = a.nsh[r];
+  const int bfix = COVERAGE ? 0 : a.b_fix[r];
+  float hm_pre[GM];
+#pragma unroll
+  for (int g = 0; g < GM; ++g)
+    hm_pre[g] = (FOLD && g < a.G) ? __ldcg(a.hmax + (int64_t)unit * a.G + g) : 0.f;
+  const int npg = max(npg_raw, 0);
   const int sink = a.sink;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nsc = max(nsh, 0);
@@ -421,7 +430,7 @@ AMASS_DEV void select_unit(const SelArgs& a, const int unit, const int nb,
   if (threadIdx.x == 0) { sh.kmin = 0xffffffffu; sh.kmax = 0u; }
   if (nsh > 0) {
     if (FOLD) {
-      nrm_fold<GM, (GM <= 4 ? 2 : 1)>(a, unit, s0, s1, sc, !CLU);
+      nrm_fold<GM, (GM <= 4 ? 2 : 1)>(a, unit, s0, s1, sc, !CLU, hm_pre);
     } else {
       const float* si = a.score + (int64_t)unit * a.MP;
       constexpr int kB = 8;
@@ -514,7 +523,7 @@ AMASS_DEV void select_unit(const SelArgs& a, const int unit, const int nb,
       if constexpr (CLU) above = cl_allreduce(&sh.x_above, above, iadd);
       b_used = above + 1;
     } else {
-      const int b = a.b_fix[r];
+      const int b = bfix;
       b_used = b;
       tau = find_tau<false, true, CLU>(sc, lo_sel - s0, s1 - s0, b, 0.f, 0.f,
                                        kmin, kmax, sh);
