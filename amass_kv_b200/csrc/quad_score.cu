@@ -326,9 +326,22 @@ AMASS_DEV void load_qfrag(QFrag<D>& f, const QuadArgs& a, int r, int h,
 // The (1+R) x 2-limb integer dot products of one item: acc[comp][limb][4]
 // (comp 0 = mu, 1+k = V column k), C-fragment layout (rows pages m, m+8;
 // cols query heads 2c, 2c+1).
+// Shared-memory image of one tile's V rows for items whose V slice does not
+// fit the register pipeline (rank 8): row = 4 lane slices of V_BYTES + 16 B,
+// so the 8 lanes of a 16-byte load phase hit 8 different bank quads.
+template <int D, int R, int VB>
+struct VStage {
+  static constexpr int RB = (VB == 8) ? R : R / 2;
+  static constexpr int V_BYTES = (D / 4) * RB;
+  static constexpr int SLICE = V_BYTES + 16;
+  static constexpr int ROW = 4 * SLICE;
+  static constexpr int BYTES = 16 * ROW;
+};
+
 template <int D, int R, int VB>
 AMASS_DEV void item_dots(const Item<D, R, VB>& it, const QFrag<D>& qf,
-                         const QuadArgs& a, int lane, int (*acc)[2][4]) {
+                         const QuadArgs& a, int lane, int (*acc)[2][4],
+                         const uint8_t* vsm = nullptr) {
   using I = Item<D, R, VB>;
   constexpr int KS = D / 32;                 // m16n8k32 steps
   constexpr int RB = I::RB;
@@ -355,6 +368,18 @@ AMASS_DEV void item_dots(const Item<D, R, VB>& it, const QFrag<D>& qf,
       for (int j = 0; j < 2 * RB; ++j) {
         wva[j] = va[s * 2 * RB + j];
         wvb[j] = vb[s * 2 * RB + j];
+      }
+    } else if (vsm) {
+      using VSt = VStage<D, R, VB>;
+      const int m = lane >> 2;
+      const uint8_t* Va = vsm + m * VSt::ROW + c * VSt::SLICE + s * 8 * RB;
+      const uint8_t* Vb = Va + 8 * VSt::ROW;
+#pragma unroll
+      for (int j = 0; j < 2 * RB; j += 4) {
+        const uint4 x = *reinterpret_cast<const uint4*>(Va + 4 * j);
+        const uint4 y = *reinterpret_cast<const uint4*>(Vb + 4 * j);
+        wva[j] = x.x; wva[j + 1] = x.y; wva[j + 2] = x.z; wva[j + 3] = x.w;
+        wvb[j] = y.x; wvb[j + 1] = y.y; wvb[j + 2] = y.z; wvb[j + 3] = y.w;
       }
     } else {
       const int8_t* Va = a.V + (int64_t)it.rowa * (D * RB) + c * I::V_BYTES + s * 8 * RB;
@@ -558,6 +583,29 @@ AMASS_DEV void stage_coords(const Item<D, R, VB>& it, const QuadArgs& a,
   }
 }
 
+// V-row staging of one tile (rank-8 items): lane (m, c) copies the lane
+// slices of its own pages m and m+8, 16-byte cp.async pieces; pages past
+// n_sel_hi are zero-filled.
+template <int D, int R, int VB>
+AMASS_DEV void stage_v(const Item<D, R, VB>& it, const QuadArgs& a, int lane,
+                       uint32_t vbase) {
+  using VSt = VStage<D, R, VB>;
+  const int m = lane >> 2;
+  constexpr int NPC = VSt::V_BYTES / 16;            // pieces per lane slice
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int row = half ? it.rowb : it.rowa;
+    const bool ok = half ? it.vb : it.va;
+    const int8_t* src = a.V + (int64_t)row * (D * VSt::RB);
+    const uint32_t dst = vbase + (m + 8 * half) * VSt::ROW;
+    for (int k = lane & 3; k < 4 * NPC; k += 4) {
+      const int sl = k / NPC, pc = k - sl * NPC;
+      cp_async16(dst + sl * VSt::SLICE + pc * 16,
+                 src + sl * VSt::V_BYTES + pc * 16, ok);
+    }
+  }
+}
+
 template <int D, int R, int VB, int CB, bool TS = false>
 __global__ void __launch_bounds__(kQuadWarps * 32, TS ? 2 : 1)
 r8_score_kernel(QuadArgs a) {
@@ -611,6 +659,11 @@ r8_score_kernel(QuadArgs a) {
   const int m = lane >> 2, c = lane & 3;
   uint8_t* wbuf = r8dyn + warp * 2 * kBuf;
   const uint32_t wbuf_s = smem_u32(wbuf);
+  // rank-8 V rows go through one warp-private shared stage: the next
+  // tile's rows are copied while this tile's token logits are computed
+  constexpr bool VS = !Item<D, R, VB>::V_PRE;
+  uint8_t* vbuf = r8dyn + kQuadWarps * 2 * kBuf + warp * VStage<D, R, VB>::BYTES;
+  const uint32_t vbuf_s = smem_u32(vbuf);
   QFrag<D> qf;
   int qr = -1;
   // three-deep pipeline as the quad scorer (block ids two tiles ahead,
@@ -628,6 +681,10 @@ r8_score_kernel(QuadArgs a) {
   load_data(cur, a, lane);
   stage_coords<D, R, VB, CB>(cur, a, lane, wbuf_s);
   cp_async_commit();
+  if constexpr (VS) {
+    stage_v<D, R, VB>(cur, a, lane, vbuf_s);
+    cp_async_commit();
+  }
   if (!a.ctok) csp_cur = page_scales(cur);
   if (t + 1 < t_hi) load_idx(nxt, a, prefix, nshs, (t + 1) * a.n_kv + h, lane, &rh);
   constexpr float kL2e = 1.4426950408889634f, kLn2 = 0.6931471805599453f;
@@ -645,9 +702,18 @@ r8_score_kernel(QuadArgs a) {
       qr = cur.r;
     }
     int acc[1 + R][2][4];
-    item_dots(cur, qf, a, lane, acc);
-    cp_async_wait<1>();                    // this tile's coordinates landed
-    __syncwarp();
+    if constexpr (VS) {
+      cp_async_wait<1>();                  // this tile's coordinates and V
+      __syncwarp();
+      item_dots(cur, qf, a, lane, acc, vbuf);
+      __syncwarp();                        // every lane is done with vbuf
+      if (more) stage_v<D, R, VB>(nxt, a, lane, vbuf_s);
+      cp_async_commit();
+    } else {
+      item_dots(cur, qf, a, lane, acc);
+      cp_async_wait<1>();                  // this tile's coordinates landed
+      __syncwarp();
+    }
     const uint8_t* cb = wbuf + ((t - t_lo) & 1) * kBuf;
     const __half* csb = reinterpret_cast<const __half*>(cb + kCBytes);
     const int sl_r = __ldg(a.sl + cur.r);
@@ -906,7 +972,8 @@ template <int D, int CB, int VB, int R, bool TS>
 int launch_r8_k(const QuadArgs& a, cudaStream_t st) {
   auto k = r8_score_kernel<D, R, VB, CB, TS>;
   constexpr int RC = R8Tok<R, CB>::RC;
-  const size_t smem = (size_t)kQuadWarps * 2 * (16 * 16 * RC + 16 * 16 * 2);
+  constexpr size_t vst = Item<D, R, VB>::V_PRE ? 0 : VStage<D, R, VB>::BYTES;
+  const size_t smem = (size_t)kQuadWarps * (2 * (16 * 16 * RC + 16 * 16 * 2) + vst);
   static int ps = 0;
   static unsigned long long attr = 0;
   if (first_on_device(attr))
