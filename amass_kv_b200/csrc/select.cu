@@ -79,12 +79,16 @@ int launch_cluster_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block,
 }
 
 // CTAs per unit for top-b selection: a cluster of up to 8 when the units
-// alone would leave most of the GPU idle (units x CTAs kept within about 4
-// CTAs per SM).  Measured on B200: C5 (128 units of ~4.6K pages) whole tier
-// step 234.9 us -> 216.9 (2 CTAs) -> 211.1 (4).  Coverage selection stays at
-// one CTA per unit: its mass-weighted walk merges more levels across the
-// cluster and was slower (C2, 8 units: 45.4 -> 55.2 us at 2 CTAs).
-inline int select_cluster_size(int units) {
+// are long (max_pages above 4096) and alone would leave most of the GPU idle
+// (units x CTAs kept within about 4 CTAs per SM).  Measured on B200, whole
+// step: C5 (128 units of up to 8191 pages) 176.2 us at 1 CTA per unit,
+// 158.3 at 2, 152.9 at 4; the C3 batch split 8 ways (64 units of up to 4094
+// pages) 36.7 us at 1 CTA per unit against 49.8 with 4-CTA clusters, and
+// 56.0 vs 56.5 split 4 ways.  Coverage selection stays at one CTA per unit:
+// its mass-weighted walk merges more levels across the cluster and was
+// slower (C2, 8 units: 45.4 -> 55.2 us at 2 CTAs).
+inline int select_cluster_size(int units, int max_pages) {
+  if (max_pages <= 4096) return 1;
   int cl = 1;
   while (cl < 8 && (long long)units * cl * 2 <= (long long)num_sms() * 4) cl *= 2;
   return cl;
@@ -93,7 +97,7 @@ inline int select_cluster_size(int units) {
 template <bool FOLD, bool LIN, bool COV>
 int launch_select(const SelArgs& a, int units, cudaStream_t st) {
   const bool g4 = FOLD && a.G <= 4;
-  const int cl = COV ? 1 : select_cluster_size(units);
+  const int cl = COV ? 1 : select_cluster_size(units, a.MP);
   static unsigned long long configured[4] = {0, 0, 0, 0};
   if (cl > 1) {
     auto k = g4 ? select_kernel<FOLD, LIN, COV, 4, true>

@@ -58,7 +58,8 @@ struct SelArgs {
   float coverage;
 };
 
-// nrm fold of one unit (reference quad_score.py:293-315): sc[p - p_lo] =
+// nrm fold of one unit (reference quad_score.py:293-315; 2^x in hardware,
+// relative error ~2^-22): sc[p - p_lo] =
 // sum_g exp(S_g[p] - hmax_g) for p in [p_lo, p_hi) (p_lo a multiple of 4);
 // writes score; resets hmax to -inf when `reset` (after the barrier).
 // GM: the largest G this instantiation serves (registers hold GM x KQ
@@ -100,10 +101,10 @@ AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int p_lo, int p_hi,
 #pragma unroll
           for (int g = 0; g < GM; ++g) {
             if (g < a.G) {
-              s4[0] += expf(v[i][g].x - hm[g]);
-              s4[1] += expf(v[i][g].y - hm[g]);
-              s4[2] += expf(v[i][g].z - hm[g]);
-              s4[3] += expf(v[i][g].w - hm[g]);
+              s4[0] += ex2_approx((v[i][g].x - hm[g]) * kLog2e);
+              s4[1] += ex2_approx((v[i][g].y - hm[g]) * kLog2e);
+              s4[2] += ex2_approx((v[i][g].z - hm[g]) * kLog2e);
+              s4[3] += ex2_approx((v[i][g].w - hm[g]) * kLog2e);
             }
           }
 #pragma unroll
@@ -132,7 +133,7 @@ AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int p_lo, int p_hi,
           float s1 = 0.f;
 #pragma unroll
           for (int g = 0; g < GM; ++g)
-            if (g < a.G) s1 += expf(v[i][g] - hm[g]);
+            if (g < a.G) s1 += ex2_approx((v[i][g] - hm[g]) * kLog2e);
           sc[p - p_lo] = s1;
           so[p] = s1;
         }
@@ -579,9 +580,19 @@ AMASS_DEV void select_unit(const SelArgs& a, const int unit, const int nb,
     bits &= bits - 1;
     tab[off++] = p_lo + i;
   }
-  for (int p = all + rank * kSelThreads + threadIdx.x; p < a.MP;
-       p += nb * kSelThreads)
-    tab[p] = -1;
+  if (nb == 1 && (a.MP & 3) == 0 &&
+      (reinterpret_cast<uintptr_t>(a.tab) & 15) == 0) {
+    // -1 padding in 16-byte stores past the first multiple of 4
+    const int p4 = min((all + 3) & ~3, a.MP);
+    if (all + (int)threadIdx.x < p4) tab[all + threadIdx.x] = -1;
+    int4* t4 = reinterpret_cast<int4*>(tab);
+    for (int q4 = p4 / 4 + threadIdx.x; q4 < a.MP / 4; q4 += kSelThreads)
+      t4[q4] = make_int4(-1, -1, -1, -1);
+  } else {
+    for (int p = all + rank * kSelThreads + threadIdx.x; p < a.MP;
+         p += nb * kSelThreads)
+      tab[p] = -1;
+  }
   if (threadIdx.x == 0 && rank == 0) a.cnt[unit] = all;
   if constexpr (CLU) cg::this_cluster().sync();   // peers' reads of sh done
 }

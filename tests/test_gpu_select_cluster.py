@@ -1,6 +1,6 @@
-"""Top-b selection at batch sizes that pick each CTA-per-unit form (a
-thread-block cluster of 8, 4 or 2 CTAs per unit for few units, one CTA for
-many), on the plain score input and on the folded per-head (nrm) input,
+"""Top-b selection at batch sizes and unit lengths that pick each
+CTA-per-unit form (a thread-block cluster of 8, 4 or 2 CTAs per unit for few
+units longer than 4096 pages, one CTA otherwise), on the plain score input and on the folded per-head (nrm) input,
 against the oracle's threshold rule.  Random continuous scores (no ties):
 tables and counts must match exactly; the folded scores within 1e-5."""
 import numpy as np
@@ -22,9 +22,10 @@ def dev():
 
 @pytest.mark.parametrize("n_req", [2, 12, 25, 80])     # 16 / 96 / 200 / 640 units
 @pytest.mark.parametrize("fold", [False, True])
-def test_topb_cluster_forms_vs_oracle(dev, n_req, fold):
-    rng = np.random.default_rng(100 + n_req + 7 * fold)
-    n_kv, G, page, MP = 8, 4, 16, 1024
+@pytest.mark.parametrize("MP", [1024, 5000])
+def test_topb_cluster_forms_vs_oracle(dev, n_req, fold, MP):
+    rng = np.random.default_rng(100 + n_req + 7 * fold + MP)
+    n_kv, G, page = 8, 4, 16
     ctxs = rng.integers(1, MP * page + 1, n_req).astype(np.int32)
     ctxs[0] = MP * page                                 # a full-length unit
     if n_req > 2:
