@@ -482,6 +482,17 @@ merge_kernel(DecArgs a) {
   const int r = live ? idx / H : 0, h = live ? idx - r * H : 0;
   const int kv = h / a.G, g = h - kv * a.G;
   const int u = r * a.n_kv + kv;
+  // the first round's run weights, loaded before the run count is known
+  // (slots past the unit's runs are masked below): one round trip fewer
+  float m_pre = -INFINITY, l_pre = 0.f;
+  {
+    const int ch0 = part + lane * WPH;
+    if (live && ch0 < a.split) {
+      const int64_t sl0 = (int64_t)u * a.split + ch0;
+      m_pre = a.m_part[sl0 * a.G + g];
+      l_pre = a.l_part[sl0 * a.G + g];
+    }
+  }
   // the decode's run split, once per CTA: pages of all units and of the
   // units before this CTA's first unit (every thread's loads in flight
   // together), the largest unit; then each row adds the few units between
@@ -537,8 +548,13 @@ merge_kernel(DecArgs a) {
       const int ch = part + (base + lane) * WPH;
       float m = -INFINITY, l = 0.f;
       if (base + lane < mine) {
-        m = a.m_part[(s0 + ch) * a.G + g];
-        l = a.l_part[(s0 + ch) * a.G + g];
+        if (base == 0) {
+          m = m_pre;
+          l = l_pre;
+        } else {
+          m = a.m_part[(s0 + ch) * a.G + g];
+          l = a.l_part[(s0 + ch) * a.G + g];
+        }
         if (!(l > 0.f)) m = -INFINITY;
       }
       float M = m;
