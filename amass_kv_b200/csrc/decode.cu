@@ -468,8 +468,9 @@ constexpr int kMergeThreads = 256;
 template <int D>
 __global__ void __launch_bounds__(kMergeThreads)
 merge_kernel(DecArgs a) {
-  grid_dep_wait();     // inputs written by the previous kernel
-  grid_dep_launch();
+  // Before the wait only the unit page counts are read: they come from the
+  // kernel before the decode, which had completed when the decode (which
+  // waits for it first thing) let this grid start.
   constexpr int PER = D / 32;
   __shared__ float sM[8], sL[8];
   __shared__ float sacc[8][D];
@@ -482,17 +483,6 @@ merge_kernel(DecArgs a) {
   const int r = live ? idx / H : 0, h = live ? idx - r * H : 0;
   const int kv = h / a.G, g = h - kv * a.G;
   const int u = r * a.n_kv + kv;
-  // the first round's run weights, loaded before the run count is known
-  // (slots past the unit's runs are masked below): one round trip fewer
-  float m_pre = -INFINITY, l_pre = 0.f;
-  {
-    const int ch0 = part + lane * WPH;
-    if (live && ch0 < a.split) {
-      const int64_t sl0 = (int64_t)u * a.split + ch0;
-      m_pre = a.m_part[sl0 * a.G + g];
-      l_pre = a.l_part[sl0 * a.G + g];
-    }
-  }
   // the decode's run split, once per CTA: pages of all units and of the
   // units before this CTA's first unit (every thread's loads in flight
   // together), the largest unit; then each row adds the few units between
@@ -536,12 +526,27 @@ merge_kernel(DecArgs a) {
   float Mrun = -INFINITY;
   float L = 0.f;
   const int c = live ? max(a.cnt[u], 0) : 0;
+  int mine = 0;
   if (c > 0) {
     for (int v = u_lo; v < u; ++v) pre += max(a.cnt[v], 0);
     const int share = range_share(tot, cmx, a.dec_warps, a.split, a.pps_min);
     const int nact = (pre + c - 1) / share - pre / share + 1;
-    const int mine = nact > part ? (nact - part + WPH - 1) / WPH : 0;
+    mine = nact > part ? (nact - part + WPH - 1) / WPH : 0;
+  }
+  grid_dep_wait();     // the decode's partials
+  grid_dep_launch();
+  if (mine > 0) {
     const int64_t s0 = (int64_t)u * a.split;
+    // the first round's run weights, one load per lane
+    float m_pre = -INFINITY, l_pre = 0.f;
+    {
+      const int ch0 = part + lane * WPH;
+      if (lane < mine) {
+        const int64_t sl0 = s0 + ch0;
+        m_pre = a.m_part[sl0 * a.G + g];
+        l_pre = a.l_part[sl0 * a.G + g];
+      }
+    }
     // all run weights of a round in one parallel round of loads (lane =
     // run), then independent acc loads per run
     for (int base = 0; base < mine; base += 32) {

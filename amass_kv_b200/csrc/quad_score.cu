@@ -258,7 +258,7 @@ AMASS_DEV void load_idx(Item<D, R, VB>& it, const QuadArgs& a,
 }
 
 // data phase: the 16-byte summary loads of an item whose block ids are known
-template <int D, int R, int VB>
+template <int D, int R, int VB, bool S2 = true>
 AMASS_DEV void load_data(Item<D, R, VB>& it, const QuadArgs& a, int lane) {
   using I = Item<D, R, VB>;
   const int c = lane & 3;
@@ -286,8 +286,10 @@ AMASS_DEV void load_data(Item<D, R, VB>& it, const QuadArgs& a, int lane) {
   it.mus = ms;
   load_halves<R>(it.vs[0], a.Vs + (int64_t)it.rowa * R);
   load_halves<R>(it.vs[1], a.Vs + (int64_t)it.rowb * R);
-  load_halves<R>(it.s2[0], a.sig2 + (int64_t)it.rowa * R);
-  load_halves<R>(it.s2[1], a.sig2 + (int64_t)it.rowb * R);
+  if constexpr (S2) {     // sig2: quad scorer only
+    load_halves<R>(it.s2[0], a.sig2 + (int64_t)it.rowa * R);
+    load_halves<R>(it.s2[1], a.sig2 + (int64_t)it.rowb * R);
+  }
 }
 
 // q operand of one (request, kv-head): limbs for B fragments + limb scales
@@ -606,8 +608,108 @@ AMASS_DEV void stage_v(const Item<D, R, VB>& it, const QuadArgs& a, int lane,
   }
 }
 
+// byte kk of four words, as one A-fragment word
+template <int KK>
+AMASS_DEV uint32_t byte_col4(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
+  const uint32_t x = __byte_perm(w0, w1, KK | ((4 + KK) << 4));
+  const uint32_t y = __byte_perm(w2, w3, KK | ((4 + KK) << 4));
+  return __byte_perm(x, y, 0x5410);
+}
+
+// The r8 scorer's integer dots of one tile: accmu = the two-limb mu dots,
+// qtl[half][jj][k] = q~ of rank column k for page (m + 8 * half) and query
+// head 2c + jj, in float.  V comes from the warp's shared stage (vsm) or,
+// when it fits, from the item's registers.  Int8 rank-8 V runs as two passes
+// of four columns: column k reads bytes k % 4 of the odd or even words of a
+// d-row, so a pass loads only its 8 words per page and step and holds only
+// its four columns' accumulators (the one-pass form needs 255 registers).
+template <int D, int R, int VB>
+AMASS_DEV void r8_dots(const Item<D, R, VB>& it, const QFrag<D>& qf,
+                       const QuadArgs& a, int lane, const uint8_t* vsm,
+                       int (*accmu)[4], float (*qtl)[2][R]) {
+  using I = Item<D, R, VB>;
+  constexpr float vdiv = (VB == 8) ? 1.f : 1.f / 16.f;
+  if constexpr (!(VB == 8 && R == 8 && !I::V_PRE)) {
+    int acc[1 + R][2][4];
+    item_dots(it, qf, a, lane, acc, vsm);
+#pragma unroll
+    for (int l = 0; l < 2; ++l)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) accmu[l][i] = acc[0][l][i];
+#pragma unroll
+    for (int half = 0; half < 2; ++half)
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj)
+#pragma unroll
+        for (int k = 0; k < R; ++k)
+          qtl[half][jj][k] = (float)(128 * acc[1 + k][0][2 * half + jj] +
+                                     acc[1 + k][1][2 * half + jj]) *
+                             (qf.sq[jj] * vdiv) * it.vsf(half, k);
+  } else {
+    using VSt = VStage<D, R, VB>;
+    constexpr int KS = D / 32;
+    const int m = lane >> 2, c = lane & 3;
+    const uint32_t* Va = reinterpret_cast<const uint32_t*>(
+        vsm + m * VSt::ROW + c * VSt::SLICE);
+    const uint32_t* Vb = Va + 8 * VSt::ROW / 4;
+    const uint32_t* mwa = reinterpret_cast<const uint32_t*>(it.mu[0]);
+    const uint32_t* mwb = reinterpret_cast<const uint32_t*>(it.mu[1]);
+#pragma unroll
+    for (int l = 0; l < 2; ++l)
+      accmu[l][0] = accmu[l][1] = accmu[l][2] = accmu[l][3] = 0;
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      int acc[4][2][4];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+        for (int l = 0; l < 2; ++l)
+          acc[kk][l][0] = acc[kk][l][1] = acc[kk][l][2] = acc[kk][l][3] = 0;
+#pragma unroll
+      for (int s = 0; s < KS; ++s) {
+        const uint32_t* bh = qf.bh[s];
+        const uint32_t* bl = qf.bl[s];
+        if (p == 0) {
+          const uint32_t am[4] = {mwa[2 * s], mwb[2 * s], mwa[2 * s + 1], mwb[2 * s + 1]};
+          mma_s8(accmu[0], am, bh[0], bh[1]);
+          mma_s8(accmu[1], am, bl[0], bl[1]);
+        }
+        // words 2*dd + p of the step's 16 (d-rows dd = 0..7, 8 rank bytes each)
+        uint32_t wa[8], wb[8];
+#pragma unroll
+        for (int dd = 0; dd < 8; ++dd) {
+          wa[dd] = Va[16 * s + 2 * dd + p];
+          wb[dd] = Vb[16 * s + 2 * dd + p];
+        }
+#define AMASS_R8_COL(KK)                                                      \
+        {                                                                     \
+          const uint32_t av[4] = {                                            \
+              byte_col4<KK>(wa[0], wa[1], wa[2], wa[3]),                      \
+              byte_col4<KK>(wb[0], wb[1], wb[2], wb[3]),                      \
+              byte_col4<KK>(wa[4], wa[5], wa[6], wa[7]),                      \
+              byte_col4<KK>(wb[4], wb[5], wb[6], wb[7])};                     \
+          mma_s8(acc[KK][0], av, bh[0], bh[1]);                               \
+          mma_s8(acc[KK][1], av, bl[0], bl[1]);                               \
+        }
+        AMASS_R8_COL(0) AMASS_R8_COL(1) AMASS_R8_COL(2) AMASS_R8_COL(3)
+#undef AMASS_R8_COL
+      }
+#pragma unroll
+      for (int half = 0; half < 2; ++half)
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            qtl[half][jj][4 * p + kk] =
+                (float)(128 * acc[kk][0][2 * half + jj] + acc[kk][1][2 * half + jj]) *
+                (qf.sq[jj] * vdiv) * it.vsf(half, 4 * p + kk);
+    }
+  }
+}
+
 template <int D, int R, int VB, int CB, bool TS = false>
-__global__ void __launch_bounds__(kQuadWarps * 32, TS ? 2 : 1)
+__global__ void __launch_bounds__(kQuadWarps * 32,
+                                  (TS && R <= 4) ? 2 : 1)
 r8_score_kernel(QuadArgs a) {
   grid_dep_wait();
   grid_dep_launch();
@@ -678,7 +780,7 @@ r8_score_kernel(QuadArgs a) {
   };
   int t = t_lo;
   load_idx(cur, a, prefix, nshs, t * a.n_kv + h, lane, &rh);
-  load_data(cur, a, lane);
+  load_data<D, R, VB, false>(cur, a, lane);
   stage_coords<D, R, VB, CB>(cur, a, lane, wbuf_s);
   cp_async_commit();
   if constexpr (VS) {
@@ -692,7 +794,7 @@ r8_score_kernel(QuadArgs a) {
     const bool more = t + 1 < t_hi;
     if (t + 2 < t_hi) load_idx(nn, a, prefix, nshs, (t + 2) * a.n_kv + h, lane, &rh);
     if (more) {
-      load_data(nxt, a, lane);
+      load_data<D, R, VB, false>(nxt, a, lane);
       stage_coords<D, R, VB, CB>(nxt, a, lane, wbuf_s + ((t + 1 - t_lo) & 1) * kBuf);
       if (!a.ctok) csp_nxt = page_scales(nxt);
     }
@@ -701,23 +803,23 @@ r8_score_kernel(QuadArgs a) {
       load_qfrag(qf, a, cur.r, h, lane);
       qr = cur.r;
     }
-    int acc[1 + R][2][4];
+    int accmu[2][4];
+    float qtl[2][2][R];                    // q~ [page half][head jj][rank]
     if constexpr (VS) {
       cp_async_wait<1>();                  // this tile's coordinates and V
       __syncwarp();
-      item_dots(cur, qf, a, lane, acc, vbuf);
+      r8_dots(cur, qf, a, lane, vbuf, accmu, qtl);
       __syncwarp();                        // every lane is done with vbuf
       if (more) stage_v<D, R, VB>(nxt, a, lane, vbuf_s);
       cp_async_commit();
     } else {
-      item_dots(cur, qf, a, lane, acc);
+      r8_dots(cur, qf, a, lane, nullptr, accmu, qtl);
       cp_async_wait<1>();                  // this tile's coordinates landed
       __syncwarp();
     }
     const uint8_t* cb = wbuf + ((t - t_lo) & 1) * kBuf;
     const __half* csb = reinterpret_cast<const __half*>(cb + kCBytes);
     const int sl_r = __ldg(a.sl + cur.r);
-    constexpr float vdiv = (VB == 8) ? 1.f : 1.f / 16.f;
     float best[2] = {-INFINITY, -INFINITY};
     float Sv[2][2];
     float qsqv[2] = {0.f, 0.f};
@@ -728,22 +830,11 @@ r8_score_kernel(QuadArgs a) {
       qsqv[1] = __ldg(qr_ + min(2 * c + 1, a.G - 1));
     }
     if constexpr (TS) {
-      // token split (G <= 4, rank <= 4): lane c evaluates tokens 4c..4c+3
+      // token split (G <= 4): lane c evaluates tokens 4c..4c+3
       // of its two pages for all four head slots, so each token's code is
       // decoded once per quad of lanes instead of four times and no logits
       // are spent on head slots >= 4; the per-(page, head) log-sum-exp is
       // then combined across the quad's lanes
-      float qtl[2][2][R];
-#pragma unroll
-      for (int half = 0; half < 2; ++half)
-#pragma unroll
-        for (int jj = 0; jj < 2; ++jj) {
-          const int idx = 2 * half + jj;
-#pragma unroll
-          for (int k = 0; k < R; ++k)
-            qtl[half][jj][k] = (float)(128 * acc[1 + k][0][idx] + acc[1 + k][1][idx]) *
-                               (qf.sq[jj] * vdiv) * cur.vsf(half, k);
-        }
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         const int pl = m + 8 * half;
@@ -764,8 +855,11 @@ r8_score_kernel(QuadArgs a) {
           const uint2 x = *reinterpret_cast<const uint2*>(rowp);
           cw[0] = x.x; cw[1] = x.y;
         } else {
-          const uint4 x = *reinterpret_cast<const uint4*>(rowp);
-          cw[0] = x.x; cw[1] = x.y; cw[2] = x.z; cw[3] = x.w;
+#pragma unroll
+          for (int w4 = 0; w4 < RCT; w4 += 4) {
+            const uint4 x = *reinterpret_cast<const uint4*>(rowp + 4 * w4);
+            cw[w4] = x.x; cw[w4 + 1] = x.y; cw[w4 + 2] = x.z; cw[w4 + 3] = x.w;
+          }
         }
         float csv[4];
         if (a.ctok) {
@@ -831,7 +925,7 @@ r8_score_kernel(QuadArgs a) {
 #pragma unroll
           for (int gg = 0; gg < 4; ++gg) ag = gg == g ? agg[gg] : ag;
           const int idx = 2 * half + jj;
-          const float qmu = (float)(128 * acc[0][0][idx] + acc[0][1][idx]) * qf.sq[jj] *
+          const float qmu = (float)(128 * accmu[0][idx] + accmu[1][idx]) * qf.sq[jj] *
                             mus * a.scale;
           float S = qmu + ag;
           if (a.resid) {
@@ -850,15 +944,7 @@ r8_score_kernel(QuadArgs a) {
         const int pl = m + 8 * half;                 // page within the tile
         const int p = cur.p0 + pl;
         const float mus = half ? __high2float(cur.mus) : __low2float(cur.mus);
-        float qt[2][R];
-  #pragma unroll
-        for (int jj = 0; jj < 2; ++jj) {
-          const int idx = 2 * half + jj;
-  #pragma unroll
-          for (int k = 0; k < R; ++k)
-            qt[jj][k] = (float)(128 * acc[1 + k][0][idx] + acc[1 + k][1][idx]) *
-                        (qf.sq[jj] * vdiv) * cur.vsf(half, k);
-        }
+        const float (*qt)[R] = qtl[half];
         const float csp = half ? __high2float(csp_cur) : __low2float(csp_cur);
         // token logits in the log2 domain: two passes (max, then sum)
         float tk2[2][PG];
@@ -904,7 +990,7 @@ r8_score_kernel(QuadArgs a) {
             agg = mx == -INFINITY ? -INFINITY : (mx + lg2_approx(sm)) * kLn2;
           }
           const int idx = 2 * half + jj;
-          const float qmu = (float)(128 * acc[0][0][idx] + acc[0][1][idx]) * qf.sq[jj] *
+          const float qmu = (float)(128 * accmu[0][idx] + accmu[1][idx]) * qf.sq[jj] *
                             mus * a.scale;
           float S = qmu + agg;
           if (a.resid) {
@@ -962,9 +1048,7 @@ int launch_r8_k(const QuadArgs& a, cudaStream_t st);
 
 template <int D, int CB, int VB, int R = 8>
 int launch_r8(const QuadArgs& a, cudaStream_t st) {
-  if constexpr (R <= 4) {
-    if (a.G <= 4) return launch_r8_k<D, CB, VB, R, true>(a, st);
-  }
+  if (a.G <= 4) return launch_r8_k<D, CB, VB, R, true>(a, st);
   return launch_r8_k<D, CB, VB, R, false>(a, st);
 }
 
