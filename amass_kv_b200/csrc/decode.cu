@@ -537,29 +537,30 @@ merge_kernel(DecArgs a) {
   grid_dep_launch();
   if (mine > 0) {
     const int64_t s0 = (int64_t)u * a.split;
-    // the first round's run weights, one load per lane
-    float m_pre = -INFINITY, l_pre = 0.f;
-    {
-      const int ch0 = part + lane * WPH;
-      if (lane < mine) {
-        const int64_t sl0 = s0 + ch0;
-        m_pre = a.m_part[sl0 * a.G + g];
-        l_pre = a.l_part[sl0 * a.G + g];
+    const float* accb = a.acc_part + (s0 * a.G + g) * D + lane * PER;
+    // partials in batches of kB, every load of a batch issued before any
+    // use: a round's run weights (lane = run) and its first batch of acc
+    // rows travel together, one memory round trip
+    constexpr int kB = 8;
+    auto load_batch = [&](float2 (*xs)[PER / 2], int j0, int base, int n) {
+#pragma unroll
+      for (int jj = 0; jj < kB; ++jj) {
+        const int j = min(j0 + jj, n - 1);              // clamped: weight 0
+        const float* ap = accb + (int64_t)(part + (base + j) * WPH) * a.G * D;
+#pragma unroll
+        for (int i = 0; i < PER; i += 2)
+          xs[jj][i / 2] = __ldcg(reinterpret_cast<const float2*>(ap + i));
       }
-    }
-    // all run weights of a round in one parallel round of loads (lane =
-    // run), then independent acc loads per run
+    };
     for (int base = 0; base < mine; base += 32) {
-      const int ch = part + (base + lane) * WPH;
+      const int n = min(32, mine - base);
+      float2 xs[kB][PER / 2];
+      load_batch(xs, 0, base, n);
       float m = -INFINITY, l = 0.f;
-      if (base + lane < mine) {
-        if (base == 0) {
-          m = m_pre;
-          l = l_pre;
-        } else {
-          m = a.m_part[(s0 + ch) * a.G + g];
-          l = a.l_part[(s0 + ch) * a.G + g];
-        }
+      if (lane < n) {
+        const int64_t sl = s0 + part + (base + lane) * WPH;
+        m = a.m_part[sl * a.G + g];
+        l = a.l_part[sl * a.G + g];
         if (!(l > 0.f)) m = -INFINITY;
       }
       float M = m;
@@ -574,17 +575,18 @@ merge_kernel(DecArgs a) {
       float racc[PER];
 #pragma unroll
       for (int i = 0; i < PER; ++i) racc[i] = 0.f;
-      const int n = min(32, mine - base);
-#pragma unroll 8
-      for (int j = 0; j < n; ++j) {
-        const float wj = __shfl_sync(0xffffffffu, w, j);
-        const int chj = part + (base + j) * WPH;
-        const float* ap = a.acc_part + ((s0 + chj) * a.G + g) * D + lane * PER;
+      for (int j0 = 0; j0 < n; j0 += kB) {
+        if (j0 > 0) load_batch(xs, j0, base, n);
 #pragma unroll
-        for (int i = 0; i < PER; i += 2) {
-          const float2 x = __ldcg(reinterpret_cast<const float2*>(ap + i));
-          racc[i] += wj * x.x;
-          racc[i + 1] += wj * x.y;
+        for (int jj = 0; jj < kB; ++jj) {
+          const int j = j0 + jj;
+          const float wsh = __shfl_sync(0xffffffffu, w, j & 31);
+          const float wj = j < n ? wsh : 0.f;
+#pragma unroll
+          for (int i = 0; i < PER; i += 2) {
+            racc[i] += wj * xs[jj][i / 2].x;
+            racc[i + 1] += wj * xs[jj][i / 2].y;
+          }
         }
       }
       if (base == 0 || Mrun == -INFINITY) {
