@@ -35,8 +35,9 @@ nrm_combine_kernel(SelArgs a) {
   nrm_fold(a, unit, 0, nsh, sc);
 }
 
-template <bool FOLD, bool LIN, bool COVERAGE, int GM = 8, bool CLU = false>
-__global__ void __launch_bounds__(kSelThreads, 4)
+template <bool FOLD, bool LIN, bool COVERAGE, int GM = 8, bool CLU = false,
+          int NT = kSelThreads>
+__global__ void __launch_bounds__(NT, 1024 / NT)
 select_kernel(SelArgs a) {
   grid_dep_wait();     // inputs written by the previous kernel
   grid_dep_launch();
@@ -48,8 +49,8 @@ select_kernel(SelArgs a) {
     nb = (int)cl.num_blocks();
     rank = (int)cl.block_rank();
   }
-  select_unit<FOLD, LIN, COVERAGE, GM, CLU>(a, blockIdx.x / nb, nb, rank, sc,
-                                            sh);
+  select_unit<FOLD, LIN, COVERAGE, GM, CLU, NT>(a, blockIdx.x / nb, nb, rank,
+                                                sc, sh);
 }
 
 constexpr int kMaxSmem = 160 * 1024;
@@ -98,7 +99,7 @@ template <bool FOLD, bool LIN, bool COV>
 int launch_select(const SelArgs& a, int units, cudaStream_t st) {
   const bool g4 = FOLD && a.G <= 4;
   const int cl = COV ? 1 : select_cluster_size(units, a.MP);
-  static unsigned long long configured[4] = {0, 0, 0, 0};
+  static unsigned long long configured[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   if (cl > 1) {
     auto k = g4 ? select_kernel<FOLD, LIN, COV, 4, true>
                 : select_kernel<FOLD, LIN, COV, 8, true>;
@@ -113,12 +114,29 @@ int launch_select(const SelArgs& a, int units, cudaStream_t st) {
     return launch_status();
   }
   const size_t smem = (size_t)a.MP * sizeof(float);
-  auto k = g4 ? select_kernel<FOLD, LIN, COV, 4> : select_kernel<FOLD, LIN, COV, 8>;
-  if (first_on_device(configured[g4 ? 1 : 0])) {
+  // one CTA per unit; with few units (at most one or two per SM) wider CTAs
+  // shorten each unit's fold / histogram / compaction latency
+  const int nt = units <= num_sms() ? 1024 : units <= 2 * num_sms() ? 512 : 256;
+  using K = void (*)(SelArgs);
+  K k;
+  int ci;
+  if (nt == 1024) {
+    k = g4 ? select_kernel<FOLD, LIN, COV, 4, false, 1024>
+           : select_kernel<FOLD, LIN, COV, 8, false, 1024>;
+    ci = 4;
+  } else if (nt == 512) {
+    k = g4 ? select_kernel<FOLD, LIN, COV, 4, false, 512>
+           : select_kernel<FOLD, LIN, COV, 8, false, 512>;
+    ci = 6;
+  } else {
+    k = g4 ? select_kernel<FOLD, LIN, COV, 4> : select_kernel<FOLD, LIN, COV, 8>;
+    ci = 0;
+  }
+  if (first_on_device(configured[ci + (g4 ? 1 : 0)])) {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          kMaxSmem);
   }
-  if (int rc = launch_pdl(k, dim3(units), dim3(kSelThreads), smem, st, a)) return rc;
+  if (int rc = launch_pdl(k, dim3(units), dim3(nt), smem, st, a)) return rc;
   return launch_status();
 }
 

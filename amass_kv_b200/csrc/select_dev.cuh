@@ -23,13 +23,16 @@
 namespace amass {
 namespace {
 
+// threads of a selection CTA: 256 (four CTAs per SM) by default; 512 or
+// 1024 when there are few units, so one unit's latency chain is spread over
+// more threads (NT template parameter below)
 constexpr int kSelThreads = 256;
-constexpr int kSelWarps = kSelThreads / 32;
+constexpr int kSelMaxWarps = 32;
 constexpr int kBins = 1024;
 constexpr int kCand = 64;
 
 
-template <typename T, typename Op>
+template <int NT, typename T, typename Op>
 AMASS_DEV T block_reduce(T v, T* red, Op op) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
@@ -39,7 +42,7 @@ AMASS_DEV T block_reduce(T v, T* red, Op op) {
   __syncthreads();
   v = red[0];
 #pragma unroll
-  for (int w = 1; w < kSelWarps; ++w) v = op(v, red[w]);
+  for (int w = 1; w < NT / 32; ++w) v = op(v, red[w]);
   return v;
 }
 
@@ -64,7 +67,7 @@ struct SelArgs {
 // writes score; resets hmax to -inf when `reset` (after the barrier).
 // GM: the largest G this instantiation serves (registers hold GM x KQ
 // 16-byte loads per thread, all issued before any use).
-template <int GM = 8, int KQ = 1>
+template <int GM = 8, int KQ = 1, int NT = kSelThreads>
 AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int p_lo, int p_hi,
                         float* sc, bool reset = true,
                         const float* hm_in = nullptr) {
@@ -79,14 +82,14 @@ AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int p_lo, int p_hi,
   // batches of pages per thread: every load of a batch issues before any
   // use, so a long unit costs a few memory round trips, not one per page
   if ((a.SHS & 3) == 0 && (reinterpret_cast<uintptr_t>(a.score_h) & 15) == 0) {
-    // 16-byte loads: thread owns page quads tid, tid + kSelThreads, ...
+    // 16-byte loads: thread owns page quads tid, tid + NT, ...
     constexpr int kQ = KQ;
     const int nq = (nsh + 3) >> 2;
-    for (int q0 = (p_lo >> 2) + threadIdx.x; q0 < nq; q0 += kQ * kSelThreads) {
+    for (int q0 = (p_lo >> 2) + threadIdx.x; q0 < nq; q0 += kQ * NT) {
       float4 v[kQ][GM];
 #pragma unroll
       for (int i = 0; i < kQ; ++i) {
-        const int q = q0 + i * kSelThreads;
+        const int q = q0 + i * NT;
 #pragma unroll
         for (int g = 0; g < GM; ++g)
           v[i][g] = (g < a.G && q < nq)
@@ -95,7 +98,7 @@ AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int p_lo, int p_hi,
       }
 #pragma unroll
       for (int i = 0; i < kQ; ++i) {
-        const int q = q0 + i * kSelThreads;
+        const int q = q0 + i * NT;
         if (q < nq) {
           float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -117,18 +120,18 @@ AMASS_DEV void nrm_fold(const SelArgs& a, int unit, int p_lo, int p_hi,
     }
   } else {
     constexpr int kB = 8;
-    for (int p0 = p_lo + threadIdx.x; p0 < nsh; p0 += kB * kSelThreads) {
+    for (int p0 = p_lo + threadIdx.x; p0 < nsh; p0 += kB * NT) {
       float v[kB][GM];
 #pragma unroll
       for (int i = 0; i < kB; ++i) {
-        const int p = p0 + i * kSelThreads;
+        const int p = p0 + i * NT;
 #pragma unroll
         for (int g = 0; g < GM; ++g)
           v[i][g] = (g < a.G && p < nsh) ? __ldcg(sh + (int64_t)g * a.SHS + p) : 0.f;
       }
 #pragma unroll
       for (int i = 0; i < kB; ++i) {
-        const int p = p0 + i * kSelThreads;
+        const int p = p0 + i * NT;
         if (p < nsh) {
           float s1 = 0.f;
 #pragma unroll
@@ -149,10 +152,10 @@ struct SelShared {
   float hmass[kBins];
   uint32_t cand[kCand];
   float cmass[kCand];
-  float red[kSelWarps];
-  int wsum[kSelWarps];
-  uint32_t wc[kSelWarps];
-  float wm[kSelWarps];
+  float red[kSelMaxWarps];
+  int wsum[kSelMaxWarps];
+  uint32_t wc[kSelMaxWarps];
+  float wm[kSelMaxWarps];
   int hit;
   int maxd;
   int ncand;
@@ -195,7 +198,7 @@ AMASS_DEV T cl_allreduce(T* slot, T v, Op op) {
 // CLU: the unit's pages are spread over the CTAs of a cluster (sc / lo_p /
 // hi_p are this CTA's slice); histograms and candidates are merged across
 // the cluster, so every CTA walks the same merged bins to the same tau.
-template <bool COV, bool LIN, bool CLU = false>
+template <bool COV, bool LIN, bool CLU = false, int NT = kSelThreads>
 AMASS_DEV uint32_t find_tau(const float* sc, int lo_p, int hi_p, int k,
                             float need, float shift_v, uint32_t kmin,
                             uint32_t kmax, SelShared& sh) {
@@ -208,13 +211,13 @@ AMASS_DEV uint32_t find_tau(const float* sc, int lo_p, int hi_p, int k,
     const uint64_t width = (uint64_t)(hi - lo) + 1;
     int shift = 0;
     while (((width - 1) >> shift) >= (uint64_t)kBins) ++shift;
-    for (int i = threadIdx.x; i < kBins; i += kSelThreads) {
+    for (int i = threadIdx.x; i < kBins; i += NT) {
       sh.hist[i] = 0;
       if (COV) sh.hmass[i] = 0.f;
     }
     if (threadIdx.x == 0) sh.ncand = 0;
     __syncthreads();
-    for (int p = lo_p + threadIdx.x; p < hi_p; p += kSelThreads) {
+    for (int p = lo_p + threadIdx.x; p < hi_p; p += NT) {
       const float v = sc[p];
       const uint32_t key = float_key(v);
       if (key >= lo && key <= hi) {
@@ -226,7 +229,7 @@ AMASS_DEV uint32_t find_tau(const float* sc, int lo_p, int hi_p, int k,
     if constexpr (CLU) {
       cg::cluster_group cl = cg::this_cluster();
       cl.sync();                       // every slice's histogram is built
-      for (int i = threadIdx.x; i < kBins; i += kSelThreads) {
+      for (int i = threadIdx.x; i < kBins; i += NT) {
         uint32_t c = 0;
         float mm = 0.f;
         for (unsigned q = 0; q < cl.num_blocks(); ++q) {
@@ -240,10 +243,10 @@ AMASS_DEV uint32_t find_tau(const float* sc, int lo_p, int hi_p, int k,
     } else {
       __syncthreads();
     }
-    // bin scan by the whole block: warp w owns the w-th 1/kSelWarps of the
+    // bin scan by the whole block: warp w owns the w-th 1/(NT / 32) of the
     // bins counted from the top, each lane kPL consecutive bins
     {
-      constexpr int kPW = kBins / kSelWarps, kPL = kPW / 32;
+      constexpr int kPW = kBins / (NT / 32), kPL = kPW / 32;
       const int d0 = warp * kPW + lane * kPL;          // descending index
       uint32_t cl = 0;
       float ml = 0.f;
@@ -320,7 +323,7 @@ AMASS_DEV uint32_t find_tau(const float* sc, int lo_p, int hi_p, int k,
     const uint32_t bhi = bend < (uint64_t)hi ? (uint32_t)bend : hi;
     if (blo == bhi) return blo;
     if (cnt_bin <= (uint32_t)kCand) {
-      for (int p = lo_p + threadIdx.x; p < hi_p; p += kSelThreads) {
+      for (int p = lo_p + threadIdx.x; p < hi_p; p += NT) {
         const float v = sc[p];
         const uint32_t key = float_key(v);
         if (key >= blo && key <= bhi) {
@@ -405,12 +408,13 @@ AMASS_DEV uint32_t find_tau(const float* sc, int lo_p, int hi_p, int k,
 // ranks' counts; used when there are few units, so a long unit's latency is
 // spread over several SMs.
 // Selection of one (request, kv-head) unit by the calling CTA (all
-// kSelThreads threads): the nrm fold (FOLD), the threshold search and the
+// NT threads): the nrm fold (FOLD), the threshold search and the
 // ascending compaction.  CLU: the unit is spread over the nb CTAs of a
 // thread-block cluster and this CTA is `rank`.  `sc` holds at least this
 // CTA's slice of the scored pages; the caller separates consecutive calls
 // with a barrier.
-template <bool FOLD, bool LIN, bool COVERAGE, int GM = 8, bool CLU = false>
+template <bool FOLD, bool LIN, bool COVERAGE, int GM = 8, bool CLU = false,
+          int NT = kSelThreads>
 AMASS_DEV void select_unit(const SelArgs& a, const int unit, const int nb,
                            const int rank, float* sc, SelShared& sh) {
   const int r = unit / a.n_kv;
@@ -431,20 +435,20 @@ AMASS_DEV void select_unit(const SelArgs& a, const int unit, const int nb,
   if (threadIdx.x == 0) { sh.kmin = 0xffffffffu; sh.kmax = 0u; }
   if (nsh > 0) {
     if (FOLD) {
-      nrm_fold<GM, (GM <= 4 ? 2 : 1)>(a, unit, s0, s1, sc, !CLU, hm_pre);
+      nrm_fold<GM, (GM <= 4 && NT <= 256 ? 2 : 1), NT>(a, unit, s0, s1, sc, !CLU, hm_pre);
     } else {
       const float* si = a.score + (int64_t)unit * a.MP;
       constexpr int kB = 8;
-      for (int p0 = s0 + threadIdx.x; p0 < s1; p0 += kB * kSelThreads) {
+      for (int p0 = s0 + threadIdx.x; p0 < s1; p0 += kB * NT) {
         float v[kB];
 #pragma unroll
         for (int i = 0; i < kB; ++i) {
-          const int p = p0 + i * kSelThreads;
+          const int p = p0 + i * NT;
           v[i] = p < s1 ? __ldcg(si + p) : 0.f;
         }
 #pragma unroll
         for (int i = 0; i < kB; ++i) {
-          const int p = p0 + i * kSelThreads;
+          const int p = p0 + i * NT;
           if (p < s1) sc[p - s0] = v[i];
         }
       }
@@ -465,7 +469,7 @@ AMASS_DEV void select_unit(const SelArgs& a, const int unit, const int nb,
   int b_used = 1;
   if (!keep_all) {
     uint32_t kmin = 0xffffffffu, kmax = 0;
-    for (int p = lo_sel + threadIdx.x; p < s1; p += kSelThreads) {
+    for (int p = lo_sel + threadIdx.x; p < s1; p += NT) {
       const uint32_t key = float_key(sc[p - s0]);
       kmin = min(kmin, key);
       kmax = max(kmax, key);
@@ -492,41 +496,41 @@ AMASS_DEV void select_unit(const SelArgs& a, const int unit, const int nb,
       float shiftv = 0.f;
       if (!LIN) {
         float vmax = -INFINITY;
-        for (int p = s0 + threadIdx.x; p < s1; p += kSelThreads)
+        for (int p = s0 + threadIdx.x; p < s1; p += NT)
           vmax = fmaxf(vmax, sc[p - s0]);
-        shiftv = block_reduce(vmax, sh.red,
+        shiftv = block_reduce<NT>(vmax, sh.red,
                               [](float x, float y) { return fmaxf(x, y); });
         if constexpr (CLU)
           shiftv = cl_allreduce(&sh.x_vmax, shiftv,
                                 [](float x, float y) { return fmaxf(x, y); });
       }
       float tot = 0.f, alw = 0.f;
-      for (int p = s0 + threadIdx.x; p < s1; p += kSelThreads) {
+      for (int p = s0 + threadIdx.x; p < s1; p += NT) {
         const float m = LIN ? sc[p - s0] : expf(sc[p - s0] - shiftv);
         tot += m;
         if (p < sink) alw += m;
       }
       auto add = [](float x, float y) { return x + y; };
-      tot = block_reduce(tot, sh.red, add);
-      alw = block_reduce(alw, sh.red, add);
+      tot = block_reduce<NT>(tot, sh.red, add);
+      alw = block_reduce<NT>(alw, sh.red, add);
       if constexpr (CLU) {
         tot = cl_allreduce(&sh.x_tot, tot, add);
         alw = cl_allreduce(&sh.x_alw, alw, add);
       }
       const float need = fmaxf(a.coverage * tot - alw, 0.f);
-      tau = find_tau<true, LIN, CLU>(sc, lo_sel - s0, s1 - s0, 0, need, shiftv,
+      tau = find_tau<true, LIN, CLU, NT>(sc, lo_sel - s0, s1 - s0, 0, need, shiftv,
                                      kmin, kmax, sh);
       int above = 0;
-      for (int p = lo_sel + threadIdx.x; p < s1; p += kSelThreads)
+      for (int p = lo_sel + threadIdx.x; p < s1; p += NT)
         above += float_key(sc[p - s0]) > tau;
       auto iadd = [](int x, int y) { return x + y; };
-      above = block_reduce(above, reinterpret_cast<int*>(sh.red), iadd);
+      above = block_reduce<NT>(above, reinterpret_cast<int*>(sh.red), iadd);
       if constexpr (CLU) above = cl_allreduce(&sh.x_above, above, iadd);
       b_used = above + 1;
     } else {
       const int b = bfix;
       b_used = b;
-      tau = find_tau<false, true, CLU>(sc, lo_sel - s0, s1 - s0, b, 0.f, 0.f,
+      tau = find_tau<false, true, CLU, NT>(sc, lo_sel - s0, s1 - s0, b, 0.f, 0.f,
                                        kmin, kmax, sh);
     }
   }
@@ -537,7 +541,7 @@ AMASS_DEV void select_unit(const SelArgs& a, const int unit, const int nb,
   // block-wide exclusive scan of the per-thread counts
   int32_t* tab = a.tab + (int64_t)unit * a.MP;
   const int c0 = s0, c1 = (rank == nb - 1) ? max(npg, s1) : s1;
-  const int per = (c1 - c0 + kSelThreads - 1) / kSelThreads;
+  const int per = (c1 - c0 + NT - 1) / NT;
   const int p_lo = c0 + threadIdx.x * per, p_hi = min(p_lo + per, c1);
   auto keep_page = [&](int p) {
     return keep_all || p < sink || p >= nsh || float_key(sc[p - s0]) >= tau;
@@ -557,7 +561,7 @@ AMASS_DEV void select_unit(const SelArgs& a, const int unit, const int nb,
   __syncthreads();
   int off = 0, total = 0;
 #pragma unroll
-  for (int w = 0; w < kSelWarps; ++w) {
+  for (int w = 0; w < (NT / 32); ++w) {
     const int v = sh.wsum[w];
     if (w < warp) off += v;
     total += v;
@@ -586,11 +590,11 @@ AMASS_DEV void select_unit(const SelArgs& a, const int unit, const int nb,
     const int p4 = min((all + 3) & ~3, a.MP);
     if (all + (int)threadIdx.x < p4) tab[all + threadIdx.x] = -1;
     int4* t4 = reinterpret_cast<int4*>(tab);
-    for (int q4 = p4 / 4 + threadIdx.x; q4 < a.MP / 4; q4 += kSelThreads)
+    for (int q4 = p4 / 4 + threadIdx.x; q4 < a.MP / 4; q4 += NT)
       t4[q4] = make_int4(-1, -1, -1, -1);
   } else {
-    for (int p = all + rank * kSelThreads + threadIdx.x; p < a.MP;
-         p += nb * kSelThreads)
+    for (int p = all + rank * NT + threadIdx.x; p < a.MP;
+         p += nb * NT)
       tab[p] = -1;
   }
   if (threadIdx.x == 0 && rank == 0) a.cnt[unit] = all;
