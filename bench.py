@@ -45,6 +45,7 @@ METRIC = "sparse decode µs/layer/step & HBM TB/s frac, B=64 ctx=32K " \
          "Llama-8B geometry"
 UNIT = "us/layer/step"
 N_REQ, N_KV, G, D, PAGE = 64, 8, 4, 128, 16
+SPLIT = 128                 # split-K partial slots per (request, kv-head)
 RANK_Q, V_BITS, BUDGET, COMBINE = 2, 4, 0.05, "nrm"
 SCORER = "quad"                     # --scorer: quad (headline) or clse
 
@@ -182,7 +183,7 @@ class Batch:
             st.quad_resid = (torch.rand((Lx, NBx, n_kv), generator=gd,
                                         device=dev) * 50 + 10).half()
             st.c_bits, st.c_grain = 4, "token"
-        ensure_stage_b_buffers(st, dev, 128)
+        ensure_stage_b_buffers(st, dev, SPLIT)
         self.st = st
         self.scale = 1.0 / math.sqrt(D)
         self.out = torch.empty(n_req, n_kv * G, D, dtype=torch.bfloat16,
@@ -936,7 +937,7 @@ def run_c5(args):
     st.quad_mu, st.mu_scale = b["quad_mu"], b["mu_scale"]
     st.quad_V, st.V_scale, st.quad_sig2 = (b["quad_V"], b["V_scale"],
                                            b["quad_sig2"])
-    ensure_stage_b_buffers(st, dev, 128)
+    ensure_stage_b_buffers(st, dev, SPLIT)
     hot_slots = min(8192, max(1, int(round(0.10 * NB))))
     n_vslots = 2 * n5
     tier = T.Tier(num_layers=1, num_blocks=NB, n_kv=C5_KV, page=PAGE, d=D,
@@ -1295,7 +1296,7 @@ def run_select_workload(args):
     stq.quad_mu, stq.mu_scale = b["quad_mu"], b["mu_scale"]
     stq.quad_V, stq.V_scale, stq.quad_sig2 = (b["quad_V"], b["V_scale"],
                                               b["quad_sig2"])
-    ensure_stage_b_buffers(stq, dev, 128)
+    ensure_stage_b_buffers(stq, dev, SPLIT)
     out = torch.empty_like(q)
     st = stq
     if c4:
@@ -1306,7 +1307,7 @@ def run_select_workload(args):
         st8.r8_mu, st8.mu_scale = b["r8_mu"], b["mu_scale"]
         st8.r8_Vk, st8.Vk_scale = b["r8_Vk"], b["Vk_scale"]
         st8.r8_c, st8.c_scale = b["r8_c"], b["c_scale"]
-        ensure_stage_b_buffers(st8, dev, 128)
+        ensure_stage_b_buffers(st8, dev, SPLIT)
         st = st8
 
     def stage(k, which=None):
@@ -1532,11 +1533,15 @@ def main():
     ap.add_argument("--batch", type=int, default=None,
                     help="batch size of the c2/c4/c5 workloads (default: the "
                          "config's; smaller only for profiling captures)")
+    ap.add_argument("--split", type=int, default=SPLIT,
+                    help="split-K partial slots per unit (the decode's run "
+                         "floor is ceil(max pages / (split - 1)))")
     ap.add_argument("--requests", type=int, default=N_REQ,
                     help="batch size per GPU (64 = BASELINE C3; smaller only "
                          "for profiling captures)")
     args = ap.parse_args()
     globals()["N_REQ"] = args.requests
+    globals()["SPLIT"] = args.split
     globals()["SCORER"] = args.scorer
     args.warmup = max(args.warmup, 3)
     if args.repeats is None:
