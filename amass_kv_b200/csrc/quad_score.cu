@@ -325,6 +325,60 @@ AMASS_DEV void load_qfrag(QFrag<D>& f, const QuadArgs& a, int r, int h,
   f.sq[1] = __ldg(qsr + g1);
 }
 
+// The q operand straight from the bf16 query (the quad scorer's form: no
+// separate limb launch).  Lane (m, c) holds query head m of kv head h (the
+// A-fragment row group of this lane) over d in [c*D/4, (c+1)*D/4); the four
+// lanes of a quad cover the row, so max|q| is a quad reduction.  Limbs and
+// scale are the q-limb prologue's, bit for bit: s = max|q|/16256,
+// qi = rn(q/s), hi = nearest(qi/128), lo = qi - 128*hi.
+template <int D>
+AMASS_DEV void qfrag_from_q(QFrag<D>& f, const QuadArgs& a, int r, int h,
+                            int lane) {
+  constexpr int SL = D / 4;                  // d values per lane
+  const int m = lane >> 2, c = lane & 3;
+  const bool gv = m < a.G;
+  const __nv_bfloat16* qp = a.q + (int64_t)r * a.q_st +
+                            (int64_t)(h * a.G + (gv ? m : 0)) * a.q_sh + c * SL;
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < SL; i += 8) {
+    const uint4 x = __ldg(reinterpret_cast<const uint4*>(qp + i));
+    const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&x);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 v = __bfloat1622float2(p2[e]);
+      mx = fmaxf(mx, fmaxf(fabsf(v.x), fabsf(v.y)));
+    }
+  }
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  const float sq = mx > 0.f ? mx / 16256.f : 1.f;
+  const float inv = 1.f / sq;
+#pragma unroll
+  for (int i = 0; i < SL; i += 8) {
+    const uint4 x = __ldg(reinterpret_cast<const uint4*>(qp + i));
+    const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&x);
+    uint32_t wh[2] = {0u, 0u}, wl[2] = {0u, 0u};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float2 v2 = __bfloat1622float2(p2[e >> 1]);
+      const float v = (e & 1) ? v2.y : v2.x;
+      const int qi = __float2int_rn(v * inv);               // |qi| <= 16256
+      const int h8 = (qi >= 0 ? qi + 64 : qi - 63) / 128;   // |h8| <= 127
+      const int l8 = qi - 128 * h8;                         // |l8| <= 64
+      wh[e >> 2] |= (uint32_t)(h8 & 0xff) << (8 * (e & 3));
+      wl[e >> 2] |= (uint32_t)(l8 & 0xff) << (8 * (e & 3));
+    }
+    const int s = i / 8;                      // words 2s, 2s + 1 of the slice
+    f.bh[s][0] = gv ? wh[0] : 0u; f.bh[s][1] = gv ? wh[1] : 0u;
+    f.bl[s][0] = gv ? wl[0] : 0u; f.bl[s][1] = gv ? wl[1] : 0u;
+  }
+  // column scales: query heads 2c, 2c + 1 (the rows of lane quads 2c, 2c + 1)
+  const int g0 = min(2 * c, a.G - 1), g1 = min(2 * c + 1, a.G - 1);
+  f.sq[0] = __shfl_sync(0xffffffffu, sq, 4 * g0);
+  f.sq[1] = __shfl_sync(0xffffffffu, sq, 4 * g1);
+}
+
 // The (1+R) x 2-limb integer dot products of one item: acc[comp][limb][4]
 // (comp 0 = mu, 1+k = V column k), C-fragment layout (rows pages m, m+8;
 // cols query heads 2c, 2c+1).
@@ -465,7 +519,10 @@ constexpr int quad_min_blocks() {
   return (D / 4) * ((VB == 8) ? R : R / 2) <= 32 ? 2 : 1;
 }
 
-template <int D, int R, int VB, bool WRITE_H>
+// QIN: the q limbs are split from the bf16 query by each warp (and the page
+// parameters derived in the prologue when asked) -- no limb launch; else
+// they come from q_limbs_kernel.
+template <int D, int R, int VB, bool WRITE_H, bool QIN>
 __global__ void __launch_bounds__(kQuadWarps * 32, (quad_min_blocks<D, R, VB>()))
 quad_score_kernel(QuadArgs a) {
   grid_dep_wait();     // inputs written by the previous kernel
@@ -474,10 +531,28 @@ quad_score_kernel(QuadArgs a) {
   __shared__ int nshs[kQuadMaxReq];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0) {
+    // this step's page parameters: derived here from seq_lens (CTA 0 writes
+    // them for the select and decode launches), or read
+    const double bud = a.dv_sl ? a.dv_budget[0] : 0.0;
     int run = 0;
     for (int base = 0; base < a.n_req; base += 32) {
       const int r = base + lane;
-      const int nsh = r < a.n_req ? max(a.nsh[r], 0) : 0;
+      int nsh = 0;
+      if (r < a.n_req) {
+        if (a.dv_sl) {
+          int32_t npg_r, nsh_r, b_r;
+          derive_one(a.dv_sl[r], bud, a.page, a.dv_win, a.dv_sink, &npg_r,
+                     &nsh_r, &b_r);
+          if (blockIdx.x == 0) {
+            a.dv_npg[r] = npg_r;
+            a.dv_nsh[r] = nsh_r;
+            a.dv_b[r] = b_r;
+          }
+          nsh = max(nsh_r, 0);
+        } else {
+          nsh = max(a.nsh[r], 0);
+        }
+      }
       const int t = (nsh + 15) / 16;
       int incl = t;
 #pragma unroll
@@ -526,7 +601,8 @@ quad_score_kernel(QuadArgs a) {
     if (t + 2 < t_hi) load_idx(nn, a, prefix, nshs, (t + 2) * a.n_kv + h, lane, &rh);
     if (more) load_data(nxt, a, lane);
     if (cur.r != qr) {
-      load_qfrag(qf, a, cur.r, h, lane);
+      if constexpr (QIN) qfrag_from_q(qf, a, cur.r, h, lane);
+      else load_qfrag(qf, a, cur.r, h, lane);
       qr = cur.r;
     }
     score_item<D, R, VB, WRITE_H>(cur, qf, a, lane);
@@ -1075,22 +1151,38 @@ int launch_r8_k(const QuadArgs& a, cudaStream_t st) {
   return launch_status();
 }
 
+// Batches of at least kQuadQinReq requests split q in the scorer (each warp
+// changes request rarely, so its limb split is amortised: C3 step 117.2 ->
+// 115.9 us on B200); smaller batches keep the limb launch, where a warp's
+// one or two tiles would wait on its own split (8 requests: 33.9 -> 35.0 us).
+constexpr int kQuadQinReq = 32;
+
 template <int D, int R, int VB>
 int launch_quad(const QuadArgs& a, bool write_h, cudaStream_t st) {
-  auto k = write_h ? quad_score_kernel<D, R, VB, true>
-                   : quad_score_kernel<D, R, VB, false>;
-  static int per_sm[2] = {0, 0};
-  int& ps = per_sm[write_h ? 1 : 0];
+  const bool qin = a.n_req >= kQuadQinReq;
+  using K = void (*)(QuadArgs);
+  K k;
+  if (qin) k = write_h ? quad_score_kernel<D, R, VB, true, true>
+                       : quad_score_kernel<D, R, VB, false, true>;
+  else k = write_h ? quad_score_kernel<D, R, VB, true, false>
+                   : quad_score_kernel<D, R, VB, false, false>;
+  static int per_sm[4] = {0, 0, 0, 0};
+  int& ps = per_sm[(write_h ? 1 : 0) + (qin ? 2 : 0)];
   if (ps == 0) {
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ps, k, kQuadWarps * 32, 0);
     if (ps < 1) ps = 1;
   }
-  const int heads = a.n_req * a.n_kv * a.G;
-  if (int rc = launch_pdl(q_limbs_kernel<D>, dim3((heads + 7) / 8), dim3(256), 0, st, a)) return rc;
+  QuadArgs b = a;
+  if (!qin) {
+    const int heads = a.n_req * a.n_kv * a.G;
+    if (int rc = launch_pdl(q_limbs_kernel<D>, dim3((heads + 7) / 8), dim3(256), 0, st, a))
+      return rc;
+    b.dv_sl = nullptr;          // derived by the limb launch; the scorer reads nsh
+  }
   int grid = num_sms() * ps;
   const int per = a.n_kv > kQuadWarps ? a.n_kv / kQuadWarps : 1;
   grid = (grid / per) * per;   // warps per grid a multiple of n_kv
-  if (int rc = launch_pdl(k, dim3(grid), dim3(kQuadWarps * 32), 0, st, a)) return rc;
+  if (int rc = launch_pdl(k, dim3(grid), dim3(kQuadWarps * 32), 0, st, b)) return rc;
   return launch_status();
 }
 

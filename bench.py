@@ -46,6 +46,8 @@ METRIC = "sparse decode µs/layer/step & HBM TB/s frac, B=64 ctx=32K " \
 UNIT = "us/layer/step"
 N_REQ, N_KV, G, D, PAGE = 64, 8, 4, 128, 16
 SPLIT = 128                 # split-K partial slots per (request, kv-head)
+QUAD_QIN_REQ = 32           # quad scorer splits q itself from this batch size
+                            # (kQuadQinReq in csrc/quad_score.cu)
 RANK_Q, V_BITS, BUDGET, COMBINE = 2, 4, 0.05, "nrm"
 SCORER = "quad"                     # --scorer: quad (headline) or clse
 
@@ -193,8 +195,11 @@ class Batch:
         self.stages = (0, 1, 2)
         self.stage_names = {0: "derive+quad_score", 1: "select",
                             2: "sparse_decode+merge"}
-        # q-limbs (+ derive), score, select, decode, merge; CLSE: + derive
-        self.launches_per_step = 6 if self.clse else 5
+        # quad: score (q limbs and derive inside it from 32 requests up,
+        # else a q-limb launch before it), select, decode, merge; CLSE:
+        # derive, q-limbs, score, select, decode, merge
+        self.launches_per_step = 6 if self.clse else \
+            (4 if n_req >= QUAD_QIN_REQ else 5)
         self.pps_min = None
 
     def stage(self, layer, k, q=None):
