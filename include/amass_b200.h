@@ -68,7 +68,8 @@ int amass_derive_page_params(const int32_t* seq_lens, const double* budget64,
  *              resets it to -inf.
  * q8_ws (n_req, H, 2, d) int8 (16-byte aligned) and qs_ws (n_req, H) fp32
  * are caller scratch for the exact two-limb int8 form of q the integer MMAs
- * use (|dq| <= max|q_head| / 32512).
+ * use (|dq| <= max|q_head| / 32512); from 32 requests up the scorer splits
+ * q itself (same limbs) and leaves the scratch untouched.
  * Pages p < n_sel_hi[r] are written; others are left untouched.
  * Compiled variants: head_dim in {64, 128}, rank in {1, 2, 4, 8},
  * v_bits in {4, 8} (int4 needs an even rank), G <= 8, page = 16,
@@ -87,10 +88,10 @@ int amass_quad_score(const void* q, int64_t q_stride_t, int64_t q_stride_h,
 /* quad_score_derive -- derive_page_params (selection/select.py:30-54) and
  * quad_score_cuda (selection/quad_score_cuda.py:1724-1794), the first two
  * calls of the reference's _quad_select_adapter (backend/_runtime.py:
- * 183-263), in the launches of amass_quad_score alone: the q-limb prologue
- * also writes n_pages / n_sel_hi / b_fix from seq_lens and budget64 (as
- * amass_derive_page_params), and the scorer reads that n_sel_hi.  Other
- * arguments as amass_quad_score. */
+ * 183-263), in the launches of amass_quad_score alone: n_pages / n_sel_hi /
+ * b_fix are written from seq_lens and budget64 (as amass_derive_page_params)
+ * by the q-limb launch, or from 32 requests up by the scorer's own prologue
+ * (one launch).  Other arguments as amass_quad_score. */
 int amass_quad_score_derive(
     const int32_t* seq_lens, const double* budget64, int32_t* n_pages,
     int32_t* n_sel_hi, int32_t* b_fix, int window_pages, int sink_pages,
