@@ -218,6 +218,84 @@ AMASS_DEV void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" :: "n"(N));
 }
 
+// --------------------------------------------------------------------------
+// mbarrier + bulk-copy (cp.async.bulk, no multicast) helpers
+// --------------------------------------------------------------------------
+AMASS_DEV void mbar_init(uint32_t bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(count));
+}
+// make the initialised barriers visible to the async proxy (bulk copies)
+AMASS_DEV void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+AMASS_DEV void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(bar) : "memory");
+}
+AMASS_DEV void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+               :: "r"(bar), "r"(bytes) : "memory");
+}
+// this thread's earlier cp.async copies arrive on bar when they land (the
+// arrival counts against the barrier's expected count)
+AMASS_DEV void cp_async_mbar_arrive(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];"
+               :: "r"(bar) : "memory");
+}
+// one poll: suspends the thread for at most ~1 us (suspend-time hint) while
+// the phase is incomplete
+AMASS_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 1000;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+AMASS_DEV uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// bounded wait for the phase of parity `parity` to complete: false when
+// about a second passed (the caller records the fault and unwinds)
+constexpr uint64_t kMbarWaitNs = 1000000000ull;
+AMASS_DEV bool mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (global_ns() - t0 > kMbarWaitNs) return false;
+  }
+}
+// one contiguous global -> shared bulk copy completing on bar (16-byte
+// aligned addresses, size a multiple of 16)
+AMASS_DEV void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                        uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1], %2, [%3];"
+      :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+AMASS_DEV uint4 lds128(uint32_t a) {
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(a));
+  return r;
+}
+AMASS_DEV uint32_t lds32(uint32_t a) {
+  uint32_t r;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(r) : "r"(a));
+  return r;
+}
+AMASS_DEV uint16_t lds16(uint32_t a) {
+  uint16_t r;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(r) : "r"(a));
+  return r;
+}
+
 // read-only global loads that do not allocate in L1 (streamed summaries)
 AMASS_DEV uint4 ldg_nc_v4(const void* p) {
   uint4 r;

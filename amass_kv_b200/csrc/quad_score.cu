@@ -513,6 +513,46 @@ AMASS_DEV void score_item(const Item<D, R, VB>& it, const QFrag<D>& qf,
   }
 }
 
+// Warp 0's prologue of the quad scorers: this step's page parameters
+// (derived here from seq_lens, CTA 0 writing them for the select and decode
+// launches, or read) and the per-request tile offsets prefix[0..n_req].
+AMASS_DEV void quad_prologue(const QuadArgs& a, int* prefix, int* nshs,
+                             int lane) {
+  // this step's page parameters: derived here from seq_lens (CTA 0 writes
+  // them for the select and decode launches), or read
+  const double bud = a.dv_sl ? a.dv_budget[0] : 0.0;
+  int run = 0;
+  for (int base = 0; base < a.n_req; base += 32) {
+    const int r = base + lane;
+    int nsh = 0;
+    if (r < a.n_req) {
+      if (a.dv_sl) {
+        int32_t npg_r, nsh_r, b_r;
+        derive_one(a.dv_sl[r], bud, a.page, a.dv_win, a.dv_sink, &npg_r,
+                   &nsh_r, &b_r);
+        if (blockIdx.x == 0) {
+          a.dv_npg[r] = npg_r;
+          a.dv_nsh[r] = nsh_r;
+          a.dv_b[r] = b_r;
+        }
+        nsh = max(nsh_r, 0);
+      } else {
+        nsh = max(a.nsh[r], 0);
+      }
+    }
+    const int t = (nsh + 15) / 16;
+    int incl = t;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int x = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += x;
+    }
+    if (r < a.n_req) { prefix[r] = run + incl - t; nshs[r] = nsh; }
+    run += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  if (lane == 0) prefix[a.n_req] = run;
+}
+
 // two CTAs per SM (<= 128 registers) when a lane's V slice is <= 32 bytes
 template <int D, int R, int VB>
 constexpr int quad_min_blocks() {
@@ -530,41 +570,7 @@ quad_score_kernel(QuadArgs a) {
   __shared__ int prefix[kQuadMaxReq + 1];   // per-request tile offsets
   __shared__ int nshs[kQuadMaxReq];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (warp == 0) {
-    // this step's page parameters: derived here from seq_lens (CTA 0 writes
-    // them for the select and decode launches), or read
-    const double bud = a.dv_sl ? a.dv_budget[0] : 0.0;
-    int run = 0;
-    for (int base = 0; base < a.n_req; base += 32) {
-      const int r = base + lane;
-      int nsh = 0;
-      if (r < a.n_req) {
-        if (a.dv_sl) {
-          int32_t npg_r, nsh_r, b_r;
-          derive_one(a.dv_sl[r], bud, a.page, a.dv_win, a.dv_sink, &npg_r,
-                     &nsh_r, &b_r);
-          if (blockIdx.x == 0) {
-            a.dv_npg[r] = npg_r;
-            a.dv_nsh[r] = nsh_r;
-            a.dv_b[r] = b_r;
-          }
-          nsh = max(nsh_r, 0);
-        } else {
-          nsh = max(a.nsh[r], 0);
-        }
-      }
-      const int t = (nsh + 15) / 16;
-      int incl = t;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int x = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += x;
-      }
-      if (r < a.n_req) { prefix[r] = run + incl - t; nshs[r] = nsh; }
-      run += __shfl_sync(0xffffffffu, incl, 31);
-    }
-    if (lane == 0) prefix[a.n_req] = run;
-  }
+  if (warp == 0) quad_prologue(a, prefix, nshs, lane);
   __syncthreads();
   // warp gw owns head gw % n_kv and a contiguous range of tiles, so its q
   // operand changes only when the range crosses into the next request; the
@@ -610,6 +616,234 @@ quad_score_kernel(QuadArgs a) {
     cur = nxt;
     nxt = nn;
     ++t;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Pipelined quad scorer (8 kv heads, a lane's V slice in registers).
+//
+// A CTA owns one contiguous range of 16-page tiles and scores all 8 heads of
+// each: warp h < 8 is the consumer for kv head h, warp 8 the producer.  The
+// producer streams each tile's summaries into a ring of S shared-memory
+// stages: per page, the block's mu row and V-code row (all heads, 1 KB each
+// at C3 geometry -- contiguous in the reference's (L, NB, n_kv, ...) slabs)
+// as two bulk copies (cp.async.bulk, complete_tx on the stage's full
+// barrier), and its three scale rows (16 + 32 + 32 B) as 16-byte cp.async
+// pieces that arrive on the same barrier.  Block-table entries are read one
+// tile ahead.  Consumers wait on the full barrier, move their head's slice
+// into registers (rows padded by 16 B, so the 8 lanes of a 16-byte shared
+// load phase hit distinct banks), release the stage (empty barrier, one
+// arrival per warp) and run the same integer-MMA math and epilogue as
+// quad_score_kernel, so the two kernels' scores are bit-identical.  Up to S
+// tiles (S x 34.5 KB per CTA, two CTAs per SM) are in flight without holding
+// registers, where the register pipeline holds one tile per warp.
+//
+// Every mbarrier wait is bounded (about a second of %globaltimer): on expiry
+// the warp records the fault in g_quad_pipe_fault (1 = consumer, 2 =
+// producer) and unwinds; the producer waits (bounded) for its last copies to
+// land before it returns.
+// ---------------------------------------------------------------------------
+constexpr int kPipeHeads = 8;
+constexpr int kPipeThreads = (kPipeHeads + 1) * 32;
+// two stages per CTA: three measured slower in the step (64 requests 115.1
+// vs 114.3 us) -- the larger ring keeps the select's CTAs off the SMs longer
+constexpr int kPipeStages = 2;
+__device__ int g_quad_pipe_fault;
+
+template <int D, int R, int VB>
+struct PipeLayout {
+  static constexpr int RB = (VB == 8) ? R : R / 2;
+  static constexpr int MU_ROW = kPipeHeads * D;        // bytes per block
+  static constexpr int V_ROW = kPipeHeads * D * RB;
+  static constexpr int MS_ROW = kPipeHeads * 2;
+  static constexpr int VS_ROW = kPipeHeads * R * 2;
+  static constexpr int MU_P = MU_ROW + 16;             // padded smem rows
+  static constexpr int V_P = V_ROW + 16;
+  static constexpr int OFF_V = 16 * MU_P;
+  static constexpr int OFF_MS = OFF_V + 16 * V_P;
+  static constexpr int OFF_VS = OFF_MS + 16 * MS_ROW;
+  static constexpr int OFF_S2 = OFF_VS + 16 * VS_ROW;
+  static constexpr int STAGE = OFF_S2 + 16 * VS_ROW;
+  static constexpr uint32_t TX = MU_ROW + V_ROW;       // bulk bytes per page
+  static_assert(MS_ROW % 16 == 0 && VS_ROW % 16 == 0 && STAGE % 16 == 0,
+                "16-byte copy pieces");
+};
+
+template <int D, int R, int VB, int S>
+constexpr size_t pipe_smem_bytes(int n_req) {
+  return (size_t)S * PipeLayout<D, R, VB>::STAGE + 16 * S +
+         4 * (2 * (size_t)n_req + 1);
+}
+
+// R fp16 values at shared address p into RW words (as load_halves)
+template <int R>
+AMASS_DEV void lds_halves(uint32_t* w, uint32_t p) {
+  if constexpr (R == 1) {
+    w[0] = lds16(p);
+  } else {
+#pragma unroll
+    for (int k = 0; k < R / 2; ++k) w[k] = lds32(p + 4 * k);
+  }
+}
+
+template <int D, int R, int VB, bool WRITE_H, bool QIN, int S>
+__global__ void __launch_bounds__(kPipeThreads, 2)
+quad_score_pipe_kernel(QuadArgs a) {
+  using PL = PipeLayout<D, R, VB>;
+  using I = Item<D, R, VB>;
+  static_assert(I::V_PRE, "the pipelined scorer keeps the V slice in registers");
+  extern __shared__ __align__(128) uint8_t pipe_smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(pipe_smem + S * PL::STAGE);
+  int* prefix = reinterpret_cast<int*>(bars + 2 * S);
+  int* nshs = prefix + a.n_req + 1;
+  grid_dep_wait();     // inputs written by the previous kernel
+  grid_dep_launch();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t ring = smem_u32(pipe_smem);
+  const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * S;
+  if (warp == 0) quad_prologue(a, prefix, nshs, lane);
+  if (threadIdx.x == 32) {
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full0 + 8 * s, 1 + 32);     // expect_tx arrive + 32 lanes
+      mbar_init(empty0 + 8 * s, kPipeHeads);
+    }
+    mbar_init_fence();
+  }
+  __syncthreads();
+  const int T = prefix[a.n_req];
+  const int t_lo = (int)((int64_t)T * blockIdx.x / gridDim.x);
+  const int t_hi = (int)((int64_t)T * (blockIdx.x + 1) / gridDim.x);
+  if (t_lo >= t_hi) return;
+  int rq;
+  {
+    int lo = 0, hi = a.n_req - 1;     // request of tile t_lo
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (prefix[mid] <= t_lo) lo = mid; else hi = mid - 1;
+    }
+    rq = lo;
+  }
+
+  if (warp == kPipeHeads) {
+    // ---- producer ----
+    // block ids of the next kIdsAhead tiles stay in flight (slot j = tile
+    // t + j), so a tile's copies never wait on its block-table read
+    constexpr int kIdsAhead = 4;
+    int pr = rq;
+    int blk_q[kIdsAhead];
+    bool ok_q[kIdsAhead];
+    auto fetch = [&](int t, int& blk, bool& ok) {
+      ok = false;
+      blk = 0;
+      if (t >= t_hi) return;
+      while (prefix[pr + 1] <= t) ++pr;
+      const int p = (t - prefix[pr]) * 16 + (lane & 15);
+      ok = lane < 16 && p < nshs[pr];
+      if (ok) blk = __ldg(a.bt + (int64_t)pr * a.bt_stride + p);
+    };
+#pragma unroll
+    for (int j = 0; j < kIdsAhead; ++j) fetch(t_lo + j, blk_q[j], ok_q[j]);
+    int issued = 0;
+    for (int t = t_lo; t < t_hi; ++t) {
+      const int i = t - t_lo, s = i % S;
+      const int blk = blk_q[0];
+      const bool ok = ok_q[0];
+#pragma unroll
+      for (int j = 0; j + 1 < kIdsAhead; ++j) {
+        blk_q[j] = blk_q[j + 1];
+        ok_q[j] = ok_q[j + 1];
+      }
+      fetch(t + kIdsAhead, blk_q[kIdsAhead - 1], ok_q[kIdsAhead - 1]);
+      if (i >= S && !mbar_wait(empty0 + 8 * s, ((i / S) - 1) & 1)) {
+        atomicCAS(&g_quad_pipe_fault, 0, 2);
+        break;
+      }
+      const uint32_t full = full0 + 8 * s;
+      const int nv = __popc(__ballot_sync(0xffffffffu, ok));
+      if (lane == 0) mbar_arrive_expect_tx(full, (uint32_t)nv * PL::TX);
+      __syncwarp();
+      if (ok) {
+        const uint32_t st = ring + s * PL::STAGE;
+        const int64_t b = blk;
+        bulk_g2s(st + lane * PL::MU_P, a.mu + b * PL::MU_ROW, PL::MU_ROW, full);
+        bulk_g2s(st + PL::OFF_V + lane * PL::V_P, a.V + b * PL::V_ROW,
+                 PL::V_ROW, full);
+        const uint8_t* ms = reinterpret_cast<const uint8_t*>(a.mus) + b * PL::MS_ROW;
+        const uint8_t* vs = reinterpret_cast<const uint8_t*>(a.Vs) + b * PL::VS_ROW;
+        const uint8_t* s2 = reinterpret_cast<const uint8_t*>(a.sig2) + b * PL::VS_ROW;
+#pragma unroll
+        for (int k = 0; k < PL::MS_ROW; k += 16)
+          cp_async16(st + PL::OFF_MS + lane * PL::MS_ROW + k, ms + k, true);
+#pragma unroll
+        for (int k = 0; k < PL::VS_ROW; k += 16) {
+          cp_async16(st + PL::OFF_VS + lane * PL::VS_ROW + k, vs + k, true);
+          cp_async16(st + PL::OFF_S2 + lane * PL::VS_ROW + k, s2 + k, true);
+        }
+      }
+      cp_async_mbar_arrive(full);
+      issued = i + 1;
+    }
+    // the last fills (at most S) land before this warp leaves
+    for (int j = issued > S ? issued - S : 0; j < issued; ++j)
+      if (!mbar_wait(full0 + 8 * (j % S), (j / S) & 1)) {
+        atomicCAS(&g_quad_pipe_fault, 0, 2);
+        break;
+      }
+    return;
+  }
+
+  // ---- consumers: warp h scores kv head h of every tile ----
+  const int h = warp;
+  const int m = lane >> 2, c = lane & 3;
+  int cr = rq, qr = -1;
+  QFrag<D> qf;
+  for (int t = t_lo; t < t_hi; ++t) {
+    const int i = t - t_lo, s = i % S;
+    while (prefix[cr + 1] <= t) ++cr;
+    Item<D, R, VB> it;
+    it.r = cr;
+    it.h = h;
+    it.p0 = (t - prefix[cr]) * 16;
+    const int nsh = nshs[cr];
+    it.va = it.p0 + m < nsh;
+    it.vb = it.p0 + m + 8 < nsh;
+    it.rowa = it.rowb = 0;
+    if (!mbar_wait(full0 + 8 * s, (i / S) & 1)) {
+      atomicCAS(&g_quad_pipe_fault, 0, 1);
+      break;
+    }
+    const uint32_t st = ring + s * PL::STAGE;
+    const uint32_t ma = st + m * PL::MU_P + h * D + c * (D / 4);
+    const uint32_t va = st + PL::OFF_V + m * PL::V_P + h * D * PL::RB +
+                        c * I::V_BYTES;
+#pragma unroll
+    for (int k = 0; k < I::MU_U4; ++k) {
+      it.mu[0][k] = lds128(ma + 16 * k);
+      it.mu[1][k] = lds128(ma + 8 * PL::MU_P + 16 * k);
+    }
+#pragma unroll
+    for (int k = 0; k < I::V_U4; ++k) {
+      it.v[0][k] = lds128(va + 16 * k);
+      it.v[1][k] = lds128(va + 8 * PL::V_P + 16 * k);
+    }
+    const uint32_t msa = st + PL::OFF_MS + m * PL::MS_ROW + 2 * h;
+    it.mus = __halves2half2(__ushort_as_half(lds16(msa)),
+                            __ushort_as_half(lds16(msa + 8 * PL::MS_ROW)));
+    const uint32_t vsa = st + PL::OFF_VS + m * PL::VS_ROW + h * R * 2;
+    const uint32_t s2a = st + PL::OFF_S2 + m * PL::VS_ROW + h * R * 2;
+    lds_halves<R>(it.vs[0], vsa);
+    lds_halves<R>(it.vs[1], vsa + 8 * PL::VS_ROW);
+    lds_halves<R>(it.s2[0], s2a);
+    lds_halves<R>(it.s2[1], s2a + 8 * PL::VS_ROW);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty0 + 8 * s);
+    if (cr != qr) {
+      if constexpr (QIN) qfrag_from_q(qf, a, cr, h, lane);
+      else load_qfrag(qf, a, cr, h, lane);
+      qr = cr;
+    }
+    score_item<D, R, VB, WRITE_H>(it, qf, a, lane);
   }
 }
 
@@ -1157,9 +1391,71 @@ int launch_r8_k(const QuadArgs& a, cudaStream_t st) {
 // one or two tiles would wait on its own split (8 requests: 33.9 -> 35.0 us).
 constexpr int kQuadQinReq = 32;
 
+// Which scorer serves a call (amass_quad_pipeline): 1 (default) the
+// pipelined scorer from kQuadQinReq requests up where the geometry allows,
+// 2 wherever the geometry allows, 0 never.  Measured on B200 (layer-step,
+// us, pipelined vs register-pipelined): 64 requests 114.3 vs 114.7, 32
+// requests 70.0 vs 70.0, 16 requests 48.7 vs 48.6, 8 requests 33.0 vs 34.2,
+// C2 (1 request) 42.7 vs 42.0, C5 (16 requests) 154.7 vs 151.7 -- below 32
+// requests the ring's shared memory keeps the next kernels' CTAs off the SMs
+// for longer than the scorer gains.
+int g_quad_pipe_mode = 1;
+long long g_quad_pipe_launches = 0;   // host count of pipelined launches
+
+// The pipelined scorer when the geometry allows it: 8 kv heads, a lane's V
+// slice of at most 32 bytes (int4 rank 2 or int8 rank 1 at head_dim 128),
+// 16-byte aligned scale slabs, the ring and the request table within the
+// shared-memory budget of two CTAs per SM.  Returns -1 when it does not
+// apply.
+template <int D, int R, int VB>
+int launch_quad_pipe(const QuadArgs& a, bool write_h, bool qin,
+                     cudaStream_t st) {
+  constexpr int S = kPipeStages;
+  if constexpr (Item<D, R, VB>::V_BYTES > 32) {
+    return -1;        // wider V slices exceed the consumers' register budget
+  } else {
+    if (g_quad_pipe_mode == 0 || (g_quad_pipe_mode == 1 && !qin) ||
+        a.n_kv != kPipeHeads)
+      return -1;
+    if ((reinterpret_cast<uintptr_t>(a.mus) |
+         reinterpret_cast<uintptr_t>(a.Vs) |
+         reinterpret_cast<uintptr_t>(a.sig2)) & 15)
+      return -1;
+    const size_t smem = pipe_smem_bytes<D, R, VB, S>(a.n_req);
+    if (smem > 110 * 1024) return -1;
+    using K = void (*)(QuadArgs);
+    K k;
+    if (qin) k = write_h ? quad_score_pipe_kernel<D, R, VB, true, true, S>
+                         : quad_score_pipe_kernel<D, R, VB, false, true, S>;
+    else k = write_h ? quad_score_pipe_kernel<D, R, VB, true, false, S>
+                     : quad_score_pipe_kernel<D, R, VB, false, false, S>;
+    static unsigned long long attr_set[4] = {0, 0, 0, 0};
+    if (first_on_device(attr_set[(write_h ? 1 : 0) + (qin ? 2 : 0)]))
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           110 * 1024);
+    QuadArgs b = a;
+    if (!qin) {
+      const int heads = a.n_req * a.n_kv * a.G;
+      if (int rc = launch_pdl(q_limbs_kernel<D>, dim3((heads + 7) / 8),
+                              dim3(256), 0, st, a))
+        return rc;
+      b.dv_sl = nullptr;
+    }
+    if (int rc = launch_pdl(k, dim3(2 * num_sms()), dim3(kPipeThreads), smem,
+                            st, b))
+      return rc;
+    ++g_quad_pipe_launches;
+    return launch_status();
+  }
+}
+
 template <int D, int R, int VB>
 int launch_quad(const QuadArgs& a, bool write_h, cudaStream_t st) {
   const bool qin = a.n_req >= kQuadQinReq;
+  {
+    const int rc = launch_quad_pipe<D, R, VB>(a, write_h, qin, st);
+    if (rc >= 0) return rc;
+  }
   using K = void (*)(QuadArgs);
   K k;
   if (qin) k = write_h ? quad_score_kernel<D, R, VB, true, true>
@@ -1474,4 +1770,32 @@ extern "C" int amass_clse_score(
   if (head_dim == 128) return by_rank(std::integral_constant<int, 128>{});
   if (head_dim == 64) return by_rank(std::integral_constant<int, 64>{});
   return AMASS_ERR_UNSUPPORTED;
+}
+
+extern "C" int amass_quad_pipeline(int mode) {
+  using namespace amass;
+  const int prev = g_quad_pipe_mode;
+  if (mode >= 0 && mode <= 2) g_quad_pipe_mode = mode;
+  return prev;
+}
+
+extern "C" int amass_quad_pipeline_status(int* fault, long long* launches,
+                                          int clear) {
+  using namespace amass;
+  if (fault) {
+    if (cudaMemcpyFromSymbol(fault, g_quad_pipe_fault, sizeof(int)) !=
+        cudaSuccess)
+      return AMASS_ERR_CUDA;
+    if (clear) {
+      const int zero = 0;
+      if (cudaMemcpyToSymbol(g_quad_pipe_fault, &zero, sizeof(int)) !=
+          cudaSuccess)
+        return AMASS_ERR_CUDA;
+    }
+  }
+  if (launches) {
+    *launches = g_quad_pipe_launches;
+    if (clear) g_quad_pipe_launches = 0;
+  }
+  return AMASS_OK;
 }

@@ -298,6 +298,11 @@ def _timed_repeats(run_one, steps, repeats, world, dev, clk_index=None):
             run_one(i)
             i += 1
         e1.record()
+    if clk is not None:
+        # wait with the GIL released so the sampler thread runs while the
+        # queued steps execute
+        while not ev[-1][1].query():
+            time.sleep(0.0005)
     torch.cuda.synchronize()
     if clk is not None:
         clk.__exit__(None, None, None)
@@ -529,14 +534,21 @@ def run_gpu(args):
     job_gbs = tot_bytes / (med * 1e-3) / 1e9
 
     launches = batch_launches(batch, args)
+    import ctypes
+    n_pipe = ctypes.c_longlong(0)
+    _lib.call("amass_quad_pipeline_status", None, ctypes.addressof(n_pipe), 0)
+    quad_kernel = ("quad_score_pipe_kernel (bulk-copy ring)" if n_pipe.value
+                   else "quad_score_kernel (register pipeline)")
     names = dict(batch.stage_names)
     parity = cpu = None
-    ctx32 = None
+    ctx32 = score_layout = None
     if world == 1:
         if not args.no_cpu_baseline:
             parity, cpu = _oracle_check(batch)
         if not args.no_ctx32k:
             ctx32 = _ctx32k(args, dev, peak, peak_kind)
+        if not args.no_score_layout and not batch.clse:
+            score_layout = _score_layout(batch, args, peak)
     # secondary layouts at N > 1: the same batch replicated on every rank
     # (weak scaling, identical per-rank work) and the kv-head-sharded form
     layouts = None
@@ -585,6 +597,7 @@ def run_gpu(args):
                 "timing": f"median of {args.repeats} timed loops of "
                           f"{args.steps} steps (max over ranks per loop)",
                 "selected_pages_per_step": int(alg[0]["pages"]),
+                "quad_scorer": None if SCORER == "clse" else quad_kernel,
             },
             "repeats_us": [round(x * 1e3, 2) for x in reps],
             "step_roofline": {"bound": "hbm", "achieved": round(job_gbs, 1),
@@ -614,6 +627,8 @@ def run_gpu(args):
             line["layouts"] = layouts
         if ctx32 is not None:
             line["ctx32k"] = ctx32
+        if score_layout is not None:
+            line["score_layout"] = score_layout
         if parity is not None:
             line["parity"] = parity
             line["cpu_baseline"] = cpu
@@ -628,6 +643,53 @@ def run_gpu(args):
         sys.stdout.flush()
         sys.stderr.flush()
         os._exit(0)
+
+
+def _score_layout(batch, args, peak):
+    """What bounds the quad scorer: the batch's scoring stage (derive + quad
+    score) timed on its own with the batch's block table (each request's
+    blocks drawn from one random permutation of the pool, as a long-running
+    paged cache leaves them) and again with each request's blocks contiguous
+    in the same pool.  Same requests, pages and bytes; only the addresses of
+    the 1 KB per-block summary rows change.  Device time, CUDA graphs."""
+    import torch
+    n = batch.n_req
+    npg = [(int(c) + PAGE - 1) // PAGE for c in batch.ctxs]
+    contig = torch.zeros_like(batch.bt)
+    o = 0
+    for i, m in enumerate(npg):
+        contig[i, :m] = torch.arange(o, o + m, dtype=torch.int32,
+                                     device=contig.device)
+        o += m
+    sb = float(np.mean([batch.algorithmic_bytes(l)["score"]
+                        for l in range(batch.layers)]))
+    orig = batch.bt
+    out = {}
+    try:
+        for name, bt in (("random", orig), ("contiguous", contig)):
+            batch.bt = bt
+            gs = batch.capture("global", stages=(0,))
+            for i in range(args.warmup):
+                gs[i % batch.layers].replay()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(args.steps):
+                gs[i % batch.layers].replay()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) / args.steps * 1e3
+            out[name] = {"us": round(us, 2),
+                         "gbs": round(sb / (us * 1e-6) / 1e9, 1),
+                         "frac": round(sb / (us * 1e-6) / 1e9 / peak, 4)}
+            del gs
+    finally:
+        batch.bt = orig
+    out["score_bytes"] = int(sb)
+    out["note"] = ("derive + quad score of the timed batch, block table as "
+                   "timed (random) vs each request's blocks contiguous; same "
+                   "pages and bytes")
+    return out
 
 
 def batch_launches(batch, args):
@@ -1525,6 +1587,12 @@ def main():
                          "default: enough for about 1000 steps, 5..50)")
     ap.add_argument("--no-ctx32k", action="store_true",
                     help="skip the all-32K-context secondary measurement")
+    ap.add_argument("--quad-pipe", type=int, default=1, choices=[0, 1, 2],
+                    help="quad scorer choice (amass_quad_pipeline): 1 the "
+                         "library default, 2 pipelined wherever it applies, "
+                         "0 register-pipelined for every call")
+    ap.add_argument("--no-score-layout", action="store_true",
+                    help="skip the scorer's contiguous-block-table timing")
     ap.add_argument("--no-layouts", action="store_true",
                     help="N > 1: skip the weak and kv-head-sharded layouts")
     ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
@@ -1553,7 +1621,11 @@ def main():
         args.repeats = max(5, min(50, 1000 // max(args.steps, 1)))
     if args.impl == "reference":
         run_reference(args)
-    elif args.workload == "c5":
+        return
+    if args.quad_pipe != 1:
+        from amass_kv_b200 import _lib
+        _lib.load().amass_quad_pipeline(args.quad_pipe)
+    if args.workload == "c5":
         run_c5(args)
     elif args.workload in ("c2", "c4"):
         run_select_workload(args)

@@ -103,6 +103,28 @@ int amass_quad_score_derive(
     int head_dim, int page, int rank, int v_bits, int max_pages, int write_h,
     void* stream);
 
+/* quad_pipeline -- no counterpart in the reference (a choice between two
+ * kernels of this library for amass_quad_score / amass_quad_score_derive).
+ * The pipelined scorer (a producer warp streams each 16-page tile's summary
+ * rows into a shared-memory ring with bulk copies; eight consumer warps
+ * score them) serves calls with 8 kv heads, a V-code slice of at most 32
+ * bytes per lane (int4 rank 2 or int8 rank 1 at head_dim 128), 16-byte
+ * aligned scale slabs and a request table that fits beside the ring in
+ * 110 KB of shared memory (up to 1113 requests at head_dim 128).
+ * mode 1 (default): those calls from 32 requests up; mode 2: all of them;
+ * mode 0: none -- the register-pipelined scorer serves every call.  Both
+ * give bit-identical scores.  Other values only query.  Returns the
+ * previous mode.  Process-wide; not synchronised with calls in flight. */
+int amass_quad_pipeline(int mode);
+
+/* quad_pipeline_status -- no counterpart in the reference.  fault (may be
+ * null) receives the pipelined scorer's device fault word: 0, or 1 / 2 when a
+ * consumer / the producer warp gave up a bounded barrier wait (its scores
+ * are then incomplete); launches (may be null) the number of pipelined
+ * launches this process issued.  clear = 1 resets both.  Synchronous copy
+ * from the current device. */
+int amass_quad_pipeline_status(int* fault, long long* launches, int clear);
+
 /* nrm combine -- replaces the two passes of selection/quad_score.py:276-315
  * (CUDA twin quad_score_cuda.py:1446-1547): with hmax[r,kv,g] = the per-head
  * page max that amass_quad_score accumulated, score[r,kv,p] =
