@@ -1154,6 +1154,60 @@ def run_c5(args):
     hot_b = C5_KV * hot_slots * page_bytes
     stg_b = n_vslots * C5_KV * page_bytes
     saved = 1.0 - (kb + summ + hot_b + stg_b) / (2 * kb + summ)
+    # mem-kv: K tiered too (reference tier/tier.py:70-84 offload_k); the same
+    # batch and selection through a second tier whose pinned pools hold K and
+    # V, whole step score -> select -> plan -> decode with install
+    del tier, r5
+    torch.cuda.empty_cache()
+    tkv = T.Tier(num_layers=1, num_blocks=NB, n_kv=C5_KV, page=PAGE, d=D,
+                 hot_slots=hot_slots, max_reqs=n5, max_pages=MP,
+                 n_vslots=n_vslots, offload_k=True, device=dev)
+    tkv.pool.host[0].copy_(kv[:, 1].permute(0, 2, 1, 3).cpu())
+    tkv.pool_k.host[0].copy_(kv[:, 0].permute(0, 2, 1, 3).cpu())
+    tkv.residency.pool_valid.fill_(1)
+    rkv = tkv.residency
+
+    def kv_step():
+        stage(0)
+        stage(1)
+        rkv.gather_plan(0, st.page_table, st.page_cnt, bt, sl, n5)
+        T.mem_decode_ptrsel(qbuf, kv, bt, sl, st, out, tkv, 0, scale=scale,
+                            entry_slots=rkv.miss_pages, install=True)
+
+    set_q(0)
+    kv_step()
+    torch.cuda.synchronize()
+    gkv = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gkv):
+        kv_step()
+    for _ in range(warm):
+        next_q()
+        gkv.replay()
+    torch.cuda.synchronize()
+    kv_full, kv_eq, kv_miss, kv_sel = [], True, [], []
+    for i in range(steps):
+        next_q()
+        e0.record()
+        gkv.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        kv_full.append(e0.elapsed_time(e1) * 1e3)
+        kv_miss.append(int(rkv.fetch_cnt.sum()))
+        kv_sel.append(int(st.page_cnt.sum()))
+        graphs[5].replay()
+        torch.cuda.synchronize()
+        kv_eq = kv_eq and bool(torch.equal(out, out_res))
+    saved_kv = 1.0 - (summ + 2 * hot_b + 2 * stg_b) / (2 * kb + summ)
+    mem_kv = {"value": round(float(np.median(kv_full)), 2), "unit": UNIT,
+              "vram_saved_frac": round(saved_kv, 4),
+              "hit_rate": round(1.0 - float(np.sum(kv_miss)) /
+                                max(1, float(np.sum(kv_sel))), 4),
+              "miss_pages_per_step": round(float(np.mean(kv_miss)), 1),
+              "tiered_equals_resident": kv_eq,
+              "note": "K and V in pinned host pools, hot K and V slots; "
+                      "vram_saved = 1 - (summaries + hot K/V + staging K/V)"
+                      " / (K + V + summaries)"}
+    del gkv, tkv, rkv
     if rank == 0:
         hbm, kind = _peaks()
         line = {
@@ -1192,6 +1246,7 @@ def run_c5(args):
             "selected_pages_per_step": round(float(np.mean(selected)), 1),
             "vram_saved_frac": round(saved, 4),
             "tiered_equals_resident": equal,
+            "mem_kv": mem_kv,
             "hbm_peak_gbs": hbm, "peak_kind": kind,
             "clocks": clk.summary(),
         }
