@@ -109,8 +109,8 @@ int amass_quad_score_derive(
  * rows into a shared-memory ring with bulk copies; eight consumer warps
  * score them) serves calls with 8 kv heads, a V-code slice of at most 32
  * bytes per lane (int4 rank 2 or int8 rank 1 at head_dim 128), 16-byte
- * aligned scale slabs and a request table that fits beside the ring in
- * 110 KB of shared memory (up to 1113 requests at head_dim 128).
+ * aligned scale slabs (any batch up to the scorer's 4096 requests: the
+ * request table fits beside the ring).
  * mode 1 (default): those calls from 32 requests up; mode 2: all of them;
  * mode 0: none -- the register-pipelined scorer serves every call.  Both
  * give bit-identical scores.  Other values only query.  Returns the

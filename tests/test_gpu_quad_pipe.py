@@ -99,3 +99,27 @@ def test_pipelined_scorer_bitwise(n_req, combine, geom):
         else:
             np.testing.assert_allclose(pipe["score"][rq, :, :n],
                                        w.max(axis=1), rtol=1e-4, atol=1e-4)
+
+
+def test_pipelined_scorer_large_request_table():
+    """1200 short requests: the request table (prefix and page counts) in
+    shared memory beside the ring, most CTAs crossing many request
+    boundaries; scores equal the register-pipelined scorer's."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(7)
+    n_req = 1200
+    ctxs = tuple(int(x) for x in rng.integers(17, 120, n_req))
+    case = make_quad_case(77, n_req=n_req, n_kv=8, G=4, d=128, ctxs=ctxs,
+                          r=2, v_bits=4, heavy=1)
+    _status(clear=1)
+    wide = _run(case, dev, "nrm", 2)
+    assert _status() == (0, 1)
+    reg = _run(case, dev, "nrm", 0)
+    nsh = wide["nsh"]
+    for rq in range(n_req):
+        n = int(nsh[rq])
+        if n > 0:
+            assert np.array_equal(wide["score_h"][rq, ..., :n],
+                                  reg["score_h"][rq, ..., :n]), rq
