@@ -41,6 +41,7 @@ _SIGS = {
                                 _P, _F, _I, _I, _I, _I, _I, _I, _I, _I, _I,
                                 _P],
     "amass_quad_pipeline": [_I],
+    "amass_quad_pack": [_I],
     "amass_quad_pipeline_status": [_P, _P, _I],
     "amass_r8_score": [_P, _L, _L, _P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _P,
                        _P, _P, _F, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P],

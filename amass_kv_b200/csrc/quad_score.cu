@@ -300,26 +300,36 @@ struct QFrag {
   float sq[2];
 };
 
-template <int D>
+//
+// PK (G <= 4): packed limbs -- B column n < 4 holds the hi limb of query head
+// n, column n >= 4 the lo limb of head n - 4, both in bh (bl unused), so one
+// m16n8k32 forms both limb sums; lane quads c and c ^ 2 then hold the hi and
+// lo sums of the same heads 2(c & 1), 2(c & 1) + 1.
+template <int D, bool PK = false>
 AMASS_DEV void load_qfrag(QFrag<D>& f, const QuadArgs& a, int r, int h,
                           int lane) {
   constexpr int KS = D / 32;
   const int m = lane >> 2, c = lane & 3;
   const int H = a.n_kv * a.G;
-  const bool gv = m < a.G;
-  const int64_t qrow = (int64_t)r * H + h * a.G + (gv ? m : 0);
+  const int hm = PK ? (m & 3) : m;           // query head of this B column
+  const bool gv = hm < a.G;
+  const int64_t qrow = (int64_t)r * H + h * a.G + (gv ? hm : 0);
   const int8_t* qh = a.q8 + qrow * 2 * D + c * (D / 4);
   const int8_t* ql = qh + D;
+  if (PK && m >= 4) qh = ql;                 // the lo-limb columns
 #pragma unroll
   for (int i = 0; i < KS / 2; ++i) {
     const uint4 x = __ldg(reinterpret_cast<const uint4*>(qh) + i);
-    const uint4 y = __ldg(reinterpret_cast<const uint4*>(ql) + i);
     f.bh[2 * i][0] = gv ? x.x : 0u; f.bh[2 * i][1] = gv ? x.y : 0u;
     f.bh[2 * i + 1][0] = gv ? x.z : 0u; f.bh[2 * i + 1][1] = gv ? x.w : 0u;
-    f.bl[2 * i][0] = gv ? y.x : 0u; f.bl[2 * i][1] = gv ? y.y : 0u;
-    f.bl[2 * i + 1][0] = gv ? y.z : 0u; f.bl[2 * i + 1][1] = gv ? y.w : 0u;
+    if constexpr (!PK) {
+      const uint4 y = __ldg(reinterpret_cast<const uint4*>(ql) + i);
+      f.bl[2 * i][0] = gv ? y.x : 0u; f.bl[2 * i][1] = gv ? y.y : 0u;
+      f.bl[2 * i + 1][0] = gv ? y.z : 0u; f.bl[2 * i + 1][1] = gv ? y.w : 0u;
+    }
   }
-  const int g0 = min(2 * c, a.G - 1), g1 = min(2 * c + 1, a.G - 1);
+  const int cq = PK ? (c & 1) : c;
+  const int g0 = min(2 * cq, a.G - 1), g1 = min(2 * cq + 1, a.G - 1);
   const float* qsr = a.qs + (int64_t)r * H + h * a.G;
   f.sq[0] = __ldg(qsr + g0);
   f.sq[1] = __ldg(qsr + g1);
@@ -331,14 +341,16 @@ AMASS_DEV void load_qfrag(QFrag<D>& f, const QuadArgs& a, int r, int h,
 // lanes of a quad cover the row, so max|q| is a quad reduction.  Limbs and
 // scale are the q-limb prologue's, bit for bit: s = max|q|/16256,
 // qi = rn(q/s), hi = nearest(qi/128), lo = qi - 128*hi.
-template <int D>
+// PK: the packed-limb columns of load_qfrag.
+template <int D, bool PK = false>
 AMASS_DEV void qfrag_from_q(QFrag<D>& f, const QuadArgs& a, int r, int h,
                             int lane) {
   constexpr int SL = D / 4;                  // d values per lane
   const int m = lane >> 2, c = lane & 3;
-  const bool gv = m < a.G;
+  const int hm = PK ? (m & 3) : m;           // query head of this B column
+  const bool gv = hm < a.G;
   const __nv_bfloat16* qp = a.q + (int64_t)r * a.q_st +
-                            (int64_t)(h * a.G + (gv ? m : 0)) * a.q_sh + c * SL;
+                            (int64_t)(h * a.G + (gv ? hm : 0)) * a.q_sh + c * SL;
   float mx = 0.f;
 #pragma unroll
   for (int i = 0; i < SL; i += 8) {
@@ -370,11 +382,19 @@ AMASS_DEV void qfrag_from_q(QFrag<D>& f, const QuadArgs& a, int r, int h,
       wl[e >> 2] |= (uint32_t)(l8 & 0xff) << (8 * (e & 3));
     }
     const int s = i / 8;                      // words 2s, 2s + 1 of the slice
-    f.bh[s][0] = gv ? wh[0] : 0u; f.bh[s][1] = gv ? wh[1] : 0u;
-    f.bl[s][0] = gv ? wl[0] : 0u; f.bl[s][1] = gv ? wl[1] : 0u;
+    if constexpr (PK) {
+      const bool lo_col = m >= 4;
+      f.bh[s][0] = gv ? (lo_col ? wl[0] : wh[0]) : 0u;
+      f.bh[s][1] = gv ? (lo_col ? wl[1] : wh[1]) : 0u;
+    } else {
+      f.bh[s][0] = gv ? wh[0] : 0u; f.bh[s][1] = gv ? wh[1] : 0u;
+      f.bl[s][0] = gv ? wl[0] : 0u; f.bl[s][1] = gv ? wl[1] : 0u;
+    }
   }
-  // column scales: query heads 2c, 2c + 1 (the rows of lane quads 2c, 2c + 1)
-  const int g0 = min(2 * c, a.G - 1), g1 = min(2 * c + 1, a.G - 1);
+  // column scales: query heads 2c, 2c + 1 (the rows of lane quads 2c, 2c + 1;
+  // PK: 2(c & 1), 2(c & 1) + 1)
+  const int cq = PK ? (c & 1) : c;
+  const int g0 = min(2 * cq, a.G - 1), g1 = min(2 * cq + 1, a.G - 1);
   f.sq[0] = __shfl_sync(0xffffffffu, sq, 4 * g0);
   f.sq[1] = __shfl_sync(0xffffffffu, sq, 4 * g1);
 }
@@ -510,6 +530,120 @@ AMASS_DEV void score_item(const Item<D, R, VB>& it, const QFrag<D>& qf,
       if (pv && c == 0)
         a.score[((int64_t)it.r * a.n_kv + it.h) * a.MP + (half ? pb : pa)] = mx;
     }
+  }
+}
+
+// Packed-limb form of item_dots + score_item (G <= 4, qf from the PK loads):
+// one m16n8k32 per (component, k-step) gives the hi-limb sums in columns 0-3
+// and the lo-limb sums in columns 4-7.  Lane quads c and c ^ 2 swap half their
+// sums so each lane holds both limbs of one page row (c < 2: row m, c >= 2:
+// row m + 8) for heads 2(c & 1), 2(c & 1) + 1, and evaluates the same
+// expressions as score_item on them: the scores are bit-identical.
+template <int R, int VB, int K>
+struct VColsPK {
+  static AMASS_DEV void run(int (*acc)[4], const uint32_t* wa,
+                            const uint32_t* wb, const uint32_t* b) {
+    constexpr int RB = (VB == 8) ? R : R / 2;
+    uint32_t x[4];
+    x[0] = vcol4<R, VB, K>(wa);
+    x[1] = vcol4<R, VB, K>(wb);
+    x[2] = vcol4<R, VB, K>(wa + RB);
+    x[3] = vcol4<R, VB, K>(wb + RB);
+    mma_s8(acc[1 + K], x, b[0], b[1]);
+    if constexpr (K + 1 < R) VColsPK<R, VB, K + 1>::run(acc, wa, wb, b);
+  }
+};
+
+template <int D, int R, int VB, bool WRITE_H>
+AMASS_DEV void score_item_pk(const Item<D, R, VB>& it, const QFrag<D>& qf,
+                             const QuadArgs& a, int lane) {
+  using I = Item<D, R, VB>;
+  static_assert(I::V_PRE, "packed limbs: V slice in registers");
+  constexpr int KS = D / 32;
+  constexpr int RB = I::RB;
+  const int m = lane >> 2, c = lane & 3;
+  const int half = c >> 1;                   // 0: row m, 1: row m + 8
+  int acc[1 + R][4];
+#pragma unroll
+  for (int i = 0; i <= R; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0;
+  const uint32_t* mwa = reinterpret_cast<const uint32_t*>(it.mu[0]);
+  const uint32_t* mwb = reinterpret_cast<const uint32_t*>(it.mu[1]);
+  const uint32_t* va = reinterpret_cast<const uint32_t*>(it.v[0]);
+  const uint32_t* vb = reinterpret_cast<const uint32_t*>(it.v[1]);
+#pragma unroll
+  for (int s = 0; s < KS; ++s) {
+    const uint32_t am[4] = {mwa[2 * s], mwb[2 * s], mwa[2 * s + 1], mwb[2 * s + 1]};
+    mma_s8(acc[0], am, qf.bh[s][0], qf.bh[s][1]);
+    uint32_t wva[2 * RB], wvb[2 * RB];
+#pragma unroll
+    for (int j = 0; j < 2 * RB; ++j) {
+      wva[j] = va[s * 2 * RB + j];
+      wvb[j] = vb[s * 2 * RB + j];
+    }
+    VColsPK<R, VB, 0>::run(acc, wva, wvb, qf.bh[s]);
+  }
+  // hi sums of row m + 8 go to the lo lanes, lo sums of row m to the hi lanes
+  int hi[1 + R][2], lo[1 + R][2];
+#pragma unroll
+  for (int i = 0; i <= R; ++i)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int got = __shfl_xor_sync(0xffffffffu, half ? acc[i][j] : acc[i][2 + j], 2);
+      hi[i][j] = half ? got : acc[i][j];
+      lo[i][j] = half ? acc[i][2 + j] : got;
+    }
+  const float* sq = qf.sq;
+  constexpr float vdiv = (VB == 8) ? 1.f : 1.f / 16.f;
+  const float mus = half ? __high2float(it.mus) : __low2float(it.mus);
+  // this lane's row of scale words (selects: a runtime row index into the
+  // item's arrays would put them in local memory)
+  uint32_t vsw[I::RW], s2w[I::RW];
+#pragma unroll
+  for (int w = 0; w < I::RW; ++w) {
+    vsw[w] = half ? it.vs[1][w] : it.vs[0][w];
+    s2w[w] = half ? it.s2[1][w] : it.s2[0][w];
+  }
+  auto h16 = [](uint32_t w, int k) {
+    return __half2float(__ushort_as_half((uint16_t)((k & 1) ? (w >> 16) : w)));
+  };
+  float S[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    float quad = 0.f;
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      const float vs = h16(vsw[k >> 1], k);
+      const float s2 = h16(s2w[k >> 1], k);
+      const float qt = (float)(128 * hi[1 + k][j] + lo[1 + k][j]) *
+                       (sq[j] * vdiv) * vs;
+      quad += s2 * qt * qt;
+    }
+    const float qmu = (float)(128 * hi[0][j] + lo[0][j]) * sq[j];
+    S[j] = qmu * mus * a.scale + quad * a.coef;
+  }
+  const int p = it.p0 + m + 8 * half;
+  const bool pv = half ? it.vb : it.va;
+  const int cq = c & 1;
+  if constexpr (WRITE_H) {
+    float* base = a.score_h + ((int64_t)it.r * a.n_kv + it.h) * a.G * a.SHS;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int g = 2 * cq + j;
+      float mx = -INFINITY;
+      if (g < a.G && pv) { base[(int64_t)g * a.SHS + p] = S[j]; mx = S[j]; }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      if (lane == cq && g < a.G && mx > -INFINITY)
+        atomic_max_float(a.hmax + ((int64_t)it.r * a.n_kv + it.h) * a.G + g, mx);
+    }
+  } else {
+    float mx = (2 * cq < a.G) ? S[0] : -INFINITY;
+    if (2 * cq + 1 < a.G) mx = fmaxf(mx, S[1]);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    if (pv && cq == 0)
+      a.score[((int64_t)it.r * a.n_kv + it.h) * a.MP + p] = mx;
   }
 }
 
@@ -686,7 +820,7 @@ AMASS_DEV void lds_halves(uint32_t* w, uint32_t p) {
   }
 }
 
-template <int D, int R, int VB, bool WRITE_H, bool QIN, int S>
+template <int D, int R, int VB, bool WRITE_H, bool QIN, int S, bool PK>
 __global__ void __launch_bounds__(kPipeThreads, 2)
 quad_score_pipe_kernel(QuadArgs a) {
   using PL = PipeLayout<D, R, VB>;
@@ -839,11 +973,12 @@ quad_score_pipe_kernel(QuadArgs a) {
     __syncwarp();
     if (lane == 0) mbar_arrive(empty0 + 8 * s);
     if (cr != qr) {
-      if constexpr (QIN) qfrag_from_q(qf, a, cr, h, lane);
-      else load_qfrag(qf, a, cr, h, lane);
+      if constexpr (QIN) qfrag_from_q<D, PK>(qf, a, cr, h, lane);
+      else load_qfrag<D, PK>(qf, a, cr, h, lane);
       qr = cr;
     }
-    score_item<D, R, VB, WRITE_H>(it, qf, a, lane);
+    if constexpr (PK) score_item_pk<D, R, VB, WRITE_H>(it, qf, a, lane);
+    else score_item<D, R, VB, WRITE_H>(it, qf, a, lane);
   }
 }
 
@@ -1401,6 +1536,9 @@ constexpr int kQuadQinReq = 32;
 // for longer than the scorer gains.
 int g_quad_pipe_mode = 1;
 long long g_quad_pipe_launches = 0;   // host count of pipelined launches
+// amass_quad_pack: the pipelined scorer's packed-limb form for G <= 4 (1,
+// default) or the two-limb form (0); bit-identical scores.
+int g_quad_pack = 1;
 
 // The pipelined scorer when the geometry allows it: 8 kv heads, a lane's V
 // slice of at most 32 bytes (int4 rank 2 or int8 rank 1 at head_dim 128),
@@ -1424,13 +1562,17 @@ int launch_quad_pipe(const QuadArgs& a, bool write_h, bool qin,
     const size_t smem = pipe_smem_bytes<D, R, VB, S>(a.n_req);
     if (smem > 110 * 1024) return -1;
     using K = void (*)(QuadArgs);
+    // G <= 4: packed limbs (half the MMAs, half the epilogue per lane)
+    const bool pk = a.G <= 4 && g_quad_pack;
     K k;
-    if (qin) k = write_h ? quad_score_pipe_kernel<D, R, VB, true, true, S>
-                         : quad_score_pipe_kernel<D, R, VB, false, true, S>;
-    else k = write_h ? quad_score_pipe_kernel<D, R, VB, true, false, S>
-                     : quad_score_pipe_kernel<D, R, VB, false, false, S>;
-    static unsigned long long attr_set[4] = {0, 0, 0, 0};
-    if (first_on_device(attr_set[(write_h ? 1 : 0) + (qin ? 2 : 0)]))
+#define AMASS_PIPE_K(W, Q)                                              \
+    (pk ? quad_score_pipe_kernel<D, R, VB, W, Q, S, true>               \
+        : quad_score_pipe_kernel<D, R, VB, W, Q, S, false>)
+    if (qin) k = write_h ? AMASS_PIPE_K(true, true) : AMASS_PIPE_K(false, true);
+    else k = write_h ? AMASS_PIPE_K(true, false) : AMASS_PIPE_K(false, false);
+#undef AMASS_PIPE_K
+    static unsigned long long attr_set[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (first_on_device(attr_set[(write_h ? 1 : 0) + (qin ? 2 : 0) + (pk ? 4 : 0)]))
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            110 * 1024);
     QuadArgs b = a;
@@ -1776,6 +1918,13 @@ extern "C" int amass_quad_pipeline(int mode) {
   using namespace amass;
   const int prev = g_quad_pipe_mode;
   if (mode >= 0 && mode <= 2) g_quad_pipe_mode = mode;
+  return prev;
+}
+
+extern "C" int amass_quad_pack(int on) {
+  using namespace amass;
+  const int prev = g_quad_pack;
+  if (on == 0 || on == 1) g_quad_pack = on;
   return prev;
 }
 

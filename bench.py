@@ -1646,6 +1646,10 @@ def main():
                     help="quad scorer choice (amass_quad_pipeline): 1 the "
                          "library default, 2 pipelined wherever it applies, "
                          "0 register-pipelined for every call")
+    ap.add_argument("--quad-pack", type=int, default=1, choices=[0, 1],
+                    help="pipelined scorer limb form (amass_quad_pack): 1 "
+                         "packed limbs for G <= 4 (library default), 0 the "
+                         "two-limb form")
     ap.add_argument("--no-score-layout", action="store_true",
                     help="skip the scorer's contiguous-block-table timing")
     ap.add_argument("--no-layouts", action="store_true",
@@ -1680,6 +1684,9 @@ def main():
     if args.quad_pipe != 1:
         from amass_kv_b200 import _lib
         _lib.load().amass_quad_pipeline(args.quad_pipe)
+    if args.quad_pack != 1:
+        from amass_kv_b200 import _lib
+        _lib.load().amass_quad_pack(args.quad_pack)
     if args.workload == "c5":
         run_c5(args)
     elif args.workload in ("c2", "c4"):

@@ -117,6 +117,15 @@ int amass_quad_score_derive(
  * previous mode.  Process-wide; not synchronised with calls in flight. */
 int amass_quad_pipeline(int mode);
 
+/* quad_pack -- no counterpart in the reference (a choice between two forms
+ * of the pipelined scorer).  on = 1 (default): when a kv head has at most 4
+ * query heads, the two int8 limbs of q share one integer MMA's 8 columns
+ * (hi limbs in columns 0-3, lo limbs in 4-7), half the MMAs and half the
+ * per-lane epilogue of the two-limb form; on = 0: the two-limb form.  Both
+ * give bit-identical scores.  Other values only query.  Returns the
+ * previous setting.  Process-wide; not synchronised with calls in flight. */
+int amass_quad_pack(int on);
+
 /* quad_pipeline_status -- no counterpart in the reference.  fault (may be
  * null) receives the pipelined scorer's device fault word: 0, or 1 / 2 when a
  * consumer / the producer warp gave up a bounded barrier wait (its scores

@@ -31,15 +31,17 @@ def _status(clear=0):
     return f.value, n.value
 
 
-def _run(case, dev, combine, mode):
+def _run(case, dev, combine, mode, pack=1):
     lib = _lib.load()
     prev = lib.amass_quad_pipeline(mode)
+    prev_pack = lib.amass_quad_pack(pack)
     try:
         c = DevCase.from_case(case, dev, budget=0.1, combine=combine)
         S.select_pages_quad(c.st, 0, c.q, c.bt, c.sl, c.n_req, c.scale)
         torch.cuda.synchronize()
     finally:
         lib.amass_quad_pipeline(prev)
+        lib.amass_quad_pack(prev_pack)
     st = c.st
     return dict(nsh=st.n_sel_hi.cpu().numpy(), score=st.score.cpu().numpy(),
                 score_h=(st.score_h.cpu().numpy() if st.score_h is not None
@@ -99,6 +101,39 @@ def test_pipelined_scorer_bitwise(n_req, combine, geom):
         else:
             np.testing.assert_allclose(pipe["score"][rq, :, :n],
                                        w.max(axis=1), rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("G", [4, 3, 2, 1])
+@pytest.mark.parametrize("n_req", [9, 40])
+def test_packed_limbs_bitwise(G, n_req):
+    """Packed limbs (G <= 4: hi and lo limbs in one MMA's 8 columns, lane
+    quads c and c ^ 2 swapping half their sums) against the pipelined
+    scorer's two-limb form: per-head scores and page maxima bitwise equal,
+    for every G the packed form serves, both q-limb forms, both combines."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(300 + G + n_req)
+    ctxs = [int(x) for x in rng.integers(17, 2400, n_req)]
+    ctxs[0] = 16 * 21 + 3                        # ragged last tile
+    case = make_quad_case(91 + G + n_req, n_req=n_req, n_kv=8, G=G, d=128,
+                          ctxs=tuple(ctxs), r=2, v_bits=4, heavy=2)
+    for combine in ("nrm", "max"):
+        _status(clear=1)
+        pk = _run(case, dev, combine, 2, pack=1)
+        two = _run(case, dev, combine, 2, pack=0)
+        assert _status() == (0, 2)
+        nsh = pk["nsh"]
+        for rq in range(n_req):
+            n = int(nsh[rq])
+            if n <= 0:
+                continue
+            if combine == "nrm":
+                assert np.array_equal(pk["score_h"][rq, ..., :n],
+                                      two["score_h"][rq, ..., :n]), rq
+            assert np.array_equal(pk["score"][rq, :, :n],
+                                  two["score"][rq, :, :n]), rq
+        assert np.array_equal(pk["cnt"], two["cnt"])
 
 
 def test_pipelined_scorer_large_request_table():
