@@ -554,9 +554,14 @@ struct VColsPK {
   }
 };
 
+// WRITE_H: the per-head page maxima are kept per lane in rmx[2] (heads
+// 2(c & 1), 2(c & 1) + 1) across the tiles of one request and folded into
+// hmax by flush_hmax when the warp moves to another request or finishes --
+// one warp reduction and one atomic per (request, head) run instead of per
+// tile.  max is exact, so hmax is the same.
 template <int D, int R, int VB, bool WRITE_H>
 AMASS_DEV void score_item_pk(const Item<D, R, VB>& it, const QFrag<D>& qf,
-                             const QuadArgs& a, int lane) {
+                             const QuadArgs& a, int lane, float* rmx) {
   using I = Item<D, R, VB>;
   static_assert(I::V_PRE, "packed limbs: V slice in registers");
   constexpr int KS = D / 32;
@@ -629,14 +634,10 @@ AMASS_DEV void score_item_pk(const Item<D, R, VB>& it, const QFrag<D>& qf,
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const int g = 2 * cq + j;
-      float mx = -INFINITY;
-      if (g < a.G && pv) { base[(int64_t)g * a.SHS + p] = S[j]; mx = S[j]; }
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-      if (lane == cq && g < a.G && mx > -INFINITY)
-        atomic_max_float(a.hmax + ((int64_t)it.r * a.n_kv + it.h) * a.G + g, mx);
+      if (g < a.G && pv) {
+        base[(int64_t)g * a.SHS + p] = S[j];
+        rmx[j] = fmaxf(rmx[j], S[j]);
+      }
     }
   } else {
     float mx = (2 * cq < a.G) ? S[0] : -INFINITY;
@@ -644,6 +645,25 @@ AMASS_DEV void score_item_pk(const Item<D, R, VB>& it, const QFrag<D>& qf,
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     if (pv && cq == 0)
       a.score[((int64_t)it.r * a.n_kv + it.h) * a.MP + p] = mx;
+  }
+}
+
+// Folds the lanes' running maxima of score_item_pk into hmax of (r, h) and
+// resets them (whole warp).
+AMASS_DEV void flush_hmax(const QuadArgs& a, int r, int h, int lane,
+                          float* rmx) {
+  const int cq = lane & 1;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    float mx = rmx[j];
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    const int g = 2 * cq + j;
+    if (lane == cq && g < a.G && mx > -INFINITY)
+      atomic_max_float(a.hmax + ((int64_t)r * a.n_kv + h) * a.G + g, mx);
+    rmx[j] = -INFINITY;
   }
 }
 
@@ -820,6 +840,7 @@ AMASS_DEV void lds_halves(uint32_t* w, uint32_t p) {
   }
 }
 
+// PK: packed limbs (score_item_pk), else the two-limb form
 template <int D, int R, int VB, bool WRITE_H, bool QIN, int S, bool PK>
 __global__ void __launch_bounds__(kPipeThreads, 2)
 quad_score_pipe_kernel(QuadArgs a) {
@@ -932,6 +953,8 @@ quad_score_pipe_kernel(QuadArgs a) {
   const int m = lane >> 2, c = lane & 3;
   int cr = rq, qr = -1;
   QFrag<D> qf;
+  float rmx[2] = {-INFINITY, -INFINITY};   // PK: running per-head maxima
+  bool done = true;
   for (int t = t_lo; t < t_hi; ++t) {
     const int i = t - t_lo, s = i % S;
     while (prefix[cr + 1] <= t) ++cr;
@@ -943,8 +966,10 @@ quad_score_pipe_kernel(QuadArgs a) {
     it.va = it.p0 + m < nsh;
     it.vb = it.p0 + m + 8 < nsh;
     it.rowa = it.rowb = 0;
-    if (!mbar_wait(full0 + 8 * s, (i / S) & 1)) {
-      atomicCAS(&g_quad_pipe_fault, 0, 1);
+    // warp-uniform verdict: the score epilogue shuffles over all 32 lanes
+    if (!__all_sync(0xffffffffu, mbar_wait(full0 + 8 * s, (i / S) & 1))) {
+      if (lane == 0) atomicCAS(&g_quad_pipe_fault, 0, 1);
+      done = false;
       break;
     }
     const uint32_t st = ring + s * PL::STAGE;
@@ -973,13 +998,17 @@ quad_score_pipe_kernel(QuadArgs a) {
     __syncwarp();
     if (lane == 0) mbar_arrive(empty0 + 8 * s);
     if (cr != qr) {
+      if constexpr (PK && WRITE_H)
+        if (qr >= 0) flush_hmax(a, qr, h, lane, rmx);
       if constexpr (QIN) qfrag_from_q<D, PK>(qf, a, cr, h, lane);
       else load_qfrag<D, PK>(qf, a, cr, h, lane);
       qr = cr;
     }
-    if constexpr (PK) score_item_pk<D, R, VB, WRITE_H>(it, qf, a, lane);
+    if constexpr (PK) score_item_pk<D, R, VB, WRITE_H>(it, qf, a, lane, rmx);
     else score_item<D, R, VB, WRITE_H>(it, qf, a, lane);
   }
+  if constexpr (PK && WRITE_H)
+    if (done && qr >= 0) flush_hmax(a, qr, h, lane, rmx);
 }
 
 // ---------------------------------------------------------------------------
@@ -1563,7 +1592,7 @@ int launch_quad_pipe(const QuadArgs& a, bool write_h, bool qin,
     if (smem > 110 * 1024) return -1;
     using K = void (*)(QuadArgs);
     // G <= 4: packed limbs (half the MMAs, half the epilogue per lane)
-    const bool pk = a.G <= 4 && g_quad_pack;
+    const int pk = a.G <= 4 ? g_quad_pack : 0;
     K k;
 #define AMASS_PIPE_K(W, Q)                                              \
     (pk ? quad_score_pipe_kernel<D, R, VB, W, Q, S, true>               \
@@ -1571,8 +1600,8 @@ int launch_quad_pipe(const QuadArgs& a, bool write_h, bool qin,
     if (qin) k = write_h ? AMASS_PIPE_K(true, true) : AMASS_PIPE_K(false, true);
     else k = write_h ? AMASS_PIPE_K(true, false) : AMASS_PIPE_K(false, false);
 #undef AMASS_PIPE_K
-    static unsigned long long attr_set[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (first_on_device(attr_set[(write_h ? 1 : 0) + (qin ? 2 : 0) + (pk ? 4 : 0)]))
+    static unsigned long long attr_set[8] = {};
+    if (first_on_device(attr_set[(write_h ? 1 : 0) + (qin ? 2 : 0) + 4 * pk]))
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            110 * 1024);
     QuadArgs b = a;

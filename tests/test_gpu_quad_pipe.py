@@ -107,9 +107,10 @@ def test_pipelined_scorer_bitwise(n_req, combine, geom):
 @pytest.mark.parametrize("n_req", [9, 40])
 def test_packed_limbs_bitwise(G, n_req):
     """Packed limbs (G <= 4: hi and lo limbs in one MMA's 8 columns, lane
-    quads c and c ^ 2 swapping half their sums) against the pipelined
-    scorer's two-limb form: per-head scores and page maxima bitwise equal,
-    for every G the packed form serves, both q-limb forms, both combines."""
+    quads c and c ^ 2 swapping half their sums; per-head maxima folded once
+    per request run) against the pipelined scorer's two-limb form: per-head
+    scores, page maxima and the selected pages bitwise equal, for every G the
+    packed form serves, both q-limb forms, both combines."""
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     dev = torch.device("cuda", 0)
@@ -120,9 +121,8 @@ def test_packed_limbs_bitwise(G, n_req):
                           ctxs=tuple(ctxs), r=2, v_bits=4, heavy=2)
     for combine in ("nrm", "max"):
         _status(clear=1)
-        pk = _run(case, dev, combine, 2, pack=1)
         two = _run(case, dev, combine, 2, pack=0)
-        assert _status() == (0, 2)
+        pk = _run(case, dev, combine, 2, pack=1)
         nsh = pk["nsh"]
         for rq in range(n_req):
             n = int(nsh[rq])
@@ -134,6 +134,8 @@ def test_packed_limbs_bitwise(G, n_req):
             assert np.array_equal(pk["score"][rq, :, :n],
                                   two["score"][rq, :, :n]), rq
         assert np.array_equal(pk["cnt"], two["cnt"])
+        assert np.array_equal(pk["pages"], two["pages"])
+        assert _status() == (0, 2)
 
 
 def test_pipelined_scorer_large_request_table():
