@@ -716,7 +716,8 @@ constexpr int quad_min_blocks() {
 // QIN: the q limbs are split from the bf16 query by each warp (and the page
 // parameters derived in the prologue when asked) -- no limb launch; else
 // they come from q_limbs_kernel.
-template <int D, int R, int VB, bool WRITE_H, bool QIN>
+// PK: packed limbs (score_item_pk; G <= 4, V slice in registers)
+template <int D, int R, int VB, bool WRITE_H, bool QIN, bool PK = false>
 __global__ void __launch_bounds__(kQuadWarps * 32, (quad_min_blocks<D, R, VB>()))
 quad_score_kernel(QuadArgs a) {
   grid_dep_wait();     // inputs written by the previous kernel
@@ -752,6 +753,7 @@ quad_score_kernel(QuadArgs a) {
   Item<D, R, VB> cur, nxt, nn;
   QFrag<D> qf;
   int qr = -1;
+  float rmx[2] = {-INFINITY, -INFINITY};   // PK: running per-head maxima
   int t = t_lo;
   load_idx(cur, a, prefix, nshs, t * a.n_kv + h, lane, &rh);
   load_data(cur, a, lane);
@@ -761,16 +763,20 @@ quad_score_kernel(QuadArgs a) {
     if (t + 2 < t_hi) load_idx(nn, a, prefix, nshs, (t + 2) * a.n_kv + h, lane, &rh);
     if (more) load_data(nxt, a, lane);
     if (cur.r != qr) {
-      if constexpr (QIN) qfrag_from_q(qf, a, cur.r, h, lane);
-      else load_qfrag(qf, a, cur.r, h, lane);
+      if constexpr (PK && WRITE_H)
+        if (qr >= 0) flush_hmax(a, qr, h, lane, rmx);
+      if constexpr (QIN) qfrag_from_q<D, PK>(qf, a, cur.r, h, lane);
+      else load_qfrag<D, PK>(qf, a, cur.r, h, lane);
       qr = cur.r;
     }
-    score_item<D, R, VB, WRITE_H>(cur, qf, a, lane);
+    if constexpr (PK) score_item_pk<D, R, VB, WRITE_H>(cur, qf, a, lane, rmx);
+    else score_item<D, R, VB, WRITE_H>(cur, qf, a, lane);
     if (!more) break;
     cur = nxt;
     nxt = nn;
     ++t;
   }
+  if constexpr (PK && WRITE_H) flush_hmax(a, qr, h, lane, rmx);
 }
 
 // ---------------------------------------------------------------------------
@@ -1565,7 +1571,7 @@ constexpr int kQuadQinReq = 32;
 // for longer than the scorer gains.
 int g_quad_pipe_mode = 1;
 long long g_quad_pipe_launches = 0;   // host count of pipelined launches
-// amass_quad_pack: the pipelined scorer's packed-limb form for G <= 4 (1,
+// amass_quad_pack: the quad scorers' packed-limb form for G <= 4 (1,
 // default) or the two-limb form (0); bit-identical scores.
 int g_quad_pack = 1;
 
@@ -1629,12 +1635,17 @@ int launch_quad(const QuadArgs& a, bool write_h, cudaStream_t st) {
   }
   using K = void (*)(QuadArgs);
   K k;
-  if (qin) k = write_h ? quad_score_kernel<D, R, VB, true, true>
-                       : quad_score_kernel<D, R, VB, false, true>;
-  else k = write_h ? quad_score_kernel<D, R, VB, true, false>
-                   : quad_score_kernel<D, R, VB, false, false>;
-  static int per_sm[4] = {0, 0, 0, 0};
-  int& ps = per_sm[(write_h ? 1 : 0) + (qin ? 2 : 0)];
+  // G <= 4 with the V slice in registers: packed limbs
+  constexpr bool kPkOk = Item<D, R, VB>::V_PRE;
+  const bool pk = kPkOk && a.G <= 4 && g_quad_pack;
+#define AMASS_QUAD_K(W, Q)                                               \
+    (pk ? quad_score_kernel<D, R, VB, W, Q, kPkOk>                       \
+        : quad_score_kernel<D, R, VB, W, Q, false>)
+  if (qin) k = write_h ? AMASS_QUAD_K(true, true) : AMASS_QUAD_K(false, true);
+  else k = write_h ? AMASS_QUAD_K(true, false) : AMASS_QUAD_K(false, false);
+#undef AMASS_QUAD_K
+  static int per_sm[8] = {};
+  int& ps = per_sm[(write_h ? 1 : 0) + (qin ? 2 : 0) + (pk ? 4 : 0)];
   if (ps == 0) {
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ps, k, kQuadWarps * 32, 0);
     if (ps < 1) ps = 1;

@@ -118,8 +118,10 @@ int amass_quad_score_derive(
 int amass_quad_pipeline(int mode);
 
 /* quad_pack -- no counterpart in the reference (a choice between two forms
- * of the pipelined scorer).  on = 1 (default): when a kv head has at most 4
- * query heads, the two int8 limbs of q share one integer MMA's 8 columns
+ * of the quad scorers).  on = 1 (default): when a kv head has at most 4
+ * query heads and a lane's V-code slice fits its registers (at head_dim
+ * 128: int4 V up to rank 4, int8 V up to rank 2), the two int8 limbs of q
+ * share one integer MMA's 8 columns
  * (hi limbs in columns 0-3, lo limbs in 4-7), half the MMAs and half the
  * per-lane epilogue of the two-limb form; on = 0: the two-limb form.  Both
  * give bit-identical scores.  Other values only query.  Returns the
