@@ -94,6 +94,7 @@ class ClockSampler:
         self.samples, self.reasons = [], 0
         self.max_mhz = None
         self._stop = threading.Event()
+        self._lock = threading.Lock()
         try:
             import pynvml
             import torch
@@ -108,15 +109,26 @@ class ClockSampler:
         except Exception:
             self._nv = None
 
-    def _run(self):
+    def sample(self) -> bool:
+        """One reading (also called from the launching thread between timed
+        loops, where the sampler thread may not get the GIL while the host
+        queues graph replays)."""
         nv = self._nv
+        if nv is None:
+            return False
+        try:
+            mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+            rs = int(nv.nvmlDeviceGetCurrentClocksEventReasons(self._h))
+        except Exception:
+            return False
+        with self._lock:
+            self.samples.append(mhz)
+            self.reasons |= rs
+        return True
+
+    def _run(self):
         while not self._stop.is_set():
-            try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(
-                    self._h, nv.NVML_CLOCK_SM))
-                self.reasons |= int(
-                    nv.nvmlDeviceGetCurrentClocksEventReasons(self._h))
-            except Exception:
+            if not self.sample():
                 break
             time.sleep(0.001)
 
@@ -298,6 +310,8 @@ def _timed_repeats(run_one, steps, repeats, world, dev, clk_index=None):
             run_one(i)
             i += 1
         e1.record()
+        if clk is not None:
+            clk.sample()      # between loops: outside every timed interval
     if clk is not None:
         # wait with the GIL released so the sampler thread runs while the
         # queued steps execute
