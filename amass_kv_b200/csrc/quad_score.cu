@@ -300,7 +300,6 @@ struct QFrag {
   float sq[2];
 };
 
-//
 // PK (G <= 4): packed limbs -- B column n < 4 holds the hi limb of query head
 // n, column n >= 4 the lo limb of head n - 4, both in bh (bl unused), so one
 // m16n8k32 forms both limb sums; lane quads c and c ^ 2 then hold the hi and
